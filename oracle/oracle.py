@@ -1,0 +1,354 @@
+"""ctypes bindings for the checker libraries.
+
+TEST INFRASTRUCTURE ONLY: imported by tests/, the smoke entry and bench.py's
+cpu_baseline / reference legs.  The product package never imports this.
+
+  * ``Oracle`` wraps ``oracle/_build/libhxoracle.so``: the C restatement of the
+    reference's CPU arithmetic (oracle/hx_oracle.c).
+  * ``Reference`` wraps ``oracle/_ref/libhexaref.so``: the reference's own CPU
+    sources compiled by oracle/Makefile (present only where the HexaTrain tree
+    was available at build time; the built file travels with the repository
+    snapshot).
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+from dataclasses import dataclass
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ORACLE_SO = os.path.join(HERE, "_build", "libhxoracle.so")
+REF_SO = os.path.join(HERE, "_ref", "libhexaref.so")
+
+_f32p = np.ctypeslib.ndpointer(dtype=np.float32, flags="C_CONTIGUOUS")
+_u32p = np.ctypeslib.ndpointer(dtype=np.uint32, flags="C_CONTIGUOUS")
+_u8p = np.ctypeslib.ndpointer(dtype=np.uint8, flags="C_CONTIGUOUS")
+
+
+class LmConfig(C.Structure):
+    """Mirror of hxo_lm_config (oracle/hx_oracle.h)."""
+
+    _fields_ = [
+        ("vocab", C.c_uint32),
+        ("tokens", C.c_uint32),
+        ("dim", C.c_uint32),
+        ("ffn", C.c_uint32),
+        ("layers", C.c_uint32),
+        ("heads", C.c_uint32),
+        ("eps", C.c_float),
+        ("learned_position", C.c_int),
+    ]
+
+    @staticmethod
+    def make(V, T, D, F, L, H, eps=1e-5, learned_position=False):
+        return LmConfig(V, T, D, F, L, H, eps, int(bool(learned_position)))
+
+
+def build(quiet: bool = True) -> None:
+    """Build the checker libraries with oracle/Makefile (reference part only
+    when the HexaTrain tree is present)."""
+    out = subprocess.run(["make", "-s", "-C", HERE, "all"], capture_output=True, text=True)
+    if out.returncode != 0:
+        raise RuntimeError("oracle build failed:\n" + out.stdout + out.stderr)
+    if not quiet:
+        print(out.stdout)
+
+
+def _ptr(a):
+    return None if a is None else a.ctypes.data_as(C.c_void_p)
+
+
+def param_count(cfg: LmConfig) -> int:
+    V, T, D, F, L = cfg.vocab, cfg.tokens, cfg.dim, cfg.ffn, cfg.layers
+    return 2 * V * D + (T * D if cfg.learned_position else 0) + L * (4 * D * D + 4 * D + 2 * D * F)
+
+
+@dataclass
+class MlpStep:
+    loss: float
+    w1_next: np.ndarray
+    w2_next: np.ndarray
+    z1: np.ndarray
+    h: np.ndarray
+    p: np.ndarray
+    e: np.ndarray
+    dp: np.ndarray
+    dw2: np.ndarray
+    dh: np.ndarray
+    mask: np.ndarray
+    dz1: np.ndarray
+    dw1: np.ndarray
+
+
+@dataclass
+class LmStep:
+    loss: float
+    accuracy: float
+    grads: np.ndarray
+    logits: np.ndarray
+    probs: np.ndarray
+    dlogits: np.ndarray
+    output: np.ndarray
+    layer_input_grads: np.ndarray
+    head_probs: np.ndarray
+
+
+def _mlp_call(fn, B, I, H, O, x, y, w1, w2, lr):
+    f = lambda *s: np.zeros(s, np.float32)
+    out = MlpStep(0.0, f(I, H), f(H, O), f(B, H), f(B, H), f(B, O), f(B, O), f(B, O),
+                  f(H, O), f(B, H), np.zeros((B, H), np.uint8), f(B, H), f(I, H))
+    loss = C.c_float()
+    rc = fn(B, I, H, O, *[np.ascontiguousarray(a, np.float32) for a in (x, y, w1, w2)], C.c_float(lr),
+            C.byref(loss), out.w1_next, out.w2_next, out.z1, out.h, out.p, out.e, out.dp, out.dw2,
+            out.dh, out.mask, out.dz1, out.dw1)
+    if rc != 0:
+        raise ValueError("mlp step rejected its arguments")
+    out.loss = loss.value
+    return out
+
+
+class Oracle:
+    """The C restatement (oracle/hx_oracle.c)."""
+
+    def __init__(self, path: str = ORACLE_SO):
+        if not os.path.exists(path):
+            build()
+        self.lib = L = C.CDLL(path)
+        L.hxo_mlp_step.restype = C.c_int
+        L.hxo_mlp_step.argtypes = [C.c_int] * 4 + [_f32p] * 4 + [C.c_float, C.POINTER(C.c_float)] + \
+            [_f32p] * 9 + [_u8p, _f32p, _f32p]
+        L.hxo_matmul.argtypes = [C.c_int] * 3 + [_f32p] * 3
+        L.hxo_mse.restype = C.c_float
+        L.hxo_mse.argtypes = [C.c_size_t, _f32p, _f32p]
+        L.hxo_linear_forward_backward.restype = C.c_float
+        L.hxo_linear_forward_backward.argtypes = [C.c_int, C.c_int] + [_f32p] * 8
+        L.hxo_sgd.argtypes = [C.c_size_t, _f32p, _f32p, C.c_float]
+        L.hxo_lm_param_count.restype = C.c_size_t
+        L.hxo_lm_param_count.argtypes = [C.POINTER(LmConfig)]
+        L.hxo_lm_fixed_position.argtypes = [C.POINTER(LmConfig), _f32p]
+        L.hxo_lm_forward_backward.restype = C.c_int
+        L.hxo_lm_forward_backward.argtypes = [C.POINTER(LmConfig), _u32p, _u32p, _f32p,
+                                              C.POINTER(C.c_float), C.POINTER(C.c_float), _f32p] + [C.c_void_p] * 7
+        L.hxo_lm_batch_gradients.restype = C.c_int
+        L.hxo_lm_batch_gradients.argtypes = [C.POINTER(LmConfig), C.c_int, _u32p, _f32p, _f32p,
+                                             C.POINTER(C.c_float), C.c_int]
+        L.hxo_adam.argtypes = [C.c_size_t] + [_f32p] * 4 + [C.c_float] * 6 + [C.c_void_p] * 5
+        L.hxo_adam_correction.restype = C.c_float
+        L.hxo_adam_correction.argtypes = [C.c_double, C.c_int]
+        L.hxo_muon.argtypes = [C.c_int, C.c_int] + [_f32p] * 3 + [C.c_float, C.c_float, C.c_int, C.c_int,
+                                                                   C.c_float, C.c_float, C.c_float, C.c_int,
+                                                                   _f32p, _f32p]
+        L.hxo_round_bf16.restype = C.c_float
+        L.hxo_round_bf16.argtypes = [C.c_float]
+
+    # -- MLP -------------------------------------------------------------
+    def mlp_step(self, x, y, w1, w2, lr) -> MlpStep:
+        B, I = x.shape
+        H, O = w2.shape
+        return _mlp_call(self.lib.hxo_mlp_step, B, I, H, O, x, y, w1, w2, lr)
+
+    def matmul(self, a, b):
+        a = np.ascontiguousarray(a, np.float32)
+        b = np.ascontiguousarray(b, np.float32)
+        out = np.zeros((a.shape[0], b.shape[1]), np.float32)
+        self.lib.hxo_matmul(a.shape[0], b.shape[1], a.shape[1], a, b, out)
+        return out
+
+    def mse(self, p, y):
+        p = np.ascontiguousarray(p, np.float32).ravel()
+        y = np.ascontiguousarray(y, np.float32).ravel()
+        return self.lib.hxo_mse(p.size, p, y)
+
+    def linear_forward_backward(self, x, target, w):
+        B, D = x.shape
+        f = lambda *s: np.zeros(s, np.float32)
+        pred, err, dp, dw, dx = f(B, D), f(B, D), f(B, D), f(D, D), f(B, D)
+        loss = self.lib.hxo_linear_forward_backward(B, D, *[np.ascontiguousarray(a, np.float32) for a in (x, target, w)],
+                                                    pred, err, dp, dw, dx)
+        return loss, pred, err, dp, dw, dx
+
+    def sgd(self, w, dw, lr):
+        w = np.array(w, np.float32, copy=True)
+        self.lib.hxo_sgd(w.size, w.ravel(), np.ascontiguousarray(dw, np.float32).ravel(), lr)
+        return w
+
+    # -- LM ----------------------------------------------------------------
+    def param_count(self, cfg: LmConfig) -> int:
+        return int(self.lib.hxo_lm_param_count(C.byref(cfg)))
+
+    def fixed_position(self, cfg: LmConfig):
+        out = np.zeros((cfg.tokens, cfg.dim), np.float32)
+        self.lib.hxo_lm_fixed_position(C.byref(cfg), out)
+        return out
+
+    def lm_forward_backward(self, cfg: LmConfig, inputs, targets, params, want_all=True) -> LmStep:
+        T, V, D, L, H = cfg.tokens, cfg.vocab, cfg.dim, cfg.layers, cfg.heads
+        inputs = np.ascontiguousarray(inputs, np.uint32)
+        targets = np.ascontiguousarray(targets, np.uint32)
+        params = np.ascontiguousarray(params, np.float32)
+        grads = np.zeros(self.param_count(cfg), np.float32)
+        z = lambda *s: np.zeros(s, np.float32) if want_all else None
+        logits, probs, dlogits = z(T, V), z(T, V), z(T, V)
+        output, dout, lig, hp = z(T, D), z(T, D), z(L, T, D), z(L, H, T, T)
+        loss, acc = C.c_float(), C.c_float()
+        rc = self.lib.hxo_lm_forward_backward(C.byref(cfg), inputs, targets, params, C.byref(loss), C.byref(acc),
+                                              grads, _ptr(logits), _ptr(probs), _ptr(dlogits), _ptr(output),
+                                              _ptr(dout), _ptr(lig), _ptr(hp))
+        if rc != 0:
+            raise ValueError("invalid LM configuration or tokens")
+        return LmStep(loss.value, acc.value, grads, logits, probs, dlogits, output, lig, hp)
+
+    def lm_batch_gradients(self, cfg: LmConfig, tokens, params, threads=1):
+        tokens = np.ascontiguousarray(tokens, np.uint32)
+        B = tokens.shape[0]
+        grads = np.zeros(self.param_count(cfg), np.float32)
+        loss = C.c_float()
+        rc = self.lib.hxo_lm_batch_gradients(C.byref(cfg), B, tokens, np.ascontiguousarray(params, np.float32),
+                                             grads, C.byref(loss), threads)
+        if rc != 0:
+            raise ValueError("invalid LM configuration or tokens")
+        return grads, loss.value
+
+    def adam(self, w, g, m, v, lr, c1, c2, beta1=0.9, beta2=0.999, eps=1e-8):
+        w, g, m, v = [np.ascontiguousarray(a, np.float32).ravel() for a in (w, g, m, v)]
+        outs = [np.zeros_like(w) for _ in range(5)]
+        self.lib.hxo_adam(w.size, w, g, m, v, lr, beta1, beta2, eps, c1, c2, *[_ptr(o) for o in outs])
+        return tuple(outs)  # m_next, v_next, m_hat, v_hat, w_next
+
+    def adam_correction(self, beta: float, step: int) -> float:
+        return float(self.lib.hxo_adam_correction(beta, step))
+
+    def muon(self, w, g, buf, lr, momentum=0.95, nesterov=True, ns_steps=5,
+             abc=(3.4445, -4.7750, 2.0315), bf16_inputs=True):
+        w = np.ascontiguousarray(w, np.float32)
+        rows, cols = w.shape
+        w_next = np.zeros_like(w)
+        buf_next = np.zeros_like(w)
+        self.lib.hxo_muon(rows, cols, w, np.ascontiguousarray(g, np.float32), np.ascontiguousarray(buf, np.float32),
+                          lr, momentum, int(nesterov), ns_steps, abc[0], abc[1], abc[2], int(bf16_inputs),
+                          w_next, buf_next)
+        return w_next, buf_next
+
+    def round_bf16(self, x: float) -> float:
+        return float(self.lib.hxo_round_bf16(x))
+
+
+class Reference:
+    """The reference's own CPU code (oracle/_ref/libhexaref.so)."""
+
+    def __init__(self, path: str = REF_SO):
+        if not os.path.exists(path):
+            raise FileNotFoundError(path)
+        self.lib = L = C.CDLL(path)
+        L.hxr_last_error.restype = C.c_char_p
+        L.hxr_param_count.restype = C.c_int
+        L.hxr_param_count.argtypes = [C.POINTER(LmConfig)]
+        L.hxr_matmul.argtypes = [C.c_int] * 3 + [_f32p] * 3
+        L.hxr_linear_forward_backward.restype = C.c_float
+        L.hxr_linear_forward_backward.argtypes = [C.c_int, C.c_int] + [_f32p] * 3 + [C.c_float] + [_f32p] * 6
+        L.hxr_mlp_step.restype = C.c_int
+        L.hxr_mlp_step.argtypes = [C.c_int] * 4 + [_f32p] * 4 + [C.c_float, C.POINTER(C.c_float)] + \
+            [_f32p] * 9 + [_u8p, _f32p, _f32p]
+        L.hxr_lm_fixed_position.argtypes = [C.POINTER(LmConfig), _f32p]
+        L.hxr_lm_initial_parameters.restype = C.c_int
+        L.hxr_lm_initial_parameters.argtypes = [C.POINTER(LmConfig), C.c_uint32, _f32p]
+        L.hxr_lm_validate.restype = C.c_int
+        L.hxr_lm_validate.argtypes = [C.POINTER(LmConfig)]
+        L.hxr_lm_forward_backward.restype = C.c_int
+        L.hxr_lm_forward_backward.argtypes = [C.POINTER(LmConfig), _u32p, _u32p, _f32p, C.c_float,
+                                              C.POINTER(C.c_float), C.POINTER(C.c_float), _f32p] + [C.c_void_p] * 7
+        L.hxr_lm_adam.restype = C.c_int
+        L.hxr_lm_adam.argtypes = [C.POINTER(LmConfig)] + [_f32p] * 4 + [C.c_float] * 6 + [C.c_void_p] * 5
+        L.hxr_lm_train_step.restype = C.c_int
+        L.hxr_lm_train_step.argtypes = [C.POINTER(LmConfig), C.c_int, _u32p, _f32p, _f32p, _f32p, C.c_float,
+                                        C.c_int, C.c_int, C.POINTER(C.c_float)]
+        L.hxr_lm_gradient_check.restype = C.c_int
+        L.hxr_lm_gradient_check.argtypes = [C.c_uint32, C.c_float, C.POINTER(C.c_float), C.POINTER(C.c_float)]
+
+    def last_error(self) -> str:
+        return self.lib.hxr_last_error().decode()
+
+    def mlp_step(self, x, y, w1, w2, lr) -> MlpStep:
+        B, I = x.shape
+        H, O = w2.shape
+        return _mlp_call(self.lib.hxr_mlp_step, B, I, H, O, x, y, w1, w2, lr)
+
+    def matmul(self, a, b):
+        a = np.ascontiguousarray(a, np.float32)
+        b = np.ascontiguousarray(b, np.float32)
+        out = np.zeros((a.shape[0], b.shape[1]), np.float32)
+        self.lib.hxr_matmul(a.shape[0], b.shape[1], a.shape[1], a, b, out)
+        return out
+
+    def linear_forward_backward(self, x, target, w, lr=0.0):
+        B, D = x.shape
+        f = lambda *s: np.zeros(s, np.float32)
+        pred, err, dp, dw, dx, wn = f(B, D), f(B, D), f(B, D), f(D, D), f(B, D), f(D, D)
+        loss = self.lib.hxr_linear_forward_backward(B, D, *[np.ascontiguousarray(a, np.float32) for a in (x, target, w)],
+                                                    lr, pred, err, dp, dw, dx, wn)
+        return loss, pred, err, dp, dw, dx, wn
+
+    def param_count(self, cfg):
+        return int(self.lib.hxr_param_count(C.byref(cfg)))
+
+    def validate(self, cfg) -> bool:
+        return self.lib.hxr_lm_validate(C.byref(cfg)) == 0
+
+    def fixed_position(self, cfg):
+        out = np.zeros((cfg.tokens, cfg.dim), np.float32)
+        self.lib.hxr_lm_fixed_position(C.byref(cfg), out)
+        return out
+
+    def initial_parameters(self, cfg, seed):
+        out = np.zeros(self.param_count(cfg), np.float32)
+        if self.lib.hxr_lm_initial_parameters(C.byref(cfg), seed, out) != 0:
+            raise ValueError(self.last_error())
+        return out
+
+    def lm_forward_backward(self, cfg, inputs, targets, params, lr=0.0) -> LmStep:
+        T, V, D, L, H = cfg.tokens, cfg.vocab, cfg.dim, cfg.layers, cfg.heads
+        z = lambda *s: np.zeros(s, np.float32)
+        grads = z(self.param_count(cfg))
+        logits, probs, dlogits, output, lig, hp = z(T, V), z(T, V), z(T, V), z(T, D), z(L, T, D), z(L, H, T, T)
+        nxt = z(self.param_count(cfg))
+        loss, acc = C.c_float(), C.c_float()
+        rc = self.lib.hxr_lm_forward_backward(C.byref(cfg), np.ascontiguousarray(inputs, np.uint32),
+                                              np.ascontiguousarray(targets, np.uint32),
+                                              np.ascontiguousarray(params, np.float32), lr, C.byref(loss),
+                                              C.byref(acc), grads, _ptr(nxt), _ptr(logits), _ptr(probs),
+                                              _ptr(dlogits), _ptr(output), _ptr(lig), _ptr(hp))
+        if rc != 0:
+            raise ValueError(self.last_error())
+        step = LmStep(loss.value, acc.value, grads, logits, probs, dlogits, output, lig, hp)
+        step.next = nxt
+        return step
+
+    def adam(self, cfg, w, g, m, v, lr, c1, c2, beta1=0.9, beta2=0.999, eps=1e-8):
+        outs = [np.zeros_like(w) for _ in range(5)]
+        rc = self.lib.hxr_lm_adam(C.byref(cfg), *[np.ascontiguousarray(a, np.float32) for a in (w, g, m, v)],
+                                  lr, beta1, beta2, eps, c1, c2, *[_ptr(o) for o in outs])
+        if rc != 0:
+            raise ValueError(self.last_error())
+        return tuple(outs)
+
+    def lm_train_step(self, cfg, tokens, params, m, v, lr, step, threads=1):
+        """In-place batched Adam step; returns the mean loss."""
+        loss = C.c_float()
+        tokens = np.ascontiguousarray(tokens, np.uint32)
+        rc = self.lib.hxr_lm_train_step(C.byref(cfg), tokens.shape[0], tokens, params, m, v, lr, step, threads,
+                                        C.byref(loss))
+        if rc != 0:
+            raise ValueError(self.last_error())
+        return loss.value
+
+    def gradient_check(self, seed=20260725, eps=1e-3):
+        a, r = C.c_float(), C.c_float()
+        ok = self.lib.hxr_lm_gradient_check(seed, eps, C.byref(a), C.byref(r))
+        return bool(ok), a.value, r.value
+
+
+def reference_available() -> bool:
+    return os.path.exists(REF_SO)
