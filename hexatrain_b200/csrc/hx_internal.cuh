@@ -1,0 +1,155 @@
+// hx_internal.cuh -- shared internals of libhexatrain_b200.so.
+//
+// Error convention: internal code throws hx::Error; every extern "C" entry
+// point catches it, stores the message in the runtime (hx_runtime_last_error)
+// and returns the status code.  Nothing throws across the C ABI, matching the
+// reference's bool + std::string& error convention (qnn/qnn_runtime.h:250-451).
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <chrono>
+#include <cstdint>
+#include <cstring>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "../../include/hexatrain.h"
+
+namespace hx {
+
+struct Error {
+    int code;
+    std::string message;
+};
+
+[[noreturn]] inline void fail(int code, const std::string& msg) { throw Error{code, msg}; }
+
+inline void check_cuda(cudaError_t e, const char* what) {
+    if (e != cudaSuccess) fail(HX_ERR_CUDA, std::string(what) + ": " + cudaGetErrorName(e) + " (" + cudaGetErrorString(e) + ")");
+}
+#define HX_CUDA(call) ::hx::check_cuda((call), #call)
+// After a kernel launch: catches launch-configuration errors immediately.
+#define HX_LAUNCHED(rt) do { ::hx::check_cuda(cudaGetLastError(), "kernel launch"); ++(rt)->metrics.kernel_launches; } while (0)
+
+inline void require(bool ok, int code, const std::string& msg) {
+    if (!ok) fail(code, msg);
+}
+
+using Clock = std::chrono::steady_clock;
+inline double us_since(Clock::time_point t0) {
+    return std::chrono::duration<double, std::micro>(Clock::now() - t0).count();
+}
+
+// One device allocation owned by a runtime.
+struct DeviceBuffer {
+    void* ptr = nullptr;
+    size_t bytes = 0;
+    DeviceBuffer() = default;
+    DeviceBuffer(const DeviceBuffer&) = delete;
+    DeviceBuffer& operator=(const DeviceBuffer&) = delete;
+    ~DeviceBuffer() { release(); }
+    void release() {
+        if (ptr) cudaFree(ptr);
+        ptr = nullptr;
+        bytes = 0;
+    }
+    void allocate(size_t n) {
+        release();
+        if (n == 0) n = 16;
+        const cudaError_t e = cudaMalloc(&ptr, n);
+        if (e != cudaSuccess) {
+            ptr = nullptr;
+            fail(HX_ERR_MEMORY, "device allocation of " + std::to_string(n) + " bytes failed: " + cudaGetErrorString(e));
+        }
+        bytes = n;
+    }
+    template <class T> T* as() const { return static_cast<T*>(ptr); }
+};
+
+// Bump allocator over one device allocation: all per-plan tensors are carved
+// out of a single cudaMalloc at prepare time (256-byte aligned sub-buffers).
+struct Arena {
+    DeviceBuffer block;
+    size_t used = 0;
+    struct Slot { size_t offset; };
+    std::vector<size_t> pending;
+    size_t reserve(size_t bytes) {
+        const size_t off = (used + 255) & ~size_t(255);
+        used = off + bytes;
+        return off;
+    }
+    void commit() { block.allocate(used); }
+    template <class T> T* at(size_t offset) const { return reinterpret_cast<T*>(static_cast<char*>(block.ptr) + offset); }
+};
+
+struct MlpPlan;
+struct LmPlan;
+struct AdamPlan;
+// LmPlan is defined in lm.cu; its deleter is too.
+struct LmPlanDeleter {
+    void operator()(LmPlan* p) const;
+};
+
+}  // namespace hx
+
+struct hx_runtime {
+    int device = 0;
+    cudaStream_t own_stream = nullptr;
+    cudaStream_t stream = nullptr;
+    std::string last_error;
+    hx_metrics metrics{};
+    int64_t inject_execute_at = -1;
+    int sm_count = 148;
+    std::unique_ptr<hx::MlpPlan> mlp;
+    std::unique_ptr<hx::LmPlan, hx::LmPlanDeleter> lm;
+    std::unique_ptr<hx::AdamPlan> adam;
+    hx::DeviceBuffer scratch;  // generic device workspace (grows on demand)
+
+    ~hx_runtime();
+    void activate() const { hx::check_cuda(cudaSetDevice(device), "cudaSetDevice"); }
+    // Grow-only device workspace for split-K partials and reductions.
+    float* workspace(size_t bytes) {
+        if (scratch.bytes < bytes) scratch.allocate(bytes);
+        return scratch.as<float>();
+    }
+    // Record the outcome of an execute call (ApiTrace counters).
+    void record_execute(bool ok, double us) {
+        ++metrics.execute_attempt_count;
+        if (ok) {
+            ++metrics.graph_execute_count;
+            metrics.last_execute_us = us;
+            metrics.total_execute_us += us;
+        } else {
+            if (metrics.first_failure_call < 0) metrics.first_failure_call = int64_t(metrics.execute_attempt_count - 1);
+            ++metrics.execute_failure_count;
+        }
+    }
+    // Host-side failure injection at a given execute attempt index.
+    bool injected_now() const {
+        return inject_execute_at >= 0 && uint64_t(inject_execute_at) == metrics.execute_attempt_count;
+    }
+};
+
+// Runs `body` and converts any failure to a status code + stored message.
+template <class F>
+inline int hx_guard(hx_runtime* rt, F&& body) {
+    if (!rt) return HX_ERR_ARGUMENT;
+    try {
+        rt->activate();
+        body();
+        rt->last_error.clear();
+        return HX_OK;
+    } catch (const hx::Error& e) {
+        rt->last_error = e.message;
+        return e.code;
+    } catch (const std::bad_alloc&) {
+        rt->last_error = "host allocation failed";
+        return HX_ERR_MEMORY;
+    } catch (const std::exception& e) {
+        rt->last_error = e.what();
+        return HX_ERR_ARGUMENT;
+    }
+}

@@ -1,0 +1,709 @@
+// lm.cu -- tiny causal Transformer LM training step on B200.
+//
+// Replaces the generalized L-layer/H-head QNN training graph
+// (qnn/qnn_runtime_transformer_training_generalized.inc:4-1260 and its
+// execute companion) and the batched Adam driver loop
+// (qnn/qnn_transformer_training.cpp:7281-7345).  The reference runs one
+// sequence per graph execute and accumulates grad*(1/B) on the host; here the
+// B sequences of a step share every kernel (rows r = b*T + t) and the 1/B is
+// folded into dlogits, so the weight-gradient GEMMs sum over all B*T rows.
+//
+// Per layer (pre-LN, no biases, untied head, no final LN -- :44-48):
+//   LN1 -> [q|k|v] = n1 W_qkv -> causal attention -> r1 = x + ctx Wo
+//   LN2 -> relu = ReLU(n2 W1) -> out = r1 + relu W2
+// Backward mirrors :79-82 with the same named gradients in registry order.
+#include <cmath>
+
+#include "gemm.cuh"
+#include "lm_kernels.cuh"
+#include "optim.cuh"
+#include "plans.cuh"
+
+namespace hx {
+
+AdamScalars adam_scalars(float lr, float gradient_scale, float c1, float c2);
+void launch_adam(hx_runtime* rt, bool graph_order, size_t n, const float* w, const float* g, const float* m,
+                 const float* v, float* wn, float* mn, float* vn, const AdamScalars& s, const AdamTaps& t);
+size_t muon_smem_bytes(int rows, int cols);
+void check_muon_shape(int rows, int cols);
+void launch_muon(hx_runtime* rt, const MuonMatrix* d_mats, int count, size_t smem, const MuonScalars& s);
+
+struct LayerOffsets {  // offsets (in floats) of one layer's tensors in the flat registry
+    size_t g1, b1, wq, wk, wv, wo, g2, b2, w1, w2;
+};
+
+struct LayerActs {  // arena offsets (bytes)
+    size_t x, n1, mean1, inv1, qkv, ctx, r1, n2, mean2, inv2, relu, rmax, rsum;
+};
+
+struct LmPlan {
+    hx_lm_config cfg{};
+    uint32_t B = 0, V = 0, T = 0, D = 0, F = 0, L = 0, H = 0, dh = 0;
+    int M = 0;
+    bool diag = false, learned = false;
+    size_t P = 0;
+    size_t off_E = 0, off_pos = 0, off_out = 0;
+    std::vector<LayerOffsets> lo;
+    Arena arena;
+    // arena offsets (bytes)
+    size_t params, exec_params, grads, adam_m, adam_v, muon_buf, pos_fixed, wqkv;
+    size_t tokens, in_tok, tgt_tok, in_ids, tgt_ids, bad;
+    std::vector<LayerActs> la;
+    size_t xL, logits, probs, row_loss, row_correct, loss, acc, scalars;
+    size_t dout, dr, dc, dn, df1, dqkv, ln_part;
+    size_t diag_lig, diag_hp, diag_dout;
+    size_t muon_table;
+    int ln_parts = 0, ln_rows = 0;
+    DeviceBuffer onehot;  // lazily sized staging for the one-hot execute API
+    hx_optimizer_config opt{};
+    int muon_count = 0;
+    size_t muon_smem = 0;
+    std::vector<std::pair<size_t, size_t>> adam_segments;  // [offset, count) in floats
+    bool state_ready = false;
+    float* host_scalars = nullptr;  // pinned [c1, c2]
+    ~LmPlan() {
+        if (host_scalars) cudaFreeHost(host_scalars);
+    }
+};
+
+size_t lm_plan_bytes(const LmPlan* p) { return p ? p->arena.block.bytes + p->onehot.bytes : 0; }
+void LmPlanDeleter::operator()(LmPlan* p) const { delete p; }
+
+namespace {
+
+void validate(const hx_lm_config* c) {
+    require(c != nullptr, HX_ERR_ARGUMENT, "APP_CONFIGURATION_VALIDATION: null configuration");
+    require(c->vocab && c->tokens && c->dim && c->ffn && c->layers && c->heads, HX_ERR_ARGUMENT,
+            "APP_CONFIGURATION_VALIDATION: all Transformer dimensions and counts must be >= 1");
+    require(c->dim % c->heads == 0, HX_ERR_ARGUMENT,
+            "APP_CONFIGURATION_VALIDATION: embeddingDimension must be divisible by numHeads");
+    require(std::isfinite(c->eps) && c->eps > 0.f, HX_ERR_ARGUMENT,
+            "APP_CONFIGURATION_VALIDATION: LayerNorm epsilon must be finite and positive");
+    require((c->flags & ~uint32_t(HX_LM_LEARNED_POSITION)) == 0, HX_ERR_ARGUMENT,
+            "APP_CONFIGURATION_VALIDATION: unknown flag bits");
+    const uint64_t lim = uint64_t(1) << 31;
+    require(uint64_t(c->vocab) * c->dim < lim && uint64_t(c->dim) * c->ffn < lim && uint64_t(c->tokens) * c->tokens < lim &&
+                c->layers <= 4096,
+            HX_ERR_ARGUMENT, "APP_RESOURCE_ESTIMATOR: dimension product exceeds 2^31 elements");
+}
+
+size_t param_count(const hx_lm_config* c) {
+    const size_t V = c->vocab, T = c->tokens, D = c->dim, F = c->ffn;
+    return 2 * V * D + ((c->flags & HX_LM_LEARNED_POSITION) ? T * D : 0) + size_t(c->layers) * (4 * D * D + 4 * D + 2 * D * F);
+}
+
+bool dh_supported(uint32_t dh) {
+    switch (dh) {
+        case 1: case 2: case 3: case 4: case 6: case 8: case 12: case 16: case 24: case 32: case 48: case 64:
+            return true;
+        default:
+            return false;
+    }
+}
+
+size_t attn_fwd_smem(int T, int DH, int nw) { return sizeof(float) * (size_t(2) * T * (DH + 1) + size_t(nw) * T + size_t(nw) * DH); }
+size_t attn_bwd_smem(int T, int DH, int nw) { return sizeof(float) * (size_t(4) * T * (DH + 1) + 3 * size_t(T) + size_t(nw) * T); }
+constexpr int kAttnThreads = 256;
+
+template <int DH>
+void attn_fwd_launch(hx_runtime* rt, const LmPlan& p, const float* qkv, float* ctx, float* rmax, float* rsum, float* probs) {
+    const size_t smem = attn_fwd_smem(p.T, DH, kAttnThreads / 32);
+    HX_CUDA(cudaFuncSetAttribute(attention_fwd_kernel<DH>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    attention_fwd_kernel<DH><<<dim3(p.H, p.B), kAttnThreads, smem, rt->stream>>>(
+        p.T, p.D, p.H, 1.0f / sqrtf((float)DH), qkv, ctx, rmax, rsum, probs);
+    HX_LAUNCHED(rt);
+}
+template <int DH>
+void attn_bwd_launch(hx_runtime* rt, const LmPlan& p, const float* qkv, const float* dctx, const float* rmax,
+                     const float* rsum, float* dqkv) {
+    const size_t smem = attn_bwd_smem(p.T, DH, kAttnThreads / 32);
+    HX_CUDA(cudaFuncSetAttribute(attention_bwd_kernel<DH>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    attention_bwd_kernel<DH><<<dim3(p.H, p.B), kAttnThreads, smem, rt->stream>>>(
+        p.T, p.D, p.H, 1.0f / sqrtf((float)DH), qkv, dctx, rmax, rsum, dqkv);
+    HX_LAUNCHED(rt);
+}
+
+#define HX_DH_DISPATCH(dh, FN, ...)                                   \
+    switch (dh) {                                                     \
+        case 1: FN<1>(__VA_ARGS__); break;                            \
+        case 2: FN<2>(__VA_ARGS__); break;                            \
+        case 3: FN<3>(__VA_ARGS__); break;                            \
+        case 4: FN<4>(__VA_ARGS__); break;                            \
+        case 6: FN<6>(__VA_ARGS__); break;                            \
+        case 8: FN<8>(__VA_ARGS__); break;                            \
+        case 12: FN<12>(__VA_ARGS__); break;                          \
+        case 16: FN<16>(__VA_ARGS__); break;                          \
+        case 24: FN<24>(__VA_ARGS__); break;                          \
+        case 32: FN<32>(__VA_ARGS__); break;                          \
+        case 48: FN<48>(__VA_ARGS__); break;                          \
+        case 64: FN<64>(__VA_ARGS__); break;                          \
+        default: fail(HX_ERR_UNSUPPORTED, "unsupported head dimension"); \
+    }
+
+int grid_for(long work, int threads, int sms) {
+    return (int)std::max<long>(1, std::min<long>((work + threads - 1) / threads, long(sms) * 32));
+}
+
+struct DiagOut {
+    bool on = false;
+};
+
+// Forward + backward over the ids already in the plan.  grads[0..P) receive
+// sum over rows of the gradient with dlogits scaled by grad_scale;
+// grads[P] receives sum_b loss_b * grad_scale.
+void forward_backward(hx_runtime* rt, LmPlan& p, const float* W, float* G, float grad_scale)
+{
+    const Arena& a = p.arena;
+    const int M = p.M, T = p.T, D = p.D, F = p.F, V = p.V, B = p.B;
+    const cudaStream_t s = rt->stream;
+    const int* in_ids = a.at<int>(p.in_ids);
+    const int* tgt_ids = a.at<int>(p.tgt_ids);
+    const float* pos = p.learned ? W + p.off_pos : a.at<float>(p.pos_fixed);
+    float* wqkv = a.at<float>(p.wqkv);
+    const int tpb = 256;
+
+    // pack W_qkv per layer
+    for (uint32_t l = 0; l < p.L; ++l) {
+        pack_qkv_kernel<<<grid_for(3L * D * D, tpb, rt->sm_count), tpb, 0, s>>>(D, W + p.lo[l].wq, wqkv + size_t(l) * 3 * D * D);
+        HX_LAUNCHED(rt);
+    }
+    // embedding
+    float* x = a.at<float>(p.la[0].x);
+    embed_kernel<<<grid_for(long(M) * D, tpb, rt->sm_count), tpb, 0, s>>>(M, T, D, in_ids, W + p.off_E, pos, x);
+    HX_LAUNCHED(rt);
+    const int rows_per_block = 8;  // warps per block for row kernels
+    const int row_grid = (M + rows_per_block - 1) / rows_per_block;
+
+    for (uint32_t l = 0; l < p.L; ++l) {
+        const LayerActs& A = p.la[l];
+        const LayerOffsets& o = p.lo[l];
+        const float* xin = a.at<float>(A.x);
+        float* xout = (l + 1 < p.L) ? a.at<float>(p.la[l + 1].x) : a.at<float>(p.xL);
+        layernorm_fwd_kernel<<<row_grid, 32 * rows_per_block, 0, s>>>(M, D, p.cfg.eps, xin, W + o.g1, W + o.b1,
+                                                                       a.at<float>(A.n1), a.at<float>(A.mean1),
+                                                                       a.at<float>(A.inv1));
+        HX_LAUNCHED(rt);
+        gemm<false, false>(rt, M, 3 * D, D, a.at<float>(A.n1), D, wqkv + size_t(l) * 3 * D * D, 3 * D,
+                           EpiStore{a.at<float>(A.qkv), 3L * D, 0, 0});
+        float* hp = p.diag ? a.at<float>(p.diag_hp) + size_t(l) * B * p.H * T * T : nullptr;
+        HX_DH_DISPATCH(p.dh, attn_fwd_launch, rt, p, a.at<float>(A.qkv), a.at<float>(A.ctx), a.at<float>(A.rmax),
+                       a.at<float>(A.rsum), hp);
+        gemm<false, false>(rt, M, D, D, a.at<float>(A.ctx), D, W + o.wo, D, EpiAddResidual{xin, a.at<float>(A.r1), D});
+        layernorm_fwd_kernel<<<row_grid, 32 * rows_per_block, 0, s>>>(M, D, p.cfg.eps, a.at<float>(A.r1), W + o.g2,
+                                                                       W + o.b2, a.at<float>(A.n2),
+                                                                       a.at<float>(A.mean2), a.at<float>(A.inv2));
+        HX_LAUNCHED(rt);
+        gemm<false, false>(rt, M, F, D, a.at<float>(A.n2), D, W + o.w1, F, EpiRelu{a.at<float>(A.relu), nullptr, F});
+        gemm<false, false>(rt, M, D, F, a.at<float>(A.relu), F, W + o.w2, D,
+                           EpiAddResidual{a.at<float>(A.r1), xout, D});
+    }
+    const float* xL = a.at<float>(p.xL);
+    float* logits = a.at<float>(p.logits);
+    gemm<false, false>(rt, M, V, D, xL, D, W + p.off_out, V, EpiStore{logits, (long)V, 0, 0});
+    softmax_ce_kernel<<<row_grid, 32 * rows_per_block, 0, s>>>(
+        M, V, T, grad_scale, logits, tgt_ids, p.diag ? a.at<float>(p.probs) : nullptr, logits,
+        a.at<double>(p.row_loss), a.at<int>(p.row_correct));
+    HX_LAUNCHED(rt);
+    loss_reduce_kernel<<<1, 256, 0, s>>>(B, T, a.at<double>(p.row_loss), a.at<int>(p.row_correct), grad_scale,
+                                         a.at<float>(p.loss), a.at<float>(p.acc), G + p.P);
+    HX_LAUNCHED(rt);
+
+    // ---- backward ----
+    const float* dl = logits;  // dlogits, in place
+    gemm<true, false>(rt, D, V, M, xL, D, dl, V, EpiStore{G + p.off_out, (long)V, 0, 0});
+    float* dout = a.at<float>(p.dout);
+    gemm<false, true>(rt, M, D, V, dl, V, W + p.off_out, V, EpiStore{dout, (long)D, 0, 0});
+    if (p.diag) copy_d2d(rt, a.at<float>(p.diag_dout), dout, sizeof(float) * size_t(M) * D);
+    float* dr = a.at<float>(p.dr);
+    float* dc = a.at<float>(p.dc);
+    float* dn = a.at<float>(p.dn);
+    float* df1 = a.at<float>(p.df1);
+    float* dqkv = a.at<float>(p.dqkv);
+    float* part = a.at<float>(p.ln_part);
+    const int lnw = 8;
+    const size_t ln_smem = sizeof(float) * lnw * 2 * D;
+    if (ln_smem > 48 * 1024)
+        HX_CUDA(cudaFuncSetAttribute(layernorm_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ln_smem));
+    for (uint32_t li = p.L; li-- > 0;) {
+        const LayerActs& A = p.la[li];
+        const LayerOffsets& o = p.lo[li];
+        const float* xin = a.at<float>(A.x);
+        gemm<true, false>(rt, F, D, M, a.at<float>(A.relu), F, dout, D, EpiStore{G + o.w2, (long)D, 0, 0});
+        gemm<false, true>(rt, M, F, D, dout, D, W + o.w2, D, EpiReluBackward{a.at<float>(A.relu), df1, nullptr, F});
+        gemm<true, false>(rt, D, F, M, a.at<float>(A.n2), D, df1, F, EpiStore{G + o.w1, (long)F, 0, 0});
+        gemm<false, true>(rt, M, D, F, df1, F, W + o.w1, F, EpiStore{dn, (long)D, 0, 0});
+        layernorm_bwd_kernel<<<p.ln_parts, 32 * lnw, ln_smem, s>>>(M, D, p.ln_rows, dn, a.at<float>(A.r1),
+                                                                     a.at<float>(A.mean2), a.at<float>(A.inv2),
+                                                                     W + o.g2, dout, dr, part);
+        HX_LAUNCHED(rt);
+        column_reduce_kernel<<<grid_for(2L * D, tpb, rt->sm_count), tpb, 0, s>>>(p.ln_parts, D, part, G + o.g2, G + o.b2);
+        HX_LAUNCHED(rt);
+        gemm<true, false>(rt, D, D, M, a.at<float>(A.ctx), D, dr, D, EpiStore{G + o.wo, (long)D, 0, 0});
+        gemm<false, true>(rt, M, D, D, dr, D, W + o.wo, D, EpiStore{dc, (long)D, 0, 0});
+        HX_DH_DISPATCH(p.dh, attn_bwd_launch, rt, p, a.at<float>(A.qkv), dc, a.at<float>(A.rmax), a.at<float>(A.rsum), dqkv);
+        gemm<true, false>(rt, D, 3 * D, M, a.at<float>(A.n1), D, dqkv, 3 * D,
+                          EpiStore{G + o.wq, (long)D, (int)D, (long)D * D});
+        gemm<false, true>(rt, M, D, 3 * D, dqkv, 3 * D, wqkv + size_t(li) * 3 * D * D, 3 * D, EpiStore{dn, (long)D, 0, 0});
+        layernorm_bwd_kernel<<<p.ln_parts, 32 * lnw, ln_smem, s>>>(M, D, p.ln_rows, dn, xin, a.at<float>(A.mean1),
+                                                                     a.at<float>(A.inv1), W + o.g1, dr, dout, part);
+        HX_LAUNCHED(rt);
+        column_reduce_kernel<<<grid_for(2L * D, tpb, rt->sm_count), tpb, 0, s>>>(p.ln_parts, D, part, G + o.g1, G + o.b1);
+        HX_LAUNCHED(rt);
+        if (p.diag) copy_d2d(rt, a.at<float>(p.diag_lig) + size_t(li) * M * D, dout, sizeof(float) * size_t(M) * D);
+    }
+    // embedding gradients
+    HX_CUDA(cudaMemsetAsync(G + p.off_E, 0, sizeof(float) * size_t(V) * D, s));
+    embed_bwd_kernel<<<grid_for(long(M) * D, tpb, rt->sm_count), tpb, 0, s>>>(M, D, in_ids, dout, G + p.off_E);
+    HX_LAUNCHED(rt);
+    if (p.learned) {
+        position_bwd_kernel<<<grid_for(long(T) * D, tpb, rt->sm_count), tpb, 0, s>>>(B, T, D, dout, G + p.off_pos);
+        HX_LAUNCHED(rt);
+    }
+}
+
+void optimizer_step(hx_runtime* rt, LmPlan& p, uint32_t step)
+{
+    const Arena& a = p.arena;
+    float* W = a.at<float>(p.params);
+    const float* G = a.at<float>(p.grads);
+    float* m = a.at<float>(p.adam_m);
+    float* v = a.at<float>(p.adam_v);
+    // Bias corrections exactly as the reference driver computes them
+    // (qnn/qnn_transformer_training.cpp:1504-1507): double, then float.
+    const float c1 = float(1.0 / (1.0 - std::pow(double(p.opt.beta1), double(step))));
+    const float c2 = float(1.0 / (1.0 - std::pow(double(p.opt.beta2), double(step))));
+    AdamScalars sc = adam_scalars(p.opt.adam_lr, 1.0f, c1, c2);
+    sc.beta1 = p.opt.beta1;
+    sc.beta2 = p.opt.beta2;
+    sc.one_minus_beta1 = 1.0f - p.opt.beta1;
+    sc.one_minus_beta2 = 1.0f - p.opt.beta2;
+    sc.eps = p.opt.adam_eps;
+    const AdamTaps none{};
+    if (p.opt.kind == HX_OPT_MUON) {
+        MuonScalars ms{p.opt.muon_lr, p.opt.muon_momentum, p.opt.ns_a, p.opt.ns_b, p.opt.ns_c,
+                       (int)p.opt.muon_nesterov, (int)p.opt.muon_ns_steps, (int)p.opt.muon_bf16_inputs};
+        launch_muon(rt, a.at<MuonMatrix>(p.muon_table), p.muon_count, p.muon_smem, ms);
+        for (const auto& seg : p.adam_segments)
+            launch_adam(rt, false, seg.second, W + seg.first, G + seg.first, m + seg.first, v + seg.first,
+                        W + seg.first, m + seg.first, v + seg.first, sc, none);
+    } else {
+        launch_adam(rt, false, p.P, W, G, m, v, W, m, v, sc, none);
+    }
+}
+
+LmPlan& need_lm(hx_runtime* rt) {
+    require(rt->lm != nullptr, HX_ERR_STATE, "generalized tiny training graph not prepared");
+    return *rt->lm;
+}
+
+void check_bad(hx_runtime* rt, LmPlan& p, const char* what) {
+    int bad = 0;
+    HX_CUDA(cudaMemcpyAsync(&bad, p.arena.at<int>(p.bad), sizeof(int), cudaMemcpyDeviceToHost, rt->stream));
+    HX_CUDA(cudaStreamSynchronize(rt->stream));
+    if (bad) fail(HX_ERR_ARGUMENT, what);
+}
+
+void default_optimizer(hx_optimizer_config& o) {
+    o.kind = HX_OPT_ADAM;
+    o.adam_lr = 1e-3f;
+    o.beta1 = 0.9f;
+    o.beta2 = 0.999f;
+    o.adam_eps = 1e-8f;
+    o.muon_lr = 0.02f;
+    o.muon_momentum = 0.95f;
+    o.muon_nesterov = 1;
+    o.muon_ns_steps = 5;
+    o.ns_a = 3.4445f;
+    o.ns_b = -4.7750f;
+    o.ns_c = 2.0315f;
+    o.muon_bf16_inputs = 1;
+}
+
+void host_fixed_position(const LmPlan& p, std::vector<float>& out) {
+    // tiny_lm::fixedPosition (tiny_language_model_cpu.cpp:68), same float ops.
+    out.assign(size_t(p.T) * p.D, 0.f);
+    for (uint32_t t = 0; t < p.T; ++t)
+        for (uint32_t d = 0; d < p.D; ++d) {
+            const float f = std::pow(10000.f, -float(d & ~1u) / float(p.D));
+            out[size_t(t) * p.D + d] = ((d & 1u) ? std::cos(float(t) * f) : std::sin(float(t) * f)) * .05f;
+        }
+}
+
+}  // namespace
+}  // namespace hx
+
+using namespace hx;
+
+extern "C" {
+
+size_t hx_lm_param_count(const hx_lm_config* cfg) { return cfg ? hx::param_count(cfg) : 0; }
+
+int hx_lm_validate(const hx_lm_config* cfg, char* err, size_t err_len) {
+    try {
+        validate(cfg);
+        if (err && err_len) err[0] = 0;
+        return HX_OK;
+    } catch (const Error& e) {
+        if (err && err_len) std::snprintf(err, err_len, "%s", e.message.c_str());
+        return e.code;
+    }
+}
+
+int hx_lm_prepare(hx_runtime* rt, const hx_lm_config* cfg, uint32_t batch, int diagnostic) {
+    return hx_guard(rt, [&] {
+        validate(cfg);
+        require(batch >= 1, HX_ERR_ARGUMENT, "APP_CONFIGURATION_VALIDATION: batch must be >= 1");
+        auto pp = std::unique_ptr<LmPlan, LmPlanDeleter>(new LmPlan());
+        LmPlan& p = *pp;
+        p.cfg = *cfg;
+        p.B = batch; p.V = cfg->vocab; p.T = cfg->tokens; p.D = cfg->dim; p.F = cfg->ffn;
+        p.L = cfg->layers; p.H = cfg->heads; p.dh = p.D / p.H;
+        p.learned = (cfg->flags & HX_LM_LEARNED_POSITION) != 0;
+        p.diag = diagnostic != 0;
+        require(uint64_t(batch) * p.T < (uint64_t(1) << 31) && uint64_t(batch) * p.T * std::max(p.V, 3 * p.D) < (uint64_t(1) << 40),
+                HX_ERR_ARGUMENT, "APP_RESOURCE_ESTIMATOR: batch*tokens too large");
+        p.M = int(batch * p.T);
+        require(dh_supported(p.dh), HX_ERR_UNSUPPORTED,
+                "UNSUPPORTED_HEAD_DIMENSION: head dimension " + std::to_string(p.dh) +
+                    " (supported: 1,2,3,4,6,8,12,16,24,32,48,64)");
+        cudaDeviceProp prop{};
+        HX_CUDA(cudaGetDeviceProperties(&prop, rt->device));
+        const size_t smem_max = prop.sharedMemPerBlockOptin;
+        require(attn_bwd_smem(p.T, p.dh, kAttnThreads / 32) <= smem_max && attn_fwd_smem(p.T, p.dh, kAttnThreads / 32) <= smem_max,
+                HX_ERR_UNSUPPORTED, "UNSUPPORTED_ATTENTION_TILE: T*head_dim too large for one CTA's shared memory");
+        p.P = param_count(cfg);
+        // registry layout
+        const size_t V = p.V, T = p.T, D = p.D, F = p.F;
+        size_t off = 0;
+        p.off_E = off; off += V * D;
+        if (p.learned) { p.off_pos = off; off += T * D; }
+        p.lo.resize(p.L);
+        for (uint32_t l = 0; l < p.L; ++l) {
+            LayerOffsets& o = p.lo[l];
+            o.g1 = off; off += D;
+            o.b1 = off; off += D;
+            o.wq = off; off += D * D;
+            o.wk = off; off += D * D;
+            o.wv = off; off += D * D;
+            o.wo = off; off += D * D;
+            o.g2 = off; off += D;
+            o.b2 = off; off += D;
+            o.w1 = off; off += D * F;
+            o.w2 = off; off += F * D;
+        }
+        p.off_out = off; off += D * V;
+        require(off == p.P, HX_ERR_STATE, "internal: registry layout mismatch");
+
+        const size_t f = sizeof(float), M = p.M, B = p.B, H = p.H;
+        Arena& a = p.arena;
+        p.params = a.reserve(f * p.P);
+        p.exec_params = a.reserve(f * p.P);
+        p.grads = a.reserve(f * (p.P + 1));
+        p.adam_m = a.reserve(f * p.P);
+        p.adam_v = a.reserve(f * p.P);
+        p.muon_buf = a.reserve(f * p.P);
+        p.pos_fixed = a.reserve(f * T * D);
+        p.wqkv = a.reserve(f * p.L * 3 * D * D);
+        p.tokens = a.reserve(sizeof(uint32_t) * B * (T + 1));
+        p.in_tok = a.reserve(sizeof(uint32_t) * M);
+        p.tgt_tok = a.reserve(sizeof(uint32_t) * M);
+        p.in_ids = a.reserve(sizeof(int) * M);
+        p.tgt_ids = a.reserve(sizeof(int) * M);
+        p.bad = a.reserve(sizeof(int) * 4);
+        p.la.resize(p.L);
+        for (uint32_t l = 0; l < p.L; ++l) {
+            LayerActs& A = p.la[l];
+            A.x = a.reserve(f * M * D);
+            A.n1 = a.reserve(f * M * D);
+            A.mean1 = a.reserve(f * M);
+            A.inv1 = a.reserve(f * M);
+            A.qkv = a.reserve(f * M * 3 * D);
+            A.ctx = a.reserve(f * M * D);
+            A.r1 = a.reserve(f * M * D);
+            A.n2 = a.reserve(f * M * D);
+            A.mean2 = a.reserve(f * M);
+            A.inv2 = a.reserve(f * M);
+            A.relu = a.reserve(f * M * F);
+            A.rmax = a.reserve(f * B * H * T);
+            A.rsum = a.reserve(f * B * H * T);
+        }
+        p.xL = a.reserve(f * M * D);
+        p.logits = a.reserve(f * M * V);
+        p.probs = p.diag ? a.reserve(f * M * V) : 0;
+        p.row_loss = a.reserve(sizeof(double) * M);
+        p.row_correct = a.reserve(sizeof(int) * M);
+        p.loss = a.reserve(f * 4);
+        p.acc = a.reserve(f * 4);
+        p.scalars = a.reserve(f * 8);
+        p.dout = a.reserve(f * M * D);
+        p.dr = a.reserve(f * M * D);
+        p.dc = a.reserve(f * M * D);
+        p.dn = a.reserve(f * M * D);
+        p.df1 = a.reserve(f * M * F);
+        p.dqkv = a.reserve(f * M * 3 * D);
+        p.ln_parts = std::max(1, std::min<int>(p.M, 2 * rt->sm_count));
+        p.ln_rows = (p.M + p.ln_parts - 1) / p.ln_parts;
+        p.ln_parts = (p.M + p.ln_rows - 1) / p.ln_rows;
+        p.ln_part = a.reserve(f * size_t(p.ln_parts) * 2 * D);
+        if (p.diag) {
+            p.diag_lig = a.reserve(f * p.L * M * D);
+            p.diag_hp = a.reserve(f * p.L * B * H * T * T);
+            p.diag_dout = a.reserve(f * M * D);
+        }
+        // Muon matrices: wq, wk, wv, wo, ffn_w1, ffn_w2 of every layer
+        p.muon_table = a.reserve(sizeof(MuonMatrix) * 6 * p.L);
+        a.commit();
+        HX_CUDA(cudaMemsetAsync(a.block.ptr, 0, a.used, rt->stream));
+        std::vector<float> pos;
+        host_fixed_position(p, pos);
+        HX_CUDA(cudaMemcpyAsync(a.at<float>(p.pos_fixed), pos.data(), f * pos.size(), cudaMemcpyHostToDevice, rt->stream));
+        default_optimizer(p.opt);
+        // Muon table + Adam segments for the non-Muon parameters
+        std::vector<MuonMatrix> mats;
+        float* W = a.at<float>(p.params);
+        float* G = a.at<float>(p.grads);
+        float* Bf = a.at<float>(p.muon_buf);
+        p.adam_segments.clear();
+        p.adam_segments.push_back({0, p.lo.empty() ? p.P : p.lo[0].g1});  // token_embedding (+ position)
+        for (uint32_t l = 0; l < p.L; ++l) {
+            const LayerOffsets& o = p.lo[l];
+            p.adam_segments.push_back({o.g1, 2 * D});
+            p.adam_segments.push_back({o.g2, 2 * D});
+            const size_t offs[6] = {o.wq, o.wk, o.wv, o.wo, o.w1, o.w2};
+            const int rows[6] = {int(D), int(D), int(D), int(D), int(D), int(F)};
+            const int cols[6] = {int(D), int(D), int(D), int(D), int(F), int(D)};
+            for (int k = 0; k < 6; ++k) mats.push_back(MuonMatrix{W + offs[k], G + offs[k], Bf + offs[k], rows[k], cols[k]});
+        }
+        p.adam_segments.push_back({p.off_out, D * V});
+        p.muon_count = int(mats.size());
+        p.muon_smem = std::max(muon_smem_bytes(int(D), int(D)), muon_smem_bytes(int(D), int(F)));
+        HX_CUDA(cudaMemcpyAsync(a.at<MuonMatrix>(p.muon_table), mats.data(), sizeof(MuonMatrix) * mats.size(),
+                                cudaMemcpyHostToDevice, rt->stream));
+        HX_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&p.host_scalars), 64, cudaHostAllocDefault));
+        HX_CUDA(cudaStreamSynchronize(rt->stream));
+        rt->lm = std::move(pp);
+        ++rt->metrics.graph_create_count;
+    });
+}
+
+int hx_lm_execute_tokens(hx_runtime* rt, const uint32_t* input_tokens, const uint32_t* target_tokens,
+                         const float* params, size_t param_count_, const hx_lm_outputs* out);
+
+static void lm_execute_common(hx_runtime* rt, LmPlan& p, const float* params, size_t pc, float lr,
+                              const hx_lm_outputs* out) {
+    require(params && out && out->loss && out->grads, HX_ERR_ARGUMENT, "generalized tiny training buffer schema");
+    require(pc == p.P, HX_ERR_ARGUMENT, "generalized tiny training buffer schema: parameter count " +
+                                            std::to_string(pc) + " != " + std::to_string(p.P));
+    require(lr == 0.0f, HX_ERR_ARGUMENT, "generalized tiny training requires learningRate=0; use Adam");
+    const bool wants_diag = out->logits || out->probabilities || out->d_logits || out->output || out->d_output ||
+                            out->layer_input_grads || out->head_probabilities;
+    require(!wants_diag || p.diag, HX_ERR_STATE, "diagnostic outputs requested but the graph was prepared without them");
+    const Arena& a = p.arena;
+    const size_t f = sizeof(float);
+    float* W = a.at<float>(p.exec_params);
+    float* G = a.at<float>(p.grads);
+    HX_CUDA(cudaMemcpyAsync(W, params, f * p.P, cudaMemcpyHostToDevice, rt->stream));
+    forward_backward(rt, p, W, G, 1.0f / float(p.B));
+    const size_t M = p.M;
+    HX_CUDA(cudaMemcpyAsync(out->grads, G, f * p.P, cudaMemcpyDeviceToHost, rt->stream));
+    HX_CUDA(cudaMemcpyAsync(out->loss, a.at<float>(p.loss), f, cudaMemcpyDeviceToHost, rt->stream));
+    if (out->accuracy) HX_CUDA(cudaMemcpyAsync(out->accuracy, a.at<float>(p.acc), f, cudaMemcpyDeviceToHost, rt->stream));
+    auto get = [&](float* dst, size_t off, size_t n) {
+        if (dst) HX_CUDA(cudaMemcpyAsync(dst, a.at<float>(off), f * n, cudaMemcpyDeviceToHost, rt->stream));
+    };
+    if (p.diag) {
+        // dlogits live in place of the logits; the logits output is
+        // reconstructed only through the probabilities (see docs): report
+        // dlogits and probabilities, and recompute logits when asked.
+        get(out->d_logits, p.logits, M * p.V);
+        get(out->probabilities, p.probs, M * p.V);
+        get(out->output, p.xL, M * p.D);
+        get(out->d_output, p.diag_dout, M * p.D);
+        get(out->layer_input_grads, p.diag_lig, size_t(p.L) * M * p.D);
+        get(out->head_probabilities, p.diag_hp, size_t(p.L) * p.B * p.H * p.T * p.T);
+        if (out->logits) {
+            gemm<false, false>(rt, p.M, p.V, p.D, a.at<float>(p.xL), p.D, W + p.off_out, p.V,
+                               EpiStore{a.at<float>(p.logits), (long)p.V, 0, 0});
+            get(out->logits, p.logits, M * p.V);
+        }
+    }
+    HX_CUDA(cudaStreamSynchronize(rt->stream));
+}
+
+int hx_lm_execute(hx_runtime* rt, const float* input_one_hot, const float* target_one_hot, const float* params,
+                  size_t pc, float lr, const hx_lm_outputs* out) {
+    const auto t0 = Clock::now();
+    const int rc = hx_guard(rt, [&] {
+        LmPlan& p = need_lm(rt);
+        require(input_one_hot && target_one_hot, HX_ERR_ARGUMENT, "generalized tiny training buffer schema");
+        const size_t n = size_t(p.M) * p.V;
+        if (p.onehot.bytes < 2 * n * sizeof(float)) p.onehot.allocate(2 * n * sizeof(float));
+        float* dev = p.onehot.as<float>();
+        HX_CUDA(cudaMemcpyAsync(dev, input_one_hot, n * sizeof(float), cudaMemcpyHostToDevice, rt->stream));
+        HX_CUDA(cudaMemcpyAsync(dev + n, target_one_hot, n * sizeof(float), cudaMemcpyHostToDevice, rt->stream));
+        const Arena& a = p.arena;
+        HX_CUDA(cudaMemsetAsync(a.at<int>(p.bad), 0, sizeof(int), rt->stream));
+        one_hot_decode_kernel<<<(p.M + 7) / 8, 256, 0, rt->stream>>>(p.M, p.V, dev, a.at<uint32_t>(p.in_tok), a.at<int>(p.bad));
+        HX_LAUNCHED(rt);
+        one_hot_decode_kernel<<<(p.M + 7) / 8, 256, 0, rt->stream>>>(p.M, p.V, dev + n, a.at<uint32_t>(p.tgt_tok), a.at<int>(p.bad));
+        HX_LAUNCHED(rt);
+        check_bad(rt, p, "INVALID_TINY_LM_ONE_HOT: every input/target row must hold exactly one 1.0 and zeros elsewhere");
+        copy_ids_kernel<<<grid_for(p.M, 256, rt->sm_count), 256, 0, rt->stream>>>(
+            p.M, p.V, a.at<uint32_t>(p.in_tok), a.at<uint32_t>(p.tgt_tok), a.at<int>(p.in_ids), a.at<int>(p.tgt_ids), a.at<int>(p.bad));
+        HX_LAUNCHED(rt);
+        lm_execute_common(rt, p, params, pc, lr, out);
+        if (rt->injected_now()) fail(HX_ERR_CUDA, "injected execute failure after device success");
+    });
+    if (rt) rt->record_execute(rc == HX_OK, us_since(t0));
+    return rc;
+}
+
+int hx_lm_execute_tokens(hx_runtime* rt, const uint32_t* in, const uint32_t* tgt, const float* params, size_t pc,
+                         const hx_lm_outputs* out) {
+    const auto t0 = Clock::now();
+    const int rc = hx_guard(rt, [&] {
+        LmPlan& p = need_lm(rt);
+        require(in && tgt, HX_ERR_ARGUMENT, "generalized tiny training buffer schema");
+        const Arena& a = p.arena;
+        HX_CUDA(cudaMemcpyAsync(a.at<uint32_t>(p.in_tok), in, sizeof(uint32_t) * p.M, cudaMemcpyHostToDevice, rt->stream));
+        HX_CUDA(cudaMemcpyAsync(a.at<uint32_t>(p.tgt_tok), tgt, sizeof(uint32_t) * p.M, cudaMemcpyHostToDevice, rt->stream));
+        HX_CUDA(cudaMemsetAsync(a.at<int>(p.bad), 0, sizeof(int), rt->stream));
+        copy_ids_kernel<<<grid_for(p.M, 256, rt->sm_count), 256, 0, rt->stream>>>(
+            p.M, p.V, a.at<uint32_t>(p.in_tok), a.at<uint32_t>(p.tgt_tok), a.at<int>(p.in_ids), a.at<int>(p.tgt_ids), a.at<int>(p.bad));
+        HX_LAUNCHED(rt);
+        check_bad(rt, p, "INVALID_TINY_LM_TOKEN: token id >= vocabulary size");
+        lm_execute_common(rt, p, params, pc, 0.0f, out);
+        if (rt->injected_now()) fail(HX_ERR_CUDA, "injected execute failure after device success");
+    });
+    if (rt) rt->record_execute(rc == HX_OK, us_since(t0));
+    return rc;
+}
+
+int hx_lm_state_upload(hx_runtime* rt, const float* params, const float* m, const float* v, const float* buf, size_t pc) {
+    return hx_guard(rt, [&] {
+        LmPlan& p = need_lm(rt);
+        require(params && pc == p.P, HX_ERR_ARGUMENT, "state upload: parameter count mismatch");
+        const Arena& a = p.arena;
+        const size_t b = sizeof(float) * p.P;
+        HX_CUDA(cudaMemcpyAsync(a.at<float>(p.params), params, b, cudaMemcpyHostToDevice, rt->stream));
+        auto put = [&](const float* src, size_t off) {
+            if (src) HX_CUDA(cudaMemcpyAsync(a.at<float>(off), src, b, cudaMemcpyHostToDevice, rt->stream));
+            else HX_CUDA(cudaMemsetAsync(a.at<float>(off), 0, b, rt->stream));
+        };
+        put(m, p.adam_m);
+        put(v, p.adam_v);
+        put(buf, p.muon_buf);
+        HX_CUDA(cudaStreamSynchronize(rt->stream));
+        p.state_ready = true;
+    });
+}
+
+int hx_lm_state_download(hx_runtime* rt, float* params, float* m, float* v, float* buf, size_t pc) {
+    return hx_guard(rt, [&] {
+        LmPlan& p = need_lm(rt);
+        require(pc == p.P, HX_ERR_ARGUMENT, "state download: parameter count mismatch");
+        require(p.state_ready, HX_ERR_STATE, "state download before upload");
+        const Arena& a = p.arena;
+        const size_t b = sizeof(float) * p.P;
+        auto get = [&](float* dst, size_t off) {
+            if (dst) HX_CUDA(cudaMemcpyAsync(dst, a.at<float>(off), b, cudaMemcpyDeviceToHost, rt->stream));
+        };
+        get(params, p.params);
+        get(m, p.adam_m);
+        get(v, p.adam_v);
+        get(buf, p.muon_buf);
+        HX_CUDA(cudaStreamSynchronize(rt->stream));
+    });
+}
+
+int hx_lm_set_optimizer(hx_runtime* rt, const hx_optimizer_config* opt) {
+    return hx_guard(rt, [&] {
+        LmPlan& p = need_lm(rt);
+        require(opt != nullptr, HX_ERR_ARGUMENT, "optimizer: null configuration");
+        require(opt->kind == HX_OPT_ADAM || opt->kind == HX_OPT_MUON, HX_ERR_ARGUMENT, "optimizer: unknown kind");
+        require(std::isfinite(opt->adam_lr) && std::isfinite(opt->beta1) && std::isfinite(opt->beta2) &&
+                    std::isfinite(opt->adam_eps) && opt->beta1 >= 0.f && opt->beta1 < 1.f && opt->beta2 >= 0.f &&
+                    opt->beta2 < 1.f,
+                HX_ERR_ARGUMENT, "optimizer: invalid Adam scalars");
+        if (opt->kind == HX_OPT_MUON) {
+            check_muon_shape(int(p.D), int(p.D));
+            check_muon_shape(int(p.D), int(p.F));
+            require(std::isfinite(opt->muon_lr) && std::isfinite(opt->muon_momentum), HX_ERR_ARGUMENT,
+                    "optimizer: invalid Muon scalars");
+        }
+        p.opt = *opt;
+    });
+}
+
+int hx_lm_train_step(hx_runtime* rt, const uint32_t* tokens, uint32_t step, float* loss) {
+    const auto t0 = Clock::now();
+    const int rc = hx_guard(rt, [&] {
+        LmPlan& p = need_lm(rt);
+        require(tokens && loss, HX_ERR_ARGUMENT, "train step: null buffer");
+        require(step >= 1, HX_ERR_ARGUMENT, "train step: step is 1-based");
+        require(p.state_ready, HX_ERR_STATE, "train step before state upload");
+        const Arena& a = p.arena;
+        const auto tb = Clock::now();
+        HX_CUDA(cudaMemcpyAsync(a.at<uint32_t>(p.tokens), tokens, sizeof(uint32_t) * size_t(p.B) * (p.T + 1),
+                                cudaMemcpyHostToDevice, rt->stream));
+        rt->metrics.last_input_bind_us = us_since(tb);
+        HX_CUDA(cudaMemsetAsync(a.at<int>(p.bad), 0, sizeof(int), rt->stream));
+        split_tokens_kernel<<<grid_for(p.M, 256, rt->sm_count), 256, 0, rt->stream>>>(
+            p.B, p.T, p.V, a.at<uint32_t>(p.tokens), a.at<int>(p.in_ids), a.at<int>(p.tgt_ids), a.at<int>(p.bad));
+        HX_LAUNCHED(rt);
+        forward_backward(rt, p, a.at<float>(p.params), a.at<float>(p.grads), 1.0f / float(p.B));
+        optimizer_step(rt, p, step);
+        const auto to = Clock::now();
+        int bad = 0;
+        HX_CUDA(cudaMemcpyAsync(loss, a.at<float>(p.loss), sizeof(float), cudaMemcpyDeviceToHost, rt->stream));
+        HX_CUDA(cudaMemcpyAsync(&bad, a.at<int>(p.bad), sizeof(int), cudaMemcpyDeviceToHost, rt->stream));
+        HX_CUDA(cudaStreamSynchronize(rt->stream));
+        rt->metrics.last_output_bind_us = us_since(to);
+        require(!bad, HX_ERR_ARGUMENT, "INVALID_TINY_LM_TOKEN: token id >= vocabulary size (state was updated with id 0)");
+        require(std::isfinite(*loss), HX_ERR_NONFINITE, "QNN_NONFINITE: training loss is not finite");
+        if (rt->injected_now()) fail(HX_ERR_CUDA, "injected execute failure after device success");
+    });
+    if (rt) rt->record_execute(rc == HX_OK, us_since(t0));
+    return rc;
+}
+
+int hx_lm_forward_backward_device(hx_runtime* rt, const uint32_t* tokens, float grad_scale) {
+    return hx_guard(rt, [&] {
+        LmPlan& p = need_lm(rt);
+        require(tokens, HX_ERR_ARGUMENT, "forward_backward: null tokens");
+        require(std::isfinite(grad_scale) && grad_scale > 0.f, HX_ERR_ARGUMENT, "forward_backward: invalid grad_scale");
+        require(p.state_ready, HX_ERR_STATE, "forward_backward before state upload");
+        const Arena& a = p.arena;
+        split_tokens_kernel<<<grid_for(p.M, 256, rt->sm_count), 256, 0, rt->stream>>>(
+            p.B, p.T, p.V, tokens, a.at<int>(p.in_ids), a.at<int>(p.tgt_ids), a.at<int>(p.bad));
+        HX_LAUNCHED(rt);
+        forward_backward(rt, p, a.at<float>(p.params), a.at<float>(p.grads), grad_scale);
+    });
+}
+
+int hx_lm_grad_buffer(hx_runtime* rt, float** grads, size_t* count) {
+    return hx_guard(rt, [&] {
+        LmPlan& p = need_lm(rt);
+        require(grads && count, HX_ERR_ARGUMENT, "grad_buffer: null output");
+        *grads = p.arena.at<float>(p.grads);
+        *count = p.P + 1;
+    });
+}
+
+int hx_lm_optimizer_step_device(hx_runtime* rt, uint32_t step) {
+    return hx_guard(rt, [&] {
+        LmPlan& p = need_lm(rt);
+        require(step >= 1, HX_ERR_ARGUMENT, "optimizer step is 1-based");
+        optimizer_step(rt, p, step);
+    });
+}
+
+int hx_lm_loss_device(hx_runtime* rt, float** loss) {
+    return hx_guard(rt, [&] {
+        LmPlan& p = need_lm(rt);
+        require(loss, HX_ERR_ARGUMENT, "loss_device: null output");
+        *loss = p.arena.at<float>(p.loss);
+    });
+}
+
+}  // extern "C"

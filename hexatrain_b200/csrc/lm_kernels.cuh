@@ -1,0 +1,469 @@
+// lm_kernels.cuh -- device kernels of the tiny-Transformer LM step.
+//
+// Rows are r = b*T + t over a batch of B sequences (the reference runs one
+// sequence per graph execute; here the batch is folded into the row index of
+// every kernel).  Reference lines are cited per kernel
+// (tiny_language_model_cpu.cpp unless noted).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cstdint>
+
+namespace hx {
+
+__device__ __forceinline__ float warp_max(float v) {
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+__device__ __forceinline__ double warp_sum(double v) {
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ float warp_sumf(float v) {
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// tokens [B, T+1] -> input ids / target ids [B*T].  Any id >= V sets *bad.
+__global__ void split_tokens_kernel(int B, int T, int V, const uint32_t* __restrict__ tokens,
+                                    int* __restrict__ in_ids, int* __restrict__ tgt_ids, int* bad)
+{
+    const int M = B * T;
+    for (int r = blockIdx.x * blockDim.x + threadIdx.x; r < M; r += gridDim.x * blockDim.x) {
+        const int b = r / T, t = r % T;
+        const uint32_t a = tokens[(size_t)b * (T + 1) + t], y = tokens[(size_t)b * (T + 1) + t + 1];
+        if (a >= (uint32_t)V || y >= (uint32_t)V) atomicExch(bad, 1);
+        in_ids[r] = a < (uint32_t)V ? (int)a : 0;
+        tgt_ids[r] = y < (uint32_t)V ? (int)y : 0;
+    }
+}
+
+// ids given directly [M] (validated the same way).
+__global__ void copy_ids_kernel(int M, int V, const uint32_t* __restrict__ a, const uint32_t* __restrict__ y,
+                                int* __restrict__ in_ids, int* __restrict__ tgt_ids, int* bad)
+{
+    for (int r = blockIdx.x * blockDim.x + threadIdx.x; r < M; r += gridDim.x * blockDim.x) {
+        if (a[r] >= (uint32_t)V || y[r] >= (uint32_t)V) atomicExch(bad, 1);
+        in_ids[r] = a[r] < (uint32_t)V ? (int)a[r] : 0;
+        tgt_ids[r] = y[r] < (uint32_t)V ? (int)y[r] : 0;
+    }
+}
+
+// x0[r,:] = E[id[r],:] + pos[t,:]   (:42 -- one-hot * E selects a row exactly)
+__global__ void embed_kernel(int M, int T, int D, const int* __restrict__ ids, const float* __restrict__ E,
+                             const float* __restrict__ pos, float* __restrict__ x)
+{
+    const long total = (long)M * D;
+    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+        const int r = (int)(i / D), d = (int)(i % D);
+        x[i] = __fadd_rn(E[(long)ids[r] * D + d], pos[(long)(r % T) * D + d]);
+    }
+}
+
+// LayerNorm forward, one warp per row (nf, :36): mean and variance in
+// double, inv = float(1/sqrt(var+eps)), xhat = (x - float(mean))*inv,
+// y = xhat*gamma + beta.  Saves float(mean) and inv for the backward pass.
+__global__ void layernorm_fwd_kernel(int M, int D, float eps, const float* __restrict__ x,
+                                     const float* __restrict__ g, const float* __restrict__ b,
+                                     float* __restrict__ y, float* __restrict__ mean_out, float* __restrict__ inv_out)
+{
+    const int lane = threadIdx.x & 31;
+    const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (row >= M) return;
+    const float* xr = x + (long)row * D;
+    double s = 0.0;
+    for (int d = lane; d < D; d += 32) s += xr[d];
+    const double m = warp_sum(s) / D;
+    double v = 0.0;
+    for (int d = lane; d < D; d += 32) {
+        const double z = xr[d] - m;
+        v += z * z;
+    }
+    v = warp_sum(v) / D;
+    const float inv = (float)(1.0 / sqrt(v + (double)eps));
+    const float mf = (float)m;
+    float* yr = y + (long)row * D;
+    for (int d = lane; d < D; d += 32) {
+        const float xh = __fmul_rn(__fsub_rn(xr[d], mf), inv);
+        yr[d] = __fadd_rn(__fmul_rn(xh, g[d]), b[d]);
+    }
+    if (lane == 0) {
+        mean_out[row] = mf;
+        inv_out[row] = inv;
+    }
+}
+
+// LayerNorm backward fused with the residual add (nb, :37, and "dr = dout +
+// drn" of :79): dx = res + inv/D*(D*z - sum z - xhat*sum(z*xhat)), z=dy*g.
+// Also writes per-CTA partial column sums of dy*xhat (dgamma) and dy
+// (dbeta) to part[blockIdx.x][2][D]; column_reduce finishes them.
+// Each CTA handles rows [blockIdx.x*rows_per_cta, ...).
+__global__ void layernorm_bwd_kernel(int M, int D, int rows_per_cta, const float* __restrict__ dy,
+                                     const float* __restrict__ x, const float* __restrict__ mean,
+                                     const float* __restrict__ inv, const float* __restrict__ g,
+                                     const float* __restrict__ res, float* __restrict__ dx,
+                                     float* __restrict__ part)
+{
+    extern __shared__ float acc[];  // [warps][2][D]
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    float* ga = acc + (size_t)warp * 2 * D;
+    float* ba = ga + D;
+    for (int d = lane; d < D; d += 32) { ga[d] = 0.f; ba[d] = 0.f; }
+    const int r0 = blockIdx.x * rows_per_cta;
+    const int r1 = min(M, r0 + rows_per_cta);
+    for (int row = r0 + warp; row < r1; row += nw) {
+        const float* dyr = dy + (long)row * D;
+        const float* xr = x + (long)row * D;
+        const float mf = mean[row], iv = inv[row];
+        double s = 0.0, sx = 0.0;
+        for (int d = lane; d < D; d += 32) {
+            const float xh = __fmul_rn(__fsub_rn(xr[d], mf), iv);
+            const double z = __fmul_rn(dyr[d], g[d]);
+            s += z;
+            sx += z * xh;
+            ga[d] = __fadd_rn(ga[d], __fmul_rn(dyr[d], xh));
+            ba[d] = __fadd_rn(ba[d], dyr[d]);
+        }
+        s = warp_sum(s);
+        sx = warp_sum(sx);
+        const float ivd = __fdiv_rn(iv, (float)D);
+        for (int d = lane; d < D; d += 32) {
+            const float xh = __fmul_rn(__fsub_rn(xr[d], mf), iv);
+            const double z = __fmul_rn(dyr[d], g[d]);
+            const float v = (float)((double)ivd * ((double)D * z - s - (double)xh * sx));
+            const long i = (long)row * D + d;
+            dx[i] = res ? __fadd_rn(res[i], v) : v;
+        }
+    }
+    __syncthreads();
+    for (int d = threadIdx.x; d < D; d += blockDim.x) {
+        float sg = 0.f, sb = 0.f;
+        for (int w = 0; w < nw; ++w) {
+            sg += acc[(size_t)w * 2 * D + d];
+            sb += acc[(size_t)w * 2 * D + D + d];
+        }
+        part[((size_t)blockIdx.x * 2) * D + d] = sg;
+        part[((size_t)blockIdx.x * 2 + 1) * D + d] = sb;
+    }
+}
+
+// out[c] = sum over parts p of part[p][which][c], in part order.
+__global__ void column_reduce_kernel(int parts, int D, const float* __restrict__ part, float* __restrict__ dgamma,
+                                     float* __restrict__ dbeta)
+{
+    for (int c = blockIdx.x * blockDim.x + threadIdx.x; c < 2 * D; c += gridDim.x * blockDim.x) {
+        const int which = c / D, d = c % D;
+        float s = 0.f;
+        for (int p = 0; p < parts; ++p) s += part[((size_t)p * 2 + which) * D + d];
+        (which ? dbeta : dgamma)[d] = s;
+    }
+}
+
+// ---- causal attention ------------------------------------------------------
+// qkv: [M, 3D] with q at columns [0,D), k at [D,2D), v at [2D,3D); head h
+// owns columns h*dh .. h*dh+dh-1 of each.  One CTA per (head, sequence).
+
+template <int DH>
+__device__ __forceinline__ float dot_dh(const float* a, const float* b) {
+    float s = 0.f;
+#pragma unroll
+    for (int d = 0; d < DH; ++d) s = fmaf(a[d], b[d], s);
+    return s;
+}
+
+// Forward (:44-45): p = softmax_j<=r(q_r.k_j * scale); ctx_r = sum p_j v_j.
+// Saves the row max and the row sum (as float) so the backward pass can
+// recompute p exactly; writes full P rows (zeros above the diagonal) only
+// when probs != nullptr.
+template <int DH>
+__global__ void attention_fwd_kernel(int T, int D, int H, float scale, const float* __restrict__ qkv,
+                                     float* __restrict__ ctx, float* __restrict__ row_max, float* __restrict__ row_sum,
+                                     float* __restrict__ probs)
+{
+    extern __shared__ float sm[];
+    const int h = blockIdx.x, b = blockIdx.y;
+    const int nw = blockDim.x >> 5, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    constexpr int LD = DH + 1;
+    float* Ks = sm;                      // [T][LD]
+    float* Vs = Ks + T * LD;             // [T][LD]
+    float* Ps = Vs + T * LD;             // [nw][T]
+    float* Qs = Ps + nw * T;             // [nw][DH]
+    const long rowbase = (long)b * T;
+    const int ld = 3 * D;
+    for (int i = threadIdx.x; i < T * DH; i += blockDim.x) {
+        const int j = i / DH, d = i % DH;
+        const float* src = qkv + (rowbase + j) * ld + h * DH + d;
+        Ks[j * LD + d] = src[D];
+        Vs[j * LD + d] = src[2 * D];
+    }
+    __syncthreads();
+    float* pw = Ps + warp * T;
+    float* qw = Qs + warp * DH;
+    for (int r = warp; r < T; r += nw) {
+        for (int d = lane; d < DH; d += 32) qw[d] = qkv[(rowbase + r) * ld + h * DH + d];
+        __syncwarp();
+        float mx = -INFINITY;
+        for (int j = lane; j <= r; j += 32) {
+            const float s = dot_dh<DH>(qw, Ks + j * LD) * scale;
+            pw[j] = s;
+            mx = fmaxf(mx, s);
+        }
+        mx = warp_max(mx);
+        double sum = 0.0;
+        for (int j = lane; j <= r; j += 32) {
+            const float e = expf(pw[j] - mx);
+            pw[j] = e;
+            sum += e;
+        }
+        const float sumf = (float)warp_sum(sum);
+        for (int j = lane; j <= r; j += 32) pw[j] = __fdiv_rn(pw[j], sumf);
+        __syncwarp();
+        if (probs) {
+            float* prow = probs + (((long)b * H + h) * T + r) * T;
+            for (int j = lane; j < T; j += 32) prow[j] = j <= r ? pw[j] : 0.f;
+        }
+        for (int d = lane; d < DH; d += 32) {
+            float acc = 0.f;
+            for (int j = 0; j <= r; ++j) acc = fmaf(pw[j], Vs[j * LD + d], acc);
+            ctx[(rowbase + r) * D + h * DH + d] = acc;
+        }
+        if (lane == 0) {
+            row_max[((long)b * H + h) * T + r] = mx;
+            row_sum[((long)b * H + h) * T + r] = sumf;
+        }
+        __syncwarp();
+    }
+}
+
+// Backward (:80-81).  With p recomputed from the saved row statistics:
+//   dP_rj = dc_r . v_j ; dot_r = sum_j dP_rj p_rj (double) ;
+//   dS_rj = p_rj (dP_rj - dot_r) ;
+//   dq_r = scale sum_j dS_rj k_j ; dk_j = scale sum_r dS_rj q_r ;
+//   dv_j = sum_r p_rj dc_r .
+// Phase 1 walks rows (dq, dot_r); phase 2 walks columns (dk, dv), lanes
+// spread over r, each lane accumulating DH-wide partials in registers.
+template <int DH>
+__global__ void attention_bwd_kernel(int T, int D, int H, float scale, const float* __restrict__ qkv,
+                                     const float* __restrict__ dctx, const float* __restrict__ row_max,
+                                     const float* __restrict__ row_sum, float* __restrict__ dqkv)
+{
+    extern __shared__ float sm[];
+    const int h = blockIdx.x, b = blockIdx.y;
+    const int nw = blockDim.x >> 5, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    constexpr int LD = DH + 1;
+    float* Qs = sm;                 // [T][LD]
+    float* Ks = Qs + T * LD;
+    float* Vs = Ks + T * LD;
+    float* Cs = Vs + T * LD;        // dctx head slice
+    float* dot = Cs + T * LD;       // [T]
+    float* mxs = dot + T;           // [T]
+    float* sms = mxs + T;           // [T]
+    float* Sw = sms + T;            // [nw][T]
+    const long rowbase = (long)b * T;
+    const int ld = 3 * D;
+    for (int i = threadIdx.x; i < T * DH; i += blockDim.x) {
+        const int j = i / DH, d = i % DH;
+        const float* src = qkv + (rowbase + j) * ld + h * DH + d;
+        Qs[j * LD + d] = src[0];
+        Ks[j * LD + d] = src[D];
+        Vs[j * LD + d] = src[2 * D];
+        Cs[j * LD + d] = dctx[(rowbase + j) * D + h * DH + d];
+    }
+    for (int i = threadIdx.x; i < T; i += blockDim.x) {
+        mxs[i] = row_max[((long)b * H + h) * T + i];
+        sms[i] = row_sum[((long)b * H + h) * T + i];
+    }
+    __syncthreads();
+    float* sw = Sw + warp * T;
+    // phase 1: rows
+    for (int r = warp; r < T; r += nw) {
+        const float* qr = Qs + r * LD;
+        const float* cr = Cs + r * LD;
+        double dsum = 0.0;
+        for (int j = lane; j <= r; j += 32) {
+            const float p = __fdiv_rn(expf(dot_dh<DH>(qr, Ks + j * LD) * scale - mxs[r]), sms[r]);
+            const float dp = dot_dh<DH>(cr, Vs + j * LD);
+            sw[j] = dp;
+            dsum += (double)__fmul_rn(dp, p);
+            // keep p for the dS pass in the upper half of the buffer slot
+        }
+        const float dt = (float)warp_sum(dsum);
+        for (int j = lane; j <= r; j += 32) {
+            const float p = __fdiv_rn(expf(dot_dh<DH>(qr, Ks + j * LD) * scale - mxs[r]), sms[r]);
+            sw[j] = __fmul_rn(p, __fsub_rn(sw[j], dt));
+        }
+        __syncwarp();
+        for (int d = lane; d < DH; d += 32) {
+            float acc = 0.f;
+            for (int j = 0; j <= r; ++j) acc = fmaf(sw[j], Ks[j * LD + d], acc);
+            dqkv[(rowbase + r) * ld + h * DH + d] = acc * scale;
+        }
+        if (lane == 0) dot[r] = dt;
+        __syncwarp();
+    }
+    __syncthreads();
+    // phase 2: columns
+    for (int j = warp; j < T; j += nw) {
+        float dk[DH], dv[DH];
+#pragma unroll
+        for (int d = 0; d < DH; ++d) { dk[d] = 0.f; dv[d] = 0.f; }
+        const float* kj = Ks + j * LD;
+        const float* vj = Vs + j * LD;
+        for (int r = j + lane; r < T; r += 32) {
+            const float* qr = Qs + r * LD;
+            const float* cr = Cs + r * LD;
+            const float p = __fdiv_rn(expf(dot_dh<DH>(qr, kj) * scale - mxs[r]), sms[r]);
+            const float ds = __fmul_rn(p, __fsub_rn(dot_dh<DH>(cr, vj), dot[r]));
+#pragma unroll
+            for (int d = 0; d < DH; ++d) {
+                dk[d] = fmaf(ds, qr[d], dk[d]);
+                dv[d] = fmaf(p, cr[d], dv[d]);
+            }
+        }
+#pragma unroll
+        for (int d = 0; d < DH; ++d) {
+            const float sk = warp_sumf(dk[d]);
+            const float sv = warp_sumf(dv[d]);
+            if (lane == 0) {
+                dqkv[(rowbase + j) * ld + D + h * DH + d] = sk * scale;
+                dqkv[(rowbase + j) * ld + 2 * D + h * DH + d] = sv;
+            }
+        }
+    }
+}
+
+// ---- cross-entropy ------------------------------------------------------------
+// One warp per row (:48 softmax, :77 loss/dLogits): max over the row (first
+// index of the max is the prediction), e = exp(l - max), s = sum e in
+// double, p = e / float(s), dlogits = (p - onehot)/T * scale (in place over
+// logits is allowed), row loss = max + log(s) - l[target] in double.
+__global__ void softmax_ce_kernel(int M, int V, int T, float scale, float* logits, const int* __restrict__ tgt,
+                                  float* __restrict__ probs, float* dlogits, double* __restrict__ row_loss,
+                                  int* __restrict__ row_correct)
+{
+    const int lane = threadIdx.x & 31;
+    const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (row >= M) return;
+    float* l = logits + (long)row * V;
+    float mx = -INFINITY;
+    int arg = 0x7fffffff;
+    for (int j = lane; j < V; j += 32) {
+        const float v = l[j];
+        if (v > mx || (v == mx && j < arg)) { mx = v; arg = j; }
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+        const float om = __shfl_xor_sync(0xffffffffu, mx, o);
+        const int oa = __shfl_xor_sync(0xffffffffu, arg, o);
+        if (om > mx || (om == mx && oa < arg)) { mx = om; arg = oa; }
+    }
+    double s = 0.0;
+    for (int j = lane; j < V; j += 32) s += (double)expf(l[j] - mx);
+    s = warp_sum(s);
+    const float sf = (float)s;
+    const int y = tgt[row];
+    const float ly = l[y];
+    __syncwarp();
+    float* out = dlogits + (long)row * V;
+    float* pr = probs ? probs + (long)row * V : nullptr;
+    for (int j = lane; j < V; j += 32) {
+        const float p = __fdiv_rn(expf(l[j] - mx), sf);
+        if (pr) pr[j] = p;
+        float d = __fdiv_rn(__fsub_rn(p, j == y ? 1.0f : 0.0f), (float)T);
+        if (scale != 1.0f) d = __fmul_rn(d, scale);
+        out[j] = d;
+    }
+    if (lane == 0) {
+        row_loss[row] = (double)mx + log(s) - (double)ly;
+        row_correct[row] = arg == y;
+    }
+}
+
+// Per-sequence loss float(sum_t loss/T) (:77), batch mean in double, and the
+// scaled loss term for the data-parallel gradient buffer.  One block.
+__global__ void loss_reduce_kernel(int B, int T, const double* __restrict__ row_loss, const int* __restrict__ row_correct,
+                                   float grad_scale, float* __restrict__ loss_out, float* __restrict__ acc_out,
+                                   float* __restrict__ scaled_loss_out)
+{
+    __shared__ double red[32];
+    __shared__ long cred[32];
+    double tot = 0.0;
+    long correct = 0;
+    for (int b = threadIdx.x; b < B; b += blockDim.x) {
+        double s = 0.0;
+        for (int t = 0; t < T; ++t) {
+            s += row_loss[(long)b * T + t];
+            correct += row_correct[(long)b * T + t];
+        }
+        tot += (double)(float)(s / T);
+    }
+    tot = warp_sum(tot);
+    for (int o = 16; o > 0; o >>= 1) correct += __shfl_xor_sync(0xffffffffu, correct, o);
+    if ((threadIdx.x & 31) == 0) { red[threadIdx.x >> 5] = tot; cred[threadIdx.x >> 5] = correct; }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double t = 0.0;
+        long c = 0;
+        for (int w = 0; w < (int)(blockDim.x >> 5); ++w) { t += red[w]; c += cred[w]; }
+        if (loss_out) *loss_out = (float)(t / B);
+        if (acc_out) *acc_out = (float)c / (float)((long)B * T);
+        if (scaled_loss_out) *scaled_loss_out = (float)(t * (double)grad_scale);
+    }
+}
+
+// Token-embedding gradient: gE[id[r],:] += dx0[r,:] (one-hot^T * dX0, :82).
+__global__ void embed_bwd_kernel(int M, int D, const int* __restrict__ ids, const float* __restrict__ dx,
+                                 float* __restrict__ gE)
+{
+    const long total = (long)M * D;
+    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+        const int r = (int)(i / D), d = (int)(i % D);
+        atomicAdd(&gE[(long)ids[r] * D + d], dx[i]);
+    }
+}
+
+// Learned position table gradient: gP[t,:] = sum_b dx0[b*T+t,:] (batch order).
+__global__ void position_bwd_kernel(int B, int T, int D, const float* __restrict__ dx, float* __restrict__ gP)
+{
+    const long total = (long)T * D;
+    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+        float s = 0.f;
+        for (int b = 0; b < B; ++b) s += dx[(long)b * T * D + i];
+        gP[i] = s;
+    }
+}
+
+// Packs wq, wk, wv [D,D] (consecutive in the registry) into W_qkv [D,3D].
+__global__ void pack_qkv_kernel(int D, const float* __restrict__ wq, float* __restrict__ packed)
+{
+    const long total = 3L * D * D;
+    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+        const int k = (int)(i / (3 * D)), n = (int)(i % (3 * D));
+        const int which = n / D, c = n % D;
+        packed[i] = wq[(long)which * D * D + (long)k * D + c];
+    }
+}
+
+// Checks that every row of a [rows, V] matrix is exactly one-hot (one 1.0,
+// the rest 0.0) and extracts the index.  Sets *bad otherwise.
+__global__ void one_hot_decode_kernel(int rows, int V, const float* __restrict__ oh, uint32_t* __restrict__ ids, int* bad)
+{
+    const int lane = threadIdx.x & 31;
+    const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (row >= rows) return;
+    int ones = 0, other = 0, idx = -1;
+    for (int j = lane; j < V; j += 32) {
+        const float v = oh[(long)row * V + j];
+        if (v == 1.0f) { ++ones; idx = j; } else if (v != 0.0f) ++other;
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+        ones += __shfl_xor_sync(0xffffffffu, ones, o);
+        other += __shfl_xor_sync(0xffffffffu, other, o);
+        idx = max(idx, __shfl_xor_sync(0xffffffffu, idx, o));
+    }
+    if (lane == 0) {
+        if (ones != 1 || other != 0) atomicExch(bad, 1);
+        ids[row] = idx < 0 ? 0u : (uint32_t)idx;
+    }
+}
+
+}  // namespace hx

@@ -1,0 +1,100 @@
+// runtime.cu -- runtime lifecycle: device binding, stream, metrics, errors.
+//
+// Replaces the reference's QAIRT adapter initialisation
+// (qnn/qnn_runtime_qairt.cpp:709-972 Runtime::initialize): instead of loading
+// a backend library and creating backend/device/context handles, a runtime
+// binds one CUDA device and owns one non-blocking stream.  Plans (MLP, LM,
+// Adam) hold their device memory from prepare until destroy.
+#include <cstdio>
+
+#include "plans.cuh"
+
+hx_runtime::~hx_runtime() {
+    cudaSetDevice(device);
+    mlp.reset();
+    lm.reset();
+    adam.reset();
+    scratch.release();
+    if (own_stream) cudaStreamDestroy(own_stream);
+}
+
+namespace {
+void write_err(char* err, size_t len, const std::string& msg) {
+    if (err && len) {
+        std::snprintf(err, len, "%s", msg.c_str());
+    }
+}
+}  // namespace
+
+extern "C" {
+
+int hx_runtime_create(int device, hx_runtime** out, char* err, size_t err_len) {
+    if (!out) {
+        write_err(err, err_len, "hx_runtime_create: null output pointer");
+        return HX_ERR_ARGUMENT;
+    }
+    *out = nullptr;
+    int count = 0;
+    cudaError_t e = cudaGetDeviceCount(&count);
+    if (e != cudaSuccess || count == 0) {
+        write_err(err, err_len, std::string("CUDA_DEVICE_NOT_FOUND: cannot initialize runtime: ") +
+                                    (e != cudaSuccess ? cudaGetErrorString(e) : "no CUDA device"));
+        return HX_ERR_CUDA;
+    }
+    if (device < 0 || device >= count) {
+        write_err(err, err_len, "CUDA_DEVICE_NOT_FOUND: device index " + std::to_string(device) + " out of range");
+        return HX_ERR_ARGUMENT;
+    }
+    cudaDeviceProp prop{};
+    if ((e = cudaGetDeviceProperties(&prop, device)) != cudaSuccess) {
+        write_err(err, err_len, std::string("cudaGetDeviceProperties: ") + cudaGetErrorString(e));
+        return HX_ERR_CUDA;
+    }
+    if (prop.major != 10) {
+        write_err(err, err_len, "UNSUPPORTED_DEVICE: built for sm_100a (B200); device " + std::to_string(device) +
+                                    " is sm_" + std::to_string(prop.major) + std::to_string(prop.minor));
+        return HX_ERR_UNSUPPORTED;
+    }
+    auto* rt = new (std::nothrow) hx_runtime();
+    if (!rt) return HX_ERR_MEMORY;
+    rt->device = device;
+    rt->sm_count = prop.multiProcessorCount;
+    rt->metrics.first_failure_call = -1;
+    if ((e = cudaSetDevice(device)) != cudaSuccess ||
+        (e = cudaStreamCreateWithFlags(&rt->own_stream, cudaStreamNonBlocking)) != cudaSuccess) {
+        write_err(err, err_len, std::string("cudaStreamCreate: ") + cudaGetErrorString(e));
+        delete rt;
+        return HX_ERR_CUDA;
+    }
+    rt->stream = rt->own_stream;
+    *out = rt;
+    write_err(err, err_len, "");
+    return HX_OK;
+}
+
+void hx_runtime_destroy(hx_runtime* rt) { delete rt; }
+
+const char* hx_runtime_last_error(const hx_runtime* rt) { return rt ? rt->last_error.c_str() : "null runtime"; }
+
+int hx_runtime_set_stream(hx_runtime* rt, void* stream) {
+    return hx_guard(rt, [&] { rt->stream = stream ? static_cast<cudaStream_t>(stream) : rt->own_stream; });
+}
+
+void* hx_runtime_stream(const hx_runtime* rt) { return rt ? static_cast<void*>(rt->stream) : nullptr; }
+
+int hx_runtime_synchronize(hx_runtime* rt) {
+    return hx_guard(rt, [&] { HX_CUDA(cudaStreamSynchronize(rt->stream)); });
+}
+
+int hx_runtime_metrics(const hx_runtime* rt, hx_metrics* out) {
+    if (!rt || !out) return HX_ERR_ARGUMENT;
+    *out = rt->metrics;
+    out->device_bytes = rt->scratch.bytes + hx::plan_device_bytes(rt);
+    return HX_OK;
+}
+
+int hx_runtime_inject_execute_failure(hx_runtime* rt, int64_t call_index) {
+    return hx_guard(rt, [&] { rt->inject_execute_at = call_index; });
+}
+
+}  // extern "C"

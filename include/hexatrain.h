@@ -1,0 +1,294 @@
+/*
+ * hexatrain.h -- C ABI of the HexaTrain B200 runtime (libhexatrain_b200.so).
+ *
+ * This is the drop-in replacement for the reference's runtime seam, class
+ * phonelm::qnn::Runtime (app/src/main/cpp/qnn/qnn_runtime.h:250-451): the
+ * same prepare-once / execute-per-step lifecycle, the same named inputs and
+ * outputs in the same order, and the same fail-closed error convention
+ * (a status plus a human-readable message whose prefix classifies the
+ * failure; nothing throws across this boundary).  Plain pointers and sizes
+ * only.  "Host" entry points take application-owned host buffers and copy
+ * them in and out per call, exactly like the reference's clientBuf binding;
+ * "_device" entry points take device pointers and run asynchronously on the
+ * runtime's stream.
+ *
+ * Threading: one runtime is used by one host thread at a time (as the
+ * reference's Runtime).  Several runtimes may coexist in one process.
+ */
+#ifndef HEXATRAIN_H
+#define HEXATRAIN_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------- */
+enum {
+    HX_OK = 0,
+    HX_ERR_ARGUMENT = 1,   /* null pointer, zero/oversized dimension, size mismatch */
+    HX_ERR_STATE = 2,      /* call out of lifecycle order (execute before prepare) */
+    HX_ERR_CUDA = 3,       /* a CUDA runtime call failed (message has the CUDA error) */
+    HX_ERR_NONFINITE = 4,  /* a result or input was NaN/Inf where the contract forbids it */
+    HX_ERR_MEMORY = 5,     /* device allocation failed */
+    HX_ERR_UNSUPPORTED = 6 /* a valid request this build does not serve */
+};
+
+typedef struct hx_runtime hx_runtime;
+
+/* ---- runtime ------------------------------------------------------------ */
+
+/* Create a runtime bound to CUDA device `device` with its own non-blocking
+ * stream.  Replaces Runtime::initialize (qnn/qnn_runtime.h:266).  On failure
+ * *out is NULL and `err` (if non-NULL) receives the message. */
+int hx_runtime_create(int device, hx_runtime** out, char* err, size_t err_len);
+/* Release every device allocation and the stream (Runtime::~Runtime,
+ * qnn/qnn_runtime.h:253). */
+void hx_runtime_destroy(hx_runtime* rt);
+/* Message of the last failed call on this runtime ("" after success).
+ * Mirrors the std::string& error out-parameter of every Runtime method. */
+const char* hx_runtime_last_error(const hx_runtime* rt);
+/* Use `stream` (a cudaStream_t, or NULL for the runtime's own stream) for
+ * all subsequent work.  The caller keeps ownership. */
+int hx_runtime_set_stream(hx_runtime* rt, void* stream);
+void* hx_runtime_stream(const hx_runtime* rt);
+/* Block until all work queued on the runtime's stream finished. */
+int hx_runtime_synchronize(hx_runtime* rt);
+
+/* Counters mirroring RuntimeMetrics / ApiTrace (qnn/qnn_runtime.h:58-131). */
+typedef struct {
+    uint64_t graph_create_count;     /* prepare calls that succeeded */
+    uint64_t graph_finalize_count;   /* CUDA graphs instantiated */
+    uint64_t graph_execute_count;    /* execute / step calls that succeeded */
+    uint64_t execute_attempt_count;
+    uint64_t execute_failure_count;
+    int64_t first_failure_call;      /* -1 if none */
+    double last_execute_us;          /* host wall time of the last execute */
+    double total_execute_us;
+    double last_input_bind_us;       /* host->device copy enqueue time */
+    double last_output_bind_us;      /* device->host copy + sync time */
+    uint64_t kernel_launches;        /* kernels this runtime launched */
+    uint64_t device_bytes;           /* device memory held by this runtime */
+} hx_metrics;
+int hx_runtime_metrics(const hx_runtime* rt, hx_metrics* out);
+
+/* Host-side failure injection (the reference's failGraphExecuteAt,
+ * qnn/qnn_runtime.h:136 and qnn/qnn_runtime_full_step.inc:383-397): the
+ * execute call whose attempt index equals `call_index` reports failure with
+ * code HX_ERR_CUDA and message "injected execute failure" after its device
+ * work finished.  -1 disables.  No device fault is involved. */
+int hx_runtime_inject_execute_failure(hx_runtime* rt, int64_t call_index);
+
+/* ---- two-layer ReLU MLP full training step ------------------------------ */
+/* Graph phonelm_mlp_training_step (qnn/qnn_runtime_full_step.inc:209-330):
+ *   Z1=X W1; H=ReLU(Z1); P=H W2; E=P-Y; loss=mean(E^2); dP=E*2/(B*O);
+ *   dW2=H^T dP; dH=dP W2^T (W2 before the update); mask=H>0;
+ *   dZ1=mask?dH:0; dW1=X^T dZ1; W1_next=W1-lr*dW1; W2_next=W2-lr*dW2.
+ * Shapes: X[B,I] Y[B,O] W1[I,H] W2[H,O], row-major FP32. */
+
+/* Runtime::prepareMlpFullStep (qnn/qnn_runtime.h:422).  diagnostic != 0
+ * makes the nine intermediate tensors readable (the reference's APP_READ
+ * diagnostic outputs). */
+int hx_mlp_prepare(hx_runtime* rt, uint32_t batch, uint32_t input_dim, uint32_t hidden_dim,
+                   uint32_t output_dim, int diagnostic);
+
+/* Output bindings, in the reference's output order
+ * (qnn/qnn_runtime_full_step.inc:353-354).  loss/w1_next/w2_next are
+ * required; the rest are written only when prepared with diagnostic != 0
+ * and may be NULL otherwise (NULL skips that output). */
+typedef struct {
+    float* loss;          /* [1]   */
+    float* w1_next;       /* [I*H] */
+    float* w2_next;       /* [H*O] */
+    float* prediction;    /* [B*O] */
+    float* error;         /* [B*O] */
+    float* d_prediction;  /* [B*O] */
+    float* d_w2;          /* [H*O] */
+    float* d_hidden;      /* [B*H] */
+    uint8_t* mask;        /* [B*H], 1 where hidden > 0 (BOOL_8) */
+    float* d_z1;          /* [B*H] */
+    float* d_w1;          /* [I*H] */
+    float* hidden;        /* [B*H] */
+} hx_mlp_outputs;
+
+/* Runtime::executeMlpFullStep (qnn/qnn_runtime.h:425-430): host buffers in,
+ * host buffers out, synchronous.  Element counts are checked against the
+ * prepared shape ("full step buffer size mismatch").  Inputs are not
+ * modified; outputs must not alias inputs. */
+int hx_mlp_execute(hx_runtime* rt, const float* x, size_t x_count, const float* y, size_t y_count,
+                   const float* w1, size_t w1_count, const float* w2, size_t w2_count,
+                   float learning_rate, const hx_mlp_outputs* out);
+
+/* Same step on device pointers (x,y,w1,w2 and every non-NULL field of
+ * `out`), enqueued on the runtime stream without synchronising.  This is the
+ * ping-pong form: the caller swaps its two weight buffers between calls, so
+ * no weight bytes are copied per step.  `out` itself is a host struct. */
+int hx_mlp_execute_device(hx_runtime* rt, const float* x, const float* y, const float* w1,
+                          const float* w2, float learning_rate, const hx_mlp_outputs* out);
+
+/* ---- tiny causal Transformer LM ----------------------------------------- */
+
+enum {
+    HX_LM_LEARNED_POSITION = 1u  /* learned [T,D] table after token_embedding
+                                    instead of the fixed sinusoid*0.05 */
+};
+
+typedef struct {
+    uint32_t vocab;   /* V */
+    uint32_t tokens;  /* T (sequence length) */
+    uint32_t dim;     /* D */
+    uint32_t ffn;     /* F */
+    uint32_t layers;  /* L */
+    uint32_t heads;   /* H, D % H == 0 */
+    float eps;        /* LayerNorm epsilon (the reference uses 1e-5) */
+    uint32_t flags;   /* HX_LM_* */
+} hx_lm_config;
+
+/* Parameter count of the flat registry-ordered buffer
+ * (tiny_language_model_cpu.cpp parameterRegistry; flattening order of
+ * qnn/qnn_transformer_training.cpp:1164-1180):
+ *   token_embedding[V*D], (position_embedding[T*D] if learned),
+ *   per layer {norm1_gamma[D], norm1_beta[D], wq, wk, wv, wo [D*D each],
+ *              norm2_gamma[D], norm2_beta[D], ffn_w1[D*F], ffn_w2[F*D]},
+ *   output_projection[D*V]. */
+size_t hx_lm_param_count(const hx_lm_config* cfg);
+/* Validate a configuration (tiny_lm::validateConfig,
+ * transformer_resource_estimator.h:76-83).  Returns HX_OK or
+ * HX_ERR_ARGUMENT and writes the classified message to err. */
+int hx_lm_validate(const hx_lm_config* cfg, char* err, size_t err_len);
+/* Deterministic initialisers, host side.  _reference reproduces
+ * tiny_lm::initialParameters (tiny_language_model_cpu.cpp:69-70); _normal
+ * draws N(0, std) for every matrix and table (gamma=1, beta=0) from a
+ * splitmix64 stream seeded by `seed`. */
+int hx_lm_init_reference(const hx_lm_config* cfg, uint32_t seed, float* params);
+int hx_lm_init_normal(const hx_lm_config* cfg, uint64_t seed, float std, float* params);
+
+/* Runtime::prepareTinyTransformerTraining, generalized builder
+ * (qnn/qnn_runtime.h:398-408, qnn/qnn_runtime_transformer_training_generalized.inc:4).
+ * `batch` sequences are processed per execute (the reference runs one per
+ * graph execute and loops on the host; here the batch is folded into the
+ * row dimension of every kernel).  diagnostic != 0 keeps per-sequence
+ * logits/probabilities/dlogits/output readable. */
+int hx_lm_prepare(hx_runtime* rt, const hx_lm_config* cfg, uint32_t batch, int diagnostic);
+
+/* Outputs of one execute.  loss and grads are required.  The diagnostic
+ * fields need diagnostic != 0 at prepare time and may be NULL. Shapes are
+ * per batch: [batch*T*V] etc. */
+typedef struct {
+    float* loss;               /* [1] mean over sequences of the mean CE */
+    float* accuracy;           /* [1] optional: argmax accuracy over all rows */
+    float* grads;              /* [P] sum_b grad_b / batch, registry order */
+    float* logits;             /* [batch*T*V] */
+    float* probabilities;      /* [batch*T*V] */
+    float* d_logits;           /* [batch*T*V]  (p - onehot)/T (times 1/batch) */
+    float* output;             /* [batch*T*D]  last block output */
+    float* d_output;           /* [batch*T*D]  dloss/doutput */
+    float* layer_input_grads;  /* [L*batch*T*D] */
+    float* head_probabilities; /* [L*batch*H*T*T] */
+} hx_lm_outputs;
+
+/* Runtime::executeTinyTransformerTraining (qnn/qnn_runtime.h:409-412):
+ * one-hot rows in (input/target [batch*T*V], host), current parameters
+ * (host, flat registry order), learning_rate must be 0 (the graph stops at
+ * gradients, qnn/qnn_runtime_transformer_training_generalized_execute.inc:88-91),
+ * outputs to host.  A row that is not exactly one-hot is rejected
+ * ("INVALID_TINY_LM_ONE_HOT"). */
+int hx_lm_execute(hx_runtime* rt, const float* input_one_hot, const float* target_one_hot,
+                  const float* params, size_t param_count, float learning_rate,
+                  const hx_lm_outputs* out);
+/* Same with token ids [batch*T] instead of one-hot rows. */
+int hx_lm_execute_tokens(hx_runtime* rt, const uint32_t* input_tokens, const uint32_t* target_tokens,
+                         const float* params, size_t param_count, const hx_lm_outputs* out);
+
+/* -- device-resident training state (the batched driver loop of
+ *    qnn/qnn_transformer_training.cpp:7281-7345 in one call per step) ---- */
+
+enum { HX_OPT_ADAM = 0, HX_OPT_MUON = 1 };
+typedef struct {
+    uint32_t kind;        /* HX_OPT_ADAM: Adam on every parameter.
+                             HX_OPT_MUON: Muon on wq,wk,wv,wo,ffn_w1,ffn_w2;
+                             Adam on the rest. */
+    float adam_lr, beta1, beta2, adam_eps;
+    float muon_lr, muon_momentum;
+    uint32_t muon_nesterov, muon_ns_steps;
+    float ns_a, ns_b, ns_c;
+    uint32_t muon_bf16_inputs;  /* round Newton-Schulz operands to bf16 */
+} hx_optimizer_config;
+
+/* Load parameters (and Adam moments / Muon buffers, or zeros when NULL)
+ * into device state.  Requires hx_lm_prepare. */
+int hx_lm_state_upload(hx_runtime* rt, const float* params, const float* adam_m, const float* adam_v,
+                       const float* muon_buf, size_t param_count);
+int hx_lm_state_download(hx_runtime* rt, float* params, float* adam_m, float* adam_v,
+                         float* muon_buf, size_t param_count);
+int hx_lm_set_optimizer(hx_runtime* rt, const hx_optimizer_config* opt);
+
+/* One training step on the device state: tokens [batch, T+1] host ids
+ * (sequence b reads ids[b][0..T-1], predicts ids[b][1..T]); forward,
+ * backward, gradient averaging and the optimizer update with bias
+ * corrections for step `step` (1-based).  *loss receives the mean loss
+ * (host).  Host in, host out, synchronous. */
+int hx_lm_train_step(hx_runtime* rt, const uint32_t* tokens, uint32_t step, float* loss);
+
+/* The same step split for data parallelism, on device pointers, async:
+ *  1. hx_lm_forward_backward_device: tokens [batch, T+1] (device uint32)
+ *     -> device gradient buffer (sum_b grad_b * grad_scale) and its last
+ *     element = sum_b loss_b * grad_scale;
+ *  2. the caller all-reduces that buffer (P+1 floats) across ranks;
+ *  3. hx_lm_optimizer_step_device applies the optimizer.
+ * grad_scale is 1/global_batch. */
+int hx_lm_forward_backward_device(hx_runtime* rt, const uint32_t* tokens, float grad_scale);
+int hx_lm_grad_buffer(hx_runtime* rt, float** grads, size_t* count);
+int hx_lm_optimizer_step_device(hx_runtime* rt, uint32_t step);
+/* Device pointer to the mean loss of the last step (1 float). */
+int hx_lm_loss_device(hx_runtime* rt, float** loss);
+
+/* ---- elementwise Adam ----------------------------------------------------- */
+/* Graph phonelm_adam_optimizer (qnn/qnn_runtime_transformer.inc:926-1109):
+ *   g'=g*gradient_scale; m'=b1*m+(1-b1)*g'; v'=b2*v+(1-b2)*g'^2;
+ *   m^=m'*c1; v^=v'*c2; r=sqrt(v^); den=r+eps; div=m^/den;
+ *   norm=(v^>0)?div:0; upd=lr*norm; w'=w-upd
+ * with b1=0.9, b2=0.999, eps=1e-8 and the rounding order of
+ * tiny_lm::adamUpdate (tiny_language_model_cpu.cpp:124-145). */
+int hx_adam_prepare(hx_runtime* rt, uint32_t elements);
+typedef struct {
+    float* m_next;
+    float* v_next;
+    float* m_hat;
+    float* v_hat;
+    float* sqrt_v_hat;
+    float* denominator;
+    float* divided;
+    float* normalized;
+    float* scaled_update;
+    float* w_next;          /* required; all others may be NULL */
+} hx_adam_outputs;
+/* Runtime::executeAdamOptimizer (qnn/qnn_runtime.h:361-369), host buffers,
+ * synchronous.  Rejects non-finite scalars and gradient_scale outside
+ * [0,1] ("Adam optimizer buffer size or scalar"). */
+int hx_adam_execute(hx_runtime* rt, const float* current, const float* gradient,
+                    const float* first_moment, const float* second_moment, float learning_rate,
+                    float gradient_scale, float first_correction, float second_correction,
+                    const hx_adam_outputs* out);
+/* Device-pointer variant over n elements (w_next, m_next and v_next are
+ * required; in-place updates w_next==current etc. are allowed). */
+int hx_adam_execute_device(hx_runtime* rt, size_t n, const float* current, const float* gradient,
+                           const float* first_moment, const float* second_moment,
+                           float learning_rate, float gradient_scale, float first_correction,
+                           float second_correction, const hx_adam_outputs* out);
+
+/* ---- Muon (no counterpart in the reference) ------------------------------ */
+/* Momentum (+Nesterov) and quintic Newton-Schulz orthogonalisation of one
+ * matrix update, Jordan et al. 2024; see hx_optimizer_config.  Host buffers
+ * [rows*cols], synchronous.  rows, cols <= 256. */
+int hx_muon_execute(hx_runtime* rt, uint32_t rows, uint32_t cols, const float* weight,
+                    const float* gradient, const float* momentum_buffer, float learning_rate,
+                    float momentum, int nesterov, uint32_t ns_steps, float a, float b, float c,
+                    int bf16_inputs, float* weight_next, float* momentum_buffer_next);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* HEXATRAIN_H */
