@@ -1,0 +1,377 @@
+#!/usr/bin/env python
+"""Training-step throughput of the tiny-Transformer LM step on B200.
+
+Workload (the data-parallel configuration quoted at 1/2/4/8 GPUs): vocab
+1024, T=256, d_model 256, FFN 1024, 4 layers, 8 heads, learned positions,
+N(0, 0.02) init, FP32 master weights and arithmetic, Adam (1e-3, 0.9, 0.999,
+1e-8), global batch 512 sequences of seeded Zipf(1.1) token ids, split evenly
+over ranks; per-step gradient all-reduce (NCCL) for N > 1.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Prints one JSON line (rank 0).  `value` is device-timed whole-job tokens/s
+with the step's token ids already in HBM; `e2e` is the same metric through
+the public API with host buffers (pinned host ids copied in and the loss
+read back every step).  `roofline` reports the dominant kernel class, timed
+live with CUDA events over the timed region.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+V, T, D, F, L, H = 1024, 256, 256, 1024, 4, 8
+GLOBAL_BATCH = 512
+SEED = 20260710
+WORKLOAD = "tiny_lm_train_step V1024 T256 D256 F1024 L4 H8 Adam learned-pos global_batch=512"
+METRIC = "train-step tokens/s (LM V1024 T256 D256 F1024 L4 H8, global batch 512)"
+FP32_CUDA_CORE_PEAK_TFLOPS = 148 * 128 * 2 * 1.965e9 / 1e12  # nominal, at max SM clock
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def measured_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            p = json.load(f)
+        return p, "measured"
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                       "-i", str(gpu_index), "-lms", "200"], stdout=subprocess.PIPE,
+                                      stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.p = None
+
+    def stop(self):
+        if self.p is None:
+            return None
+        self.p.terminate()
+        try:
+            out = self.p.communicate(timeout=10)[0]
+        except subprocess.TimeoutExpired:
+            self.p.kill()
+            out = self.p.communicate()[0]
+        mhz, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                mhz.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not mhz:
+            return None
+        return {"sm_mhz": statistics.median(mhz), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(mhz)}
+
+
+def physical_gpu(local_rank: int) -> int:
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        ids = [x for x in vis.split(",") if x.strip()]
+        if local_rank < len(ids) and ids[local_rank].strip().isdigit():
+            return int(ids[local_rank])
+    return local_rank
+
+
+def cpu_threads() -> int:
+    try:
+        return max(1, min(len(os.sched_getaffinity(0)), 64))
+    except AttributeError:
+        return max(1, min(os.cpu_count() or 1, 64))
+
+
+def reference_cpu_step_runner():
+    """The reference's CPU path (oracle/_ref) when built, else the oracle port."""
+    from oracle.oracle import LmConfig as OC, Oracle, Reference, reference_available
+    cfg = OC.make(V, T, D, F, L, H)
+    if reference_available():
+        ref = Reference()
+
+        def step(tokens, params, m, v, step_no, threads):
+            return ref.lm_train_step(cfg, tokens, params, m, v, 1e-3, step_no, threads)
+        return step, "reference", ref.param_count(cfg)
+    port = Oracle()
+
+    def step(tokens, params, m, v, step_no, threads):
+        g, loss = port.lm_batch_gradients(cfg, tokens, params, threads)
+        c1, c2 = port.adam_correction(0.9, step_no), port.adam_correction(0.999, step_no)
+        m[:], v[:], _, _, params[:] = port.adam(params, g, m, v, 1e-3, c1, c2)
+        return loss
+    return step, "port", port.param_count(cfg)
+
+
+def cpu_sample(steps: int, warmup: int):
+    """Times the CPU path of the step on a bounded sample: `threads`
+    sequences of the workload per step, all host threads.  The reference
+    model has no learned positions, so the sample runs its fixed-position
+    variant of the same shape (identical FLOPs)."""
+    import hexatrain_b200 as hx
+    from hexatrain_b200 import data
+    step_fn, kind, P = reference_cpu_step_runner()
+    threads = cpu_threads()
+    params = hx.LmConfig(V, T, D, F, L, H).init_normal(SEED, 0.02)
+    assert params.size == P
+    m = np.zeros_like(params)
+    v = np.zeros_like(params)
+    times = []
+    for s in range(warmup + steps):
+        toks = data.lm_tokens(SEED, threads, T, V, step=s)
+        t0 = time.perf_counter()
+        step_fn(toks, params, m, v, s + 1, threads)
+        if s >= warmup:
+            times.append(time.perf_counter() - t0)
+    tokens = threads * T * len(times)
+    return {"value": tokens / sum(times), "unit": "tokens/s", "cores": threads, "kind": kind,
+            "sample": f"{threads} sequences of T={T} per step (of the {GLOBAL_BATCH}-sequence batch), forward+"
+                      f"backward+Adam over all {P} parameters, {len(times)} timed steps after {warmup} warm-up"}
+
+
+def run_reference_arm(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    steps, warmup = max(1, args.steps), max(0, args.warmup)
+    # bounded: each step is a sample of `threads` sequences; cap the count so the run stays within minutes
+    steps = min(steps, 20)
+    warmup = min(warmup, 2)
+    cb = cpu_sample(steps, warmup)
+    line = {"impl": "reference", "metric": METRIC, "value": cb["value"], "unit": "tokens/s", "n_gpus": args.gpus,
+            "steps": steps, "warmup": warmup, "ms_per_step": None, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded Zipf(1.1) token ids)",
+            "config": {"workload": WORKLOAD, "global_batch": GLOBAL_BATCH, "seq_len": T,
+                       "parallelism": "host threads", "sample": cb["sample"]},
+            "cpu_baseline": cb,
+            "e2e": {"value": cb["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def torch_view(ptr: int, count: int):
+    import torch
+
+    class _CAI:
+        def __init__(self):
+            self.__cuda_array_interface__ = {"shape": (count,), "typestr": "<f4", "data": (ptr, False),
+                                             "version": 3, "strides": None}
+    return torch.as_tensor(_CAI(), device="cuda")
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    import hexatrain_b200 as hx
+    from hexatrain_b200 import data
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    if GLOBAL_BATCH % world:
+        raise SystemExit("global batch must divide evenly over ranks")
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local), timeout=timedelta(seconds=300))
+    B = GLOBAL_BATCH // world
+    K, W = args.steps, max(3, args.warmup)
+    cfg = hx.LmConfig(V, T, D, F, L, H, learned_position=True)
+    rt = hx.Runtime()
+    if not rt.initialize(local):
+        raise SystemExit(rt.last_error)
+    # A dedicated stream (torch's default stream has handle 0, which the C ABI
+    # reads as "the runtime's own stream"): kernels, NCCL and timing events
+    # all go to this one stream.
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    assert stream.cuda_stream != 0
+    assert rt.set_stream(stream.cuda_stream), rt.last_error
+    assert rt.prepare_lm(cfg, B), rt.last_error
+    assert rt.lm_state_upload(cfg.init_normal(SEED, 0.02)), rt.last_error
+    gptr, gcount = rt.lm_grad_buffer()
+    grads = torch_view(gptr, gcount)
+    loss_t = torch_view(rt.lm_loss_device(), 1)
+
+    def ids(step):
+        return data.lm_tokens(SEED, GLOBAL_BATCH, T, V, step=step)[rank * B:(rank + 1) * B]
+
+    dev_tokens = [torch.from_numpy(ids(s).astype(np.int32)).cuda() for s in range(W + K)]
+    torch.cuda.synchronize()
+    step_no = 0
+
+    def device_step(tok):
+        nonlocal step_no
+        step_no += 1
+        assert rt.lm_forward_backward_device(tok.data_ptr(), 1.0 / GLOBAL_BATCH), rt.last_error
+        if world > 1:
+            dist.all_reduce(grads)
+        assert rt.lm_optimizer_step_device(step_no), rt.last_error
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for s in range(W):
+        device_step(dev_tokens[s])
+    barrier()
+    clocks = ClockSampler(physical_gpu(local)) if rank == 0 else None
+    launches0 = rt.metrics().kernel_launches
+    assert rt.profile(True), rt.last_error
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    e0.record(stream)
+    for s in range(K):
+        device_step(dev_tokens[W + s])
+    e1.record(stream)
+    barrier()
+    t_ms = e0.elapsed_time(e1)
+    prof = rt.profile_read()
+    rt.profile(False)
+    launches = rt.metrics().kernel_launches - launches0
+    clk = clocks.stop() if clocks else None
+    tmax = torch.tensor([t_ms], device="cuda")
+    if world > 1:
+        dist.all_reduce(tmax, op=dist.ReduceOp.MAX)
+    t_ms = float(tmax.item())
+    final_loss = float(loss_t.item())
+
+    # ---- end to end through the public API with host buffers ----
+    pinned = [torch.from_numpy(ids(1000 + s).astype(np.int32)).pin_memory() for s in range(W + K)]
+    tok_buf = torch.empty((B, T + 1), dtype=torch.int32, device="cuda")
+    host_loss = np.zeros(1, np.float32)
+
+    def e2e_step(i):
+        if world == 1:
+            ok, lv = rt.lm_train_step(pinned[i].numpy().view(np.uint32), step_no + 1)
+            assert ok, rt.last_error
+            return lv
+        tok_buf.copy_(pinned[i], non_blocking=True)
+        device_step(tok_buf)
+        return float(loss_t.item())
+
+    for i in range(W):
+        e2e_step(i)
+        step_no += 1 if world == 1 else 0
+    barrier()
+    t0 = time.perf_counter()
+    e2 = torch.cuda.Event(enable_timing=True)
+    e3 = torch.cuda.Event(enable_timing=True)
+    e2.record(stream)
+    for i in range(K):
+        host_loss[0] = e2e_step(W + i)
+        step_no += 1 if world == 1 else 0
+    e3.record(stream)
+    barrier()
+    te_ms = max(e2.elapsed_time(e3), (time.perf_counter() - t0) * 1e3)
+    te = torch.tensor([te_ms], device="cuda")
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    te_ms = float(te.item())
+
+    if rank == 0:
+        tokens_per_step = GLOBAL_BATCH * T
+        value = tokens_per_step * K / (t_ms / 1e3)
+        peaks, peak_kind = measured_peaks()
+        dom = max(prof.items(), key=lambda kv: kv[1]["total_ms"]) if prof else ("none", None)
+        name, d = dom
+        roof = None
+        if d:
+            if d["flops"] / max(d["bytes"], 1.0) > 50:
+                achieved = d["flops"] / (d["total_ms"] / 1e3) / 1e12
+                peak = float(peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops")))
+                roof = {"kernel": name, "bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                        "frac": achieved / peak, "peak_source": f"{peak_kind} bf16 dense, sustained",
+                        "frac_of_fp32_cuda_core_nominal": achieved / FP32_CUDA_CORE_PEAK_TFLOPS,
+                        "launches_per_step": d["launches"] / K, "share_of_step": d["total_ms"] / t_ms,
+                        "traffic": traffic_from_profiles(name)}
+            else:
+                achieved = d["bytes"] / (d["total_ms"] / 1e3) / 1e9
+                peak = float(peaks["hbm_gbs"])
+                roof = {"kernel": name, "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                        "frac": achieved / peak, "peak_source": f"{peak_kind} HBM copy",
+                        "launches_per_step": d["launches"] / K, "share_of_step": d["total_ms"] / t_ms,
+                        "traffic": traffic_from_profiles(name)}
+        kernels = {k: {"ms_per_step": v["total_ms"] / K, "launches_per_step": v["launches"] / K,
+                       "tflops": v["flops"] / max(v["total_ms"], 1e-9) / 1e9,
+                       "gbs": v["bytes"] / max(v["total_ms"], 1e-9) / 1e6} for k, v in prof.items()}
+        cb = None
+        if world == 1 and not args.no_cpu_baseline:
+            cb = cpu_sample(steps=1, warmup=0)
+        line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": K, "warmup": W,
+                "ms_per_step": t_ms / K, "steps_per_s": 1e3 * K / t_ms, "higher_is_better": True,
+                "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+                "data": "synthetic (seeded Zipf(1.1) token ids, N(0,0.02) init)",
+                "config": {"workload": WORKLOAD, "global_batch": GLOBAL_BATCH, "seq_len": T,
+                           "parallelism": f"dp{world}", "per_rank_batch": B,
+                           "l2": "no flush: the per-step working set (~13 GB of activations) exceeds the 126 MB L2"},
+                "e2e": {"value": GLOBAL_BATCH * T * K / (te_ms / 1e3), "unit": "tokens/s",
+                        "h2d_bytes_per_step": B * (T + 1) * 4, "d2h_bytes_per_step": 4},
+                "roofline": roof, "kernels": kernels, "gpu_launches": int(launches), "clocks": clk,
+                "cpu_baseline": cb, "final_loss": final_loss}
+        print(json.dumps(line), flush=True)
+    rt.close()
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+def traffic_from_profiles(kernel: str):
+    """DRAM bytes per launch of a kernel class, from the committed ncu summary."""
+    path = os.path.join(ROOT, "profiles", "dram_traffic.json")
+    if not os.path.exists(path):
+        return None
+    with open(path) as f:
+        t = json.load(f)
+    e = t.get(WORKLOAD, {}).get(kernel)
+    return e.get("dram_bytes_per_launch") if e else None
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        return run_reference_arm(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -50,6 +50,11 @@ class Metrics(C.Structure):
     ]
 
 
+class ProfileEntry(C.Structure):
+    _fields_ = [("name", C.c_char * 32), ("launches", C.c_uint64), ("total_ms", C.c_double), ("flops", C.c_double),
+                ("bytes", C.c_double)]
+
+
 class MlpOutputsC(C.Structure):
     _fields_ = [(n, _fp) for n in ("loss", "w1_next", "w2_next", "prediction", "error", "d_prediction",
                                    "d_w2", "d_hidden")] + [("mask", _u8p)] + \
@@ -88,6 +93,8 @@ SIGNATURES = {
     "hx_runtime_synchronize": (C.c_int, [C.c_void_p]),
     "hx_runtime_metrics": (C.c_int, [C.c_void_p, C.POINTER(Metrics)]),
     "hx_runtime_inject_execute_failure": (C.c_int, [C.c_void_p, C.c_int64]),
+    "hx_runtime_profile": (C.c_int, [C.c_void_p, C.c_int]),
+    "hx_runtime_profile_read": (C.c_int, [C.c_void_p, C.POINTER(ProfileEntry), C.c_int, C.POINTER(C.c_int)]),
     "hx_mlp_prepare": (C.c_int, [C.c_void_p, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, C.c_int]),
     "hx_mlp_execute": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.c_void_p, C.c_size_t, C.c_void_p,
                                  C.c_size_t, C.c_void_p, C.c_size_t, C.c_float, C.POINTER(MlpOutputsC)]),

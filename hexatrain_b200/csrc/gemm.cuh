@@ -49,6 +49,7 @@ template <bool AT, bool BT, class Epi>
 void gemm(hx_runtime* rt, int M, int N, int K, const float* A, long lda, const float* B, long ldb, Epi epi)
 {
     require(M > 0 && N > 0 && K >= 0, HX_ERR_ARGUMENT, "gemm: bad shape");
+    ProfScope prof(rt, kTagGemm, 2.0 * M * N * K, 4.0 * ((double)M * K + (double)K * N + (double)M * N));
     const long mn = (long)M * N;
     if (mn >= 128L * 128 * rt->sm_count / 2)
         launch_simt<128, 128, 8, 16, 16, AT, BT>(rt, M, N, K, A, lda, B, ldb, epi);

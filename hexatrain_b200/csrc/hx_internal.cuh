@@ -85,6 +85,39 @@ struct Arena {
     template <class T> T* at(size_t offset) const { return reinterpret_cast<T*>(static_cast<char*>(block.ptr) + offset); }
 };
 
+// Kernel classes for the event profiler (hx_runtime_profile).
+enum ProfTag { kTagGemm = 0, kTagAttnFwd, kTagAttnBwd, kTagLayerNorm, kTagSoftmaxCe, kTagOptimizer, kTagEmbed,
+               kTagReduce, kTagCount };
+inline const char* prof_tag_name(int t) {
+    static const char* n[] = {"gemm", "attention_fwd", "attention_bwd", "layernorm", "softmax_ce", "optimizer",
+                              "embedding", "reduce"};
+    return (t >= 0 && t < kTagCount) ? n[t] : "other";
+}
+
+struct ProfRecord {
+    int tag;
+    cudaEvent_t a, b;
+    double flops, bytes;
+};
+
+struct Profiler {
+    bool on = false;
+    std::vector<cudaEvent_t> pool;
+    size_t used = 0;
+    std::vector<ProfRecord> recs;
+    ~Profiler() {
+        for (cudaEvent_t e : pool) cudaEventDestroy(e);
+    }
+    cudaEvent_t next() {
+        if (used == pool.size()) {
+            cudaEvent_t e;
+            check_cuda(cudaEventCreate(&e), "cudaEventCreate");
+            pool.push_back(e);
+        }
+        return pool[used++];
+    }
+};
+
 struct MlpPlan;
 struct LmPlan;
 struct AdamPlan;
@@ -107,6 +140,7 @@ struct hx_runtime {
     std::unique_ptr<hx::LmPlan, hx::LmPlanDeleter> lm;
     std::unique_ptr<hx::AdamPlan> adam;
     hx::DeviceBuffer scratch;  // generic device workspace (grows on demand)
+    hx::Profiler prof;
 
     ~hx_runtime();
     void activate() const { hx::check_cuda(cudaSetDevice(device), "cudaSetDevice"); }
@@ -132,6 +166,31 @@ struct hx_runtime {
         return inject_execute_at >= 0 && uint64_t(inject_execute_at) == metrics.execute_attempt_count;
     }
 };
+
+namespace hx {
+// Records CUDA events around the launches issued in its scope when the
+// runtime's profiler is on; no-op otherwise.
+struct ProfScope {
+    hx_runtime* rt;
+    ProfRecord rec{};
+    ProfScope(hx_runtime* r, int tag, double flops, double bytes) : rt(r) {
+        if (!rt->prof.on) return;
+        rec.tag = tag;
+        rec.flops = flops;
+        rec.bytes = bytes;
+        rec.a = rt->prof.next();
+        rec.b = rt->prof.next();
+        check_cuda(cudaEventRecord(rec.a, rt->stream), "cudaEventRecord");
+    }
+    // Closes the timed region (idempotent; the destructor calls it too).
+    void end() {
+        if (!rt->prof.on || !rec.a) return;
+        if (cudaEventRecord(rec.b, rt->stream) == cudaSuccess) rt->prof.recs.push_back(rec);
+        rec.a = nullptr;
+    }
+    ~ProfScope() { end(); }
+};
+}  // namespace hx
 
 // Runs `body` and converts any failure to a status code + stored message.
 template <class F>

@@ -54,6 +54,8 @@ struct LmPlan {
     size_t diag_lig, diag_hp, diag_dout;
     size_t muon_table;
     int ln_parts = 0, ln_rows = 0;
+    int emb_chunks = 1, emb_rows = 1;
+    size_t emb_part = 0;
     DeviceBuffer onehot;  // lazily sized staging for the one-hot execute API
     hx_optimizer_config opt{};
     int muon_count = 0;
@@ -108,6 +110,8 @@ constexpr int kAttnThreads = 256;
 template <int DH>
 void attn_fwd_launch(hx_runtime* rt, const LmPlan& p, const float* qkv, float* ctx, float* rmax, float* rsum, float* probs) {
     const size_t smem = attn_fwd_smem(p.T, DH, kAttnThreads / 32);
+    const double pairs = double(p.B) * p.H * (double(p.T) * (p.T + 1) / 2);
+    ProfScope prof(rt, kTagAttnFwd, 4.0 * pairs * DH, 4.0 * (double(p.M) * 4 * p.D + 2.0 * p.B * p.H * p.T));
     HX_CUDA(cudaFuncSetAttribute(attention_fwd_kernel<DH>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     attention_fwd_kernel<DH><<<dim3(p.H, p.B), kAttnThreads, smem, rt->stream>>>(
         p.T, p.D, p.H, 1.0f / sqrtf((float)DH), qkv, ctx, rmax, rsum, probs);
@@ -117,6 +121,8 @@ template <int DH>
 void attn_bwd_launch(hx_runtime* rt, const LmPlan& p, const float* qkv, const float* dctx, const float* rmax,
                      const float* rsum, float* dqkv) {
     const size_t smem = attn_bwd_smem(p.T, DH, kAttnThreads / 32);
+    const double pairs = double(p.B) * p.H * (double(p.T) * (p.T + 1) / 2);
+    ProfScope prof(rt, kTagAttnBwd, 8.0 * pairs * DH, 4.0 * (double(p.M) * 7 * p.D + 2.0 * p.B * p.H * p.T));
     HX_CUDA(cudaFuncSetAttribute(attention_bwd_kernel<DH>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     attention_bwd_kernel<DH><<<dim3(p.H, p.B), kAttnThreads, smem, rt->stream>>>(
         p.T, p.D, p.H, 1.0f / sqrtf((float)DH), qkv, dctx, rmax, rsum, dqkv);
@@ -169,8 +175,10 @@ void forward_backward(hx_runtime* rt, LmPlan& p, const float* W, float* G, float
     }
     // embedding
     float* x = a.at<float>(p.la[0].x);
+    ProfScope pemb(rt, kTagEmbed, 1.0 * M * D, 4.0 * 3.0 * M * D);
     embed_kernel<<<grid_for(long(M) * D, tpb, rt->sm_count), tpb, 0, s>>>(M, T, D, in_ids, W + p.off_E, pos, x);
     HX_LAUNCHED(rt);
+        pemb.end();
     const int rows_per_block = 8;  // warps per block for row kernels
     const int row_grid = (M + rows_per_block - 1) / rows_per_block;
 
@@ -179,20 +187,24 @@ void forward_backward(hx_runtime* rt, LmPlan& p, const float* W, float* G, float
         const LayerOffsets& o = p.lo[l];
         const float* xin = a.at<float>(A.x);
         float* xout = (l + 1 < p.L) ? a.at<float>(p.la[l + 1].x) : a.at<float>(p.xL);
+        ProfScope pln1(rt, kTagLayerNorm, 8.0 * M * D, 4.0 * (2.0 * M * D + 2.0 * M));
         layernorm_fwd_kernel<<<row_grid, 32 * rows_per_block, 0, s>>>(M, D, p.cfg.eps, xin, W + o.g1, W + o.b1,
                                                                        a.at<float>(A.n1), a.at<float>(A.mean1),
                                                                        a.at<float>(A.inv1));
         HX_LAUNCHED(rt);
+        pln1.end();
         gemm<false, false>(rt, M, 3 * D, D, a.at<float>(A.n1), D, wqkv + size_t(l) * 3 * D * D, 3 * D,
                            EpiStore{a.at<float>(A.qkv), 3L * D, 0, 0});
         float* hp = p.diag ? a.at<float>(p.diag_hp) + size_t(l) * B * p.H * T * T : nullptr;
         HX_DH_DISPATCH(p.dh, attn_fwd_launch, rt, p, a.at<float>(A.qkv), a.at<float>(A.ctx), a.at<float>(A.rmax),
                        a.at<float>(A.rsum), hp);
         gemm<false, false>(rt, M, D, D, a.at<float>(A.ctx), D, W + o.wo, D, EpiAddResidual{xin, a.at<float>(A.r1), D});
+        ProfScope pln2(rt, kTagLayerNorm, 8.0 * M * D, 4.0 * (2.0 * M * D + 2.0 * M));
         layernorm_fwd_kernel<<<row_grid, 32 * rows_per_block, 0, s>>>(M, D, p.cfg.eps, a.at<float>(A.r1), W + o.g2,
                                                                        W + o.b2, a.at<float>(A.n2),
                                                                        a.at<float>(A.mean2), a.at<float>(A.inv2));
         HX_LAUNCHED(rt);
+        pln2.end();
         gemm<false, false>(rt, M, F, D, a.at<float>(A.n2), D, W + o.w1, F, EpiRelu{a.at<float>(A.relu), nullptr, F});
         gemm<false, false>(rt, M, D, F, a.at<float>(A.relu), F, W + o.w2, D,
                            EpiAddResidual{a.at<float>(A.r1), xout, D});
@@ -200,13 +212,17 @@ void forward_backward(hx_runtime* rt, LmPlan& p, const float* W, float* G, float
     const float* xL = a.at<float>(p.xL);
     float* logits = a.at<float>(p.logits);
     gemm<false, false>(rt, M, V, D, xL, D, W + p.off_out, V, EpiStore{logits, (long)V, 0, 0});
+    ProfScope pce(rt, kTagSoftmaxCe, 4.0 * M * V, 4.0 * 2.0 * M * V);
     softmax_ce_kernel<<<row_grid, 32 * rows_per_block, 0, s>>>(
         M, V, T, grad_scale, logits, tgt_ids, p.diag ? a.at<float>(p.probs) : nullptr, logits,
         a.at<double>(p.row_loss), a.at<int>(p.row_correct));
     HX_LAUNCHED(rt);
+        pce.end();
+    ProfScope plr(rt, kTagReduce, 1.0 * M, 12.0 * M);
     loss_reduce_kernel<<<1, 256, 0, s>>>(B, T, a.at<double>(p.row_loss), a.at<int>(p.row_correct), grad_scale,
                                          a.at<float>(p.loss), a.at<float>(p.acc), G + p.P);
     HX_LAUNCHED(rt);
+        plr.end();
 
     // ---- backward ----
     const float* dl = logits;  // dlogits, in place
@@ -232,10 +248,12 @@ void forward_backward(hx_runtime* rt, LmPlan& p, const float* W, float* G, float
         gemm<false, true>(rt, M, F, D, dout, D, W + o.w2, D, EpiReluBackward{a.at<float>(A.relu), df1, nullptr, F});
         gemm<true, false>(rt, D, F, M, a.at<float>(A.n2), D, df1, F, EpiStore{G + o.w1, (long)F, 0, 0});
         gemm<false, true>(rt, M, D, F, df1, F, W + o.w1, F, EpiStore{dn, (long)D, 0, 0});
+        ProfScope plb2(rt, kTagLayerNorm, 12.0 * M * D, 4.0 * (4.0 * M * D + 2.0 * M));
         layernorm_bwd_kernel<<<p.ln_parts, 32 * lnw, ln_smem, s>>>(M, D, p.ln_rows, dn, a.at<float>(A.r1),
                                                                      a.at<float>(A.mean2), a.at<float>(A.inv2),
                                                                      W + o.g2, dout, dr, part);
         HX_LAUNCHED(rt);
+        plb2.end();
         column_reduce_kernel<<<grid_for(2L * D, tpb, rt->sm_count), tpb, 0, s>>>(p.ln_parts, D, part, G + o.g2, G + o.b2);
         HX_LAUNCHED(rt);
         gemm<true, false>(rt, D, D, M, a.at<float>(A.ctx), D, dr, D, EpiStore{G + o.wo, (long)D, 0, 0});
@@ -244,17 +262,26 @@ void forward_backward(hx_runtime* rt, LmPlan& p, const float* W, float* G, float
         gemm<true, false>(rt, D, 3 * D, M, a.at<float>(A.n1), D, dqkv, 3 * D,
                           EpiStore{G + o.wq, (long)D, (int)D, (long)D * D});
         gemm<false, true>(rt, M, D, 3 * D, dqkv, 3 * D, wqkv + size_t(li) * 3 * D * D, 3 * D, EpiStore{dn, (long)D, 0, 0});
+        ProfScope plb1(rt, kTagLayerNorm, 12.0 * M * D, 4.0 * (4.0 * M * D + 2.0 * M));
         layernorm_bwd_kernel<<<p.ln_parts, 32 * lnw, ln_smem, s>>>(M, D, p.ln_rows, dn, xin, a.at<float>(A.mean1),
                                                                      a.at<float>(A.inv1), W + o.g1, dr, dout, part);
         HX_LAUNCHED(rt);
+        plb1.end();
         column_reduce_kernel<<<grid_for(2L * D, tpb, rt->sm_count), tpb, 0, s>>>(p.ln_parts, D, part, G + o.g1, G + o.b1);
         HX_LAUNCHED(rt);
         if (p.diag) copy_d2d(rt, a.at<float>(p.diag_lig) + size_t(li) * M * D, dout, sizeof(float) * size_t(M) * D);
     }
     // embedding gradients
-    HX_CUDA(cudaMemsetAsync(G + p.off_E, 0, sizeof(float) * size_t(V) * D, s));
-    embed_bwd_kernel<<<grid_for(long(M) * D, tpb, rt->sm_count), tpb, 0, s>>>(M, D, in_ids, dout, G + p.off_E);
-    HX_LAUNCHED(rt);
+    ProfScope pemb2(rt, kTagEmbed, 1.0 * M * D, 4.0 * (2.0 * M * D + (p.emb_chunks + 1.0) * V * D));
+    {
+        dim3 grid(p.emb_chunks, (V + kEmbTokens - 1) / kEmbTokens, (D + 31) / 32);
+        embed_bwd_partial_kernel<<<grid, 128, 0, s>>>(M, V, D, p.emb_rows, in_ids, dout, a.at<float>(p.emb_part));
+        HX_LAUNCHED(rt);
+        embed_bwd_combine_kernel<<<grid_for(long(V) * D, tpb, rt->sm_count), tpb, 0, s>>>(
+            p.emb_chunks, V, D, a.at<float>(p.emb_part), G + p.off_E);
+        HX_LAUNCHED(rt);
+    }
+    pemb2.end();
     if (p.learned) {
         position_bwd_kernel<<<grid_for(long(T) * D, tpb, rt->sm_count), tpb, 0, s>>>(B, T, D, dout, G + p.off_pos);
         HX_LAUNCHED(rt);
@@ -445,6 +472,9 @@ int hx_lm_prepare(hx_runtime* rt, const hx_lm_config* cfg, uint32_t batch, int d
         p.ln_rows = (p.M + p.ln_parts - 1) / p.ln_parts;
         p.ln_parts = (p.M + p.ln_rows - 1) / p.ln_rows;
         p.ln_part = a.reserve(f * size_t(p.ln_parts) * 2 * D);
+        p.emb_rows = 8192;
+        p.emb_chunks = (p.M + p.emb_rows - 1) / p.emb_rows;
+        p.emb_part = a.reserve(f * size_t(p.emb_chunks) * V * D);
         if (p.diag) {
             p.diag_lig = a.reserve(f * p.L * M * D);
             p.diag_hp = a.reserve(f * p.L * B * H * T * T);

@@ -410,14 +410,43 @@ __global__ void loss_reduce_kernel(int B, int T, const double* __restrict__ row_
     }
 }
 
-// Token-embedding gradient: gE[id[r],:] += dx0[r,:] (one-hot^T * dX0, :82).
-__global__ void embed_bwd_kernel(int M, int D, const int* __restrict__ ids, const float* __restrict__ dx,
-                                 float* __restrict__ gE)
+// Token-embedding gradient gE[v,:] = sum over rows r with id[r] == v of
+// dX0[r,:] (one-hot^T * dX0, :82), deterministic: CTA (chunk c, token block,
+// 32-wide column block) walks the rows of chunk c; warp w takes rows
+// r = w, w+4, ... in increasing order and accumulates into its private
+// shared-memory table; the four warp tables are added in warp order and
+// written to part[c][v][d].  embed_bwd_combine sums the chunks in order.
+constexpr int kEmbTokens = 64;
+__global__ void embed_bwd_partial_kernel(int M, int V, int D, int chunk_rows, const int* __restrict__ ids,
+                                         const float* __restrict__ dx, float* __restrict__ part)
 {
-    const long total = (long)M * D;
+    __shared__ float acc[4][kEmbTokens][33];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int c = blockIdx.x, v0 = blockIdx.y * kEmbTokens, d0 = blockIdx.z * 32;
+    for (int i = 0; i < kEmbTokens; ++i) acc[warp][i][lane] = 0.f;
+    __syncwarp();
+    const int r0 = c * chunk_rows, r1 = min(M, r0 + chunk_rows);
+    const int d = d0 + lane;
+    for (int r = r0 + warp; r < r1; r += 4) {
+        const int v = ids[r] - v0;
+        if (v >= 0 && v < kEmbTokens && d < D) acc[warp][v][lane] += dx[(long)r * D + d];
+    }
+    __syncthreads();
+    for (int t = warp; t < kEmbTokens; t += 4) {
+        if (v0 + t >= V || d >= D) continue;
+        const float s = ((acc[0][t][lane] + acc[1][t][lane]) + acc[2][t][lane]) + acc[3][t][lane];
+        part[((long)c * V + v0 + t) * D + d] = s;
+    }
+}
+
+__global__ void embed_bwd_combine_kernel(int chunks, int V, int D, const float* __restrict__ part,
+                                         float* __restrict__ gE)
+{
+    const long total = (long)V * D;
     for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
-        const int r = (int)(i / D), d = (int)(i % D);
-        atomicAdd(&gE[(long)ids[r] * D + d], dx[i]);
+        float s = 0.f;
+        for (int c = 0; c < chunks; ++c) s += part[(long)c * total + i];
+        gE[i] = s;
     }
 }
 

@@ -57,8 +57,11 @@ void mlp_enqueue(hx_runtime* rt, const MlpPlan& pl, const MlpBinding& b)
     const float s = 2.0f / float(B * O);
     gemm<false, false>(rt, B, H, I, b.x, I, b.w1, H, EpiRelu{b.h, b.mask, H});
     gemm<false, false>(rt, B, O, H, b.h, H, b.w2, O, EpiError{b.y, b.p, b.e, b.dp, s, O});
-    mse_reduce_kernel<<<1, 1024, 0, rt->stream>>>(b.e, size_t(B) * O, b.loss);
-    HX_LAUNCHED(rt);
+    {
+        ProfScope prof(rt, kTagReduce, 2.0 * B * O, 4.0 * B * O);
+        mse_reduce_kernel<<<1, 1024, 0, rt->stream>>>(b.e, size_t(B) * O, b.loss);
+        HX_LAUNCHED(rt);
+    }
     gemm<true, false>(rt, H, O, B, b.h, H, b.dp, O, EpiSgd{b.w2, b.dw2, b.w2n, b.lr, O});
     gemm<false, true>(rt, B, H, O, b.dp, O, b.w2, O, EpiReluBackward{b.h, b.dz1, b.dh, H});
     gemm<true, false>(rt, I, H, B, b.x, I, b.dz1, H, EpiSgd{b.w1, b.dw1, b.w1n, b.lr, H});
@@ -80,7 +83,7 @@ GraphCache::Key key_of(const MlpBinding& b) {
 // the workspace), from a captured CUDA graph afterwards.
 void mlp_run(hx_runtime* rt, MlpPlan& pl, const MlpBinding& b)
 {
-    if (!pl.use_graphs) {
+    if (!pl.use_graphs || rt->prof.on) {
         mlp_enqueue(rt, pl, b);
         return;
     }

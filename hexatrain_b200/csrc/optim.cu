@@ -105,6 +105,7 @@ void launch_adam(hx_runtime* rt, bool graph_order, size_t n, const float* w, con
                  const float* v, float* wn, float* mn, float* vn, const AdamScalars& s, const AdamTaps& t)
 {
     if (n == 0) return;
+    ProfScope prof(rt, kTagOptimizer, 12.0 * n, 28.0 * n);
     const int threads = 256;
     const size_t work = graph_order ? n : (n + 3) / 4;
     const int blocks = (int)std::min<size_t>((work + threads - 1) / threads, size_t(rt->sm_count) * 16);
@@ -130,6 +131,7 @@ void check_muon_shape(int rows, int cols) {
 
 void launch_muon(hx_runtime* rt, const MuonMatrix* d_mats, int count, size_t smem, const MuonScalars& s) {
     if (count == 0) return;
+    ProfScope prof(rt, kTagOptimizer, 0.0, 0.0);
     HX_CUDA(cudaFuncSetAttribute(muon_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     muon_kernel<<<count, 1024, smem, rt->stream>>>(d_mats, s);
     HX_LAUNCHED(rt);

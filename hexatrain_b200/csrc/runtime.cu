@@ -93,6 +93,39 @@ int hx_runtime_metrics(const hx_runtime* rt, hx_metrics* out) {
     return HX_OK;
 }
 
+int hx_runtime_profile(hx_runtime* rt, int enable) {
+    return hx_guard(rt, [&] {
+        rt->prof.on = enable != 0;
+        rt->prof.recs.clear();
+        rt->prof.used = 0;
+    });
+}
+
+int hx_runtime_profile_read(hx_runtime* rt, hx_profile_entry* entries, int capacity, int* count) {
+    return hx_guard(rt, [&] {
+        hx::require(entries && count && capacity >= 0, HX_ERR_ARGUMENT, "profile_read: null output");
+        HX_CUDA(cudaStreamSynchronize(rt->stream));
+        hx_profile_entry agg[hx::kTagCount];
+        std::memset(agg, 0, sizeof(agg));
+        for (int t = 0; t < hx::kTagCount; ++t) std::snprintf(agg[t].name, sizeof(agg[t].name), "%s", hx::prof_tag_name(t));
+        for (const auto& r : rt->prof.recs) {
+            float ms = 0.f;
+            HX_CUDA(cudaEventElapsedTime(&ms, r.a, r.b));
+            hx_profile_entry& e = agg[r.tag];
+            ++e.launches;
+            e.total_ms += ms;
+            e.flops += r.flops;
+            e.bytes += r.bytes;
+        }
+        rt->prof.recs.clear();
+        rt->prof.used = 0;
+        int n = 0;
+        for (int t = 0; t < hx::kTagCount && n < capacity; ++t)
+            if (agg[t].launches) entries[n++] = agg[t];
+        *count = n;
+    });
+}
+
 int hx_runtime_inject_execute_failure(hx_runtime* rt, int64_t call_index) {
     return hx_guard(rt, [&] { rt->inject_execute_at = call_index; });
 }

@@ -273,6 +273,20 @@ class Runtime:
             self._lib.hx_runtime_metrics(self._rt, C.byref(m))
         return RuntimeMetrics(**{f: getattr(m, f) for f, _ in _lib.Metrics._fields_})
 
+    def profile(self, enable: bool) -> bool:
+        """Start/stop per-kernel-class CUDA-event timing (hx_runtime_profile)."""
+        return self._need() and self._ok(self._lib.hx_runtime_profile(self._rt, int(bool(enable))))
+
+    def profile_read(self) -> dict:
+        """{kernel class: dict(launches, total_ms, flops, bytes)}; clears the records."""
+        arr = (_lib.ProfileEntry * 16)()
+        n = C.c_int(0)
+        if not (self._need() and self._ok(self._lib.hx_runtime_profile_read(self._rt, arr, 16, C.byref(n)))):
+            raise RuntimeError(self.last_error)
+        return {arr[i].name.decode(): dict(launches=int(arr[i].launches), total_ms=float(arr[i].total_ms),
+                                           flops=float(arr[i].flops), bytes=float(arr[i].bytes))
+                for i in range(n.value)}
+
     def api_trace_summary(self) -> str:
         """KEY=VALUE counters in the style of Runtime::apiTraceSummary."""
         m = self.metrics()

@@ -81,6 +81,21 @@ int hx_runtime_metrics(const hx_runtime* rt, hx_metrics* out);
  * work finished.  -1 disables.  No device fault is involved. */
 int hx_runtime_inject_execute_failure(hx_runtime* rt, int64_t call_index);
 
+/* Per-kernel-class timing with CUDA events recorded on the runtime stream
+ * around every launch while enabled (the counterpart of RuntimeMetrics'
+ * executeUs lists, qnn/qnn_runtime.h:68, at kernel granularity).  Steps run
+ * eagerly (no CUDA graph replay) while profiling is on.  _read synchronises
+ * the stream, aggregates and clears the records. */
+typedef struct {
+    char name[32];        /* kernel class, e.g. "gemm", "attention_fwd" */
+    uint64_t launches;
+    double total_ms;      /* sum of event-timed durations */
+    double flops;         /* algorithmic FLOPs of those launches */
+    double bytes;         /* algorithmic DRAM bytes of those launches */
+} hx_profile_entry;
+int hx_runtime_profile(hx_runtime* rt, int enable);
+int hx_runtime_profile_read(hx_runtime* rt, hx_profile_entry* entries, int capacity, int* count);
+
 /* ---- two-layer ReLU MLP full training step ------------------------------ */
 /* Graph phonelm_mlp_training_step (qnn/qnn_runtime_full_step.inc:209-330):
  *   Z1=X W1; H=ReLU(Z1); P=H W2; E=P-Y; loss=mean(E^2); dP=E*2/(B*O);

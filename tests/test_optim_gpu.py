@@ -1,0 +1,71 @@
+"""GPU parity of the standalone optimizers through the C ABI."""
+import numpy as np
+import pytest
+
+import hexatrain_b200 as hx
+from conftest import golden, rel_err
+
+pytestmark = pytest.mark.gpu
+
+
+def test_adam_graph_outputs_match_golden(gpu_runtime):
+    """phonelm_adam_optimizer's ten outputs (qnn/qnn_runtime_transformer.inc:926-1109)
+    against tiny_lm::adamUpdate's values from the reference."""
+    g = golden("adam_n208.npz")
+    rt = gpu_runtime
+    n = g["w"].size
+    assert rt.prepare_adam_optimizer(n), rt.last_error
+    out = hx.AdamOptimizerOutputs()
+    assert rt.execute_adam_optimizer(g["w"], g["g"], g["m"], g["v"], float(g["lr"]), 1.0, float(g["c1"]),
+                                     float(g["c2"]), out), rt.last_error
+    # moments and bias-corrected moments: same operations, same rounding
+    assert np.array_equal(out.first_moment_next, g["m_next"])
+    assert np.array_equal(out.second_moment_next, g["v_next"])
+    assert np.array_equal(out.first_moment_hat, g["m_hat"])
+    assert np.array_equal(out.second_moment_hat, g["v_hat"])
+    np.testing.assert_array_equal(out.second_root, np.sqrt(g["v_hat"]).astype(np.float32))
+    np.testing.assert_array_equal(out.denominator, (np.sqrt(g["v_hat"]) + np.float32(1e-8)).astype(np.float32))
+    zero = g["v_hat"] == 0
+    assert zero.sum() == 5 and np.all(out.normalized_update[zero] == 0)
+    # the graph forms lr*(m^/den); the CPU reference (lr*m^)/den: one rounding apart
+    assert rel_err(out.weight_next, g["w_next"]) <= 1e-6
+    np.testing.assert_allclose(out.scaled_update, np.float32(1e-3) * out.normalized_update, rtol=1e-6)
+
+
+def test_adam_gradient_scale_and_rejections(gpu_runtime):
+    rt = gpu_runtime
+    n = 1000
+    rng = np.random.default_rng(0)
+    w, gr = rng.normal(size=n).astype(np.float32), rng.normal(size=n).astype(np.float32)
+    z = np.zeros(n, np.float32)
+    assert rt.prepare_adam_optimizer(n)
+    a, b = hx.AdamOptimizerOutputs(), hx.AdamOptimizerOutputs()
+    assert rt.execute_adam_optimizer(w, gr, z, z, 1e-3, 0.5, 10.0, 1000.0, a)
+    assert rt.execute_adam_optimizer(w, gr * np.float32(0.5), z, z, 1e-3, 1.0, 10.0, 1000.0, b)
+    assert np.array_equal(a.weight_next, b.weight_next)
+    assert not rt.execute_adam_optimizer(w, gr, z, z, 1e-3, 1.5, 10.0, 1000.0, a)
+    assert rt.last_error == "Adam optimizer buffer size or scalar"
+    assert not rt.execute_adam_optimizer(w, gr, z, z, float("inf"), 1.0, 10.0, 1000.0, a)
+    assert not rt.execute_adam_optimizer(w[:-1], gr[:-1], z[:-1], z[:-1], 1e-3, 1.0, 10.0, 1000.0, a)
+
+
+@pytest.mark.parametrize("shape", [(48, 48), (64, 16), (16, 100)])
+@pytest.mark.parametrize("bf16", [False, True])
+def test_muon_matches_oracle(gpu_runtime, oracle, shape, bf16):
+    rng = np.random.default_rng(shape[0] * 7 + shape[1])
+    w = rng.normal(0, 0.02, shape).astype(np.float32)
+    g = rng.normal(0, 1e-3, shape).astype(np.float32)
+    buf = rng.normal(0, 1e-3, shape).astype(np.float32)
+    ok, wn, bn = gpu_runtime.execute_muon(w, g, buf, 0.02, bf16_inputs=bf16)
+    assert ok, gpu_runtime.last_error
+    rw, rb = oracle.muon(w, g, buf, 0.02, bf16_inputs=bf16)
+    assert np.array_equal(bn, rb)                       # momentum buffer: same float ops
+    upd, rupd = (w - wn).astype(np.float64), (w - rw).astype(np.float64)
+    assert rel_err(upd, rupd) <= (2e-2 if bf16 else 1e-4)
+    assert np.max(np.abs(wn - rw)) <= 1e-2
+
+
+def test_muon_rejects_oversized(gpu_runtime):
+    w = np.zeros((256, 256), np.float32)
+    ok, _, _ = gpu_runtime.execute_muon(w, w, w, 0.02)
+    assert not ok and "Newton-Schulz limit" in gpu_runtime.last_error
