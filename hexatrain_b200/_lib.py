@@ -21,6 +21,9 @@ HX_ERR_MEMORY = 5
 HX_ERR_UNSUPPORTED = 6
 
 HX_LM_LEARNED_POSITION = 1
+HX_GEMM_AUTO = 0
+HX_GEMM_CUDA_CORES = 1
+HX_GEMM_TENSOR_CORES = 2
 HX_OPT_ADAM = 0
 HX_OPT_MUON = 1
 
@@ -93,6 +96,7 @@ SIGNATURES = {
     "hx_runtime_synchronize": (C.c_int, [C.c_void_p]),
     "hx_runtime_metrics": (C.c_int, [C.c_void_p, C.POINTER(Metrics)]),
     "hx_runtime_inject_execute_failure": (C.c_int, [C.c_void_p, C.c_int64]),
+    "hx_runtime_set_gemm_backend": (C.c_int, [C.c_void_p, C.c_int]),
     "hx_runtime_profile": (C.c_int, [C.c_void_p, C.c_int]),
     "hx_runtime_profile_read": (C.c_int, [C.c_void_p, C.POINTER(ProfileEntry), C.c_int, C.POINTER(C.c_int)]),
     "hx_mlp_prepare": (C.c_int, [C.c_void_p, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, C.c_int]),

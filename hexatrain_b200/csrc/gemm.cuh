@@ -3,6 +3,7 @@
 #pragma once
 
 #include "gemm_simt.cuh"
+#include "gemm_tc.cuh"
 #include "hx_internal.cuh"
 
 namespace hx {
@@ -44,12 +45,106 @@ void launch_simt(hx_runtime* rt, int M, int N, int K, const float* A, long lda, 
     }
 }
 
+// ---- tensor-core path ------------------------------------------------------
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+inline EncodeTiledFn encode_tiled() {
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        check_cuda(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q),
+                   "cudaGetDriverEntryPoint(cuTensorMapEncodeTiled)");
+        require(q == cudaDriverEntryPointSuccess && p, HX_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+        fn = reinterpret_cast<EncodeTiledFn>(p);
+    }
+    return fn;
+}
+
+// Row-major FP32 matrix [outer][inner] with leading dimension ld (elements),
+// boxes of box_inner x box_outer, zero fill out of bounds.  K-major operand
+// tiles use the 128B swizzle; MN-major ones the 128B swizzle with 32-byte
+// atoms (the layout the MMA requires for MN-major 32-bit operands).
+inline CUtensorMap make_map(const float* base, uint64_t inner, uint64_t outer, uint64_t ld, uint32_t box_inner,
+                            uint32_t box_outer, CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B) {
+    CUtensorMap m;
+    const cuuint64_t dims[2] = {inner, outer};
+    const cuuint64_t strides[1] = {ld * sizeof(float)};
+    const cuuint32_t box[2] = {box_inner, box_outer};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = encode_tiled()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides,
+                                      box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    require(r == CUDA_SUCCESS, HX_ERR_CUDA, "cuTensorMapEncodeTiled failed (" + std::to_string(int(r)) + ")");
+    return m;
+}
+
+inline bool tc_eligible(hx_runtime* rt, int M, int N, int K, const float* A, long lda, const float* B, long ldb) {
+    if (rt->gemm_backend == HX_GEMM_CUDA_CORES) return false;
+    const bool aligned = ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(B)) & 15) == 0 && lda % 4 == 0 &&
+                         ldb % 4 == 0 && K >= 8;
+    if (!aligned) return false;
+    if (rt->gemm_backend == HX_GEMM_TENSOR_CORES) return true;
+    return M >= 64 && N >= 64 && 2.0 * M * N * K >= 6.4e7;
+}
+
+template <bool AT, bool BT, class Epi>
+void launch_tc(hx_runtime* rt, int M, int N, int K, const float* A, long lda, const float* B, long ldb, Epi epi)
+{
+    // A(m,k): AT=false -> K-major rows [M][K];  AT=true -> MN-major [K][M].
+    // B(k,n): BT=false -> MN-major [K][N];      BT=true -> K-major [N][K].
+    constexpr bool A_MN = AT, B_MN = !BT;
+    constexpr CUtensorMapSwizzle mn_swz = CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B;
+    const CUtensorMap ma = A_MN ? make_map(A, M, K, lda, 32, 32, mn_swz) : make_map(A, K, M, lda, 32, 128);
+    const CUtensorMap mb = B_MN ? make_map(B, N, K, ldb, 32, 32, mn_swz) : make_map(B, K, N, ldb, 32, 128);
+    const int tiles_m = (M + kTcBM - 1) / kTcBM, tiles_n = (N + kTcBN - 1) / kTcBN;
+    const long tiles = (long)tiles_m * tiles_n;
+    int splits = 1;
+    if (tiles < rt->sm_count && K >= 2 * 256) {
+        splits = (int)((rt->sm_count + tiles - 1) / tiles);
+        splits = std::max(1, std::min(splits, K / 256));
+    }
+    int chunk = (K + splits - 1) / splits;
+    chunk = ((chunk + kTcBK - 1) / kTcBK) * kTcBK;
+    splits = (K + chunk - 1) / chunk;
+    static bool attr_set = false;
+    if (!attr_set) {
+        HX_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<A_MN, B_MN, Epi>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)kTcSmemBytes));
+        attr_set = true;
+    }
+    int* err = rt->device_error();
+    dim3 grid(tiles_n, tiles_m, splits);
+    if (splits == 1) {
+        gemm_tc_kernel<A_MN, B_MN, Epi><<<grid, kTcThreads, kTcSmemBytes, rt->stream>>>(ma, mb, M, N, K, chunk, epi,
+                                                                                       nullptr, err);
+        HX_LAUNCHED(rt);
+    } else {
+        float* ws = rt->workspace(sizeof(float) * (size_t)splits * M * N);
+        gemm_tc_kernel<A_MN, B_MN, Epi><<<grid, kTcThreads, kTcSmemBytes, rt->stream>>>(ma, mb, M, N, K, chunk, epi,
+                                                                                       ws, err);
+        HX_LAUNCHED(rt);
+        const long total = (long)M * N;
+        const int threads = 256;
+        const int blocks = (int)std::min<long>((total + threads - 1) / threads, 4L * rt->sm_count * 8);
+        splitk_reduce_kernel<Epi><<<blocks, threads, 0, rt->stream>>>(M, N, splits, ws, epi);
+        HX_LAUNCHED(rt);
+    }
+}
+
 // C = op(A) op(B) with the epilogue applied to every element.
 template <bool AT, bool BT, class Epi>
 void gemm(hx_runtime* rt, int M, int N, int K, const float* A, long lda, const float* B, long ldb, Epi epi)
 {
     require(M > 0 && N > 0 && K >= 0, HX_ERR_ARGUMENT, "gemm: bad shape");
     ProfScope prof(rt, kTagGemm, 2.0 * M * N * K, 4.0 * ((double)M * K + (double)K * N + (double)M * N));
+    if (tc_eligible(rt, M, N, K, A, lda, B, ldb)) {
+        launch_tc<AT, BT>(rt, M, N, K, A, lda, B, ldb, epi);
+        return;
+    }
     const long mn = (long)M * N;
     if (mn >= 128L * 128 * rt->sm_count / 2)
         launch_simt<128, 128, 8, 16, 16, AT, BT>(rt, M, N, K, A, lda, B, ldb, epi);

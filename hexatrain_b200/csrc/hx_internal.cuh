@@ -140,7 +140,9 @@ struct hx_runtime {
     std::unique_ptr<hx::LmPlan, hx::LmPlanDeleter> lm;
     std::unique_ptr<hx::AdamPlan> adam;
     hx::DeviceBuffer scratch;  // generic device workspace (grows on demand)
+    hx::DeviceBuffer err_flag; // device-side error word of bounded waits
     hx::Profiler prof;
+    int gemm_backend = 0;      // HX_GEMM_AUTO / HX_GEMM_CUDA_CORES / HX_GEMM_TENSOR_CORES
 
     ~hx_runtime();
     void activate() const { hx::check_cuda(cudaSetDevice(device), "cudaSetDevice"); }
@@ -148,6 +150,26 @@ struct hx_runtime {
     float* workspace(size_t bytes) {
         if (scratch.bytes < bytes) scratch.allocate(bytes);
         return scratch.as<float>();
+    }
+    int* device_error() {
+        if (!err_flag.ptr) {
+            err_flag.allocate(16);
+            hx::check_cuda(cudaMemset(err_flag.ptr, 0, 16), "cudaMemset");
+        }
+        return err_flag.as<int>();
+    }
+    // Reads (and clears) the device error word; fails if a kernel reported
+    // a timed-out pipeline wait.  Synchronises the stream.
+    void check_device_error() {
+        hx::check_cuda(cudaStreamSynchronize(stream), "cudaStreamSynchronize");
+        if (!err_flag.ptr) return;
+        int code = 0;
+        hx::check_cuda(cudaMemcpy(&code, err_flag.ptr, sizeof(int), cudaMemcpyDeviceToHost), "cudaMemcpy");
+        if (code) {
+            hx::check_cuda(cudaMemset(err_flag.ptr, 0, sizeof(int)), "cudaMemset");
+            hx::fail(HX_ERR_CUDA, "DEVICE_WAIT_TIMEOUT: a bounded pipeline wait in the tensor-core GEMM gave up (role " +
+                                      std::to_string(code) + "); results of this call are invalid");
+        }
     }
     // Record the outcome of an execute call (ApiTrace counters).
     void record_execute(bool ok, double us) {

@@ -557,7 +557,7 @@ static void lm_execute_common(hx_runtime* rt, LmPlan& p, const float* params, si
             get(out->logits, p.logits, M * p.V);
         }
     }
-    HX_CUDA(cudaStreamSynchronize(rt->stream));
+    rt->check_device_error();
 }
 
 int hx_lm_execute(hx_runtime* rt, const float* input_one_hot, const float* target_one_hot, const float* params,
@@ -687,7 +687,7 @@ int hx_lm_train_step(hx_runtime* rt, const uint32_t* tokens, uint32_t step, floa
         int bad = 0;
         HX_CUDA(cudaMemcpyAsync(loss, a.at<float>(p.loss), sizeof(float), cudaMemcpyDeviceToHost, rt->stream));
         HX_CUDA(cudaMemcpyAsync(&bad, a.at<int>(p.bad), sizeof(int), cudaMemcpyDeviceToHost, rt->stream));
-        HX_CUDA(cudaStreamSynchronize(rt->stream));
+        rt->check_device_error();
         rt->metrics.last_output_bind_us = us_since(to);
         require(!bad, HX_ERR_ARGUMENT, "INVALID_TINY_LM_TOKEN: token id >= vocabulary size (state was updated with id 0)");
         require(std::isfinite(*loss), HX_ERR_NONFINITE, "QNN_NONFINITE: training loss is not finite");

@@ -203,7 +203,7 @@ int hx_mlp_execute(hx_runtime* rt, const float* x, size_t xn, const float* y, si
             get(out->d_w1, pl.dw1, f * I * H);
             get(out->hidden, pl.h, f * B * H);
         }
-        HX_CUDA(cudaStreamSynchronize(rt->stream));
+        rt->check_device_error();
         rt->metrics.last_output_bind_us = us_since(to);
         if (rt->injected_now()) fail(HX_ERR_CUDA, "injected execute failure after device success");
     });

@@ -83,7 +83,15 @@ int hx_runtime_set_stream(hx_runtime* rt, void* stream) {
 void* hx_runtime_stream(const hx_runtime* rt) { return rt ? static_cast<void*>(rt->stream) : nullptr; }
 
 int hx_runtime_synchronize(hx_runtime* rt) {
-    return hx_guard(rt, [&] { HX_CUDA(cudaStreamSynchronize(rt->stream)); });
+    return hx_guard(rt, [&] { rt->check_device_error(); });
+}
+
+int hx_runtime_set_gemm_backend(hx_runtime* rt, int backend) {
+    return hx_guard(rt, [&] {
+        hx::require(backend == HX_GEMM_AUTO || backend == HX_GEMM_CUDA_CORES || backend == HX_GEMM_TENSOR_CORES,
+                    HX_ERR_ARGUMENT, "unknown GEMM backend");
+        rt->gemm_backend = backend;
+    });
 }
 
 int hx_runtime_metrics(const hx_runtime* rt, hx_metrics* out) {

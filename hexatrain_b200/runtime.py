@@ -273,6 +273,10 @@ class Runtime:
             self._lib.hx_runtime_metrics(self._rt, C.byref(m))
         return RuntimeMetrics(**{f: getattr(m, f) for f, _ in _lib.Metrics._fields_})
 
+    def set_gemm_backend(self, backend: int) -> bool:
+        """0 = auto (tensor cores for large aligned GEMMs), 1 = CUDA cores, 2 = tensor cores when aligned."""
+        return self._need() and self._ok(self._lib.hx_runtime_set_gemm_backend(self._rt, int(backend)))
+
     def profile(self, enable: bool) -> bool:
         """Start/stop per-kernel-class CUDA-event timing (hx_runtime_profile)."""
         return self._need() and self._ok(self._lib.hx_runtime_profile(self._rt, int(bool(enable))))

@@ -81,6 +81,13 @@ int hx_runtime_metrics(const hx_runtime* rt, hx_metrics* out);
  * work finished.  -1 disables.  No device fault is involved. */
 int hx_runtime_inject_execute_failure(hx_runtime* rt, int64_t call_index);
 
+/* GEMM engine selection.  AUTO (default) runs large FP32 GEMMs on the
+ * tensor cores as 3xTF32 (tcgen05, TMEM accumulators, TMA-fed) and small or
+ * unaligned ones on the CUDA cores; the other values force one engine where
+ * the problem allows it (tests use this to compare the two). */
+enum { HX_GEMM_AUTO = 0, HX_GEMM_CUDA_CORES = 1, HX_GEMM_TENSOR_CORES = 2 };
+int hx_runtime_set_gemm_backend(hx_runtime* rt, int backend);
+
 /* Per-kernel-class timing with CUDA events recorded on the runtime stream
  * around every launch while enabled (the counterpart of RuntimeMetrics'
  * executeUs lists, qnn/qnn_runtime.h:68, at kernel granularity).  Steps run
