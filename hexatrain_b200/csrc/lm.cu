@@ -14,6 +14,7 @@
 // Backward mirrors :79-82 with the same named gradients in registry order.
 #include <cmath>
 
+#include "attention_tiled.cuh"
 #include "gemm.cuh"
 #include "lm_kernels.cuh"
 #include "optim.cuh"
@@ -107,22 +108,44 @@ size_t attn_fwd_smem(int T, int DH, int nw) { return sizeof(float) * (size_t(2) 
 size_t attn_bwd_smem(int T, int DH, int nw) { return sizeof(float) * (size_t(4) * T * (DH + 1) + 3 * size_t(T) + size_t(nw) * T); }
 constexpr int kAttnThreads = 256;
 
+bool attn_tiled(int T, int DH) { return T <= kAttnMaxT && (DH == 8 || DH == 16 || DH == 32); }
+
 template <int DH>
 void attn_fwd_launch(hx_runtime* rt, const LmPlan& p, const float* qkv, float* ctx, float* rmax, float* rsum, float* probs) {
-    const size_t smem = attn_fwd_smem(p.T, DH, kAttnThreads / 32);
     const double pairs = double(p.B) * p.H * (double(p.T) * (p.T + 1) / 2);
     ProfScope prof(rt, kTagAttnFwd, 4.0 * pairs * DH, 4.0 * (double(p.M) * 4 * p.D + 2.0 * p.B * p.H * p.T));
+    if constexpr (DH == 8 || DH == 16 || DH == 32) {
+        if (attn_tiled(p.T, DH)) {
+            const size_t smem = AttnTiledLayout<DH>::fwd_bytes(p.T);
+            HX_CUDA(cudaFuncSetAttribute(attention_fwd_tiled_kernel<DH>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+            attention_fwd_tiled_kernel<DH><<<dim3(p.H, p.B), kAttnTiledThreads, smem, rt->stream>>>(
+                p.T, p.D, p.H, 1.0f / sqrtf((float)DH), qkv, ctx, rmax, rsum, probs);
+            HX_LAUNCHED(rt);
+            return;
+        }
+    }
+    const size_t smem = attn_fwd_smem(p.T, DH, kAttnThreads / 32);
     HX_CUDA(cudaFuncSetAttribute(attention_fwd_kernel<DH>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     attention_fwd_kernel<DH><<<dim3(p.H, p.B), kAttnThreads, smem, rt->stream>>>(
         p.T, p.D, p.H, 1.0f / sqrtf((float)DH), qkv, ctx, rmax, rsum, probs);
     HX_LAUNCHED(rt);
 }
 template <int DH>
-void attn_bwd_launch(hx_runtime* rt, const LmPlan& p, const float* qkv, const float* dctx, const float* rmax,
-                     const float* rsum, float* dqkv) {
-    const size_t smem = attn_bwd_smem(p.T, DH, kAttnThreads / 32);
+void attn_bwd_launch(hx_runtime* rt, const LmPlan& p, const float* qkv, const float* ctx, const float* dctx,
+                     const float* rmax, const float* rsum, float* dqkv) {
     const double pairs = double(p.B) * p.H * (double(p.T) * (p.T + 1) / 2);
     ProfScope prof(rt, kTagAttnBwd, 8.0 * pairs * DH, 4.0 * (double(p.M) * 7 * p.D + 2.0 * p.B * p.H * p.T));
+    if constexpr (DH == 8 || DH == 16 || DH == 32) {
+        if (attn_tiled(p.T, DH)) {
+            const size_t smem = AttnTiledLayout<DH>::bwd_bytes(p.T);
+            HX_CUDA(cudaFuncSetAttribute(attention_bwd_tiled_kernel<DH>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+            attention_bwd_tiled_kernel<DH><<<dim3(p.H, p.B), kAttnTiledThreads, smem, rt->stream>>>(
+                p.T, p.D, p.H, 1.0f / sqrtf((float)DH), qkv, ctx, dctx, rmax, rsum, dqkv);
+            HX_LAUNCHED(rt);
+            return;
+        }
+    }
+    const size_t smem = attn_bwd_smem(p.T, DH, kAttnThreads / 32);
     HX_CUDA(cudaFuncSetAttribute(attention_bwd_kernel<DH>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     attention_bwd_kernel<DH><<<dim3(p.H, p.B), kAttnThreads, smem, rt->stream>>>(
         p.T, p.D, p.H, 1.0f / sqrtf((float)DH), qkv, dctx, rmax, rsum, dqkv);
@@ -258,7 +281,8 @@ void forward_backward(hx_runtime* rt, LmPlan& p, const float* W, float* G, float
         HX_LAUNCHED(rt);
         gemm<true, false>(rt, D, D, M, a.at<float>(A.ctx), D, dr, D, EpiStore{G + o.wo, (long)D, 0, 0});
         gemm<false, true>(rt, M, D, D, dr, D, W + o.wo, D, EpiStore{dc, (long)D, 0, 0});
-        HX_DH_DISPATCH(p.dh, attn_bwd_launch, rt, p, a.at<float>(A.qkv), dc, a.at<float>(A.rmax), a.at<float>(A.rsum), dqkv);
+        HX_DH_DISPATCH(p.dh, attn_bwd_launch, rt, p, a.at<float>(A.qkv), a.at<float>(A.ctx), dc, a.at<float>(A.rmax),
+                       a.at<float>(A.rsum), dqkv);
         gemm<true, false>(rt, D, 3 * D, M, a.at<float>(A.n1), D, dqkv, 3 * D,
                           EpiStore{G + o.wq, (long)D, (int)D, (long)D * D});
         gemm<false, true>(rt, M, D, 3 * D, dqkv, 3 * D, wqkv + size_t(li) * 3 * D * D, 3 * D, EpiStore{dn, (long)D, 0, 0});

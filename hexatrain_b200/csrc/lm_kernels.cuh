@@ -204,14 +204,14 @@ __global__ void attention_fwd_kernel(int T, int D, int H, float scale, const flo
         __syncwarp();
         float mx = -INFINITY;
         for (int j = lane; j <= r; j += 32) {
-            const float s = dot_dh<DH>(qw, Ks + j * LD) * scale;
+            const float s = __fmul_rn(dot_dh<DH>(qw, Ks + j * LD), scale);
             pw[j] = s;
             mx = fmaxf(mx, s);
         }
         mx = warp_max(mx);
         double sum = 0.0;
         for (int j = lane; j <= r; j += 32) {
-            const float e = expf(pw[j] - mx);
+            const float e = expf(__fsub_rn(pw[j], mx));
             pw[j] = e;
             sum += e;
         }
@@ -281,15 +281,14 @@ __global__ void attention_bwd_kernel(int T, int D, int H, float scale, const flo
         const float* cr = Cs + r * LD;
         double dsum = 0.0;
         for (int j = lane; j <= r; j += 32) {
-            const float p = __fdiv_rn(expf(dot_dh<DH>(qr, Ks + j * LD) * scale - mxs[r]), sms[r]);
+            const float p = __fdiv_rn(expf(__fsub_rn(__fmul_rn(dot_dh<DH>(qr, Ks + j * LD), scale), mxs[r])), sms[r]);
             const float dp = dot_dh<DH>(cr, Vs + j * LD);
             sw[j] = dp;
             dsum += (double)__fmul_rn(dp, p);
-            // keep p for the dS pass in the upper half of the buffer slot
         }
         const float dt = (float)warp_sum(dsum);
         for (int j = lane; j <= r; j += 32) {
-            const float p = __fdiv_rn(expf(dot_dh<DH>(qr, Ks + j * LD) * scale - mxs[r]), sms[r]);
+            const float p = __fdiv_rn(expf(__fsub_rn(__fmul_rn(dot_dh<DH>(qr, Ks + j * LD), scale), mxs[r])), sms[r]);
             sw[j] = __fmul_rn(p, __fsub_rn(sw[j], dt));
         }
         __syncwarp();
@@ -312,7 +311,7 @@ __global__ void attention_bwd_kernel(int T, int D, int H, float scale, const flo
         for (int r = j + lane; r < T; r += 32) {
             const float* qr = Qs + r * LD;
             const float* cr = Cs + r * LD;
-            const float p = __fdiv_rn(expf(dot_dh<DH>(qr, kj) * scale - mxs[r]), sms[r]);
+            const float p = __fdiv_rn(expf(__fsub_rn(__fmul_rn(dot_dh<DH>(qr, kj), scale), mxs[r])), sms[r]);
             const float ds = __fmul_rn(p, __fsub_rn(dot_dh<DH>(cr, vj), dot[r]));
 #pragma unroll
             for (int d = 0; d < DH; ++d) {
