@@ -45,6 +45,8 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--global-batch", type=int, default=GLOBAL_BATCH,
+                    help="sequences per step (default 512; smaller values only for profiling captures)")
     return ap.parse_args()
 
 
@@ -184,17 +186,9 @@ def run_reference_arm(args):
     return 0
 
 
-def torch_view(ptr: int, count: int):
-    import torch
-
-    class _CAI:
-        def __init__(self):
-            self.__cuda_array_interface__ = {"shape": (count,), "typestr": "<f4", "data": (ptr, False),
-                                             "version": 3, "strides": None}
-    return torch.as_tensor(_CAI(), device="cuda")
-
-
 def run_ours(args):
+    global GLOBAL_BATCH
+    GLOBAL_BATCH = args.global_batch
     import torch
     import torch.distributed as dist
 
@@ -227,24 +221,20 @@ def run_ours(args):
     assert rt.set_stream(stream.cuda_stream), rt.last_error
     assert rt.prepare_lm(cfg, B), rt.last_error
     assert rt.lm_state_upload(cfg.init_normal(SEED, 0.02)), rt.last_error
-    gptr, gcount = rt.lm_grad_buffer()
-    grads = torch_view(gptr, gcount)
-    loss_t = torch_view(rt.lm_loss_device(), 1)
+    from hexatrain_b200.parallel import DataParallelLmTrainer, GpuLmBackend
+    backend = GpuLmBackend(rt)
+    trainer = DataParallelLmTrainer(backend, GLOBAL_BATCH, rank, world)
+    loss_t = backend.local_mean_loss()
+    grads = backend.grad_buffer()
 
     def ids(step):
-        return data.lm_tokens(SEED, GLOBAL_BATCH, T, V, step=step)[rank * B:(rank + 1) * B]
+        return trainer.shard(data.lm_tokens(SEED, GLOBAL_BATCH, T, V, step=step))
 
     dev_tokens = [torch.from_numpy(ids(s).astype(np.int32)).cuda() for s in range(W + K)]
     torch.cuda.synchronize()
-    step_no = 0
 
     def device_step(tok):
-        nonlocal step_no
-        step_no += 1
-        assert rt.lm_forward_backward_device(tok.data_ptr(), 1.0 / GLOBAL_BATCH), rt.last_error
-        if world > 1:
-            dist.all_reduce(grads)
-        assert rt.lm_optimizer_step_device(step_no), rt.last_error
+        trainer.step(tok)
 
     def barrier():
         if world > 1:
@@ -273,7 +263,7 @@ def run_ours(args):
     if world > 1:
         dist.all_reduce(tmax, op=dist.ReduceOp.MAX)
     t_ms = float(tmax.item())
-    final_loss = float(loss_t.item())
+    final_loss = float(grads[-1].item()) if world > 1 else float(loss_t.item())
 
     # ---- end to end through the public API with host buffers ----
     pinned = [torch.from_numpy(ids(1000 + s).astype(np.int32)).pin_memory() for s in range(W + K)]
@@ -282,16 +272,16 @@ def run_ours(args):
 
     def e2e_step(i):
         if world == 1:
-            ok, lv = rt.lm_train_step(pinned[i].numpy().view(np.uint32), step_no + 1)
+            trainer.step_count += 1
+            ok, lv = rt.lm_train_step(pinned[i].numpy().view(np.uint32), trainer.step_count)
             assert ok, rt.last_error
             return lv
         tok_buf.copy_(pinned[i], non_blocking=True)
-        device_step(tok_buf)
-        return float(loss_t.item())
+        g = trainer.step(tok_buf)
+        return float(g[-1].item())
 
     for i in range(W):
         e2e_step(i)
-        step_no += 1 if world == 1 else 0
     barrier()
     t0 = time.perf_counter()
     e2 = torch.cuda.Event(enable_timing=True)
@@ -299,7 +289,6 @@ def run_ours(args):
     e2.record(stream)
     for i in range(K):
         host_loss[0] = e2e_step(W + i)
-        step_no += 1 if world == 1 else 0
     e3.record(stream)
     barrier()
     te_ms = max(e2.elapsed_time(e3), (time.perf_counter() - t0) * 1e3)
