@@ -104,6 +104,9 @@ SIGNATURES = {
                                  C.c_size_t, C.c_void_p, C.c_size_t, C.c_float, C.POINTER(MlpOutputsC)]),
     "hx_mlp_execute_device": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_float,
                                         C.POINTER(MlpOutputsC)]),
+    "hx_mlp_execute_device_noalloc": (C.c_int, [C.c_void_p, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32,
+                                                C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_float,
+                                                C.c_void_p, C.c_void_p, C.c_void_p]),
     "hx_lm_param_count": (C.c_size_t, [C.POINTER(LmConfigC)]),
     "hx_lm_validate": (C.c_int, [C.POINTER(LmConfigC), C.c_char_p, C.c_size_t]),
     "hx_lm_init_reference": (C.c_int, [C.POINTER(LmConfigC), C.c_uint32, C.c_void_p]),

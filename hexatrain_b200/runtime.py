@@ -363,6 +363,22 @@ class Runtime:
         return self._ok(self._lib.hx_mlp_execute_device(self._rt, C.c_void_p(x), C.c_void_p(y), C.c_void_p(w1),
                                                         C.c_void_p(w2), learning_rate, C.byref(o)))
 
+    def execute_mlp_full_step_device_noalloc(self, batch_size: int, input_dimension: int, hidden_dimension: int,
+                                             output_dimension: int, x: int, y: int, w1: int, w2: int,
+                                             learning_rate: float, loss: int, w1_next: int, w2_next: int) -> bool:
+        """The device-pointer step for callers that cannot let the library
+        allocate device memory (their allocator owns the GPU's memory, or
+        cudaMalloc is not allowed on their step path).  Needs no prepare; the
+        intermediates use a fixed 4 MiB device array shared by every call on
+        the device, so calls overlapping on the GPU race.  Not part of the
+        reference's Runtime."""
+        if not self._need():
+            return False
+        return self._ok(self._lib.hx_mlp_execute_device_noalloc(
+            self._rt, batch_size, input_dimension, hidden_dimension, output_dimension, C.c_void_p(x), C.c_void_p(y),
+            C.c_void_p(w1), C.c_void_p(w2), learning_rate, C.c_void_p(loss), C.c_void_p(w1_next),
+            C.c_void_p(w2_next)))
+
     # -- tiny Transformer LM -------------------------------------------------
     def prepare_tiny_transformer_training(self, tokens: int, dimension: int, feed_forward_dimension: int,
                                           epsilon: float, diagnostic_outputs: bool, vocabulary_size: int,

@@ -150,6 +150,27 @@ int hx_mlp_execute(hx_runtime* rt, const float* x, size_t x_count, const float* 
 int hx_mlp_execute_device(hx_runtime* rt, const float* x, const float* y, const float* w1,
                           const float* w2, float learning_rate, const hx_mlp_outputs* out);
 
+/* The same step on device pointers for callers that cannot let this library
+ * allocate device memory: a process whose GPU memory already belongs to its
+ * own allocator (a host framework's caching pool), or a step path on which
+ * cudaMalloc/cudaFree are not allowed because they synchronise the device.
+ * It has no counterpart in the reference.  No hx_mlp_prepare is needed and
+ * nothing is allocated: the intermediates (2*B*H + 2*B*O floats) live in one
+ * fixed 4 MiB array of device memory that every GPU loading this library
+ * holds until the process exits; larger shapes fail with
+ * HX_ERR_UNSUPPORTED.  The first call on a device looks up that array's
+ * address (and may load the library's device code); make it before any
+ * stream capture.  All calls on a device share the array, so calls whose
+ * work overlaps on the GPU (other streams or other runtimes on the same
+ * device) race; calls on one stream are safe.  Returns after the step has
+ * finished on the runtime stream.  K is never split, so shapes that the
+ * allocating step splits may differ from it in the last bits. */
+int hx_mlp_execute_device_noalloc(hx_runtime* rt, uint32_t batch, uint32_t input_dim,
+                                  uint32_t hidden_dim, uint32_t output_dim, const float* x,
+                                  const float* y, const float* w1, const float* w2,
+                                  float learning_rate, float* loss, float* w1_next,
+                                  float* w2_next);
+
 /* ---- tiny causal Transformer LM ----------------------------------------- */
 
 enum {
