@@ -100,37 +100,16 @@ void launch_tc(hx_runtime* rt, int M, int N, int K, const float* A, long lda, co
     constexpr CUtensorMapSwizzle mn_swz = CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B;
     const CUtensorMap ma = A_MN ? make_map(A, M, K, lda, 32, 32, mn_swz) : make_map(A, K, M, lda, 32, 128);
     const CUtensorMap mb = B_MN ? make_map(B, N, K, ldb, 32, 32, mn_swz) : make_map(B, K, N, ldb, 32, 128);
-    const int tiles_m = (M + kTcBM - 1) / kTcBM, tiles_n = (N + kTcBN - 1) / kTcBN;
-    const long tiles = (long)tiles_m * tiles_n;
-    int splits = 1;
-    if (tiles < rt->sm_count && K >= 2 * 256) {
-        splits = (int)((rt->sm_count + tiles - 1) / tiles);
-        splits = std::max(1, std::min(splits, K / 256));
-    }
-    int chunk = (K + splits - 1) / splits;
-    chunk = ((chunk + kTcBK - 1) / kTcBK) * kTcBK;
-    splits = (K + chunk - 1) / chunk;
-    static bool attr_set = false;
-    if (!attr_set) {
-        HX_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<A_MN, B_MN, Epi>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     (int)kTcSmemBytes));
-        attr_set = true;
-    }
+    const TcGrid g = tc_grid(M, N, K, rt->sm_count, 64);
     int* err = rt->device_error();
-    dim3 grid(tiles_n, tiles_m, splits);
-    if (splits == 1) {
-        gemm_tc_kernel<A_MN, B_MN, Epi><<<grid, kTcThreads, kTcSmemBytes, rt->stream>>>(ma, mb, M, N, K, chunk, epi,
-                                                                                       nullptr, err);
-        HX_LAUNCHED(rt);
-    } else {
-        float* ws = rt->workspace(sizeof(float) * (size_t)splits * M * N);
-        gemm_tc_kernel<A_MN, B_MN, Epi><<<grid, kTcThreads, kTcSmemBytes, rt->stream>>>(ma, mb, M, N, K, chunk, epi,
-                                                                                       ws, err);
-        HX_LAUNCHED(rt);
+    float* ws = g.splits > 1 ? rt->workspace(sizeof(float) * (size_t)g.splits * M * N) : nullptr;
+    HX_CUDA((launch_tc_kernel<A_MN, B_MN>(rt->stream, rt->sm_count, ma, mb, g, epi, ws, err)));
+    ++rt->metrics.kernel_launches;
+    if (g.splits > 1) {
         const long total = (long)M * N;
         const int threads = 256;
         const int blocks = (int)std::min<long>((total + threads - 1) / threads, 4L * rt->sm_count * 8);
-        splitk_reduce_kernel<Epi><<<blocks, threads, 0, rt->stream>>>(M, N, splits, ws, epi);
+        splitk_reduce_kernel<Epi><<<blocks, threads, 0, rt->stream>>>(M, N, g.splits, ws, epi);
         HX_LAUNCHED(rt);
     }
 }

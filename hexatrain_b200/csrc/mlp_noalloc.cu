@@ -89,13 +89,9 @@ void gemm_noalloc(hx_runtime* rt, int M, int N, int K, const float* A, long lda,
         constexpr CUtensorMapSwizzle mn_swz = CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B;
         const CUtensorMap ma = A_MN ? make_map(A, M, K, lda, 32, 32, mn_swz) : make_map(A, K, M, lda, 32, 128);
         const CUtensorMap mb = B_MN ? make_map(B, N, K, ldb, 32, 32, mn_swz) : make_map(B, K, N, ldb, 32, 128);
-        HX_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<A_MN, B_MN, Epi>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     (int)kTcSmemBytes));
-        const int chunk = ((K + kTcBK - 1) / kTcBK) * kTcBK;
-        dim3 grid((N + kTcBN - 1) / kTcBN, (M + kTcBM - 1) / kTcBM, 1);
-        gemm_tc_kernel<A_MN, B_MN, Epi><<<grid, kTcThreads, kTcSmemBytes, rt->stream>>>(ma, mb, M, N, K, chunk, epi,
-                                                                                       nullptr, err);
-        HX_LAUNCHED(rt);
+        const TcGrid g = tc_grid(M, N, K, rt->sm_count, 1);
+        HX_CUDA((launch_tc_kernel<A_MN, B_MN>(rt->stream, rt->sm_count, ma, mb, g, epi, nullptr, err)));
+        ++rt->metrics.kernel_launches;
         return;
     }
     auto simt = [&](auto shape_tag) {
