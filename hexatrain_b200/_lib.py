@@ -86,6 +86,12 @@ class AdamOutputsC(C.Structure):
                                    "normalized", "scaled_update", "w_next")]
 
 
+class NprtInfoC(C.Structure):
+    _fields_ = [("version", C.c_uint32), ("seed", C.c_uint32), ("step", C.c_uint32), ("finite", C.c_uint32),
+                ("has_adam", C.c_uint32), ("parameter_count", C.c_uint64), ("parameter_hash", C.c_char * 32),
+                ("tokenizer_hash", C.c_char * 80)]
+
+
 # name -> (restype, argtypes).  Must match include/hexatrain.h.
 SIGNATURES = {
     "hx_runtime_create": (C.c_int, [C.c_int, C.POINTER(C.c_void_p), C.c_char_p, C.c_size_t]),
@@ -132,6 +138,17 @@ SIGNATURES = {
     "hx_muon_execute": (C.c_int, [C.c_void_p, C.c_uint32, C.c_uint32, C.c_void_p, C.c_void_p, C.c_void_p,
                                   C.c_float, C.c_float, C.c_int, C.c_uint32, C.c_float, C.c_float, C.c_float,
                                   C.c_int, C.c_void_p, C.c_void_p]),
+    "hx_nprt_encoded_bytes": (C.c_size_t, [C.c_void_p, C.c_char_p, C.c_char_p]),
+    "hx_nprt_encode": (C.c_int, [C.c_void_p, C.c_uint32, C.c_uint32, C.c_char_p, C.c_char_p, C.c_void_p, C.c_void_p,
+                                 C.c_void_p, C.c_void_p, C.c_size_t, C.POINTER(C.c_size_t), C.c_char_p, C.c_size_t]),
+    "hx_nprt_decode": (C.c_int, [C.c_void_p, C.c_uint32, C.c_char_p, C.c_void_p, C.c_size_t, C.POINTER(NprtInfoC),
+                                 C.c_void_p, C.c_void_p, C.c_void_p, C.c_char_p, C.c_size_t]),
+    "hx_nprt_checkpoint_name": (C.c_int, [C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32,
+                                          C.c_char_p, C.c_size_t]),
+    "hx_nprt_training_order": (C.c_int, [C.c_uint64, C.c_uint32, C.c_uint32, C.c_void_p]),
+    "hx_lm_checkpoint_save": (C.c_int, [C.c_void_p, C.c_char_p, C.c_uint32, C.c_uint32, C.c_char_p, C.c_char_p]),
+    "hx_lm_checkpoint_resume": (C.c_int, [C.c_void_p, C.c_char_p, C.c_uint32, C.c_uint32, C.c_char_p,
+                                          C.POINTER(NprtInfoC)]),
 }
 
 _LIB = None

@@ -70,6 +70,13 @@ struct LmPlan {
 };
 
 size_t lm_plan_bytes(const LmPlan* p) { return p ? p->arena.block.bytes + p->onehot.bytes : 0; }
+
+bool lm_prepared_config(const hx_runtime* rt, hx_lm_config* cfg, uint32_t* optimizer_kind) {
+    if (!rt || !rt->lm) return false;
+    if (cfg) *cfg = rt->lm->cfg;
+    if (optimizer_kind) *optimizer_kind = rt->lm->opt.kind;
+    return true;
+}
 void LmPlanDeleter::operator()(LmPlan* p) const { delete p; }
 
 namespace {

@@ -42,6 +42,9 @@ struct AdamPlan {
 
 struct LmPlan;  // lm.cu
 size_t lm_plan_bytes(const LmPlan* p);
+// The configuration and optimizer kind of the prepared LM plan; false if
+// no LM is prepared.
+bool lm_prepared_config(const hx_runtime* rt, hx_lm_config* cfg, uint32_t* optimizer_kind);
 
 inline size_t plan_device_bytes(const hx_runtime* rt) {
     size_t n = 0;

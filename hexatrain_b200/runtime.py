@@ -474,6 +474,24 @@ class Runtime:
             raise RuntimeError(self.last_error)
         return tuple(outs)  # params, adam_m, adam_v, muon_buffer
 
+    def lm_checkpoint_save(self, path: str, seed: int, step: int, tokenizer_kind: str | None = None,
+                           tokenizer_hash: str | None = None) -> bool:
+        """nprtSaveCheckpointV2 of the device state (qnn_transformer_training.cpp:5171-5252):
+        parameters and Adam moments, written to path.tmp and renamed."""
+        enc = (lambda s: None if s is None else s.encode())
+        return self._need() and self._ok(self._lib.hx_lm_checkpoint_save(
+            self._rt, path.encode(), seed, step, enc(tokenizer_kind), enc(tokenizer_hash)))
+
+    def lm_checkpoint_resume(self, path: str, seed: int, step: int = 0, tokenizer_hash: str | None = None):
+        """Canonical resume (qnn_transformer_training.cpp:7068-7109).  Returns
+        the CheckpointInfo, or None with last_error set (RESUME_* codes)."""
+        from .checkpoint import _info
+        info = _lib.NprtInfoC()
+        ok = self._need() and self._ok(self._lib.hx_lm_checkpoint_resume(
+            self._rt, path.encode(), seed, step, None if tokenizer_hash is None else tokenizer_hash.encode(),
+            C.byref(info)))
+        return _info(info) if ok else None
+
     def lm_set_optimizer(self, opt: OptimizerConfig) -> bool:
         return self._need() and self._ok(self._lib.hx_lm_set_optimizer(self._rt, C.byref(opt.to_c())))
 

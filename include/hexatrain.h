@@ -331,6 +331,66 @@ int hx_muon_execute(hx_runtime* rt, uint32_t rows, uint32_t cols, const float* w
                     float momentum, int nesterov, uint32_t ns_steps, float a, float b, float c,
                     int bf16_inputs, float* weight_next, float* momentum_buffer_next);
 
+/* ---- NPRTCKPTV2 / V3 checkpoint of the LM training state ----------------- */
+/* The reference's canonical resume file (qnn/qnn_transformer_training.cpp:
+ * 5164-5252 writer nprtSaveCheckpointV2, :5390-5522 reader
+ * nprtLoadCheckpointForGeneration): header (magic, V T D F L H seed step,
+ * big endian), the V3 tokenizer block at vocabulary 1024, then the
+ * parameter, Adam first-moment and Adam second-moment registries in
+ * tiny_lm::parameterRegistry order (tiny_language_model_cpu.cpp:63).  The
+ * flat buffers here (hx_lm_state_download order) are that order; a
+ * learned-position model adds "position_embedding" after
+ * "token_embedding".  Codec errors are the reference's NPRT_CKPT_* codes. */
+typedef struct {
+    uint32_t version;          /* 1, 2 or 3 (NPRTCKPTV1 / V2 / V3) */
+    uint32_t seed;
+    uint32_t step;
+    uint32_t finite;           /* 0 when any stored value is NaN or infinite */
+    uint32_t has_adam;         /* 1 for V2 / V3 */
+    uint64_t parameter_count;
+    char parameter_hash[32];   /* nprtParameterHash: "fnv1a64:" + 16 hex digits */
+    char tokenizer_hash[80];   /* V3 only */
+} hx_nprt_info;
+
+/* Bytes hx_nprt_encode writes for this configuration and tokenizer identity. */
+size_t hx_nprt_encoded_bytes(const hx_lm_config* config, const char* tokenizer_kind,
+                             const char* tokenizer_hash);
+/* nprtSaveCheckpointV2 (:5171-5252) into memory: refuses step 0 and
+ * non-finite state; at vocabulary 1024 writes NPRTCKPTV3 and needs kind
+ * "byte_bpe" and a 71-character "sha256:" hash, otherwise NPRTCKPTV2 with
+ * both NULL or empty.  Host only; needs no runtime or GPU. */
+int hx_nprt_encode(const hx_lm_config* config, uint32_t seed, uint32_t step,
+                   const char* tokenizer_kind, const char* tokenizer_hash, const float* params,
+                   const float* adam_m, const float* adam_v, uint8_t* out, size_t capacity,
+                   size_t* written, char* error, size_t error_capacity);
+/* nprtLoadCheckpointForGeneration (:5390-5522) over memory: validates and,
+ * where the pointers are non-NULL, copies the registries out.  V1 files
+ * decode with has_adam = 0.  Host only. */
+int hx_nprt_decode(const hx_lm_config* config, uint32_t expected_seed,
+                   const char* expected_tokenizer_hash, const uint8_t* data, size_t size,
+                   hx_nprt_info* info, float* params, float* adam_m, float* adam_v, char* error,
+                   size_t error_capacity);
+/* nicopedia_checkpoint::checkpointName (nicopedia_checkpoint_policy.h):
+ * "htp-seed<S>-l<L>[-t<T>-d<D>-f<F>]-step<N>.ckpt". */
+int hx_nprt_checkpoint_name(uint32_t seed, uint32_t layers, uint32_t tokens, uint32_t dimension,
+                            uint32_t feed_forward_dimension, uint32_t step, char* out,
+                            size_t capacity);
+/* nprtTrainingOrder (qnn/qnn_transformer_training.cpp:4983-4995): the
+ * record index of every (step, batch slot), a pure function of the global
+ * step, so a resumed run re-derives its data cursor.  out[steps*batch]. */
+int hx_nprt_training_order(uint64_t record_count, uint32_t steps, uint32_t batch, uint64_t* out);
+/* Writes the prepared LM's device state (parameters, Adam moments) to
+ * `path` via "<path>.tmp" and a rename.  Adam optimizer only: the format
+ * has no slot for Muon momentum. */
+int hx_lm_checkpoint_save(hx_runtime* rt, const char* path, uint32_t seed, uint32_t step,
+                          const char* tokenizer_kind, const char* tokenizer_hash);
+/* Canonical resume (:7068-7109): decodes `path`, requires the step
+ * (expected_step != 0), finite values and Adam moments (a V1 file fails
+ * with RESUME_ADAM_STATE_MISSING), then uploads the state.  Continue with
+ * hx_lm_train_step(step + 1, ...). */
+int hx_lm_checkpoint_resume(hx_runtime* rt, const char* path, uint32_t expected_seed,
+                            uint32_t expected_step, const char* tokenizer_hash, hx_nprt_info* info);
+
 #ifdef __cplusplus
 }
 #endif
