@@ -14,6 +14,7 @@
 
 #include <math.h>
 #include <pthread.h>
+#include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
 
@@ -748,4 +749,125 @@ void hxo_muon(int rows, int cols, const float* w, const float* g, const float* b
             w_next[(size_t)i * cols + j] = w[(size_t)i * cols + j] - lr * (sc * xo);
         }
     free(u); free(X); free(Xt); free(A); free(A2); free(Bm); free(BX);
+}
+
+/* ---------------------------------------------------------------------- */
+/* NPRTCKPTV2 / V3 writer (qnn/qnn_transformer_training.cpp:5123-5131 for   */
+/* the big-endian integers, :5171-5252 for the file).                       */
+
+/* Registry entry k of the layout above: its name and element count;
+ * returns 0 past the end. */
+static int nprt_entry(const hxo_lm_config* c, uint32_t k, char name[40], uint64_t* count)
+{
+    static const char* const kLayer[10] = {"norm1_gamma", "norm1_beta", "wq", "wk", "wv",
+                                           "wo", "norm2_gamma", "norm2_beta", "ffn_w1", "ffn_w2"};
+    const uint64_t V = c->vocab, T = c->tokens, D = c->dim, F = c->ffn;
+    const uint64_t sizes[10] = {D, D, D * D, D * D, D * D, D * D, D, D, D * F, F * D};
+    if (k == 0) { strcpy(name, "token_embedding"); *count = V * D; return 1; }
+    k -= 1;
+    if (c->learned_position) {
+        if (k == 0) { strcpy(name, "position_embedding"); *count = T * D; return 1; }
+        k -= 1;
+    }
+    if (k < 10u * c->layers) {
+        char buf[40];
+        snprintf(buf, sizeof buf, "layer_%03u.%s", k / 10, kLayer[k % 10]);
+        strcpy(name, buf);
+        *count = sizes[k % 10];
+        return 1;
+    }
+    if (k == 10u * c->layers) { strcpy(name, "output_projection"); *count = D * V; return 1; }
+    return 0;
+}
+
+static void put_be(uint8_t* out, size_t capacity, size_t* at, uint64_t v, int bytes)
+{
+    for (int s = 8 * (bytes - 1); s >= 0; s -= 8) {
+        if (*at < capacity && out) out[*at] = (uint8_t)(v >> s);
+        ++*at;
+    }
+}
+
+static void put_raw(uint8_t* out, size_t capacity, size_t* at, const void* src, size_t n)
+{
+    if (out && *at + n <= capacity) memcpy(out + *at, src, n);
+    *at += n;
+}
+
+size_t hxo_nprt_encode(const hxo_lm_config* c, uint32_t seed, uint32_t step, const char* kind,
+                       const char* hash, const float* params, const float* m, const float* v,
+                       uint8_t* out, size_t capacity)
+{
+    const size_t n = hxo_lm_param_count(c);
+    const int v3 = c->vocab == 1024;
+    const char* k = kind ? kind : "";
+    const char* h = hash ? hash : "";
+    if (step == 0) return 0;
+    for (size_t i = 0; i < n; ++i)
+        if (!isfinite(params[i]) || !isfinite(m[i]) || !isfinite(v[i])) return 0;
+    if (v3 && (strcmp(k, "byte_bpe") != 0 || strlen(h) != 71 || strncmp(h, "sha256:", 7) != 0)) return 0;
+    if (!v3 && (*k || *h)) return 0;
+    size_t at = 0;
+    put_raw(out, capacity, &at, v3 ? "NPRTCKPTV3\n" : "NPRTCKPTV2\n", 11);
+    const uint32_t head[8] = {c->vocab, c->tokens, c->dim, c->ffn, c->layers, c->heads, seed, step};
+    for (int i = 0; i < 8; ++i) put_be(out, capacity, &at, head[i], 4);
+    if (v3) {
+        put_be(out, capacity, &at, strlen(k), 4);
+        put_raw(out, capacity, &at, k, strlen(k));
+        put_be(out, capacity, &at, strlen(h), 4);
+        put_raw(out, capacity, &at, h, strlen(h));
+    }
+    const uint32_t entries = 2 + (c->learned_position ? 1 : 0) + 10 * c->layers;
+    const float* regs[3] = {params, m, v};
+    for (int r = 0; r < 3; ++r) {
+        put_be(out, capacity, &at, entries, 4);
+        size_t off = 0;
+        char name[40];
+        uint64_t count;
+        for (uint32_t e = 0; nprt_entry(c, e, name, &count); ++e) {
+            put_be(out, capacity, &at, strlen(name), 4);
+            put_raw(out, capacity, &at, name, strlen(name));
+            put_be(out, capacity, &at, count, 8);
+            put_raw(out, capacity, &at, regs[r] + off, count * sizeof(float));
+            off += count;
+        }
+    }
+    return at;
+}
+
+static uint64_t fnv1a(uint64_t h, const void* p, size_t n)
+{
+    const uint8_t* b = (const uint8_t*)p;
+    for (size_t i = 0; i < n; ++i) {
+        h ^= b[i];
+        h *= 1099511628211ull;
+    }
+    return h;
+}
+
+void hxo_nprt_parameter_hash(const hxo_lm_config* c, const float* params, char out[32])
+{
+    uint64_t h = 14695981039346656037ull;
+    size_t off = 0;
+    char name[40];
+    uint64_t count;
+    for (uint32_t e = 0; nprt_entry(c, e, name, &count); ++e) {
+        h = fnv1a(h, name, strlen(name));
+        h = fnv1a(h, &count, sizeof count);
+        h = fnv1a(h, params + off, count * sizeof(float));
+        off += count;
+    }
+    snprintf(out, 32, "fnv1a64:%016llx", (unsigned long long)h);
+}
+
+void hxo_nprt_training_order(uint64_t records, uint32_t steps, uint32_t batch, uint64_t* out)
+{
+    uint64_t state = 20260806;
+    for (uint64_t i = 0; i < (uint64_t)steps * batch; ++i) {
+        uint64_t x = state + i + 0x9e3779b97f4a7c15ull;
+        x = (x ^ (x >> 30)) * 0xbf58476d1ce4e5b9ull;
+        x = (x ^ (x >> 27)) * 0x94d049bb133111ebull;
+        state = x ^ (x >> 31);
+        out[i] = state % records;
+    }
 }

@@ -139,6 +139,25 @@ void hxo_muon(int rows, int cols, const float* w, const float* g, const float* b
 /* Round a float to the nearest bfloat16 (ties to even), returned as float. */
 float hxo_round_bf16(float x);
 
+/* ---- NPRTCKPTV2 / V3 checkpoint writer ------------------------------------
+ * nprtSaveCheckpointV2 (qnn/qnn_transformer_training.cpp:5171-5252): magic
+ * (V3 at vocabulary 1024 with the tokenizer block, else V2), eight big-endian
+ * u32 (V T D F L H seed step), then the parameter, first-moment and
+ * second-moment registries (u32 count; per entry u32 name length, name,
+ * big-endian u64 count, raw float32) in parameterRegistry order
+ * (tiny_language_model_cpu.cpp:63), plus "position_embedding" after
+ * "token_embedding" for a learned-position model.  Returns the bytes the
+ * file needs and writes them when out has room; returns 0 when the writer
+ * refuses (step 0, non-finite state, tokenizer identity). */
+size_t hxo_nprt_encode(const hxo_lm_config* c, uint32_t seed, uint32_t step, const char* kind,
+                       const char* hash, const float* params, const float* m, const float* v,
+                       uint8_t* out, size_t capacity);
+/* nprtParameterHash (:5080-5090): FNV-1a 64 over (name, native u64 count,
+ * values) of every parameter entry; writes "fnv1a64:%016llx". */
+void hxo_nprt_parameter_hash(const hxo_lm_config* c, const float* params, char out[32]);
+/* nprtTrainingOrder (:4983-4995): splitmix64 chain from 20260806. */
+void hxo_nprt_training_order(uint64_t records, uint32_t steps, uint32_t batch, uint64_t* out);
+
 #ifdef __cplusplus
 }
 #endif

@@ -235,6 +235,33 @@ class Oracle:
     def round_bf16(self, x: float) -> float:
         return float(self.lib.hxo_round_bf16(x))
 
+    def nprt_encode(self, cfg: LmConfig, seed, step, params, m, v, kind=None, hash=None) -> bytes:
+        """hxo_nprt_encode; raises ValueError when the writer refuses."""
+        L = self.lib
+        L.hxo_nprt_encode.restype = C.c_size_t
+        L.hxo_nprt_encode.argtypes = [C.POINTER(LmConfig), C.c_uint32, C.c_uint32, C.c_char_p, C.c_char_p,
+                                      _f32p, _f32p, _f32p, C.c_void_p, C.c_size_t]
+        args = [C.byref(cfg), seed, step, None if kind is None else kind.encode(),
+                None if hash is None else hash.encode()] + [np.ascontiguousarray(a, np.float32) for a in (params, m, v)]
+        need = L.hxo_nprt_encode(*args, None, 0)
+        if need == 0:
+            raise ValueError("oracle writer refused")
+        out = np.zeros(need, np.uint8)
+        L.hxo_nprt_encode(*args, out.ctypes.data, need)
+        return out.tobytes()
+
+    def nprt_parameter_hash(self, cfg: LmConfig, params) -> str:
+        self.lib.hxo_nprt_parameter_hash.argtypes = [C.POINTER(LmConfig), _f32p, C.c_char_p]
+        out = C.create_string_buffer(32)
+        self.lib.hxo_nprt_parameter_hash(C.byref(cfg), np.ascontiguousarray(params, np.float32), out)
+        return out.value.decode()
+
+    def nprt_training_order(self, records, steps, batch):
+        self.lib.hxo_nprt_training_order.argtypes = [C.c_uint64, C.c_uint32, C.c_uint32, C.c_void_p]
+        out = np.zeros(steps * batch, np.uint64)
+        self.lib.hxo_nprt_training_order(records, steps, batch, out.ctypes.data)
+        return out
+
 
 class Reference:
     """The reference's own CPU code (oracle/_ref/libhexaref.so)."""
@@ -348,6 +375,74 @@ class Reference:
         a, r = C.c_float(), C.c_float()
         ok = self.lib.hxr_lm_gradient_check(seed, eps, C.byref(a), C.byref(r))
         return bool(ok), a.value, r.value
+
+
+REF_CKPT_SO = os.path.join(HERE, "_ref", "libhexaref_ckpt.so")
+
+
+class ReferenceCheckpoint:
+    """The reference's own NPRTCKPT codec (oracle/_ref/libhexaref_ckpt.so):
+    nprtSaveCheckpointV2 / nprtLoadCheckpointForGeneration / nprtParameterHash
+    / nprtTrainingOrder / nprtCheckpointName from
+    qnn/qnn_transformer_training.cpp, compiled by oracle/Makefile."""
+
+    def __init__(self, path: str = REF_CKPT_SO):
+        if not os.path.exists(path):
+            raise FileNotFoundError(path)
+        self.lib = L = C.CDLL(path)
+        u = C.c_uint32
+        L.hxr_nprt_save.restype = C.c_int
+        L.hxr_nprt_save.argtypes = [C.c_char_p] + [u] * 8 + [_f32p] * 3 + [C.c_char_p, C.c_char_p]
+        L.hxr_nprt_load.restype = C.c_int
+        L.hxr_nprt_load.argtypes = [C.c_char_p] + [u] * 7 + [C.c_char_p, C.POINTER(u), C.POINTER(u),
+                                                             C.POINTER(C.c_int), C.POINTER(C.c_int)] + \
+            [C.c_void_p] * 3 + [C.c_char_p, C.c_size_t, C.c_char_p, C.c_size_t]
+        L.hxr_nprt_parameter_hash.argtypes = [u] * 6 + [_f32p, C.c_char_p, C.c_size_t]
+        L.hxr_nprt_training_order.argtypes = [C.c_uint64, u, u, C.c_void_p]
+        L.hxr_nprt_checkpoint_name.argtypes = [u] * 6 + [C.c_char_p, C.c_size_t]
+
+    @staticmethod
+    def _dims(cfg):
+        return [cfg.vocab, cfg.tokens, cfg.dim, cfg.ffn, cfg.layers, cfg.heads]
+
+    def save(self, path, cfg, seed, step, params, m, v, kind=None, hash=None) -> bool:
+        f = [np.ascontiguousarray(a, np.float32) for a in (params, m, v)]
+        return self.lib.hxr_nprt_save(path.encode(), *self._dims(cfg), seed, step, *f,
+                                      None if kind is None else kind.encode(),
+                                      None if hash is None else hash.encode()) == 1
+
+    def load(self, path, cfg, seed, n, tokenizer_hash=None):
+        """Returns (ok, error, info dict, params, m, v)."""
+        step, version = C.c_uint32(), C.c_uint32()
+        finite, has_adam = C.c_int(), C.c_int()
+        p, m, v = (np.zeros(n, np.float32) for _ in range(3))
+        ph, err = C.create_string_buffer(64), C.create_string_buffer(256)
+        ok = self.lib.hxr_nprt_load(path.encode(), *self._dims(cfg), seed,
+                                    None if tokenizer_hash is None else tokenizer_hash.encode(),
+                                    C.byref(step), C.byref(version), C.byref(finite), C.byref(has_adam),
+                                    p.ctypes.data, m.ctypes.data, v.ctypes.data, ph, 64, err, 256) == 1
+        info = dict(step=step.value, version=version.value, finite=bool(finite.value),
+                    has_adam=bool(has_adam.value), parameter_hash=ph.value.decode())
+        return ok, err.value.decode(), info, p, m, v
+
+    def parameter_hash(self, cfg, params) -> str:
+        out = C.create_string_buffer(64)
+        self.lib.hxr_nprt_parameter_hash(*self._dims(cfg), np.ascontiguousarray(params, np.float32), out, 64)
+        return out.value.decode()
+
+    def training_order(self, records, steps, batch):
+        out = np.zeros(steps * batch, np.uint64)
+        self.lib.hxr_nprt_training_order(records, steps, batch, out.ctypes.data)
+        return out
+
+    def checkpoint_name(self, seed, layers, T, D, F, step) -> str:
+        out = C.create_string_buffer(128)
+        self.lib.hxr_nprt_checkpoint_name(seed, layers, T, D, F, step, out, 128)
+        return out.value.decode()
+
+
+def reference_checkpoint_available() -> bool:
+    return os.path.exists(REF_CKPT_SO)
 
 
 def reference_available() -> bool:
