@@ -5,5 +5,6 @@ Native code lives in libhexatrain_b200.so (C ABI: include/hexatrain.h); this
 package is its host-side mirror of the reference's Runtime API and drivers.
 """
 from ._lib import NativeLibraryError, load  # noqa: F401
-from .runtime import (AdamOptimizerOutputs, LmConfig, MlpFullStepOutputs, OptimizerConfig, Runtime,  # noqa: F401
-                      RuntimeMetrics, RuntimeOptions, TinyTransformerTrainingOutputs)
+from .runtime import (AdamOptimizerOutputs, LmConfig, MlpFullStepOutputs, MomentumOptimizerOutputs,  # noqa: F401
+                      OptimizerConfig, Runtime, RuntimeMetrics, RuntimeOptions, TinyTransformerTrainingOutputs,
+                      apply_init_stability, stability_learning_rate)

@@ -26,6 +26,14 @@ HX_GEMM_CUDA_CORES = 1
 HX_GEMM_TENSOR_CORES = 2
 HX_OPT_ADAM = 0
 HX_OPT_MUON = 1
+HX_OPT_MOMENTUM = 2
+HX_STABILITY_LEGACY = 0
+HX_STABILITY_WARMUP64 = 1
+HX_STABILITY_DECAY_LINEAR = 2
+HX_STABILITY_ZERO_OUTPUT_PROJ_BRANCH_INIT = 3
+HX_STABILITY_DEPTH_SCALED_BRANCH_INIT = 4
+HX_STABILITY_RESIDUAL_BRANCH_SCALING = 5
+HX_STABILITY_GRADIENT_CLIP_1 = 6
 
 _fp = C.POINTER(C.c_float)
 _u8p = C.POINTER(C.c_uint8)
@@ -78,7 +86,8 @@ class OptimizerConfigC(C.Structure):
     _fields_ = [("kind", C.c_uint32), ("adam_lr", C.c_float), ("beta1", C.c_float), ("beta2", C.c_float),
                 ("adam_eps", C.c_float), ("muon_lr", C.c_float), ("muon_momentum", C.c_float),
                 ("muon_nesterov", C.c_uint32), ("muon_ns_steps", C.c_uint32), ("ns_a", C.c_float),
-                ("ns_b", C.c_float), ("ns_c", C.c_float), ("muon_bf16_inputs", C.c_uint32)]
+                ("ns_b", C.c_float), ("ns_c", C.c_float), ("muon_bf16_inputs", C.c_uint32),
+                ("momentum_lr", C.c_float), ("momentum", C.c_float)]
 
 
 class AdamOutputsC(C.Structure):
@@ -138,6 +147,16 @@ SIGNATURES = {
     "hx_muon_execute": (C.c_int, [C.c_void_p, C.c_uint32, C.c_uint32, C.c_void_p, C.c_void_p, C.c_void_p,
                                   C.c_float, C.c_float, C.c_int, C.c_uint32, C.c_float, C.c_float, C.c_float,
                                   C.c_int, C.c_void_p, C.c_void_p]),
+    "hx_momentum_prepare": (C.c_int, [C.c_void_p, C.c_uint32]),
+    "hx_momentum_execute": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_float, C.c_float,
+                                      C.c_void_p, C.c_void_p]),
+    "hx_momentum_execute_device": (C.c_int, [C.c_void_p, C.c_size_t, C.c_void_p, C.c_void_p, C.c_void_p, C.c_float,
+                                             C.c_float, C.c_void_p, C.c_void_p]),
+    "hx_stability_mode_error": (C.c_char_p, [C.c_uint32]),
+    "hx_stability_learning_rate": (C.c_float, [C.c_uint32, C.c_float, C.c_uint32, C.c_uint32]),
+    "hx_lm_apply_init_stability": (C.c_int, [C.POINTER(LmConfigC), C.c_uint32, C.c_void_p]),
+    "hx_lm_set_stability": (C.c_int, [C.c_void_p, C.c_uint32, C.c_uint32, C.c_float]),
+    "hx_lm_last_gradient_norm": (C.c_int, [C.c_void_p, C.POINTER(C.c_double), C.POINTER(C.c_float)]),
     "hx_nprt_encoded_bytes": (C.c_size_t, [C.c_void_p, C.c_char_p, C.c_char_p]),
     "hx_nprt_encode": (C.c_int, [C.c_void_p, C.c_uint32, C.c_uint32, C.c_char_p, C.c_char_p, C.c_void_p, C.c_void_p,
                                  C.c_void_p, C.c_void_p, C.c_size_t, C.POINTER(C.c_size_t), C.c_char_p, C.c_size_t]),

@@ -121,6 +121,7 @@ struct Profiler {
 struct MlpPlan;
 struct LmPlan;
 struct AdamPlan;
+struct MomentumPlan;
 // LmPlan is defined in lm.cu; its deleter is too.
 struct LmPlanDeleter {
     void operator()(LmPlan* p) const;
@@ -139,6 +140,7 @@ struct hx_runtime {
     std::unique_ptr<hx::MlpPlan> mlp;
     std::unique_ptr<hx::LmPlan, hx::LmPlanDeleter> lm;
     std::unique_ptr<hx::AdamPlan> adam;
+    std::unique_ptr<hx::MomentumPlan> momentum;
     hx::DeviceBuffer scratch;  // generic device workspace (grows on demand)
     hx::DeviceBuffer err_flag; // device-side error word of bounded waits
     hx::Profiler prof;

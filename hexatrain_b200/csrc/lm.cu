@@ -24,7 +24,12 @@ namespace hx {
 
 AdamScalars adam_scalars(float lr, float gradient_scale, float c1, float c2);
 void launch_adam(hx_runtime* rt, bool graph_order, size_t n, const float* w, const float* g, const float* m,
-                 const float* v, float* wn, float* mn, float* vn, const AdamScalars& s, const AdamTaps& t);
+                 const float* v, float* wn, float* mn, float* vn, const AdamScalars& s, const AdamTaps& t,
+                 const float* scale_dev = nullptr);
+void launch_momentum(hx_runtime* rt, size_t n, const float* w, const float* g, const float* vel, float* wn,
+                     float* veln, float lr, float momentum);
+void launch_clip_scale(hx_runtime* rt, const float* g, const GradTensor* tensors, int count, double* sumsq,
+                       float threshold, double* norm_out, float* scale_out);
 size_t muon_smem_bytes(int rows, int cols);
 void check_muon_shape(int rows, int cols);
 void launch_muon(hx_runtime* rt, const MuonMatrix* d_mats, int count, size_t smem, const MuonScalars& s);
@@ -62,6 +67,11 @@ struct LmPlan {
     int muon_count = 0;
     size_t muon_smem = 0;
     std::vector<std::pair<size_t, size_t>> adam_segments;  // [offset, count) in floats
+    // training-stability modes (training_stability.h) and global-norm clip
+    uint32_t stab_mode = 0, stab_total = 0;
+    float clip_threshold = 0.f;        // > 0: clip the gradient to this global norm before Adam
+    int norm_count = 0;                // tensors in the gradient-norm table
+    size_t norm_table = 0, norm_sumsq = 0, norm_value = 0, clip_scale = 0;
     bool state_ready = false;
     float* host_scalars = nullptr;  // pinned [c1, c2]
     ~LmPlan() {
@@ -330,22 +340,37 @@ void optimizer_step(hx_runtime* rt, LmPlan& p, uint32_t step)
     // (qnn/qnn_transformer_training.cpp:1504-1507): double, then float.
     const float c1 = float(1.0 / (1.0 - std::pow(double(p.opt.beta1), double(step))));
     const float c2 = float(1.0 / (1.0 - std::pow(double(p.opt.beta2), double(step))));
-    AdamScalars sc = adam_scalars(p.opt.adam_lr, 1.0f, c1, c2);
+    // Scheduled learning rates (training_stability.h stabilityLearningRate)
+    // and the global-norm clip scale, which Adam reads from device memory.
+    const float adam_lr = hx_stability_learning_rate(p.stab_mode, p.opt.adam_lr, step, p.stab_total);
+    const float* scale_dev = nullptr;
+    if (p.clip_threshold > 0.f) {
+        launch_clip_scale(rt, G, a.at<GradTensor>(p.norm_table), p.norm_count, a.at<double>(p.norm_sumsq),
+                          p.clip_threshold, a.at<double>(p.norm_value), a.at<float>(p.clip_scale));
+        scale_dev = a.at<float>(p.clip_scale);
+    }
+    AdamScalars sc = adam_scalars(adam_lr, 1.0f, c1, c2);
     sc.beta1 = p.opt.beta1;
     sc.beta2 = p.opt.beta2;
     sc.one_minus_beta1 = 1.0f - p.opt.beta1;
     sc.one_minus_beta2 = 1.0f - p.opt.beta2;
     sc.eps = p.opt.adam_eps;
     const AdamTaps none{};
-    if (p.opt.kind == HX_OPT_MUON) {
-        MuonScalars ms{p.opt.muon_lr, p.opt.muon_momentum, p.opt.ns_a, p.opt.ns_b, p.opt.ns_c,
+    if (p.opt.kind == HX_OPT_MOMENTUM) {
+        // velocity lives in the Muon buffer slot (zeroed on state upload)
+        float* vel = a.at<float>(p.muon_buf);
+        launch_momentum(rt, p.P, W, G, vel, W, vel,
+                        hx_stability_learning_rate(p.stab_mode, p.opt.momentum_lr, step, p.stab_total),
+                        p.opt.momentum);
+    } else if (p.opt.kind == HX_OPT_MUON) {
+        MuonScalars ms{hx_stability_learning_rate(p.stab_mode, p.opt.muon_lr, step, p.stab_total), p.opt.muon_momentum, p.opt.ns_a, p.opt.ns_b, p.opt.ns_c,
                        (int)p.opt.muon_nesterov, (int)p.opt.muon_ns_steps, (int)p.opt.muon_bf16_inputs};
         launch_muon(rt, a.at<MuonMatrix>(p.muon_table), p.muon_count, p.muon_smem, ms);
         for (const auto& seg : p.adam_segments)
             launch_adam(rt, false, seg.second, W + seg.first, G + seg.first, m + seg.first, v + seg.first,
                         W + seg.first, m + seg.first, v + seg.first, sc, none);
     } else {
-        launch_adam(rt, false, p.P, W, G, m, v, W, m, v, sc, none);
+        launch_adam(rt, false, p.P, W, G, m, v, W, m, v, sc, none, scale_dev);
     }
 }
 
@@ -375,6 +400,9 @@ void default_optimizer(hx_optimizer_config& o) {
     o.ns_b = -4.7750f;
     o.ns_c = 2.0315f;
     o.muon_bf16_inputs = 1;
+    // the reference's momentum candidate (qnn_transformer_training.cpp:1258-1263)
+    o.momentum_lr = 0.01f;
+    o.momentum = 0.95f;
 }
 
 void host_fixed_position(const LmPlan& p, std::vector<float>& out) {
@@ -513,6 +541,12 @@ int hx_lm_prepare(hx_runtime* rt, const hx_lm_config* cfg, uint32_t batch, int d
         }
         // Muon matrices: wq, wk, wv, wo, ffn_w1, ffn_w2 of every layer
         p.muon_table = a.reserve(sizeof(MuonMatrix) * 6 * p.L);
+        // Global gradient norm: one entry per registry tensor
+        p.norm_count = int(2 + (p.learned ? 1 : 0) + 10 * p.L);
+        p.norm_table = a.reserve(sizeof(GradTensor) * p.norm_count);
+        p.norm_sumsq = a.reserve(sizeof(double) * p.norm_count);
+        p.norm_value = a.reserve(sizeof(double));
+        p.clip_scale = a.reserve(sizeof(float));
         a.commit();
         HX_CUDA(cudaMemsetAsync(a.block.ptr, 0, a.used, rt->stream));
         std::vector<float> pos;
@@ -539,6 +573,25 @@ int hx_lm_prepare(hx_runtime* rt, const hx_lm_config* cfg, uint32_t batch, int d
         p.muon_count = int(mats.size());
         p.muon_smem = std::max(muon_smem_bytes(int(D), int(D)), muon_smem_bytes(int(D), int(F)));
         HX_CUDA(cudaMemcpyAsync(a.at<MuonMatrix>(p.muon_table), mats.data(), sizeof(MuonMatrix) * mats.size(),
+                                cudaMemcpyHostToDevice, rt->stream));
+        // Tensor order of gradientNorm (qnn/qnn_transformer_training.cpp:920-938):
+        // token embedding, per layer wq wk wv wo gamma1 beta1 gamma2 beta2 w1 w2,
+        // output projection (the learned position table follows the embedding).
+        std::vector<GradTensor> norm;
+        norm.push_back({p.off_E, (unsigned long long)V * D});
+        if (p.learned) norm.push_back({p.off_pos, (unsigned long long)T * D});
+        for (uint32_t l = 0; l < p.L; ++l) {
+            const LayerOffsets& o = p.lo[l];
+            const unsigned long long dd = (unsigned long long)D * D, df = (unsigned long long)D * F;
+            for (const GradTensor t : {GradTensor{o.wq, dd}, GradTensor{o.wk, dd}, GradTensor{o.wv, dd},
+                                       GradTensor{o.wo, dd}, GradTensor{o.g1, D}, GradTensor{o.b1, D},
+                                       GradTensor{o.g2, D}, GradTensor{o.b2, D}, GradTensor{o.w1, df},
+                                       GradTensor{o.w2, df}})
+                norm.push_back(t);
+        }
+        norm.push_back({p.off_out, (unsigned long long)D * V});
+        require(int(norm.size()) == p.norm_count, HX_ERR_STATE, "internal: gradient-norm table size");
+        HX_CUDA(cudaMemcpyAsync(a.at<GradTensor>(p.norm_table), norm.data(), sizeof(GradTensor) * norm.size(),
                                 cudaMemcpyHostToDevice, rt->stream));
         HX_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&p.host_scalars), 64, cudaHostAllocDefault));
         HX_CUDA(cudaStreamSynchronize(rt->stream));
@@ -681,7 +734,12 @@ int hx_lm_set_optimizer(hx_runtime* rt, const hx_optimizer_config* opt) {
     return hx_guard(rt, [&] {
         LmPlan& p = need_lm(rt);
         require(opt != nullptr, HX_ERR_ARGUMENT, "optimizer: null configuration");
-        require(opt->kind == HX_OPT_ADAM || opt->kind == HX_OPT_MUON, HX_ERR_ARGUMENT, "optimizer: unknown kind");
+        require(opt->kind == HX_OPT_ADAM || opt->kind == HX_OPT_MUON || opt->kind == HX_OPT_MOMENTUM,
+                HX_ERR_ARGUMENT, "optimizer: unknown kind");
+        require(opt->kind != HX_OPT_MOMENTUM || (std::isfinite(opt->momentum_lr) && std::isfinite(opt->momentum)),
+                HX_ERR_ARGUMENT, "momentum optimizer buffer size or scalar");
+        require(opt->kind == HX_OPT_ADAM || p.clip_threshold == 0.f, HX_ERR_UNSUPPORTED,
+                "gradient clipping scales the Adam gradient input; it needs the Adam optimizer");
         require(std::isfinite(opt->adam_lr) && std::isfinite(opt->beta1) && std::isfinite(opt->beta2) &&
                     std::isfinite(opt->adam_eps) && opt->beta1 >= 0.f && opt->beta1 < 1.f && opt->beta2 >= 0.f &&
                     opt->beta2 < 1.f,
@@ -693,6 +751,34 @@ int hx_lm_set_optimizer(hx_runtime* rt, const hx_optimizer_config* opt) {
                     "optimizer: invalid Muon scalars");
         }
         p.opt = *opt;
+    });
+}
+
+int hx_lm_set_stability(hx_runtime* rt, uint32_t mode, uint32_t total_steps, float clip_threshold) {
+    return hx_guard(rt, [&] {
+        LmPlan& p = need_lm(rt);
+        const char* bad = hx_stability_mode_error(mode);
+        require(bad == nullptr, HX_ERR_UNSUPPORTED, bad ? bad : "");
+        require(std::isfinite(clip_threshold) && clip_threshold >= 0.f, HX_ERR_ARGUMENT,
+                "gradient clip threshold must be finite and >= 0");
+        // GRADIENT_CLIP_1 fixes the threshold at 1 (qnn_transformer_training.cpp:1650-1653).
+        const float thr = mode == HX_STABILITY_GRADIENT_CLIP_1 ? 1.0f : clip_threshold;
+        require(thr == 0.f || p.opt.kind == HX_OPT_ADAM, HX_ERR_UNSUPPORTED,
+                "gradient clipping scales the Adam gradient input; it needs the Adam optimizer");
+        p.stab_mode = mode;
+        p.stab_total = total_steps;
+        p.clip_threshold = thr;
+    });
+}
+
+int hx_lm_last_gradient_norm(hx_runtime* rt, double* norm, float* clip_scale) {
+    return hx_guard(rt, [&] {
+        LmPlan& p = need_lm(rt);
+        require(p.clip_threshold > 0.f, HX_ERR_STATE, "no gradient clipping configured");
+        HX_CUDA(cudaStreamSynchronize(rt->stream));
+        if (norm) HX_CUDA(cudaMemcpy(norm, p.arena.at<double>(p.norm_value), sizeof(double), cudaMemcpyDeviceToHost));
+        if (clip_scale)
+            HX_CUDA(cudaMemcpy(clip_scale, p.arena.at<float>(p.clip_scale), sizeof(float), cudaMemcpyDeviceToHost));
     });
 }
 

@@ -102,7 +102,8 @@ AdamScalars adam_scalars(float lr, float gradient_scale, float c1, float c2) {
 }
 
 void launch_adam(hx_runtime* rt, bool graph_order, size_t n, const float* w, const float* g, const float* m,
-                 const float* v, float* wn, float* mn, float* vn, const AdamScalars& s, const AdamTaps& t)
+                 const float* v, float* wn, float* mn, float* vn, const AdamScalars& s, const AdamTaps& t,
+                 const float* scale_dev = nullptr)
 {
     if (n == 0) return;
     ProfScope prof(rt, kTagOptimizer, 12.0 * n, 28.0 * n);
@@ -110,9 +111,107 @@ void launch_adam(hx_runtime* rt, bool graph_order, size_t n, const float* w, con
     const size_t work = graph_order ? n : (n + 3) / 4;
     const int blocks = (int)std::min<size_t>((work + threads - 1) / threads, size_t(rt->sm_count) * 16);
     if (graph_order)
-        adam_kernel<true><<<blocks, threads, 0, rt->stream>>>(n, w, g, m, v, wn, mn, vn, s, t);
+        adam_kernel<true><<<blocks, threads, 0, rt->stream>>>(n, w, g, m, v, wn, mn, vn, s, t, scale_dev);
     else
-        adam_kernel<false><<<blocks, threads, 0, rt->stream>>>(n, w, g, m, v, wn, mn, vn, s, t);
+        adam_kernel<false><<<blocks, threads, 0, rt->stream>>>(n, w, g, m, v, wn, mn, vn, s, t, scale_dev);
+    HX_LAUNCHED(rt);
+}
+
+__global__ void momentum_kernel(size_t n, const float* w, const float* __restrict__ g, const float* vel,
+                                float* w_next, float* vel_next, float lr, float momentum)
+{
+    const size_t stride = (size_t)gridDim.x * blockDim.x;
+    const size_t tid = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    auto one = [&](float wi, float gi, float vi, float& wo, float& vo) {
+        vo = __fadd_rn(__fmul_rn(vi, momentum), gi);
+        wo = __fsub_rn(wi, __fmul_rn(vo, lr));
+    };
+    const bool vec = ((reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(g) |
+                       reinterpret_cast<uintptr_t>(vel) | reinterpret_cast<uintptr_t>(w_next) |
+                       reinterpret_cast<uintptr_t>(vel_next)) & 15) == 0;
+    size_t done = 0;
+    if (vec) {
+        const size_t n4 = n / 4;
+        for (size_t i = tid; i < n4; i += stride) {
+            const float4 a = reinterpret_cast<const float4*>(w)[i];
+            const float4 b = reinterpret_cast<const float4*>(g)[i];
+            const float4 c = reinterpret_cast<const float4*>(vel)[i];
+            float4 wo, vo;
+            one(a.x, b.x, c.x, wo.x, vo.x);
+            one(a.y, b.y, c.y, wo.y, vo.y);
+            one(a.z, b.z, c.z, wo.z, vo.z);
+            one(a.w, b.w, c.w, wo.w, vo.w);
+            reinterpret_cast<float4*>(vel_next)[i] = vo;
+            reinterpret_cast<float4*>(w_next)[i] = wo;
+        }
+        done = n4 * 4;
+    }
+    for (size_t i = done + tid; i < n; i += stride) {
+        float wo, vo;
+        one(w[i], g[i], vel[i], wo, vo);
+        vel_next[i] = vo;
+        w_next[i] = wo;
+    }
+}
+
+void launch_momentum(hx_runtime* rt, size_t n, const float* w, const float* g, const float* vel, float* wn,
+                     float* veln, float lr, float momentum)
+{
+    if (n == 0) return;
+    ProfScope prof(rt, kTagOptimizer, 3.0 * n, 20.0 * n);
+    const int threads = 256;
+    const int blocks = (int)std::min<size_t>(((n + 3) / 4 + threads - 1) / threads, size_t(rt->sm_count) * 16);
+    momentum_kernel<<<blocks, threads, 0, rt->stream>>>(n, w, g, vel, wn, veln, lr, momentum);
+    HX_LAUNCHED(rt);
+}
+
+constexpr int kNormThreads = 512;
+
+__global__ void __launch_bounds__(kNormThreads) grad_sumsq_kernel(const float* __restrict__ g,
+                                                                  const GradTensor* __restrict__ tensors,
+                                                                  double* __restrict__ sumsq)
+{
+    const GradTensor t = tensors[blockIdx.x];
+    const float* p = g + t.offset;
+    double s = 0.0;
+    for (unsigned long long i = threadIdx.x; i < t.count; i += kNormThreads) {
+        const double x = p[i];
+        s += x * x;
+    }
+    __shared__ double part[kNormThreads / 32];
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = s;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double total = 0.0;
+        for (int w = 0; w < kNormThreads / 32; ++w) total += part[w];
+        sumsq[blockIdx.x] = total;
+    }
+}
+
+__global__ void clip_scale_kernel(const double* __restrict__ sumsq, int tensors, float threshold,
+                                  double* __restrict__ norm_out, float* __restrict__ scale_out)
+{
+    if (threadIdx.x != 0 || blockIdx.x != 0) return;
+    double sum = 0.0;
+    for (int i = 0; i < tensors; ++i) {
+        const double norm = sqrt(sumsq[i]);
+        sum += norm * norm;
+    }
+    const double norm = sqrt(sum);
+    *norm_out = norm;
+    *scale_out = (threshold > 0.f && isfinite(norm) && norm > 0.0)
+                     ? float(fmin(1.0, double(threshold) / (norm + 1.0e-6)))
+                     : 1.0f;
+}
+
+void launch_clip_scale(hx_runtime* rt, const float* g, const GradTensor* tensors, int count, double* sumsq,
+                       float threshold, double* norm_out, float* scale_out)
+{
+    ProfScope prof(rt, kTagReduce, 0.0, 0.0);
+    grad_sumsq_kernel<<<count, kNormThreads, 0, rt->stream>>>(g, tensors, sumsq);
+    HX_LAUNCHED(rt);
+    clip_scale_kernel<<<1, 32, 0, rt->stream>>>(sumsq, count, threshold, norm_out, scale_out);
     HX_LAUNCHED(rt);
 }
 
@@ -209,6 +308,60 @@ int hx_adam_execute_device(hx_runtime* rt, size_t n, const float* current, const
                    out->scaled_update};
         launch_adam(rt, taps, n, current, gradient, m, v, out->w_next, out->m_next, out->v_next,
                     adam_scalars(lr, gs, c1, c2), t);
+    });
+}
+
+int hx_momentum_prepare(hx_runtime* rt, uint32_t elements) {
+    return hx_guard(rt, [&] {
+        require(elements > 0, HX_ERR_ARGUMENT, "momentum optimizer invalid runtime or shape");
+        auto pl = std::make_unique<MomentumPlan>();
+        pl->n = elements;
+        const size_t b = sizeof(float) * elements;
+        pl->w = pl->arena.reserve(b);
+        pl->g = pl->arena.reserve(b);
+        pl->vel = pl->arena.reserve(b);
+        pl->vel_next = pl->arena.reserve(b);
+        pl->w_next = pl->arena.reserve(b);
+        pl->arena.commit();
+        rt->momentum = std::move(pl);
+        ++rt->metrics.graph_create_count;
+        ++rt->metrics.graph_finalize_count;
+    });
+}
+
+int hx_momentum_execute(hx_runtime* rt, const float* current, const float* gradient, const float* velocity,
+                        float lr, float momentum, float* velocity_next, float* weight_next) {
+    const auto t0 = Clock::now();
+    const int rc = hx_guard(rt, [&] {
+        require(rt->momentum != nullptr, HX_ERR_STATE, "momentum optimizer graph not prepared");
+        const MomentumPlan& pl = *rt->momentum;
+        require(current && gradient && velocity && velocity_next && weight_next && std::isfinite(lr) &&
+                    std::isfinite(momentum),
+                HX_ERR_ARGUMENT, "momentum optimizer buffer size or scalar");
+        const size_t n = pl.n, b = n * sizeof(float);
+        const Arena& a = pl.arena;
+        HX_CUDA(cudaMemcpyAsync(a.at<float>(pl.w), current, b, cudaMemcpyHostToDevice, rt->stream));
+        HX_CUDA(cudaMemcpyAsync(a.at<float>(pl.g), gradient, b, cudaMemcpyHostToDevice, rt->stream));
+        HX_CUDA(cudaMemcpyAsync(a.at<float>(pl.vel), velocity, b, cudaMemcpyHostToDevice, rt->stream));
+        launch_momentum(rt, n, a.at<float>(pl.w), a.at<float>(pl.g), a.at<float>(pl.vel), a.at<float>(pl.w_next),
+                        a.at<float>(pl.vel_next), lr, momentum);
+        HX_CUDA(cudaMemcpyAsync(velocity_next, a.at<float>(pl.vel_next), b, cudaMemcpyDeviceToHost, rt->stream));
+        HX_CUDA(cudaMemcpyAsync(weight_next, a.at<float>(pl.w_next), b, cudaMemcpyDeviceToHost, rt->stream));
+        HX_CUDA(cudaStreamSynchronize(rt->stream));
+        if (rt->injected_now()) fail(HX_ERR_CUDA, "injected execute failure after device success");
+    });
+    if (rt) rt->record_execute(rc == HX_OK, us_since(t0));
+    return rc;
+}
+
+int hx_momentum_execute_device(hx_runtime* rt, size_t n, const float* current, const float* gradient,
+                               const float* velocity, float lr, float momentum, float* velocity_next,
+                               float* weight_next) {
+    return hx_guard(rt, [&] {
+        require(current && gradient && velocity && velocity_next && weight_next && std::isfinite(lr) &&
+                    std::isfinite(momentum),
+                HX_ERR_ARGUMENT, "momentum optimizer buffer size or scalar");
+        launch_momentum(rt, n, current, gradient, velocity, weight_next, velocity_next, lr, momentum);
     });
 }
 

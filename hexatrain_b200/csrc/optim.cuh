@@ -56,8 +56,11 @@ __device__ __forceinline__ float adam_element(float w, float g, float& m, float&
 template <bool kGraphOrder>
 __global__ void adam_kernel(size_t n, const float* w, const float* __restrict__ g, const float* m,
                             const float* v, float* w_next, float* m_next, float* v_next, AdamScalars s,
-                            AdamTaps t)
+                            AdamTaps t, const float* __restrict__ scale_dev)
 {
+    // A gradient scale computed on the device (the global-norm clip) replaces
+    // the host scalar when given.
+    if (scale_dev) s.gradient_scale = *scale_dev;
     const size_t stride = (size_t)gridDim.x * blockDim.x;
     const size_t tid = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
     const bool vec = !kGraphOrder &&
@@ -90,6 +93,30 @@ __global__ void adam_kernel(size_t n, const float* w, const float* __restrict__ 
         v_next[i] = vv;
     }
 }
+
+// ---- momentum SGD -----------------------------------------------------------
+// The reference's momentum graph (qnn/qnn_runtime_transformer.inc:799-881):
+//   scaled = velocity * momentum; velocity' = scaled + gradient;
+//   update = velocity' * lr;      w' = w - update
+// (tiny_lm::momentumUpdate, tiny_language_model_cpu.cpp:123, rounds the
+// same products).  In place is allowed.
+__global__ void momentum_kernel(size_t n, const float* w, const float* __restrict__ g, const float* vel,
+                                float* w_next, float* vel_next, float lr, float momentum);
+
+// ---- global gradient norm and clip scale ----------------------------------
+// gradientNorm (qnn/qnn_transformer_training.cpp:888-938): per tensor the
+// double sum of squares, its square root, then sqrt(sum of squared norms)
+// in the reference's tensor order; clip scale = min(1, threshold /
+// (norm + 1e-6)) when the norm is finite and positive, else 1
+// (:2432-2439).  One CTA per tensor, a fixed reduction tree, so results do
+// not depend on scheduling.
+struct GradTensor {
+    unsigned long long offset, count;
+};
+__global__ void grad_sumsq_kernel(const float* __restrict__ g, const GradTensor* __restrict__ tensors,
+                                  double* __restrict__ sumsq);
+__global__ void clip_scale_kernel(const double* __restrict__ sumsq, int tensors, float threshold,
+                                  double* __restrict__ norm_out, float* __restrict__ scale_out);
 
 // ---- Muon -----------------------------------------------------------------
 

@@ -40,6 +40,12 @@ struct AdamPlan {
     size_t w, g, m, v, out[10];
 };
 
+struct MomentumPlan {
+    uint32_t n = 0;
+    Arena arena;
+    size_t w, g, vel, vel_next, w_next;
+};
+
 struct LmPlan;  // lm.cu
 size_t lm_plan_bytes(const LmPlan* p);
 // The configuration and optimizer kind of the prepared LM plan; false if
@@ -50,6 +56,7 @@ inline size_t plan_device_bytes(const hx_runtime* rt) {
     size_t n = 0;
     if (rt->mlp) n += rt->mlp->arena.block.bytes;
     if (rt->adam) n += rt->adam->arena.block.bytes;
+    if (rt->momentum) n += rt->momentum->arena.block.bytes;
     if (rt->lm) n += lm_plan_bytes(rt->lm.get());
     return n;
 }

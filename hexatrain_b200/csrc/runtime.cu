@@ -14,6 +14,7 @@ hx_runtime::~hx_runtime() {
     mlp.reset();
     lm.reset();
     adam.reset();
+    momentum.reset();
     scratch.release();
     if (own_stream) cudaStreamDestroy(own_stream);
 }

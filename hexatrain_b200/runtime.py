@@ -98,6 +98,30 @@ class AdamOptimizerOutputs:
 
 
 @dataclass
+class MomentumOptimizerOutputs:
+    """MomentumOptimizerOutputs (qnn/qnn_runtime.h:227-229)."""
+
+    velocity_next: np.ndarray = None
+    weight_next: np.ndarray = None
+
+
+def stability_learning_rate(mode: int, base: float, step: int, total_steps: int) -> float:
+    """stabilityLearningRate (training_stability.h:88-99)."""
+    return float(_lib.load().hx_stability_learning_rate(mode, base, step, total_steps))
+
+
+def apply_init_stability(cfg: "LmConfig", mode: int, params: np.ndarray) -> np.ndarray:
+    """applyInitStability (training_stability.h:104-121) on a copy of a flat
+    registry-ordered parameter array."""
+    out = np.array(params, dtype=np.float32, copy=True).ravel()
+    rc = _lib.load().hx_lm_apply_init_stability(C.byref(cfg.to_c()), mode, out.ctypes.data)
+    if rc != 0:
+        msg = _lib.load().hx_stability_mode_error(mode)
+        raise ValueError(msg.decode() if msg else "invalid arguments")
+    return out
+
+
+@dataclass
 class OptimizerConfig:
     """hx_optimizer_config.  Defaults: Adam 1e-3/0.9/0.999/1e-8; Muon lr
     0.02, momentum 0.95 with Nesterov, 5 quintic Newton-Schulz steps
@@ -116,11 +140,14 @@ class OptimizerConfig:
     ns_b: float = -4.7750
     ns_c: float = 2.0315
     muon_bf16_inputs: bool = True
+    momentum_lr: float = 0.01
+    momentum: float = 0.95
 
     def to_c(self) -> _lib.OptimizerConfigC:
         return _lib.OptimizerConfigC(self.kind, self.adam_lr, self.beta1, self.beta2, self.adam_eps, self.muon_lr,
                                      self.muon_momentum, int(self.muon_nesterov), self.muon_ns_steps, self.ns_a,
-                                     self.ns_b, self.ns_c, int(self.muon_bf16_inputs))
+                                     self.ns_b, self.ns_c, int(self.muon_bf16_inputs), self.momentum_lr,
+                                     self.momentum)
 
 
 @dataclass(frozen=True)
@@ -492,6 +519,18 @@ class Runtime:
             C.byref(info)))
         return _info(info) if ok else None
 
+    def lm_set_stability(self, mode: int, total_steps: int = 0, clip_threshold: float = 0.0) -> bool:
+        """Step-side training-stability mode (training_stability.h) and the
+        global-norm gradient clip threshold (0 = off)."""
+        return self._need() and self._ok(self._lib.hx_lm_set_stability(self._rt, mode, total_steps, clip_threshold))
+
+    def lm_last_gradient_norm(self):
+        """(pre-clip global gradient norm, clip scale) of the last optimizer step."""
+        n, s = C.c_double(), C.c_float()
+        if not (self._need() and self._ok(self._lib.hx_lm_last_gradient_norm(self._rt, C.byref(n), C.byref(s)))):
+            raise RuntimeError(self.last_error)
+        return n.value, s.value
+
     def lm_set_optimizer(self, opt: OptimizerConfig) -> bool:
         return self._need() and self._ok(self._lib.hx_lm_set_optimizer(self._rt, C.byref(opt.to_c())))
 
@@ -551,6 +590,31 @@ class Runtime:
         rc = self._lib.hx_adam_execute(self._rt, *[ptr(a) for a in arrs], learning_rate, gradient_scale,
                                        first_correction, second_correction, C.byref(o))
         return self._ok(rc)
+
+    # -- momentum SGD --------------------------------------------------------------
+    def prepare_momentum_optimizer(self, elements: int) -> bool:
+        """Runtime::prepareMomentumOptimizer (qnn/qnn_runtime.h:353)."""
+        if not self._need():
+            return False
+        ok = self._ok(self._lib.hx_momentum_prepare(self._rt, elements))
+        if ok:
+            self._momentum_n = elements
+        return ok
+
+    def execute_momentum_optimizer(self, current, gradient, velocity, learning_rate: float, momentum: float,
+                                   outputs: "MomentumOptimizerOutputs") -> bool:
+        """Runtime::executeMomentumOptimizer (qnn/qnn_runtime.h:354-359)."""
+        if not self._need():
+            return False
+        arrs = [_f32(a).ravel() for a in (current, gradient, velocity)]
+        n = getattr(self, "_momentum_n", 0)
+        if n == 0 or any(a.size != n for a in arrs):
+            self.last_error = "momentum optimizer buffer size or scalar"
+            return False
+        outputs.velocity_next = np.empty(n, np.float32)
+        outputs.weight_next = np.empty(n, np.float32)
+        return self._ok(self._lib.hx_momentum_execute(self._rt, *[ptr(a) for a in arrs], learning_rate, momentum,
+                                                      ptr(outputs.velocity_next), ptr(outputs.weight_next)))
 
     # -- Muon --------------------------------------------------------------------
     def execute_muon(self, weight, gradient, momentum_buffer, learning_rate: float, momentum: float = 0.95,

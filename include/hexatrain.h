@@ -248,16 +248,21 @@ int hx_lm_execute_tokens(hx_runtime* rt, const uint32_t* input_tokens, const uin
 /* -- device-resident training state (the batched driver loop of
  *    qnn/qnn_transformer_training.cpp:7281-7345 in one call per step) ---- */
 
-enum { HX_OPT_ADAM = 0, HX_OPT_MUON = 1 };
+enum { HX_OPT_ADAM = 0, HX_OPT_MUON = 1, HX_OPT_MOMENTUM = 2 };
 typedef struct {
     uint32_t kind;        /* HX_OPT_ADAM: Adam on every parameter.
                              HX_OPT_MUON: Muon on wq,wk,wv,wo,ffn_w1,ffn_w2;
-                             Adam on the rest. */
+                             Adam on the rest.
+                             HX_OPT_MOMENTUM: momentum SGD on every parameter
+                             (tiny_lm::momentumUpdate,
+                             tiny_language_model_cpu.cpp:123); the velocity
+                             occupies the state's Muon-buffer slot. */
     float adam_lr, beta1, beta2, adam_eps;
     float muon_lr, muon_momentum;
     uint32_t muon_nesterov, muon_ns_steps;
     float ns_a, ns_b, ns_c;
     uint32_t muon_bf16_inputs;  /* round Newton-Schulz operands to bf16 */
+    float momentum_lr, momentum; /* HX_OPT_MOMENTUM (defaults 0.01, 0.95) */
 } hx_optimizer_config;
 
 /* Load parameters (and Adam moments / Muon buffers, or zeros when NULL)
@@ -267,6 +272,37 @@ int hx_lm_state_upload(hx_runtime* rt, const float* params, const float* adam_m,
 int hx_lm_state_download(hx_runtime* rt, float* params, float* adam_m, float* adam_v,
                          float* muon_buf, size_t param_count);
 int hx_lm_set_optimizer(hx_runtime* rt, const hx_optimizer_config* opt);
+
+/* Training-stability modes (training_stability.h:20-99). */
+enum {
+    HX_STABILITY_LEGACY = 0,
+    HX_STABILITY_WARMUP64 = 1,                     /* lr * min(1, step/64) */
+    HX_STABILITY_DECAY_LINEAR = 2,                 /* lr * (1 - (step-1)/total) */
+    HX_STABILITY_ZERO_OUTPUT_PROJ_BRANCH_INIT = 3, /* init: Wo, W2 = 0 */
+    HX_STABILITY_DEPTH_SCALED_BRANCH_INIT = 4,     /* init: Wo, W1, W2 / sqrt(2L) */
+    HX_STABILITY_RESIDUAL_BRANCH_SCALING = 5,      /* reserved; rejected as in the reference */
+    HX_STABILITY_GRADIENT_CLIP_1 = 6               /* global-norm clip at 1 before Adam */
+};
+/* validateTrainingStabilityMode (:77-81): NULL, or the reference's tag
+ * (RESIDUAL_BRANCH_SCALING_UNSUPPORTED_ON_DEVICE,
+ * UNKNOWN_TRAINING_STABILITY_MODE). */
+const char* hx_stability_mode_error(uint32_t mode);
+/* stabilityLearningRate (:88-99); `step` is 1-based. */
+float hx_stability_learning_rate(uint32_t mode, float base, uint32_t step, uint32_t total_steps);
+/* applyInitStability (:104-121) on a flat registry-ordered parameter
+ * buffer; modes other than 3 and 4 leave it unchanged.  Host only. */
+int hx_lm_apply_init_stability(const hx_lm_config* config, uint32_t mode, float* params);
+/* Selects the step-side mode for hx_lm_train_step / optimizer_step_device:
+ * the scheduled learning rate over total_steps, and a global-norm gradient
+ * clip (the reference's clipThreshold, qnn_transformer_training.cpp:
+ * 2432-2445): scale = min(1, threshold/(||g|| + 1e-6)) applied as Adam's
+ * gradient-scale input, with ||g|| summed per tensor in double in
+ * gradientNorm order (:920-938).  clip_threshold 0 disables the clip;
+ * HX_STABILITY_GRADIENT_CLIP_1 sets it to 1.  Clipping needs Adam. */
+int hx_lm_set_stability(hx_runtime* rt, uint32_t mode, uint32_t total_steps, float clip_threshold);
+/* Pre-clip global gradient norm and the clip scale of the last optimizer
+ * step (synchronises the runtime stream).  Requires an active clip. */
+int hx_lm_last_gradient_norm(hx_runtime* rt, double* norm, float* clip_scale);
 
 /* One training step on the device state: tokens [batch, T+1] host ids
  * (sequence b reads ids[b][0..T-1], predicts ids[b][1..T]); forward,
@@ -321,6 +357,20 @@ int hx_adam_execute_device(hx_runtime* rt, size_t n, const float* current, const
                            const float* first_moment, const float* second_moment,
                            float learning_rate, float gradient_scale, float first_correction,
                            float second_correction, const hx_adam_outputs* out);
+
+/* ---- momentum SGD optimizer ------------------------------------------------ */
+/* Runtime::prepareMomentumOptimizer / executeMomentumOptimizer
+ * (qnn/qnn_runtime.h:353-359, graph qnn_runtime_transformer.inc:799-925):
+ * velocity' = velocity*momentum + gradient; weight' = weight - velocity'*lr.
+ * Host buffers, synchronous ("momentum optimizer buffer size or scalar"). */
+int hx_momentum_prepare(hx_runtime* rt, uint32_t elements);
+int hx_momentum_execute(hx_runtime* rt, const float* current, const float* gradient,
+                        const float* velocity, float learning_rate, float momentum,
+                        float* velocity_next, float* weight_next);
+/* Device-pointer variant over n elements, async; in place allowed. */
+int hx_momentum_execute_device(hx_runtime* rt, size_t n, const float* current, const float* gradient,
+                               const float* velocity, float learning_rate, float momentum,
+                               float* velocity_next, float* weight_next);
 
 /* ---- Muon (no counterpart in the reference) ------------------------------ */
 /* Momentum (+Nesterov) and quintic Newton-Schulz orthogonalisation of one

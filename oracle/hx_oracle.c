@@ -871,3 +871,99 @@ void hxo_nprt_training_order(uint64_t records, uint32_t steps, uint32_t batch, u
         out[i] = state % records;
     }
 }
+
+/* ---------------------------------------------------------------------- */
+/* Momentum SGD and the training-stability modes.                           */
+
+void hxo_momentum(size_t n, const float* w, const float* g, const float* v, float lr, float momentum,
+                  float* w_next, float* v_next)
+{
+    /* tiny_language_model_cpu.cpp:123: nv = momentum*v + g; nw = w - lr*nv */
+    for (size_t i = 0; i < n; ++i) {
+        const float nv = momentum * v[i] + g[i];
+        v_next[i] = nv;
+        w_next[i] = w[i] - lr * nv;
+    }
+}
+
+float hxo_stability_learning_rate(uint32_t mode, float base, uint32_t step, uint32_t total_steps)
+{
+    if (mode == 1) {                               /* WARMUP64 */
+        const double f = (double)step / 64.0;
+        return (float)(base * (f < 1.0 ? f : 1.0));
+    }
+    if (mode == 2) {                               /* DECAY_LINEAR */
+        const double done = total_steps ? (double)total_steps : 1.0;
+        return (float)(base * (1.0 - (double)(step - 1) / done));
+    }
+    return base;
+}
+
+/* Offsets of layer l's tensors in the flat layout. */
+static void layer_offsets(const hxo_lm_config* c, uint32_t l, size_t o[10])
+{
+    const size_t V = c->vocab, T = c->tokens, D = c->dim, F = c->ffn;
+    size_t off = V * D + (c->learned_position ? T * D : 0) + (size_t)l * (4 * D * D + 4 * D + 2 * D * F);
+    const size_t sz[10] = {D, D, D * D, D * D, D * D, D * D, D, D, D * F, F * D};
+    for (int k = 0; k < 10; ++k) {  /* g1 b1 wq wk wv wo g2 b2 w1 w2 */
+        o[k] = off;
+        off += sz[k];
+    }
+}
+
+void hxo_apply_init_stability(const hxo_lm_config* c, uint32_t mode, float* p)
+{
+    const size_t D = c->dim, F = c->ffn;
+    const float s = 1.0f / sqrtf(2.0f * (float)c->layers);
+    for (uint32_t l = 0; l < c->layers; ++l) {
+        size_t o[10];
+        layer_offsets(c, l, o);
+        if (mode == 3) {         /* ZERO_OUTPUT_PROJ_BRANCH_INIT */
+            memset(p + o[5], 0, sizeof(float) * D * D);
+            memset(p + o[9], 0, sizeof(float) * F * D);
+        } else if (mode == 4) {  /* DEPTH_SCALED_BRANCH_INIT */
+            for (size_t i = 0; i < D * D; ++i) p[o[5] + i] *= s;
+            for (size_t i = 0; i < D * F; ++i) p[o[8] + i] *= s;
+            for (size_t i = 0; i < F * D; ++i) p[o[9] + i] *= s;
+        }
+    }
+}
+
+static double tensor_norm(const float* x, size_t n)
+{
+    double s = 0;
+    for (size_t i = 0; i < n; ++i) s += (double)x[i] * x[i];
+    return sqrt(s);
+}
+
+double hxo_gradient_norm(const hxo_lm_config* c, const float* g, float threshold, float* clip)
+{
+    const size_t V = c->vocab, T = c->tokens, D = c->dim, F = c->ffn;
+    double sum = 0, nrm;
+    nrm = tensor_norm(g, V * D);
+    sum += nrm * nrm;
+    if (c->learned_position) {
+        nrm = tensor_norm(g + V * D, T * D);
+        sum += nrm * nrm;
+    }
+    const int order[10] = {2, 3, 4, 5, 0, 1, 6, 7, 8, 9};  /* wq wk wv wo g1 b1 g2 b2 w1 w2 */
+    const size_t sz[10] = {D, D, D * D, D * D, D * D, D * D, D, D, D * F, F * D};
+    for (uint32_t l = 0; l < c->layers; ++l) {
+        size_t o[10];
+        layer_offsets(c, l, o);
+        for (int k = 0; k < 10; ++k) {
+            nrm = tensor_norm(g + o[order[k]], sz[order[k]]);
+            sum += nrm * nrm;
+        }
+    }
+    size_t oo[10];
+    layer_offsets(c, c->layers, oo);  /* the output projection follows the last layer */
+    nrm = tensor_norm(g + oo[0], D * V);
+    sum += nrm * nrm;
+    const double norm = sqrt(sum);
+    if (clip) {
+        const double q = (double)threshold / (norm + 1.0e-6);
+        *clip = (threshold > 0 && isfinite(norm) && norm > 0) ? (float)(q < 1.0 ? q : 1.0) : 1.0f;
+    }
+    return norm;
+}

@@ -158,6 +158,23 @@ void hxo_nprt_parameter_hash(const hxo_lm_config* c, const float* params, char o
 /* nprtTrainingOrder (:4983-4995): splitmix64 chain from 20260806. */
 void hxo_nprt_training_order(uint64_t records, uint32_t steps, uint32_t batch, uint64_t* out);
 
+/* ---- momentum SGD and training-stability modes -----------------------------
+ * tiny_lm::momentumUpdate (tiny_language_model_cpu.cpp:123):
+ * v' = momentum*v + g; w' = w - lr*v', in float, per element. */
+void hxo_momentum(size_t n, const float* w, const float* g, const float* v, float lr, float momentum,
+                  float* w_next, float* v_next);
+/* stabilityLearningRate (training_stability.h:88-99). */
+float hxo_stability_learning_rate(uint32_t mode, float base, uint32_t step, uint32_t total_steps);
+/* applyInitStability (training_stability.h:104-121) on the flat layout. */
+void hxo_apply_init_stability(const hxo_lm_config* c, uint32_t mode, float* params);
+/* gradientNorm (qnn/qnn_transformer_training.cpp:888-938): per tensor a
+ * sequential double sum of squares and its square root, summed as squares in
+ * the order token_embedding, per layer wq wk wv wo g1 b1 g2 b2 w1 w2,
+ * output_projection (a learned position table follows the embedding);
+ * returns sqrt of that sum.  *clip receives min(1, threshold/(norm+1e-6))
+ * for a finite positive norm and threshold > 0, else 1 (:2432-2439). */
+double hxo_gradient_norm(const hxo_lm_config* c, const float* grads, float threshold, float* clip);
+
 #ifdef __cplusplus
 }
 #endif

@@ -256,6 +256,34 @@ class Oracle:
         self.lib.hxo_nprt_parameter_hash(C.byref(cfg), np.ascontiguousarray(params, np.float32), out)
         return out.value.decode()
 
+    def momentum(self, w, g, v, lr, momentum):
+        L = self.lib
+        L.hxo_momentum.argtypes = [C.c_size_t, _f32p, _f32p, _f32p, C.c_float, C.c_float, _f32p, _f32p]
+        w, g, v = (np.ascontiguousarray(a, np.float32).ravel() for a in (w, g, v))
+        wn, vn = np.empty_like(w), np.empty_like(w)
+        L.hxo_momentum(w.size, w, g, v, lr, momentum, wn, vn)
+        return wn, vn
+
+    def stability_learning_rate(self, mode, base, step, total):
+        self.lib.hxo_stability_learning_rate.restype = C.c_float
+        self.lib.hxo_stability_learning_rate.argtypes = [C.c_uint32, C.c_float, C.c_uint32, C.c_uint32]
+        return self.lib.hxo_stability_learning_rate(mode, base, step, total)
+
+    def apply_init_stability(self, cfg: LmConfig, mode, params):
+        self.lib.hxo_apply_init_stability.argtypes = [C.POINTER(LmConfig), C.c_uint32, _f32p]
+        out = np.array(params, np.float32, copy=True).ravel()
+        self.lib.hxo_apply_init_stability(C.byref(cfg), mode, out)
+        return out
+
+    def gradient_norm(self, cfg: LmConfig, grads, threshold=0.0):
+        """(norm, clip scale)."""
+        self.lib.hxo_gradient_norm.restype = C.c_double
+        self.lib.hxo_gradient_norm.argtypes = [C.POINTER(LmConfig), _f32p, C.c_float, C.POINTER(C.c_float)]
+        clip = C.c_float()
+        n = self.lib.hxo_gradient_norm(C.byref(cfg), np.ascontiguousarray(grads, np.float32).ravel(), threshold,
+                                       C.byref(clip))
+        return n, clip.value
+
     def nprt_training_order(self, records, steps, batch):
         self.lib.hxo_nprt_training_order.argtypes = [C.c_uint64, C.c_uint32, C.c_uint32, C.c_void_p]
         out = np.zeros(steps * batch, np.uint64)
@@ -371,6 +399,34 @@ class Reference:
             raise ValueError(self.last_error())
         return loss.value
 
+    def momentum(self, cfg, w, g, v, lr, momentum):
+        L = self.lib
+        L.hxr_lm_momentum.restype = C.c_int
+        L.hxr_lm_momentum.argtypes = [C.POINTER(LmConfig), _f32p, _f32p, _f32p, C.c_float, C.c_float, _f32p, _f32p]
+        w, g, v = (np.ascontiguousarray(a, np.float32).ravel() for a in (w, g, v))
+        wn, vn = np.empty_like(w), np.empty_like(w)
+        if L.hxr_lm_momentum(C.byref(cfg), w, g, v, lr, momentum, wn, vn) != 0:
+            raise RuntimeError(self.last_error())
+        return wn, vn
+
+    def stability_learning_rate(self, mode, base, step, total):
+        self.lib.hxr_stability_learning_rate.restype = C.c_float
+        self.lib.hxr_stability_learning_rate.argtypes = [C.c_uint32, C.c_float, C.c_uint32, C.c_uint32]
+        return self.lib.hxr_stability_learning_rate(mode, base, step, total)
+
+    def apply_init_stability(self, cfg, mode, params):
+        self.lib.hxr_apply_init_stability.restype = C.c_int
+        self.lib.hxr_apply_init_stability.argtypes = [C.POINTER(LmConfig), C.c_uint32, _f32p]
+        out = np.array(params, np.float32, copy=True).ravel()
+        if self.lib.hxr_apply_init_stability(C.byref(cfg), mode, out) != 0:
+            raise RuntimeError(self.last_error())
+        return out
+
+    def stability_mode_error(self, mode) -> str:
+        self.lib.hxr_stability_mode_error.restype = C.c_char_p
+        self.lib.hxr_stability_mode_error.argtypes = [C.c_uint32]
+        return self.lib.hxr_stability_mode_error(mode).decode()
+
     def gradient_check(self, seed=20260725, eps=1e-3):
         a, r = C.c_float(), C.c_float()
         ok = self.lib.hxr_lm_gradient_check(seed, eps, C.byref(a), C.byref(r))
@@ -429,6 +485,11 @@ class ReferenceCheckpoint:
         out = C.create_string_buffer(64)
         self.lib.hxr_nprt_parameter_hash(*self._dims(cfg), np.ascontiguousarray(params, np.float32), out, 64)
         return out.value.decode()
+
+    def gradient_norm(self, cfg, grads) -> float:
+        self.lib.hxr_gradient_norm.restype = C.c_double
+        self.lib.hxr_gradient_norm.argtypes = [C.c_uint32] * 6 + [_f32p]
+        return self.lib.hxr_gradient_norm(*self._dims(cfg), np.ascontiguousarray(grads, np.float32).ravel())
 
     def training_order(self, records, steps, batch):
         out = np.zeros(steps * batch, np.uint64)

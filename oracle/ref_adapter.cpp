@@ -13,6 +13,7 @@
 // rows.  All arithmetic is the reference's.
 #include "cpu_reference_training.h"
 #include "tiny_language_model_cpu.h"
+#include "training_stability.h"
 
 #include <algorithm>
 #include <cmath>
@@ -247,6 +248,43 @@ int hxr_lm_forward_backward(const RefConfig* c, const uint32_t* input_tokens,
     } catch (const std::exception& ex) {
         return guard("hxr_lm_forward_backward", &gLastError, ex);
     }
+}
+
+// tiny_lm::momentumUpdate (tiny_language_model_cpu.cpp:123) over flat
+// registry-ordered buffers of configuration c.
+int hxr_lm_momentum(const RefConfig* c, const float* w, const float* g, const float* v, float lr, float momentum,
+                    float* w_next, float* v_next) {
+    try {
+        const Params W = unflatten(c, w), G = unflatten(c, g), Vv = unflatten(c, v);
+        auto r = phonelm::tiny_lm::momentumUpdate(W, G, Vv, lr, momentum);
+        flatten(r.next, w_next);
+        flatten(r.velocity, v_next);
+        return 0;
+    } catch (const std::exception& ex) {
+        return guard("hxr_lm_momentum", &gLastError, ex);
+    }
+}
+
+// phonelm::stabilityLearningRate (training_stability.h:88-99).
+float hxr_stability_learning_rate(uint32_t mode, float base, uint32_t step, uint32_t total) {
+    return phonelm::stabilityLearningRate(mode, base, step, total);
+}
+
+// phonelm::applyInitStability (training_stability.h:104-121) on flat params.
+int hxr_apply_init_stability(const RefConfig* c, uint32_t mode, float* params) {
+    try {
+        Params p = phonelm::applyInitStability(toConfig(c), unflatten(c, params), mode);
+        flatten(p, params);
+        return 0;
+    } catch (const std::exception& ex) {
+        return guard("hxr_apply_init_stability", &gLastError, ex);
+    }
+}
+
+// phonelm::validateTrainingStabilityMode (training_stability.h:77-81).
+const char* hxr_stability_mode_error(uint32_t mode) {
+    const char* e = phonelm::validateTrainingStabilityMode(mode);
+    return e ? e : "";
 }
 
 // tiny_lm::adamUpdate (tiny_language_model_cpu.cpp:124-145) over flat

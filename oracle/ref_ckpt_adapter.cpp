@@ -4,8 +4,8 @@
 // TEST INFRASTRUCTURE ONLY (the checker).  The reference keeps its writer
 // (nprtSaveCheckpointV2, qnn/qnn_transformer_training.cpp:5171-5252), reader
 // (nprtLoadCheckpointForGeneration, :5390-5522), parameter hash
-// (nprtParameterHash, :5080-5090) and training order (nprtTrainingOrder,
-// :4983-4995) in an anonymous namespace of that driver source.  This file
+// (nprtParameterHash, :5080-5090), training order (nprtTrainingOrder,
+// :4983-4995) and gradient norm (gradientNorm, :920-938) in an anonymous namespace of that driver source.  This file
 // includes the source as it lies in the HexaTrain tree (oracle/Makefile
 // points the include path there), so those functions are reachable from
 // this one translation unit; nothing of the reference is copied here.
@@ -114,6 +114,18 @@ int hxr_nprt_parameter_hash(uint32_t V, uint32_t T, uint32_t D, uint32_t F, uint
         return 1;
     } catch (...) {
         return 0;
+    }
+}
+
+// gradientNorm (qnn_transformer_training.cpp:920-938) of a flat
+// registry-ordered gradient buffer.
+double hxr_gradient_norm(uint32_t V, uint32_t T, uint32_t D, uint32_t F, uint32_t L, uint32_t H,
+                         const float* grads) {
+    try {
+        const auto c = make_config(V, T, D, F, L, H);
+        return phonelm::qnn::gradientNorm(from_flat(c, grads));
+    } catch (...) {
+        return -1.0;
     }
 }
 
