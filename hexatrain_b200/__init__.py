@@ -7,4 +7,4 @@ package is its host-side mirror of the reference's Runtime API and drivers.
 from ._lib import NativeLibraryError, load  # noqa: F401
 from .runtime import (AdamOptimizerOutputs, LmConfig, MlpFullStepOutputs, MomentumOptimizerOutputs,  # noqa: F401
                       OptimizerConfig, Runtime, RuntimeMetrics, RuntimeOptions, TinyTransformerTrainingOutputs,
-                      apply_init_stability, stability_learning_rate)
+                      apply_init_stability, sample_next_token, stability_learning_rate)

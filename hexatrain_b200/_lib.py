@@ -101,6 +101,15 @@ class NprtInfoC(C.Structure):
                 ("tokenizer_hash", C.c_char * 80)]
 
 
+class SamplingC(C.Structure):
+    _fields_ = [("greedy", C.c_uint32), ("temperature", C.c_float), ("top_k", C.c_uint32), ("seed", C.c_uint64)]
+
+
+class SamplingAuditC(C.Structure):
+    _fields_ = [("ok", C.c_uint32), ("logits_finite", C.c_uint32), ("weight_sum", C.c_double),
+                ("probability_sum", C.c_double)]
+
+
 # name -> (restype, argtypes).  Must match include/hexatrain.h.
 SIGNATURES = {
     "hx_runtime_create": (C.c_int, [C.c_int, C.POINTER(C.c_void_p), C.c_char_p, C.c_size_t]),
@@ -147,6 +156,10 @@ SIGNATURES = {
     "hx_muon_execute": (C.c_int, [C.c_void_p, C.c_uint32, C.c_uint32, C.c_void_p, C.c_void_p, C.c_void_p,
                                   C.c_float, C.c_float, C.c_int, C.c_uint32, C.c_float, C.c_float, C.c_float,
                                   C.c_int, C.c_void_p, C.c_void_p]),
+    "hx_lm_forward_tokens": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t, C.c_void_p]),
+    "hx_sample_next_token": (C.c_int, [C.c_void_p, C.c_uint32, C.POINTER(SamplingC), C.c_uint64,
+                                       C.POINTER(C.c_uint32), C.POINTER(SamplingAuditC)]),
+    "hx_lm_generate": (C.c_int, [C.c_void_p, C.c_void_p, C.c_uint32, C.c_uint32, C.POINTER(SamplingC), C.c_void_p]),
     "hx_momentum_prepare": (C.c_int, [C.c_void_p, C.c_uint32]),
     "hx_momentum_execute": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_float, C.c_float,
                                       C.c_void_p, C.c_void_p]),

@@ -197,7 +197,12 @@ struct DiagOut {
 // Forward + backward over the ids already in the plan.  grads[0..P) receive
 // sum over rows of the gradient with dlogits scaled by grad_scale;
 // grads[P] receives sum_b loss_b * grad_scale.
-void forward_backward(hx_runtime* rt, LmPlan& p, const float* W, float* G, float grad_scale)
+// Forward-only variants (executeTinyTransformerForwardOnly): stop after the
+// output projection; kHeadLastRow projects only each sequence's last row
+// into logits [B][V] (what generation samples from).
+enum ForwardMode { kFullStep = 0, kForwardAllRows = 1, kForwardLastRow = 2 };
+
+void forward_backward(hx_runtime* rt, LmPlan& p, const float* W, float* G, float grad_scale, int mode = kFullStep)
 {
     const Arena& a = p.arena;
     const int M = p.M, T = p.T, D = p.D, F = p.F, V = p.V, B = p.B;
@@ -251,7 +256,13 @@ void forward_backward(hx_runtime* rt, LmPlan& p, const float* W, float* G, float
     }
     const float* xL = a.at<float>(p.xL);
     float* logits = a.at<float>(p.logits);
+    if (mode == kForwardLastRow) {
+        gemm<false, false>(rt, B, V, D, xL + size_t(T - 1) * D, (long)T * D, W + p.off_out, V,
+                           EpiStore{logits, (long)V, 0, 0});
+        return;
+    }
     gemm<false, false>(rt, M, V, D, xL, D, W + p.off_out, V, EpiStore{logits, (long)V, 0, 0});
+    if (mode == kForwardAllRows) return;
     ProfScope pce(rt, kTagSoftmaxCe, 4.0 * M * V, 4.0 * 2.0 * M * V);
     softmax_ce_kernel<<<row_grid, 32 * rows_per_block, 0, s>>>(
         M, V, T, grad_scale, logits, tgt_ids, p.diag ? a.at<float>(p.probs) : nullptr, logits,
@@ -691,6 +702,93 @@ int hx_lm_execute_tokens(hx_runtime* rt, const uint32_t* in, const uint32_t* tgt
     });
     if (rt) rt->record_execute(rc == HX_OK, us_since(t0));
     return rc;
+}
+
+int hx_lm_forward_tokens(hx_runtime* rt, const uint32_t* tokens, const float* params, size_t pc, float* logits) {
+    const auto t0 = Clock::now();
+    const int rc = hx_guard(rt, [&] {
+        LmPlan& p = need_lm(rt);
+        require(tokens && logits, HX_ERR_ARGUMENT, "generalized tiny training forward-only buffer schema");
+        const Arena& a = p.arena;
+        const float* W = a.at<float>(p.params);
+        if (params) {
+            require(pc == p.P, HX_ERR_ARGUMENT, "generalized tiny training forward-only buffer schema");
+            for (size_t i = 0; i < pc; ++i)
+                require(std::isfinite(params[i]), HX_ERR_ARGUMENT, "generalized tiny training forward-only buffer schema");
+            HX_CUDA(cudaMemcpyAsync(a.at<float>(p.exec_params), params, sizeof(float) * p.P, cudaMemcpyHostToDevice,
+                                    rt->stream));
+            W = a.at<float>(p.exec_params);
+        } else {
+            require(p.state_ready, HX_ERR_STATE, "forward-only on the device state before state upload");
+        }
+        HX_CUDA(cudaMemcpyAsync(a.at<uint32_t>(p.in_tok), tokens, sizeof(uint32_t) * p.M, cudaMemcpyHostToDevice,
+                                rt->stream));
+        HX_CUDA(cudaMemsetAsync(a.at<int>(p.bad), 0, sizeof(int), rt->stream));
+        copy_ids_kernel<<<grid_for(p.M, 256, rt->sm_count), 256, 0, rt->stream>>>(
+            p.M, p.V, a.at<uint32_t>(p.in_tok), a.at<uint32_t>(p.in_tok), a.at<int>(p.in_ids), a.at<int>(p.tgt_ids),
+            a.at<int>(p.bad));
+        HX_LAUNCHED(rt);
+        check_bad(rt, p, "INVALID_TINY_LM_TOKEN: token id >= vocabulary size");
+        forward_backward(rt, p, W, a.at<float>(p.grads), 1.0f, kForwardAllRows);
+        const size_t n = size_t(p.M) * p.V;
+        HX_CUDA(cudaMemcpyAsync(logits, a.at<float>(p.logits), sizeof(float) * n, cudaMemcpyDeviceToHost, rt->stream));
+        rt->check_device_error();
+        for (size_t i = 0; i < n; ++i)
+            require(std::isfinite(logits[i]), HX_ERR_NONFINITE, "QNN_NONFINITE: forward-only logits are not finite");
+        if (rt->injected_now()) fail(HX_ERR_CUDA, "injected execute failure after device success");
+    });
+    if (rt) rt->record_execute(rc == HX_OK, us_since(t0));
+    return rc;
+}
+
+int hx_lm_generate(hx_runtime* rt, const uint32_t* prompts, uint32_t prompt_len, uint32_t max_new,
+                   const hx_sampling* sampling, uint32_t* out) {
+    return hx_guard(rt, [&] {
+        LmPlan& p = need_lm(rt);
+        require(prompts && sampling && out, HX_ERR_ARGUMENT, "generation: null buffer");
+        require(prompt_len > 0, HX_ERR_ARGUMENT, "PROMPT_EMPTY: prompt is empty");
+        require(p.state_ready, HX_ERR_STATE, "generation before state upload");
+        const uint32_t B = p.B, T = p.T, V = p.V;
+        std::vector<std::vector<uint32_t>> history(B);
+        for (uint32_t b = 0; b < B; ++b) {
+            history[b].assign(prompts + size_t(b) * prompt_len, prompts + size_t(b + 1) * prompt_len);
+            for (uint32_t t : history[b])
+                require(t < V, HX_ERR_ARGUMENT, "INVALID_TINY_LM_TOKEN: token id >= vocabulary size");
+        }
+        const Arena& a = p.arena;
+        std::vector<uint32_t> window(size_t(B) * T);
+        std::vector<float> rows(size_t(B) * V);
+        for (uint32_t step = 0; step < max_new; ++step) {
+            // buildTokenContext (nicopedia_byte_bpe.h:278-291): the last T
+            // tokens, right-aligned, left-padded with token 0.
+            for (uint32_t b = 0; b < B; ++b) {
+                const auto& h = history[b];
+                const size_t keep = std::min<size_t>(h.size(), T), pad = T - keep;
+                uint32_t* w = window.data() + size_t(b) * T;
+                std::fill(w, w + pad, 0u);
+                std::copy(h.end() - keep, h.end(), w + pad);
+            }
+            HX_CUDA(cudaMemcpyAsync(a.at<uint32_t>(p.in_tok), window.data(), sizeof(uint32_t) * p.M,
+                                    cudaMemcpyHostToDevice, rt->stream));
+            copy_ids_kernel<<<grid_for(p.M, 256, rt->sm_count), 256, 0, rt->stream>>>(
+                p.M, p.V, a.at<uint32_t>(p.in_tok), a.at<uint32_t>(p.in_tok), a.at<int>(p.in_ids),
+                a.at<int>(p.tgt_ids), a.at<int>(p.bad));
+            HX_LAUNCHED(rt);
+            forward_backward(rt, p, a.at<float>(p.params), a.at<float>(p.grads), 1.0f, kForwardLastRow);
+            HX_CUDA(cudaMemcpyAsync(rows.data(), a.at<float>(p.logits), sizeof(float) * rows.size(),
+                                    cudaMemcpyDeviceToHost, rt->stream));
+            rt->check_device_error();
+            for (uint32_t b = 0; b < B; ++b) {
+                hx_sampling sb = *sampling;
+                sb.seed = sampling->seed + b;  // stream b samples with seed + b
+                uint32_t tok = 0;
+                if (hx_sample_next_token(rows.data() + size_t(b) * V, V, &sb, step, &tok, nullptr) != HX_OK)
+                    fail(HX_ERR_NONFINITE, "generation step produced non-finite logits on prepared graph");
+                out[size_t(b) * max_new + step] = tok;
+                history[b].push_back(tok);
+            }
+        }
+    });
 }
 
 int hx_lm_state_upload(hx_runtime* rt, const float* params, const float* m, const float* v, const float* buf, size_t pc) {

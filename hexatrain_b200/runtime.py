@@ -105,6 +105,21 @@ class MomentumOptimizerOutputs:
     weight_next: np.ndarray = None
 
 
+def sample_next_token(logits, step: int = 0, greedy: bool = True, temperature: float = 0.0, top_k: int = 0,
+                      seed: int = 0):
+    """greedyArgmax / sampleTopKChecked (nicopedia_generation.h:286-395).
+    Returns (token, audit dict); raises ValueError on non-finite input."""
+    row = np.ascontiguousarray(logits, np.float32).ravel()
+    tok, audit = C.c_uint32(), _lib.SamplingAuditC()
+    s = _lib.SamplingC(int(greedy), temperature, top_k, seed)
+    rc = _lib.load().hx_sample_next_token(row.ctypes.data, row.size, C.byref(s), step, C.byref(tok), C.byref(audit))
+    info = dict(ok=bool(audit.ok), logits_finite=bool(audit.logits_finite), weight_sum=audit.weight_sum,
+                probability_sum=audit.probability_sum)
+    if rc != 0:
+        raise ValueError(f"sampling failed ({rc}): {info}")
+    return int(tok.value), info
+
+
 def stability_learning_rate(mode: int, base: float, step: int, total_steps: int) -> float:
     """stabilityLearningRate (training_stability.h:88-99)."""
     return float(_lib.load().hx_stability_learning_rate(mode, base, step, total_steps))
@@ -500,6 +515,34 @@ class Runtime:
         if not self._ok(self._lib.hx_lm_state_download(self._rt, *[ptr(a) for a in outs], n)):
             raise RuntimeError(self.last_error)
         return tuple(outs)  # params, adam_m, adam_v, muon_buffer
+
+    def execute_tiny_transformer_forward_only_tokens(self, tokens, params=None):
+        """executeTinyTransformerForwardOnly (qnn/qnn_runtime.h:418-421) on
+        token ids [batch, T]; params None uses the device state.  Returns
+        logits [batch*T, V] or None (last_error set)."""
+        if not self._need():
+            return None
+        cfg = self._lm_cfg
+        t = np.ascontiguousarray(tokens, np.uint32).ravel()
+        logits = np.empty((t.size, cfg.vocabulary_size), np.float32)
+        p = None if params is None else _f32(params).ravel()
+        ok = self._ok(self._lib.hx_lm_forward_tokens(self._rt, ptr(t), None if p is None else ptr(p),
+                                                     0 if p is None else p.size, ptr(logits)))
+        return logits if ok else None
+
+    def lm_generate(self, prompts, max_new: int, greedy: bool = True, temperature: float = 0.0, top_k: int = 0,
+                    seed: int = 0):
+        """The prepared generation loop on the device state: prompts [batch,
+        prompt_len] ids -> generated ids [batch, max_new] (None on failure)."""
+        if not self._need():
+            return None
+        pr = np.ascontiguousarray(prompts, np.uint32)
+        if pr.ndim == 1:
+            pr = pr[None, :]
+        out = np.zeros((pr.shape[0], max_new), np.uint32)
+        s = _lib.SamplingC(int(greedy), temperature, top_k, seed)
+        ok = self._ok(self._lib.hx_lm_generate(self._rt, ptr(pr), pr.shape[1], max_new, C.byref(s), ptr(out)))
+        return out if ok else None
 
     def lm_checkpoint_save(self, path: str, seed: int, step: int, tokenizer_kind: str | None = None,
                            tokenizer_hash: str | None = None) -> bool:

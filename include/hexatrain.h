@@ -358,6 +358,41 @@ int hx_adam_execute_device(hx_runtime* rt, size_t n, const float* current, const
                            float learning_rate, float gradient_scale, float first_correction,
                            float second_correction, const hx_adam_outputs* out);
 
+/* ---- forward-only LM and generation -------------------------------------- */
+/* executeTinyTransformerForwardOnly (qnn/qnn_runtime.h:418-421,
+ * qnn_runtime_transformer_training_generalized_execute.inc:320-...):
+ * logits [batch*T, V] for token ids [batch*T] under `params` (host,
+ * registry order, checked finite), or under the device state when params is
+ * NULL.  No target and no backward.  Non-finite logits fail with
+ * HX_ERR_NONFINITE.  Synchronous.  Requires hx_lm_prepare. */
+int hx_lm_forward_tokens(hx_runtime* rt, const uint32_t* tokens, const float* params,
+                         size_t param_count, float* logits);
+
+typedef struct {
+    uint32_t greedy;      /* 1: greedyArgmax (first maximum) */
+    float temperature;    /* <= 0 or non-finite: greedy */
+    uint32_t top_k;       /* 0: the whole vocabulary */
+    uint64_t seed;
+} hx_sampling;
+typedef struct {
+    uint32_t ok, logits_finite;
+    double weight_sum, probability_sum;
+} hx_sampling_audit;
+/* greedyArgmax / sampleTopKChecked (nicopedia_generation.h:286-395) on one
+ * logit row: top-K by (logit desc, index asc), temperature softmax in
+ * double, u = top 53 bits of splitmix64(seed + step * 0x9E3779B97F4A7C15)
+ * / 2^53, first cumulative probability >= u.  Host only.  Non-finite
+ * logits or weights fail with HX_ERR_NONFINITE and ok = 0. */
+int hx_sample_next_token(const float* logits, uint32_t vocab, const hx_sampling* sampling,
+                         uint64_t step, uint32_t* token, hx_sampling_audit* audit);
+/* The prepared generation loop (qnn/qnn_prepared_generation.cpp:392-430)
+ * for `batch` independent streams on the device state: each step feeds
+ * the last T tokens of every stream (left-padded with 0, buildTokenContext),
+ * projects only the last row and samples it (stream b with seed + b).
+ * prompts [batch*prompt_len], out [batch*max_new].  Synchronous. */
+int hx_lm_generate(hx_runtime* rt, const uint32_t* prompts, uint32_t prompt_len, uint32_t max_new,
+                   const hx_sampling* sampling, uint32_t* out);
+
 /* ---- momentum SGD optimizer ------------------------------------------------ */
 /* Runtime::prepareMomentumOptimizer / executeMomentumOptimizer
  * (qnn/qnn_runtime.h:353-359, graph qnn_runtime_transformer.inc:799-925):

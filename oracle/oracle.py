@@ -422,6 +422,17 @@ class Reference:
             raise RuntimeError(self.last_error())
         return out
 
+    def sample_next_token(self, logits, step=0, greedy=False, temperature=1.0, top_k=0, seed=0):
+        """(token, ok) from the reference's greedyArgmax / sampleTopKChecked."""
+        L = self.lib
+        L.hxr_sample_next_token.restype = C.c_uint32
+        L.hxr_sample_next_token.argtypes = [_f32p, C.c_uint32, C.c_int, C.c_float, C.c_uint32, C.c_uint64,
+                                            C.c_uint64, C.POINTER(C.c_int)]
+        row = np.ascontiguousarray(logits, np.float32).ravel()
+        ok = C.c_int()
+        tok = L.hxr_sample_next_token(row, row.size, int(greedy), temperature, top_k, seed, step, C.byref(ok))
+        return int(tok), bool(ok.value)
+
     def stability_mode_error(self, mode) -> str:
         self.lib.hxr_stability_mode_error.restype = C.c_char_p
         self.lib.hxr_stability_mode_error.argtypes = [C.c_uint32]

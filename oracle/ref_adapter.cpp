@@ -14,6 +14,7 @@
 #include "cpu_reference_training.h"
 #include "tiny_language_model_cpu.h"
 #include "training_stability.h"
+#include "nicopedia_generation.h"
 
 #include <algorithm>
 #include <cmath>
@@ -263,6 +264,18 @@ int hxr_lm_momentum(const RefConfig* c, const float* w, const float* g, const fl
     } catch (const std::exception& ex) {
         return guard("hxr_lm_momentum", &gLastError, ex);
     }
+}
+
+// nicopedia_gen::greedyArgmax / sampleTopKChecked (nicopedia_generation.h:286-395).
+uint32_t hxr_sample_next_token(const float* logits, uint32_t vocab, int greedy, float temperature, uint32_t top_k,
+                               uint64_t seed, uint64_t step, int* ok) {
+    if (greedy) {
+        *ok = 1;
+        return phonelm::nicopedia_gen::greedyArgmax(logits, vocab);
+    }
+    const auto r = phonelm::nicopedia_gen::sampleTopKChecked(logits, vocab, temperature, top_k, seed, step);
+    *ok = r.ok ? 1 : 0;
+    return r.value;
 }
 
 // phonelm::stabilityLearningRate (training_stability.h:88-99).
