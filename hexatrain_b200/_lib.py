@@ -160,6 +160,11 @@ SIGNATURES = {
     "hx_sample_next_token": (C.c_int, [C.c_void_p, C.c_uint32, C.POINTER(SamplingC), C.c_uint64,
                                        C.POINTER(C.c_uint32), C.POINTER(SamplingAuditC)]),
     "hx_lm_generate": (C.c_int, [C.c_void_p, C.c_void_p, C.c_uint32, C.c_uint32, C.POINTER(SamplingC), C.c_void_p]),
+    "hx_bridge_environment_report": (C.c_char_p, []),
+    "hx_bridge_status_report": (C.c_char_p, []),
+    "hx_bridge_run_execution_mode": (C.c_char_p, [C.c_void_p]),
+    "hx_bridge_request_stop": (None, []),
+    "hx_bridge_clear_stop": (None, []),
     "hx_momentum_prepare": (C.c_int, [C.c_void_p, C.c_uint32]),
     "hx_momentum_execute": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_float, C.c_float,
                                       C.c_void_p, C.c_void_p]),

@@ -54,13 +54,47 @@ def build(verbose: bool = False, extra=()) -> str:
     with cf.ThreadPoolExecutor(max_workers=min(8, os.cpu_count() or 1)) as ex:
         objs = list(ex.map(lambda s: _compile(s, extra), sources))
     if _stale(LIB, objs):
-        cmd = [NVCC] + ARCH + ["-shared", "-o", LIB] + objs + ["-lcudart_static", "-ldl", "-lrt", "-lpthread"]
+        cmd = [NVCC] + ARCH + ["-shared", "-o", LIB, "-Xlinker", "-soname=libhexatrain_b200.so"] + objs + \
+            ["-lcudart_static", "-ldl", "-lrt", "-lpthread"]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
+    build_jni(verbose)
     if verbose:
         print(LIB)
     return LIB
+
+
+JNI_SRC = os.path.join(HERE, "jni", "native_bridge_b200.cpp")
+JNI_LIB = os.path.join(HERE, "libhexatrain_b200_jni.so")
+
+
+def jni_include_dirs():
+    """Directories holding a JDK's jni.h (and its platform jni_md.h), from
+    HX_JNI_INCLUDE or JAVA_HOME; None when no JDK is present."""
+    base = os.environ.get("HX_JNI_INCLUDE") or (
+        os.path.join(os.environ["JAVA_HOME"], "include") if os.environ.get("JAVA_HOME") else None)
+    if not base or not os.path.exists(os.path.join(base, "jni.h")):
+        return None
+    return [base] + [os.path.join(base, d) for d in ("linux",) if os.path.isdir(os.path.join(base, d))]
+
+
+def build_jni(verbose: bool = False, include_dirs=None, out: str = JNI_LIB):
+    """The JNI wrapper library (NativeBridge symbols over the bridge core).
+    Skipped, returning None, when no jni.h is available."""
+    inc = include_dirs or jni_include_dirs()
+    if not inc:
+        if verbose:
+            print("no jni.h (set JAVA_HOME or HX_JNI_INCLUDE): JNI bridge not built")
+        return None
+    if not _stale(out, [JNI_SRC, LIB, os.path.join(ROOT, "include", "hexatrain_bridge.h")]):
+        return out
+    cmd = ["g++", "-std=c++17", "-O2", "-fPIC", "-shared", "-o", out, JNI_SRC, f"-I{os.path.join(ROOT, 'include')}"]
+    cmd += [f"-I{d}" for d in inc] + [f"-L{HERE}", "-lhexatrain_b200", "-Wl,-rpath,$ORIGIN"]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"JNI bridge build failed:\n{r.stdout}\n{r.stderr}")
+    return out
 
 
 if __name__ == "__main__":

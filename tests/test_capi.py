@@ -10,13 +10,16 @@ import hexatrain_b200 as hx
 from conftest import HAS_GPU, ROOT, golden
 from hexatrain_b200 import _lib, data
 
-HEADER = os.path.join(ROOT, "include", "hexatrain.h")
+HEADERS = [os.path.join(ROOT, "include", h) for h in sorted(os.listdir(os.path.join(ROOT, "include")))
+           if h.endswith(".h")]
 
 
 def declared_symbols():
-    text = open(HEADER).read()
-    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
-    return sorted(set(re.findall(r"\b(hx_[a-z0-9_]+)\s*\(", text)))
+    names = set()
+    for path in HEADERS:
+        text = re.sub(r"/\*.*?\*/", "", open(path).read(), flags=re.S)
+        names.update(re.findall(r"\b(hx_[a-z0-9_]+)\s*\(", text))
+    return sorted(names)
 
 
 def test_library_exports_every_declared_symbol():
