@@ -168,80 +168,99 @@ __global__ void splitk_reduce_kernel(int M, int N, int splits, const float* __re
 }
 
 // ---- epilogues -----------------------------------------------------------
+// Each epilogue is split into prefetch(m, n) -- the one global value it reads
+// for element (m, n), 0 if none -- and finish(m, n, v, pre).  The tensor-core
+// epilogue issues the prefetches of a whole chunk before finishing any of
+// them, so those loads are in flight together; operator() is the fused form.
 
 struct EpiStore {  // C[m*ldc + n] = v, with an optional column split:
+    static constexpr bool kReads = false;  // prefetch() loads from global memory
     // column n goes to C + (n / split) * split_stride + m*ldc + n % split
     float* c;
     long ldc;
     int split;           // 0 = no split
     long split_stride;
-    __device__ void operator()(int m, int n, float v) const {
+    __device__ float prefetch(int, int) const { return 0.f; }
+    __device__ void finish(int m, int n, float v, float) const {
         if (split) c[(long)(n / split) * split_stride + (long)m * ldc + (n % split)] = v;
         else c[(long)m * ldc + n] = v;
     }
+    __device__ void operator()(int m, int n, float v) const { finish(m, n, v, 0.f); }
 };
 
 struct EpiAddResidual {  // out = res + v   (r1 = x + ctx*Wo ; out = r1 + relu*W2)
+    static constexpr bool kReads = true;  // prefetch() loads from global memory
     const float* res;
     float* out;
     long ld;
-    __device__ void operator()(int m, int n, float v) const {
-        const long i = (long)m * ld + n;
-        out[i] = __fadd_rn(res[i], v);
-    }
+    __device__ float prefetch(int m, int n) const { return res[(long)m * ld + n]; }
+    __device__ void finish(int m, int n, float v, float r) const { out[(long)m * ld + n] = __fadd_rn(r, v); }
+    __device__ void operator()(int m, int n, float v) const { finish(m, n, v, prefetch(m, n)); }
 };
 
 struct EpiRelu {  // h = max(0, z) ; optional mask = h > 0
+    static constexpr bool kReads = false;  // prefetch() loads from global memory
     float* h;
     uint8_t* mask;
     long ld;
-    __device__ void operator()(int m, int n, float v) const {
+    __device__ float prefetch(int, int) const { return 0.f; }
+    __device__ void finish(int m, int n, float v, float) const {
         const long i = (long)m * ld + n;
         const float r = (0.f < v) ? v : 0.f;
         h[i] = r;
         if (mask) mask[i] = r > 0.f ? 1 : 0;
     }
+    __device__ void operator()(int m, int n, float v) const { finish(m, n, v, 0.f); }
 };
 
 struct EpiReluBackward {  // dz = (act > 0) ? v : 0 ; optional raw store of v
+    static constexpr bool kReads = true;  // prefetch() loads from global memory
     const float* act;
     float* dz;
     float* raw;
     long ld;
-    __device__ void operator()(int m, int n, float v) const {
+    __device__ float prefetch(int m, int n) const { return act[(long)m * ld + n]; }
+    __device__ void finish(int m, int n, float v, float a) const {
         const long i = (long)m * ld + n;
         if (raw) raw[i] = v;
-        dz[i] = act[i] > 0.f ? v : 0.f;
+        dz[i] = a > 0.f ? v : 0.f;
     }
+    __device__ void operator()(int m, int n, float v) const { finish(m, n, v, prefetch(m, n)); }
 };
 
 struct EpiError {  // P = v ; E = P - Y ; dP = (P - Y) * s
+    static constexpr bool kReads = true;  // prefetch() loads from global memory
     const float* y;
     float* p;
     float* e;
     float* dp;
     float s;
     long ld;
-    __device__ void operator()(int m, int n, float v) const {
+    __device__ float prefetch(int m, int n) const { return y[(long)m * ld + n]; }
+    __device__ void finish(int m, int n, float v, float yv) const {
         const long i = (long)m * ld + n;
-        const float err = __fsub_rn(v, y[i]);
+        const float err = __fsub_rn(v, yv);
         if (p) p[i] = v;
         if (e) e[i] = err;
         dp[i] = __fmul_rn(err, s);
     }
+    __device__ void operator()(int m, int n, float v) const { finish(m, n, v, prefetch(m, n)); }
 };
 
 struct EpiSgd {  // dW = v (optional) ; W_next = W - lr*dW (two roundings, as the reference)
+    static constexpr bool kReads = true;  // prefetch() loads from global memory
     const float* w;
     float* dw;
     float* w_next;
     float lr;
     long ld;
-    __device__ void operator()(int m, int n, float v) const {
+    __device__ float prefetch(int m, int n) const { return w[(long)m * ld + n]; }
+    __device__ void finish(int m, int n, float v, float wv) const {
         const long i = (long)m * ld + n;
         if (dw) dw[i] = v;
-        w_next[i] = __fsub_rn(w[i], __fmul_rn(lr, v));
+        w_next[i] = __fsub_rn(wv, __fmul_rn(lr, v));
     }
+    __device__ void operator()(int m, int n, float v) const { finish(m, n, v, prefetch(m, n)); }
 };
 
 }  // namespace hx

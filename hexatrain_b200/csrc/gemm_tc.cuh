@@ -35,7 +35,8 @@
 //               end of a unit, stage the 32x64 block through shared memory
 //               16 columns at a time so that each store instruction writes
 //               two 64-byte row segments (coalesced), applying the epilogue
-//               functor (or storing split-K partials).
+//               functor (or storing split-K partials); the epilogue's own
+//               global inputs for a chunk are loaded before any is used.
 // Operands may be K-major or MN-major (instruction-descriptor bits 15/16).
 // K-major tiles use the 128-byte swizzle; MN-major tiles arrive as four
 // 32-wide TMA boxes (LBO = 4 KB) in the 128-byte/32-byte-atom swizzle, the
@@ -327,16 +328,33 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                 for (int j = 0; j < 16; ++j) stg[lane * kTcStageLd + j] = acc[c * 16 + j];
                 __syncwarp();
                 const int n = cbase + c * 16 + csub;
+                if (partial) {
 #pragma unroll 4
-                for (int i = 0; i < 16; ++i) {
-                    const int r = 2 * i + rsub;
-                    const int row = rbase + r;
-                    const float v = stg[r * kTcStageLd + csub];
-                    if (row < g.M && n < g.N) {
-                        if (partial)
-                            partial[((long)t.z * g.M + row) * g.N + n] = v;
-                        else
-                            epi(row, n, v);
+                    for (int i = 0; i < 16; ++i) {
+                        const int row = rbase + 2 * i + rsub;
+                        if (row < g.M && n < g.N)
+                            partial[((long)t.z * g.M + row) * g.N + n] = stg[(2 * i + rsub) * kTcStageLd + csub];
+                    }
+                } else if constexpr (Epi::kReads) {
+                    // the chunk's global epilogue inputs, all loads in flight together
+                    float pre[16];
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        const int row = rbase + 2 * i + rsub;
+                        pre[i] = (row < g.M && n < g.N) ? epi.prefetch(row, n) : 0.f;
+                    }
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        const int r = 2 * i + rsub;
+                        const int row = rbase + r;
+                        if (row < g.M && n < g.N) epi.finish(row, n, stg[r * kTcStageLd + csub], pre[i]);
+                    }
+                } else {
+#pragma unroll 4
+                    for (int i = 0; i < 16; ++i) {
+                        const int r = 2 * i + rsub;
+                        const int row = rbase + r;
+                        if (row < g.M && n < g.N) epi.finish(row, n, stg[r * kTcStageLd + csub], 0.f);
                     }
                 }
             }
