@@ -24,6 +24,8 @@ HX_LM_LEARNED_POSITION = 1
 HX_GEMM_AUTO = 0
 HX_GEMM_CUDA_CORES = 1
 HX_GEMM_TENSOR_CORES = 2
+HX_ATTN_AUTO = 0
+HX_ATTN_CUDA_CORES = 1
 HX_OPT_ADAM = 0
 HX_OPT_MUON = 1
 HX_OPT_MOMENTUM = 2
@@ -121,6 +123,7 @@ SIGNATURES = {
     "hx_runtime_metrics": (C.c_int, [C.c_void_p, C.POINTER(Metrics)]),
     "hx_runtime_inject_execute_failure": (C.c_int, [C.c_void_p, C.c_int64]),
     "hx_runtime_set_gemm_backend": (C.c_int, [C.c_void_p, C.c_int]),
+    "hx_runtime_set_attention_backend": (C.c_int, [C.c_void_p, C.c_int]),
     "hx_runtime_profile": (C.c_int, [C.c_void_p, C.c_int]),
     "hx_runtime_profile_read": (C.c_int, [C.c_void_p, C.POINTER(ProfileEntry), C.c_int, C.POINTER(C.c_int)]),
     "hx_mlp_prepare": (C.c_int, [C.c_void_p, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, C.c_int]),

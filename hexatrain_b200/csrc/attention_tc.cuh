@@ -1,0 +1,328 @@
+// attention_tc.cuh -- causal multi-head attention on the 5th-generation
+// tensor cores for head dimension 32 and sequences of at most 256 tokens.
+//
+// Products run in "3xTF32" (hi*hi + hi*lo + lo*hi with hi = the nearest TF32
+// value, lo = x - hi; see gemm_tc.cuh), so they carry FP32 accuracy; the
+// softmax runs on the CUDA cores in FP32 with the row sum in double.
+//
+// Forward (tiny_language_model_cpu.cpp:44-45: scores, causal softmax,
+// context), one CTA per (head, sequence), query rows in tiles of 128:
+//   warp 8 lane 0  TMA: Q, K, V rows [128t, 128t+128) of this head for each
+//                  tile t, Q/K in the 128-byte swizzle (K-major operands),
+//                  V in the 128-byte/32-byte-atom swizzle (MN-major B);
+//                  then the MMA issuer.
+//   warps 0-7      split each landed tile into hi (in place) and lo; then
+//                  the softmax of tile t, one TMEM lane (query row) per
+//                  thread pair: warp w reads lanes 32(w%4).. and the 32-key
+//                  chunks c = w/4, w/4 + 2, ...
+// Per tile t (N = 128(t+1) keys):
+//   S  = Q_t K[0:N]^T          12 MMAs M128 N(N) K8 into TMEM columns [0, N)
+//   m  = max_j<=r S[r][j] * scale        (pass 1 over the chunks)
+//   e  = exp(S * scale - m) (0 where j > r), sum = sum_j e   (pass 2)
+//        e is split into hi (written back over S) and lo (a 6-slot ring of
+//        32-column TMEM chunks); each finished chunk is handed to the MMA
+//        issuer, which computes E_c V_c into a fresh 32-column accumulator
+//        (one of two, alternating) with A read from TMEM (3 MMAs M128 N32
+//        K8 per 8 keys) and frees the slot; the softmax threads drain every
+//        chunk's accumulator into FP32 registers with round-to-nearest adds.
+//   ctx[r] = (E V)[r] / sum;  row max m and float(sum) are saved for the
+//        backward.
+// Accuracy: the MMA's FP32 accumulation truncates, so no accumulator runs
+// longer than one 32-deep chunk, and within a chunk the small hi*lo and
+// lo*hi terms are issued before hi*hi: only four full-magnitude truncations
+// per chunk.  ctx matches an FP64 evaluation to a few 1e-7 of the row max.
+// TMEM: S [0,256), chunk accumulators [256,320), ring [320,512).
+// Every mbarrier wait is bounded; after the first timeout the CTA records an
+// error code, stops waiting (later waits return at once), keeps the same
+// control flow through its named barriers, drains its MMAs and loads and
+// frees TMEM.
+#pragma once
+
+#include "gemm_tc.cuh"
+
+namespace hx {
+
+constexpr int kAtcDH = 32, kAtcMaxT = 256, kAtcTile = 128;
+constexpr int kAtcSoftWarps = 8;
+constexpr int kAtcSoftThreads = 32 * kAtcSoftWarps;
+constexpr int kAtcThreads = kAtcSoftThreads + 32;
+constexpr int kAtcRing = 6;
+constexpr uint32_t kAtcCols = 512, kAtcColS = 0, kAtcColO = 256, kAtcColRing = 320;
+constexpr int kAtcTileFloats = kAtcTile * kAtcDH;  // 128 rows x 32 fp32 = 16 KB
+
+struct AtcFwdSmem {
+    float qh[2 * kAtcTileFloats], ql[2 * kAtcTileFloats];
+    float kh[2 * kAtcTileFloats], kl[2 * kAtcTileFloats];
+    float vh[2 * kAtcTileFloats], vl[2 * kAtcTileFloats];
+    float red_max[2][kAtcTile];
+    double red_sum[2][kAtcTile];
+    uint64_t ld[2], conv[2], pv_done[2], s_ready, ring_full[kAtcRing], ring_empty[kAtcRing];
+    uint64_t acc_full[2], acc_empty[2], drain;
+    uint32_t tmem_addr;
+    int abort;
+};
+constexpr size_t kAtcFwdSmemBytes = sizeof(AtcFwdSmem) + 1024;  // + alignment slack
+static_assert(kAtcFwdSmemBytes <= 232448, "attention forward shared memory exceeds the 227 KB per-CTA limit");
+
+enum AtcError { kAtcErrLoad = 11, kAtcErrMma = 12, kAtcErrSoftmax = 13, kAtcErrEpilogue = 14 };
+
+// Bounded wait; after the first failure anywhere in the CTA it returns
+// false at once, so a broken CTA finishes in bounded time.
+__device__ __forceinline__ bool atc_wait(int& abort, int* err, int code, uint64_t* bar, uint32_t parity) {
+    volatile int* ab = &abort;
+    if (*ab) return false;
+    if (tc::mbar_wait(bar, parity)) return true;
+    if (err) atomicCAS(err, 0, code);
+    *ab = 1;
+    return false;
+}
+
+// Barrier among the 256 softmax threads only (the issuer warp never joins).
+__device__ __forceinline__ void atc_soft_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+
+// hi = nearest TF32 (in place), lo = x - hi, for n4 float4s.
+__device__ __forceinline__ void atc_split(float* hi, float* lo, int n4, int t, int nt) {
+    float4* h4 = reinterpret_cast<float4*>(hi);
+    float4* l4 = reinterpret_cast<float4*>(lo);
+    for (int i = t; i < n4; i += nt) {
+        const float4 x = h4[i];
+        const float4 h = tf32_hi(x);
+        h4[i] = h;
+        l4[i] = make_float4(x.x - h.x, x.y - h.y, x.z - h.z, x.w - h.w);
+    }
+}
+
+__global__ void __launch_bounds__(kAtcThreads, 1)
+attention_fwd_tc_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid_constant__ CUtensorMap map_v, int T,
+                        int D, int H, float scale, float* __restrict__ ctx, float* __restrict__ row_max,
+                        float* __restrict__ row_sum, int* __restrict__ err)
+{
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    const uint32_t pad = (1024u - (tc::smem_u32(smem_raw) & 1023u)) & 1023u;
+    AtcFwdSmem& sm = *reinterpret_cast<AtcFwdSmem*>(smem_raw + pad);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int h = blockIdx.x, b = blockIdx.y;
+    const int ntile = T > kAtcTile ? 2 : 1;
+    const int y0 = b * T;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < 2; ++i) {
+            tc::mbar_init(&sm.ld[i], 1);
+            tc::mbar_init(&sm.conv[i], kAtcSoftThreads);
+            tc::mbar_init(&sm.pv_done[i], 1);
+            tc::mbar_init(&sm.acc_full[i], 1);
+            tc::mbar_init(&sm.acc_empty[i], kAtcSoftWarps);
+        }
+        tc::mbar_init(&sm.s_ready, 1);
+        for (int i = 0; i < kAtcRing; ++i) {
+            tc::mbar_init(&sm.ring_full[i], 4);  // the four warps that own a chunk's 128 lanes
+            tc::mbar_init(&sm.ring_empty[i], 1);
+        }
+        tc::mbar_init(&sm.drain, 1);
+        sm.abort = 0;
+        tc::fence_mbar_init();
+    }
+    if (warp == kAtcSoftWarps) {
+        tc::tmem_alloc(&sm.tmem_addr, kAtcCols);
+        tc::tmem_relinquish();
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+    const uint32_t tmem = sm.tmem_addr;
+
+    if (warp == kAtcSoftWarps) {
+        if (lane == 0) {
+            // ---------------- loads ----------------
+            tc::prefetch_tensormap(&map_qk);
+            tc::prefetch_tensormap(&map_v);
+            for (int t = 0; t < ntile; ++t) {
+                tc::mbar_arrive_expect_tx(&sm.ld[t], 3 * kAtcTileFloats * 4);
+                const int y = y0 + kAtcTile * t;
+                tc::tma_load_2d(sm.qh + t * kAtcTileFloats, &map_qk, &sm.ld[t], h * kAtcDH, y);
+                tc::tma_load_2d(sm.kh + t * kAtcTileFloats, &map_qk, &sm.ld[t], D + h * kAtcDH, y);
+                tc::tma_load_2d(sm.vh + t * kAtcTileFloats, &map_v, &sm.ld[t], 2 * D + h * kAtcDH, y);
+            }
+            // ---------------- MMA issuer ----------------
+            const uint32_t qh = tc::smem_u32(sm.qh), ql = tc::smem_u32(sm.ql);
+            const uint32_t kh = tc::smem_u32(sm.kh), kl = tc::smem_u32(sm.kl);
+            const uint32_t vh = tc::smem_u32(sm.vh), vl = tc::smem_u32(sm.vl);
+            constexpr uint32_t idesc_pv = tc::idesc_tf32(kAtcTile, kAtcDH, false, true);
+            uint32_t gch = 0;  // chunks handed over so far (ring position)
+            for (int t = 0; t < ntile; ++t) {
+                atc_wait(sm.abort, err, kAtcErrMma, &sm.conv[t], 0);
+                if (t > 0) atc_wait(sm.abort, err, kAtcErrMma, &sm.pv_done[t - 1], 0);  // S columns free again
+                tc::tc_fence_after();
+                const uint32_t idesc_s = tc::idesc_tf32(kAtcTile, kAtcTile * (t + 1), false, false);
+                const uint32_t qo = uint32_t(t) * kAtcTileFloats * 4;
+                // corrections (hi*lo, lo*hi) first, then hi*hi
+#pragma unroll
+                for (int k = 0; k < kAtcDH / 8; ++k) {
+                    const uint64_t ah = tc::smem_desc(qh + qo + 32 * k, 16, 1024, tc::kLayoutSw128);
+                    const uint64_t al = tc::smem_desc(ql + qo + 32 * k, 16, 1024, tc::kLayoutSw128);
+                    const uint64_t bh = tc::smem_desc(kh + 32 * k, 16, 1024, tc::kLayoutSw128);
+                    const uint64_t bl = tc::smem_desc(kl + 32 * k, 16, 1024, tc::kLayoutSw128);
+                    tc::mma_tf32(tmem + kAtcColS, ah, bl, idesc_s, k > 0 ? 1u : 0u);
+                    tc::mma_tf32(tmem + kAtcColS, al, bh, idesc_s, 1u);
+                }
+#pragma unroll
+                for (int k = 0; k < kAtcDH / 8; ++k) {
+                    const uint64_t ah = tc::smem_desc(qh + qo + 32 * k, 16, 1024, tc::kLayoutSw128);
+                    const uint64_t bh = tc::smem_desc(kh + 32 * k, 16, 1024, tc::kLayoutSw128);
+                    tc::mma_tf32(tmem + kAtcColS, ah, bh, idesc_s, 1u);
+                }
+                tc::mma_commit(&sm.s_ready);
+                const int nch = 4 * (t + 1);
+                for (int c = 0; c < nch; ++c, ++gch) {
+                    const int slot = gch % kAtcRing;
+                    const int buf = gch & 1;
+                    atc_wait(sm.abort, err, kAtcErrMma, &sm.ring_full[slot], (gch / kAtcRing) & 1);
+                    atc_wait(sm.abort, err, kAtcErrMma, &sm.acc_empty[buf], ((gch >> 1) & 1) ^ 1);
+                    tc::tc_fence_after();
+                    const uint32_t acc = tmem + kAtcColO + 32 * buf;
+                    // V rows are 128-byte K-rows: 8 keys = 1024 bytes
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        const uint32_t key = 32 * c + 8 * k;
+                        const uint64_t bh = tc::smem_desc(vh + key * 128, 4096, 512, tc::kLayoutSw128Base32);
+                        const uint64_t bl = tc::smem_desc(vl + key * 128, 4096, 512, tc::kLayoutSw128Base32);
+                        tc::mma_tf32_ts(acc, tmem + kAtcColS + key, bl, idesc_pv, k > 0 ? 1u : 0u);
+                        tc::mma_tf32_ts(acc, tmem + kAtcColRing + 32 * slot + 8 * k, bh, idesc_pv, 1u);
+                    }
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        const uint32_t key = 32 * c + 8 * k;
+                        const uint64_t bh = tc::smem_desc(vh + key * 128, 4096, 512, tc::kLayoutSw128Base32);
+                        tc::mma_tf32_ts(acc, tmem + kAtcColS + key, bh, idesc_pv, 1u);
+                    }
+                    tc::mma_commit(&sm.ring_empty[slot]);
+                    tc::mma_commit(&sm.acc_full[buf]);
+                }
+                tc::mma_commit(&sm.pv_done[t]);
+            }
+            // every MMA above has completed, and every load has landed,
+            // before TMEM is freed and the CTA exits
+            tc::mma_commit(&sm.drain);
+            tc::mbar_wait(&sm.drain, 0);
+            for (int t = 0; t < ntile; ++t) tc::mbar_wait(&sm.ld[t], 0);
+        }
+    } else {
+        const int st = threadIdx.x;
+        const int q = warp & 3, grp = warp >> 2;
+        // ---------------- hi/lo split of the landed tiles ----------------
+        for (int t = 0; t < ntile; ++t) {
+            atc_wait(sm.abort, err, kAtcErrLoad, &sm.ld[t], 0);
+            const int o = t * kAtcTileFloats;
+            atc_split(sm.qh + o, sm.ql + o, kAtcTileFloats / 4, st, kAtcSoftThreads);
+            atc_split(sm.kh + o, sm.kl + o, kAtcTileFloats / 4, st, kAtcSoftThreads);
+            atc_split(sm.vh + o, sm.vl + o, kAtcTileFloats / 4, st, kAtcSoftThreads);
+            tc::fence_proxy_async_smem();
+            tc::mbar_arrive(&sm.conv[t]);
+        }
+        // ---------------- softmax and epilogue ----------------
+        const uint32_t lane_base = tmem + (uint32_t(32 * q) << 16);
+        const int rl = 32 * q + lane;
+        uint32_t gch = 0;
+        for (int t = 0; t < ntile; ++t) {
+            const int nch = 4 * (t + 1);
+            const int r = kAtcTile * t + rl;
+            const bool valid = r < T;
+            const int last_vis = 4 * t + q;  // later chunks hold no key visible to this warp's rows
+            atc_wait(sm.abort, err, kAtcErrSoftmax, &sm.s_ready, t & 1);
+            tc::tc_fence_after();
+            float mx = -INFINITY;
+            for (int c = grp; c <= last_vis; c += 2) {
+                uint32_t v[32];
+                tc::tmem_ld_32x32b_x32(lane_base + kAtcColS + 32 * c, v);
+                tc::tmem_ld_wait();
+#pragma unroll
+                for (int i = 0; i < 32; ++i)
+                    if (32 * c + i <= r) mx = fmaxf(mx, __fmul_rn(__uint_as_float(v[i]), scale));
+            }
+            sm.red_max[grp][rl] = mx;
+            atc_soft_sync();
+            mx = fmaxf(mx, sm.red_max[grp ^ 1][rl]);
+            double sum = 0.0;
+            float oacc[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) oacc[i] = 0.f;
+            int drained = 0;  // chunks of this tile added into oacc
+            // adds chunk d's accumulator (this thread's row, 16 columns) into
+            // oacc and releases it; every softmax warp drains every chunk
+            auto drain_chunk = [&](int d) {
+                const uint32_t g = gch + d;
+                const int buf = g & 1;
+                atc_wait(sm.abort, err, kAtcErrEpilogue, &sm.acc_full[buf], (g >> 1) & 1);
+                tc::tc_fence_after();
+                if (d <= last_vis) {  // otherwise this warp's rows of the chunk are zero
+                    uint32_t o[16];
+                    tc::tmem_ld_32x32b_x16(lane_base + kAtcColO + 32 * buf + 16 * grp, o);
+                    tc::tmem_ld_wait();
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) oacc[i] = __fadd_rn(oacc[i], __uint_as_float(o[i]));
+                }
+                tc::tc_fence_before();
+                __syncwarp();
+                if (lane == 0) tc::mbar_arrive(&sm.acc_empty[buf]);
+            };
+            for (int c = grp; c < nch; c += 2) {
+                const uint32_t g = gch + c;
+                const int slot = g % kAtcRing;
+                atc_wait(sm.abort, err, kAtcErrSoftmax, &sm.ring_empty[slot], ((g / kAtcRing) & 1) ^ 1);
+                tc::tc_fence_after();
+                uint32_t eh[32], el[32];
+                if (c <= last_vis) {
+                    tc::tmem_ld_32x32b_x32(lane_base + kAtcColS + 32 * c, eh);
+                    tc::tmem_ld_wait();
+                    float p0 = 0.f, p1 = 0.f;
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) {
+                        const float s = __uint_as_float(eh[i]);
+                        const float e = (valid && 32 * c + i <= r) ? expf(__fsub_rn(__fmul_rn(s, scale), mx)) : 0.f;
+                        if (i & 1) p1 += e; else p0 += e;
+                        const float hi = tf32_round(e);
+                        eh[i] = __float_as_uint(hi);
+                        el[i] = __float_as_uint(e - hi);
+                    }
+                    sum += double(p0) + double(p1);
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) { eh[i] = 0u; el[i] = 0u; }
+                }
+                tc::tmem_st_32x32b_x32(lane_base + kAtcColS + 32 * c, eh);
+                tc::tmem_st_32x32b_x32(lane_base + kAtcColRing + 32 * slot, el);
+                tc::tmem_st_wait();
+                tc::tc_fence_before();
+                __syncwarp();
+                if (lane == 0) tc::mbar_arrive(&sm.ring_full[slot]);
+                // chunks handed over at least one round ago are done or nearly
+                for (; drained <= c - 2; ++drained) drain_chunk(drained);
+            }
+            for (; drained < nch; ++drained) drain_chunk(drained);
+            gch += nch;
+            sm.red_sum[grp][rl] = sum;
+            atc_soft_sync();
+            const float sumf = float(sum + sm.red_sum[grp ^ 1][rl]);
+            if (valid) {
+                float* dst = ctx + (long)(y0 + r) * D + h * kAtcDH + 16 * grp;
+#pragma unroll
+                for (int i = 0; i < 16; i += 4)
+                    *reinterpret_cast<float4*>(dst + i) =
+                        make_float4(__fdiv_rn(oacc[i], sumf), __fdiv_rn(oacc[i + 1], sumf),
+                                    __fdiv_rn(oacc[i + 2], sumf), __fdiv_rn(oacc[i + 3], sumf));
+                if (grp == 0) {
+                    row_max[((long)b * H + h) * T + r] = mx;
+                    row_sum[((long)b * H + h) * T + r] = sumf;
+                }
+            }
+        }
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    if (warp == kAtcSoftWarps) {
+        tc::tc_fence_after();
+        tc::tmem_dealloc(tmem, kAtcCols);
+    }
+}
+
+}  // namespace hx

@@ -22,10 +22,16 @@
 //   then a butterfly over the warp), P = exp(S - max) / float(sum),
 //   O_blk = P V.  Row max and row sum are saved; P is written out only on
 //   request.
-// Backward (:80-81), with P recomputed bit-identically from the saved
-//   statistics (same score routine, same FMA order) and D_r = dO_r . O_r:
+// Backward (:79-81), with P recomputed from the saved row max by the same
+//   score routine and FMA order, its row sum recomputed from these same
+//   exponentials in the forward's summation order (bit-identical to the
+//   forward's after this forward; after the tensor-core forward it keeps
+//   sum_j P[r][j] = 1 to FP32 rounding, which the wq/wk gradients of
+//   near-uniform attention are sensitive to), and, as the reference,
+//   D_r = sum_j P[r][j] dP[r][j] (float products summed in double):
 //   dV += P^T dO_blk, dP = dO_blk V^T, dS = P * (dP - D), dQ_blk = scale dS K,
-//   dK += scale dS^T Q_blk.
+//   dK += scale dS^T Q_blk.  Taking D from P and dP (rather than dO . O)
+//   keeps sum_j dS[r][j] = 0 whatever engine produced the forward output.
 // Limits: T <= 256, DH in {8, 16, 32}.
 #pragma once
 
@@ -57,7 +63,7 @@ struct AttnTiledLayout {
     }
     static size_t fwd_bytes(int T) { return sizeof(float) * (size_t(3) * tpad(T) * LD + blk_floats(T)); }
     static size_t bwd_bytes(int T) {
-        return sizeof(float) * (size_t(4) * tpad(T) * LD + blk_floats(T) + size_t(3) * T);
+        return sizeof(float) * (size_t(4) * tpad(T) * LD + blk_floats(T) + size_t(T));
     }
 };
 
@@ -307,9 +313,8 @@ attention_fwd_tiled_kernel(int T, int D, int H, float scale, const float* __rest
 template <int DH>
 __global__ void __launch_bounds__(kAttnTiledThreads, 1)
 attention_bwd_tiled_kernel(int T, int D, int H, float scale, const float* __restrict__ qkv,
-                           const float* __restrict__ ctx, const float* __restrict__ dctx,
-                           const float* __restrict__ row_max, const float* __restrict__ row_sum,
-                           float* __restrict__ dqkv)
+                           const float* __restrict__ dctx,
+                           const float* __restrict__ row_max, float* __restrict__ dqkv)
 {
     using Lay = AttnTiledLayout<DH>;
     constexpr int LD = Lay::LD, CW = DH / 4;
@@ -321,9 +326,7 @@ attention_bwd_tiled_kernel(int T, int D, int H, float scale, const float* __rest
     float* Vs = Ks + tpad * LD;
     float* Os = Vs + tpad * LD;          // dO (the incoming gradient of the context)
     float* Blk = Os + tpad * LD;         // [64][ldp] P, then dS, then [8][64][LD] dQ partials
-    float* Dr = Blk + Lay::blk_floats(T);  // [T] D_r = dO_r . O_r
-    float* Mx = Dr + T;                  // [T]
-    float* Sm = Mx + T;                  // [T]
+    float* Mx = Blk + Lay::blk_floats(T);  // [T]
     const int h = blockIdx.x, b = blockIdx.y;
     const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
     const long rowbase = (long)b * T;
@@ -332,27 +335,8 @@ attention_bwd_tiled_kernel(int T, int D, int H, float scale, const float* __rest
     attn_load_tile<DH>(Ks, qkv + rowbase * ld + D + h * DH, ld, T, tpad);
     attn_load_tile<DH>(Vs, qkv + rowbase * ld + 2 * D + h * DH, ld, T, tpad);
     attn_load_tile<DH>(Os, dctx + rowbase * D + h * DH, D, T, tpad);
-    for (int i = t; i < T; i += kAttnTiledThreads) {
-        Mx[i] = row_max[((long)b * H + h) * T + i];
-        Sm[i] = row_sum[((long)b * H + h) * T + i];
-    }
+    for (int i = t; i < T; i += kAttnTiledThreads) Mx[i] = row_max[((long)b * H + h) * T + i];
     attn_cp_async_wait_all();
-    __syncthreads();
-    // D_r = dO_r . O_r, one thread per row, FMA order d = 0..DH-1
-    for (int r = t; r < T; r += kAttnTiledThreads) {
-        const float* o = ctx + (rowbase + r) * D + h * DH;
-        float acc = 0.f;
-#pragma unroll
-        for (int d = 0; d < DH; d += 4) {
-            const float4 a = *reinterpret_cast<const float4*>(Os + r * LD + d);
-            const float4 c = *reinterpret_cast<const float4*>(o + d);
-            acc = fmaf(a.x, c.x, acc);
-            acc = fmaf(a.y, c.y, acc);
-            acc = fmaf(a.z, c.z, acc);
-            acc = fmaf(a.w, c.w, acc);
-        }
-        Dr[r] = acc;
-    }
     __syncthreads();
     // dK / dV accumulators: thread -> keys 4*kr .. 4*kr+3, columns [kc, kc+CW)
     const int kr = t >> 2, kc = (t & 3) * CW;
@@ -376,13 +360,24 @@ attention_bwd_tiled_kernel(int T, int D, int H, float scale, const float* __rest
             for (int i = 0; i < 8; ++i) {
                 const int r = q0 + 8 * warp + i;
                 const bool rv = r < T;
-                const float mx = rv ? Mx[r] : 0.f, sumf = rv ? Sm[r] : 1.f;
+                const float mx = rv ? Mx[r] : 0.f;
+                double sum = 0.0;
+#pragma unroll
+                for (int c = 0; c < 8; ++c) {
+                    const int j = lane + 32 * c;
+                    if (c < nc && rv && j <= r) {
+                        s[i][c] = expf(__fsub_rn(__fmul_rn(s[i][c], scale), mx));
+                        sum += s[i][c];
+                    }
+                }
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+                const float sumf = rv ? (float)sum : 1.f;
                 float* prow = Blk + (8 * warp + i) * ldp;
 #pragma unroll
                 for (int c = 0; c < 8; ++c) {
                     const int j = lane + 32 * c;
-                    if (c < nc)
-                        prow[j] = (rv && j <= r) ? __fdiv_rn(expf(__fsub_rn(__fmul_rn(s[i][c], scale), mx)), sumf) : 0.f;
+                    if (c < nc) prow[j] = (rv && j <= r) ? __fdiv_rn(s[i][c], sumf) : 0.f;
                 }
             }
         }
@@ -406,12 +401,20 @@ attention_bwd_tiled_kernel(int T, int D, int H, float scale, const float* __rest
                 }
             }
         }
-        // 4. dS = P * (dP - D), from this thread's own P entries
+        // 4. D_r = sum_j P dP (lane partials, then a butterfly over the
+        //    warp, in double), dS = P * (dP - D), from this thread's own P
+        //    entries (written by this thread in step 1)
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
             const int r = q0 + 8 * warp + i;
-            const float dr = r < T ? Dr[r] : 0.f;
             const float* prow = Blk + (8 * warp + i) * ldp;
+            double dot = 0.0;
+#pragma unroll
+            for (int c = 0; c < 8; ++c)
+                if (c < nc) dot += double(__fmul_rn(prow[lane + 32 * c], dp[i][c]));
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+            const float dr = float(dot);
 #pragma unroll
             for (int c = 0; c < 8; ++c)
                 if (c < nc) dp[i][c] = r < T ? __fmul_rn(prow[lane + 32 * c], __fsub_rn(dp[i][c], dr)) : 0.f;

@@ -145,6 +145,7 @@ struct hx_runtime {
     hx::DeviceBuffer err_flag; // device-side error word of bounded waits
     hx::Profiler prof;
     int gemm_backend = 0;      // HX_GEMM_AUTO / HX_GEMM_CUDA_CORES / HX_GEMM_TENSOR_CORES
+    int attention_backend = 0; // HX_ATTN_AUTO / HX_ATTN_CUDA_CORES
 
     ~hx_runtime();
     void activate() const { hx::check_cuda(cudaSetDevice(device), "cudaSetDevice"); }
@@ -169,8 +170,9 @@ struct hx_runtime {
         hx::check_cuda(cudaMemcpy(&code, err_flag.ptr, sizeof(int), cudaMemcpyDeviceToHost), "cudaMemcpy");
         if (code) {
             hx::check_cuda(cudaMemset(err_flag.ptr, 0, sizeof(int)), "cudaMemset");
-            hx::fail(HX_ERR_CUDA, "DEVICE_WAIT_TIMEOUT: a bounded pipeline wait in the tensor-core GEMM gave up (role " +
-                                      std::to_string(code) + "); results of this call are invalid");
+            hx::fail(HX_ERR_CUDA, std::string("DEVICE_WAIT_TIMEOUT: a bounded pipeline wait in the tensor-core ") +
+                                      (code >= 10 ? "attention" : "GEMM") + " gave up (role " + std::to_string(code) +
+                                      "); results of this call are invalid");
         }
     }
     // Record the outcome of an execute call (ApiTrace counters).

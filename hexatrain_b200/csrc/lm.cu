@@ -14,6 +14,7 @@
 // Backward mirrors :79-82 with the same named gradients in registry order.
 #include <cmath>
 
+#include "attention_tc.cuh"
 #include "attention_tiled.cuh"
 #include "gemm.cuh"
 #include "lm_kernels.cuh"
@@ -127,10 +128,31 @@ constexpr int kAttnThreads = 256;
 
 bool attn_tiled(int T, int DH) { return T <= kAttnMaxT && (DH == 8 || DH == 16 || DH == 32); }
 
+// Tensor-core attention: head dimension 32, T <= 256, no probability
+// output, 16-byte aligned rows (the model width is a multiple of 32).
+bool attn_tc(hx_runtime* rt, int T, int DH, const float* probs) {
+    return rt->attention_backend == HX_ATTN_AUTO && DH == kAtcDH && T <= kAtcMaxT && !probs;
+}
+
+void attn_fwd_tc_launch(hx_runtime* rt, const LmPlan& p, const float* qkv, float* ctx, float* rmax, float* rsum) {
+    const uint64_t rows = uint64_t(p.B) * p.T, w = 3 * uint64_t(p.D);
+    const CUtensorMap mqk = make_map(qkv, w, rows, w, 32, kAtcTile);
+    const CUtensorMap mv = make_map(qkv, w, rows, w, 32, kAtcTile, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
+    HX_CUDA(cudaFuncSetAttribute(attention_fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)kAtcFwdSmemBytes));
+    attention_fwd_tc_kernel<<<dim3(p.H, p.B), kAtcThreads, kAtcFwdSmemBytes, rt->stream>>>(
+        mqk, mv, p.T, p.D, p.H, 1.0f / sqrtf((float)kAtcDH), ctx, rmax, rsum, rt->device_error());
+    HX_LAUNCHED(rt);
+}
+
 template <int DH>
 void attn_fwd_launch(hx_runtime* rt, const LmPlan& p, const float* qkv, float* ctx, float* rmax, float* rsum, float* probs) {
     const double pairs = double(p.B) * p.H * (double(p.T) * (p.T + 1) / 2);
     ProfScope prof(rt, kTagAttnFwd, 4.0 * pairs * DH, 4.0 * (double(p.M) * 4 * p.D + 2.0 * p.B * p.H * p.T));
+    if (attn_tc(rt, p.T, DH, probs)) {
+        attn_fwd_tc_launch(rt, p, qkv, ctx, rmax, rsum);
+        return;
+    }
     if constexpr (DH == 8 || DH == 16 || DH == 32) {
         if (attn_tiled(p.T, DH)) {
             const size_t smem = AttnTiledLayout<DH>::fwd_bytes(p.T);
@@ -148,16 +170,16 @@ void attn_fwd_launch(hx_runtime* rt, const LmPlan& p, const float* qkv, float* c
     HX_LAUNCHED(rt);
 }
 template <int DH>
-void attn_bwd_launch(hx_runtime* rt, const LmPlan& p, const float* qkv, const float* ctx, const float* dctx,
-                     const float* rmax, const float* rsum, float* dqkv) {
+void attn_bwd_launch(hx_runtime* rt, const LmPlan& p, const float* qkv, const float* dctx, const float* rmax,
+                     const float* rsum, float* dqkv) {
     const double pairs = double(p.B) * p.H * (double(p.T) * (p.T + 1) / 2);
-    ProfScope prof(rt, kTagAttnBwd, 8.0 * pairs * DH, 4.0 * (double(p.M) * 7 * p.D + 2.0 * p.B * p.H * p.T));
+    ProfScope prof(rt, kTagAttnBwd, 8.0 * pairs * DH, 4.0 * (double(p.M) * 6 * p.D + 2.0 * p.B * p.H * p.T));
     if constexpr (DH == 8 || DH == 16 || DH == 32) {
         if (attn_tiled(p.T, DH)) {
             const size_t smem = AttnTiledLayout<DH>::bwd_bytes(p.T);
             HX_CUDA(cudaFuncSetAttribute(attention_bwd_tiled_kernel<DH>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
             attention_bwd_tiled_kernel<DH><<<dim3(p.H, p.B), kAttnTiledThreads, smem, rt->stream>>>(
-                p.T, p.D, p.H, 1.0f / sqrtf((float)DH), qkv, ctx, dctx, rmax, rsum, dqkv);
+                p.T, p.D, p.H, 1.0f / sqrtf((float)DH), qkv, dctx, rmax, dqkv);
             HX_LAUNCHED(rt);
             return;
         }
@@ -309,8 +331,8 @@ void forward_backward(hx_runtime* rt, LmPlan& p, const float* W, float* G, float
         HX_LAUNCHED(rt);
         gemm<true, false>(rt, D, D, M, a.at<float>(A.ctx), D, dr, D, EpiStore{G + o.wo, (long)D, 0, 0});
         gemm<false, true>(rt, M, D, D, dr, D, W + o.wo, D, EpiStore{dc, (long)D, 0, 0});
-        HX_DH_DISPATCH(p.dh, attn_bwd_launch, rt, p, a.at<float>(A.qkv), a.at<float>(A.ctx), dc, a.at<float>(A.rmax),
-                       a.at<float>(A.rsum), dqkv);
+        HX_DH_DISPATCH(p.dh, attn_bwd_launch, rt, p, a.at<float>(A.qkv), dc, a.at<float>(A.rmax), a.at<float>(A.rsum),
+                       dqkv);
         gemm<true, false>(rt, D, 3 * D, M, a.at<float>(A.n1), D, dqkv, 3 * D,
                           EpiStore{G + o.wq, (long)D, (int)D, (long)D * D});
         gemm<false, true>(rt, M, D, 3 * D, dqkv, 3 * D, wqkv + size_t(li) * 3 * D * D, 3 * D, EpiStore{dn, (long)D, 0, 0});

@@ -95,6 +95,14 @@ int hx_runtime_set_gemm_backend(hx_runtime* rt, int backend) {
     });
 }
 
+int hx_runtime_set_attention_backend(hx_runtime* rt, int backend) {
+    return hx_guard(rt, [&] {
+        hx::require(backend == HX_ATTN_AUTO || backend == HX_ATTN_CUDA_CORES, HX_ERR_ARGUMENT,
+                    "unknown attention backend");
+        rt->attention_backend = backend;
+    });
+}
+
 int hx_runtime_metrics(const hx_runtime* rt, hx_metrics* out) {
     if (!rt || !out) return HX_ERR_ARGUMENT;
     *out = rt->metrics;

@@ -319,6 +319,10 @@ class Runtime:
         """0 = auto (tensor cores for large aligned GEMMs), 1 = CUDA cores, 2 = tensor cores when aligned."""
         return self._need() and self._ok(self._lib.hx_runtime_set_gemm_backend(self._rt, int(backend)))
 
+    def set_attention_backend(self, backend: int) -> bool:
+        """0 = auto (tensor cores for head dimension 32, T <= 256), 1 = CUDA cores everywhere."""
+        return self._need() and self._ok(self._lib.hx_runtime_set_attention_backend(self._rt, int(backend)))
+
     def profile(self, enable: bool) -> bool:
         """Start/stop per-kernel-class CUDA-event timing (hx_runtime_profile)."""
         return self._need() and self._ok(self._lib.hx_runtime_profile(self._rt, int(bool(enable))))

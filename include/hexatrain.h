@@ -88,6 +88,14 @@ int hx_runtime_inject_execute_failure(hx_runtime* rt, int64_t call_index);
 enum { HX_GEMM_AUTO = 0, HX_GEMM_CUDA_CORES = 1, HX_GEMM_TENSOR_CORES = 2 };
 int hx_runtime_set_gemm_backend(hx_runtime* rt, int backend);
 
+/* Attention engine selection.  AUTO (default) runs causal attention with
+ * head dimension 32 and at most 256 tokens on the tensor cores (3xTF32
+ * products, softmax on the CUDA cores) unless attention probabilities are
+ * requested as a diagnostic output; CUDA_CORES forces the FP32 CUDA-core
+ * kernels everywhere (tests use this to compare the two). */
+enum { HX_ATTN_AUTO = 0, HX_ATTN_CUDA_CORES = 1 };
+int hx_runtime_set_attention_backend(hx_runtime* rt, int backend);
+
 /* Per-kernel-class timing with CUDA events recorded on the runtime stream
  * around every launch while enabled (the counterpart of RuntimeMetrics'
  * executeUs lists, qnn/qnn_runtime.h:68, at kernel granularity).  Steps run
