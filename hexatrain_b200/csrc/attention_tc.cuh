@@ -7,18 +7,19 @@
 //
 // Forward (tiny_language_model_cpu.cpp:44-45: scores, causal softmax,
 // context), one CTA per (head, sequence), query rows in tiles of 128:
-//   warp 8 lane 0  TMA: Q, K, V rows [128t, 128t+128) of this head for each
+//   warp 16 lane 0 TMA: Q, K, V rows [128t, 128t+128) of this head for each
 //                  tile t, Q/K in the 128-byte swizzle (K-major operands),
 //                  V in the 128-byte/32-byte-atom swizzle (MN-major B);
 //                  then the MMA issuer.
-//   warps 0-7      split each landed tile into hi (in place) and lo; then
+//   warps 0-15     split each landed tile into hi (in place) and lo; then
 //                  the softmax of tile t, one TMEM lane (query row) per
-//                  thread pair: warp w reads lanes 32(w%4).. and the 32-key
-//                  chunks c = w/4, w/4 + 2, ...
+//                  four threads: warp w reads lanes 32(w%4).. and the
+//                  32-key chunks c = w/4, w/4 + 4, ...
 // Per tile t (N = 128(t+1) keys):
 //   S  = Q_t K[0:N]^T          12 MMAs M128 N(N) K8 into TMEM columns [0, N)
 //   m  = max_j<=r S[r][j] * scale        (pass 1 over the chunks)
-//   e  = exp(S * scale - m) (0 where j > r), sum = sum_j e   (pass 2)
+//   e  = exp(S * scale - m) (0 where j > r), sum = sum_j e   (pass 2),
+//        as 2^(S * scale * log2 e - m * log2 e) with the hardware ex2
 //        e is split into hi (written back over S) and lo (a 6-slot ring of
 //        32-column TMEM chunks); each finished chunk is handed to the MMA
 //        issuer, which computes E_c V_c into a fresh 32-column accumulator
@@ -43,19 +44,20 @@
 namespace hx {
 
 constexpr int kAtcDH = 32, kAtcMaxT = 256, kAtcTile = 128;
-constexpr int kAtcSoftWarps = 8;
+constexpr int kAtcSoftWarps = 16, kAtcGroups = 4;  // warps w, w+4, w+8, w+12 share lane quadrant w%4
 constexpr int kAtcSoftThreads = 32 * kAtcSoftWarps;
 constexpr int kAtcThreads = kAtcSoftThreads + 32;
 constexpr int kAtcRing = 6;
 constexpr uint32_t kAtcCols = 512, kAtcColS = 0, kAtcColO = 256, kAtcColRing = 320;
 constexpr int kAtcTileFloats = kAtcTile * kAtcDH;  // 128 rows x 32 fp32 = 16 KB
+constexpr float kAtcLog2e = 1.4426950408889634f;
 
 struct AtcFwdSmem {
     float qh[2 * kAtcTileFloats], ql[2 * kAtcTileFloats];
     float kh[2 * kAtcTileFloats], kl[2 * kAtcTileFloats];
     float vh[2 * kAtcTileFloats], vl[2 * kAtcTileFloats];
-    float red_max[2][kAtcTile];
-    double red_sum[2][kAtcTile];
+    float red_max[kAtcGroups][kAtcTile];
+    double red_sum[kAtcGroups][kAtcTile];
     uint64_t ld[2], conv[2], pv_done[2], s_ready, ring_full[kAtcRing], ring_empty[kAtcRing];
     uint64_t acc_full[2], acc_empty[2], drain;
     uint32_t tmem_addr;
@@ -77,8 +79,8 @@ __device__ __forceinline__ bool atc_wait(int& abort, int* err, int code, uint64_
     return false;
 }
 
-// Barrier among the 256 softmax threads only (the issuer warp never joins).
-__device__ __forceinline__ void atc_soft_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+// Barrier among the softmax threads only (the issuer warp never joins).
+__device__ __forceinline__ void atc_soft_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kAtcSoftThreads) : "memory"); }
 
 // hi = nearest TF32 (in place), lo = x - hi, for n4 float4s.
 __device__ __forceinline__ void atc_split(float* hi, float* lo, int n4, int t, int nt) {
@@ -220,98 +222,116 @@ attention_fwd_tc_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid
             tc::mbar_arrive(&sm.conv[t]);
         }
         // ---------------- softmax and epilogue ----------------
+        // e = 2^(s * scale * log2(e) - m * log2(e)): one FFMA and one ex2
+        // per score; the per-row constant's rounding cancels in e / sum.
+        const float c1 = scale * kAtcLog2e;
         const uint32_t lane_base = tmem + (uint32_t(32 * q) << 16);
         const int rl = 32 * q + lane;
         uint32_t gch = 0;
         for (int t = 0; t < ntile; ++t) {
             const int nch = 4 * (t + 1);
             const int r = kAtcTile * t + rl;
-            const bool valid = r < T;
-            const int last_vis = 4 * t + q;  // later chunks hold no key visible to this warp's rows
+            const int lim = r < T ? r : -1;                   // last key visible to this row
+            const int diag = 4 * t + q;                       // chunk on this warp's diagonal
+            const bool rows_valid = kAtcTile * t + 32 * q + 31 < T;  // every row of the warp is < T
             atc_wait(sm.abort, err, kAtcErrSoftmax, &sm.s_ready, t & 1);
             tc::tc_fence_after();
-            float mx = -INFINITY;
-            for (int c = grp; c <= last_vis; c += 2) {
+            // pass 1: max of the raw scores (scale > 0 commutes with max)
+            float mraw = -INFINITY;
+            for (int c = grp; c <= diag; c += kAtcGroups) {
                 uint32_t v[32];
                 tc::tmem_ld_32x32b_x32(lane_base + kAtcColS + 32 * c, v);
                 tc::tmem_ld_wait();
+                if (c < diag && rows_valid) {
 #pragma unroll
-                for (int i = 0; i < 32; ++i)
-                    if (32 * c + i <= r) mx = fmaxf(mx, __fmul_rn(__uint_as_float(v[i]), scale));
+                    for (int i = 0; i < 32; ++i) mraw = fmaxf(mraw, __uint_as_float(v[i]));
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 32; ++i)
+                        if (32 * c + i <= lim) mraw = fmaxf(mraw, __uint_as_float(v[i]));
+                }
             }
-            sm.red_max[grp][rl] = mx;
+            sm.red_max[grp][rl] = mraw;
             atc_soft_sync();
-            mx = fmaxf(mx, sm.red_max[grp ^ 1][rl]);
+            mraw = fmaxf(fmaxf(sm.red_max[0][rl], sm.red_max[1][rl]), fmaxf(sm.red_max[2][rl], sm.red_max[3][rl]));
+            const float m = __fmul_rn(mraw, scale);
+            const float negml = __fmul_rn(m, -kAtcLog2e);
             double sum = 0.0;
-            float oacc[16];
+            float oacc[8];
 #pragma unroll
-            for (int i = 0; i < 16; ++i) oacc[i] = 0.f;
+            for (int i = 0; i < 8; ++i) oacc[i] = 0.f;
             int drained = 0;  // chunks of this tile added into oacc
-            // adds chunk d's accumulator (this thread's row, 16 columns) into
+            // adds chunk d's accumulator (this thread's row, 8 columns) into
             // oacc and releases it; every softmax warp drains every chunk
             auto drain_chunk = [&](int d) {
                 const uint32_t g = gch + d;
                 const int buf = g & 1;
                 atc_wait(sm.abort, err, kAtcErrEpilogue, &sm.acc_full[buf], (g >> 1) & 1);
                 tc::tc_fence_after();
-                if (d <= last_vis) {  // otherwise this warp's rows of the chunk are zero
-                    uint32_t o[16];
-                    tc::tmem_ld_32x32b_x16(lane_base + kAtcColO + 32 * buf + 16 * grp, o);
+                if (d <= diag) {  // otherwise this warp's rows of the chunk are zero
+                    uint32_t o[8];
+                    tc::tmem_ld_32x32b_x8(lane_base + kAtcColO + 32 * buf + 8 * grp, o);
                     tc::tmem_ld_wait();
 #pragma unroll
-                    for (int i = 0; i < 16; ++i) oacc[i] = __fadd_rn(oacc[i], __uint_as_float(o[i]));
+                    for (int i = 0; i < 8; ++i) oacc[i] = __fadd_rn(oacc[i], __uint_as_float(o[i]));
                 }
                 tc::tc_fence_before();
                 __syncwarp();
                 if (lane == 0) tc::mbar_arrive(&sm.acc_empty[buf]);
             };
-            for (int c = grp; c < nch; c += 2) {
+            // pass 2: e, its hi/lo split, the hand-over to the MMA issuer
+            for (int c = grp; c < nch; c += kAtcGroups) {
                 const uint32_t g = gch + c;
                 const int slot = g % kAtcRing;
                 atc_wait(sm.abort, err, kAtcErrSoftmax, &sm.ring_empty[slot], ((g / kAtcRing) & 1) ^ 1);
                 tc::tc_fence_after();
-                uint32_t eh[32], el[32];
-                if (c <= last_vis) {
-                    tc::tmem_ld_32x32b_x32(lane_base + kAtcColS + 32 * c, eh);
-                    tc::tmem_ld_wait();
-                    float p0 = 0.f, p1 = 0.f;
+                const bool full = c < diag && rows_valid;
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) {
-                        const float s = __uint_as_float(eh[i]);
-                        const float e = (valid && 32 * c + i <= r) ? expf(__fsub_rn(__fmul_rn(s, scale), mx)) : 0.f;
-                        if (i & 1) p1 += e; else p0 += e;
-                        const float hi = tf32_round(e);
-                        eh[i] = __float_as_uint(hi);
-                        el[i] = __float_as_uint(e - hi);
+                for (int half = 0; half < 2; ++half) {  // 16 columns at a time keeps 32 values live
+                    const uint32_t col = 32 * c + 16 * half;
+                    uint32_t eh[16], el[16];
+                    if (c <= diag) {
+                        tc::tmem_ld_32x32b_x16(lane_base + kAtcColS + col, eh);
+                        tc::tmem_ld_wait();
+                        float p0 = 0.f, p1 = 0.f;
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) {
+                            float e = tc::exp2_approx(fmaf(__uint_as_float(eh[i]), c1, negml));
+                            if (!full && int(col) + i > lim) e = 0.f;
+                            if (i & 1) p1 += e; else p0 += e;
+                            eh[i] = tc::tf32_rna_bits(e);
+                            el[i] = __float_as_uint(e - __uint_as_float(eh[i]));
+                        }
+                        sum += double(p0) + double(p1);
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) { eh[i] = 0u; el[i] = 0u; }
                     }
-                    sum += double(p0) + double(p1);
-                } else {
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) { eh[i] = 0u; el[i] = 0u; }
+                    tc::tmem_st_32x32b_x16(lane_base + kAtcColS + col, eh);
+                    tc::tmem_st_32x32b_x16(lane_base + kAtcColRing + 32 * slot + 16 * half, el);
                 }
-                tc::tmem_st_32x32b_x32(lane_base + kAtcColS + 32 * c, eh);
-                tc::tmem_st_32x32b_x32(lane_base + kAtcColRing + 32 * slot, el);
                 tc::tmem_st_wait();
                 tc::tc_fence_before();
                 __syncwarp();
                 if (lane == 0) tc::mbar_arrive(&sm.ring_full[slot]);
-                // chunks handed over at least one round ago are done or nearly
-                for (; drained <= c - 2; ++drained) drain_chunk(drained);
+                // chunks handed over a round ago are done or nearly
+                for (; drained <= c - kAtcGroups; ++drained) drain_chunk(drained);
             }
             for (; drained < nch; ++drained) drain_chunk(drained);
             gch += nch;
             sm.red_sum[grp][rl] = sum;
             atc_soft_sync();
-            const float sumf = float(sum + sm.red_sum[grp ^ 1][rl]);
-            if (valid) {
-                float* dst = ctx + (long)(y0 + r) * D + h * kAtcDH + 16 * grp;
+            const float sumf =
+                float(((sm.red_sum[0][rl] + sm.red_sum[1][rl]) + sm.red_sum[2][rl]) + sm.red_sum[3][rl]);
+            if (r < T) {
+                float* dst = ctx + (long)(y0 + r) * D + h * kAtcDH + 8 * grp;
 #pragma unroll
-                for (int i = 0; i < 16; i += 4)
+                for (int i = 0; i < 8; i += 4)
                     *reinterpret_cast<float4*>(dst + i) =
                         make_float4(__fdiv_rn(oacc[i], sumf), __fdiv_rn(oacc[i + 1], sumf),
                                     __fdiv_rn(oacc[i + 2], sumf), __fdiv_rn(oacc[i + 3], sumf));
                 if (grp == 0) {
-                    row_max[((long)b * H + h) * T + r] = mx;
+                    row_max[((long)b * H + h) * T + r] = m;
                     row_sum[((long)b * H + h) * T + r] = sumf;
                 }
             }
