@@ -15,6 +15,7 @@
 #include <cmath>
 
 #include "attention_tc.cuh"
+#include "attention_tc_bwd.cuh"
 #include "attention_tiled.cuh"
 #include "gemm.cuh"
 #include "lm_kernels.cuh"
@@ -58,6 +59,7 @@ struct LmPlan {
     std::vector<LayerActs> la;
     size_t xL, logits, probs, row_loss, row_correct, loss, acc, scalars;
     size_t dout, dr, dc, dn, df1, dqkv, ln_part;
+    size_t attn_bstat;  // tensor-core attention backward: per (sequence, head, row) sum and D
     size_t diag_lig, diag_hp, diag_dout;
     size_t muon_table;
     int ln_parts = 0, ln_rows = 0;
@@ -169,11 +171,40 @@ void attn_fwd_launch(hx_runtime* rt, const LmPlan& p, const float* qkv, float* c
         p.T, p.D, p.H, 1.0f / sqrtf((float)DH), qkv, ctx, rmax, rsum, probs);
     HX_LAUNCHED(rt);
 }
+// dQ kernel (queries on lanes, writes the backward's row statistics), then
+// the dK/dV kernel (keys on lanes, one CTA per 128-key block).
+void attn_bwd_tc_launch(hx_runtime* rt, const LmPlan& p, const float* qkv, const float* dctx, const float* rmax,
+                        float* dqkv) {
+    const uint64_t rows = uint64_t(p.B) * p.T, w = 3 * uint64_t(p.D);
+    constexpr CUtensorMapSwizzle mn = CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B;
+    const CUtensorMap mqk = make_map(qkv, w, rows, w, 32, kAtcTile);
+    const CUtensorMap mmn = make_map(qkv, w, rows, w, 32, kAtcTile, mn);
+    const CUtensorMap mdo = make_map(dctx, p.D, rows, p.D, 32, kAtcTile);
+    const CUtensorMap mdo_mn = make_map(dctx, p.D, rows, p.D, 32, kAtcTile, mn);
+    float* bstat = p.arena.at<float>(p.attn_bstat);
+    const float scale = 1.0f / sqrtf((float)kAtcDH);
+    HX_CUDA(cudaFuncSetAttribute(attention_bwd_dq_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)kAtcDqSmemBytes));
+    attention_bwd_dq_tc_kernel<<<dim3(p.H, p.B), kAtcThreads, kAtcDqSmemBytes, rt->stream>>>(
+        mqk, mmn, p.T, p.D, p.H, scale, qkv, dctx, rmax, bstat, dqkv, rt->device_error());
+    HX_LAUNCHED(rt);
+    HX_CUDA(cudaFuncSetAttribute(attention_bwd_dkdv_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)kAtcKvSmemBytes));
+    const int ntile = p.T > uint32_t(kAtcTile) ? 2 : 1;
+    attention_bwd_dkdv_tc_kernel<<<dim3(p.H, p.B, ntile), kAtcThreads, kAtcKvSmemBytes, rt->stream>>>(
+        mqk, mmn, mdo, mdo_mn, p.T, p.D, p.H, scale, rmax, bstat, dqkv, rt->device_error());
+    HX_LAUNCHED(rt);
+}
+
 template <int DH>
 void attn_bwd_launch(hx_runtime* rt, const LmPlan& p, const float* qkv, const float* dctx, const float* rmax,
                      const float* rsum, float* dqkv) {
     const double pairs = double(p.B) * p.H * (double(p.T) * (p.T + 1) / 2);
     ProfScope prof(rt, kTagAttnBwd, 8.0 * pairs * DH, 4.0 * (double(p.M) * 6 * p.D + 2.0 * p.B * p.H * p.T));
+    if (attn_tc(rt, p.T, DH, nullptr)) {
+        attn_bwd_tc_launch(rt, p, qkv, dctx, rmax, dqkv);
+        return;
+    }
     if constexpr (DH == 8 || DH == 16 || DH == 32) {
         if (attn_tiled(p.T, DH)) {
             const size_t smem = AttnTiledLayout<DH>::bwd_bytes(p.T);
@@ -560,6 +591,7 @@ int hx_lm_prepare(hx_runtime* rt, const hx_lm_config* cfg, uint32_t batch, int d
         p.dn = a.reserve(f * M * D);
         p.df1 = a.reserve(f * M * F);
         p.dqkv = a.reserve(f * M * 3 * D);
+        p.attn_bstat = a.reserve(f * 2 * B * H * T);
         p.ln_parts = std::max(1, std::min<int>(p.M, 2 * rt->sm_count));
         p.ln_rows = (p.M + p.ln_parts - 1) / p.ln_parts;
         p.ln_parts = (p.M + p.ln_rows - 1) / p.ln_rows;
