@@ -66,8 +66,9 @@ inline EncodeTiledFn encode_tiled() {
 
 // Row-major FP32 matrix [outer][inner] with leading dimension ld (elements),
 // boxes of box_inner x box_outer, zero fill out of bounds.  K-major operand
-// tiles use the 128B swizzle; MN-major ones the 128B swizzle with 32-byte
-// atoms (the layout the MMA requires for MN-major 32-bit operands).
+// tiles use the 128B swizzle; MN-major B tiles the 128B swizzle with 32-byte
+// atoms (the layout the MMA requires for MN-major 32-bit operands); MN-major
+// A tiles, read by threads rather than the MMA, no swizzle.
 inline CUtensorMap make_map(const float* base, uint64_t inner, uint64_t outer, uint64_t ld, uint32_t box_inner,
                             uint32_t box_outer, CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B) {
     CUtensorMap m;
@@ -98,8 +99,8 @@ void launch_tc(hx_runtime* rt, int M, int N, int K, const float* A, long lda, co
     // B(k,n): BT=false -> MN-major [K][N];      BT=true -> K-major [N][K].
     constexpr bool A_MN = AT, B_MN = !BT;
     constexpr CUtensorMapSwizzle mn_swz = CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B;
-    const CUtensorMap ma = A_MN ? make_map(A, M, K, lda, 32, 32, mn_swz) : make_map(A, K, M, lda, 32, 128);
-    const CUtensorMap mb = B_MN ? make_map(B, N, K, ldb, 32, 32, mn_swz) : make_map(B, K, N, ldb, 32, 128);
+    const CUtensorMap ma = A_MN ? make_map(A, M, K, lda, 128, 32, CU_TENSOR_MAP_SWIZZLE_NONE) : make_map(A, K, M, lda, 32, 128);
+    const CUtensorMap mb = B_MN ? make_map(B, N, K, ldb, 32, 32, mn_swz) : make_map(B, K, N, ldb, 32, kTcBN);
     const TcGrid g = tc_grid(M, N, K, rt->sm_count, 64);
     int* err = rt->device_error();
     float* ws = g.splits > 1 ? rt->workspace(sizeof(float) * (size_t)g.splits * M * N) : nullptr;

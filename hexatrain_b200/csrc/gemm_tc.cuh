@@ -1,46 +1,59 @@
 // gemm_tc.cuh -- FP32-accurate GEMM on the 5th-generation tensor cores.
 //
-// C[M,N] = op(A)[M,K] * op(B)[K,N] in "3xTF32": every operand x is split in
-// shared memory into hi = x rounded to the nearest TF32 value and
-// lo = x - hi (exact in FP32), and the accumulator collects
-// hi*hi + hi*lo + lo*hi in FP32 in TMEM.  The dropped lo*lo term and the
-// truncation of lo to TF32 leave a relative error near 2^-21 per product,
-// against 2^-11 for plain TF32 -- close to a CUDA-core FP32 GEMM.
+// C[M,N] = op(A)[M,K] * op(B)[K,N] in "3xTF32": every operand x is split
+// into hi = x rounded to the nearest TF32 value and lo = x - hi (exact in
+// FP32), and the accumulator collects hi*hi + hi*lo + lo*hi in FP32 in TMEM.
+// The dropped lo*lo term and the truncation of lo to TF32 leave a relative
+// error near 2^-21 per product, against 2^-11 for plain TF32 -- close to a
+// CUDA-core FP32 GEMM.
 //
 // The MMA's FP32 accumulation truncates, which biases long sums toward
-// zero; so each 32-deep k-block is accumulated fresh in TMEM and drained
-// into FP32 registers with round-to-nearest adds.  Measured against fp64 on
-// random matrices this matches a CUDA-core FP32 GEMM (max error ~4e-7 of
-// max|C| at K = 1024..16384).
+// zero; so each 32-deep k-block is accumulated fresh in TMEM, with the small
+// hi*lo and lo*hi terms issued before hi*hi (four full-magnitude truncations
+// per k-block), and drained into FP32 registers with round-to-nearest adds.
+//
+// Tile shape.  A kind::tf32 MMA with M = 128, K = 8 costs about 120 cycles
+// whether N is 64 or 128, and about 140 at N = 256 with A read from TMEM
+// (measured on B200: 592 vs 1020 TFLOP/s of TF32 per GPU), so tiles are
+// 128 x 256.  A lives in TMEM: the A tile of each k-block is split by four
+// warps, one tile row per thread, straight from the landed raw tile into a
+// TMEM slot (hi 32 columns, lo 32 columns); the MMA reads only B (hi and lo)
+// from shared memory.  TMEM: the 256-column accumulator and three A slots.
+// The accumulator is single-buffered; the drain warps release it as soon as
+// their TMEM loads have landed, before adding.
 //
 // Persistent: the grid is at most one CTA per SM, and each CTA walks work
-// units u = blockIdx.x, blockIdx.x + gridDim.x, ...  A unit is one 128x128
+// units u = blockIdx.x, blockIdx.x + gridDim.x, ...  A unit is one 128x256
 // output tile of one K split; units are numbered with the N tile fastest so
 // that CTAs running together share A row blocks in L2.  The operand ring and
-// the accumulator buffers run on across unit boundaries, so the epilogue of
-// one tile overlaps the k-loop of the next.
+// the A slots run on across unit boundaries, so the epilogue of one tile
+// overlaps the next tile's first k-block.
 //
-// Roles (16 warps):
-//   warp 0      TMA producer: 128B-swizzled tiles of A and B per 32-deep
-//               k-block into a 3-stage ring (full[] barriers, expect_tx);
-//   warp 1      TMEM owner and MMA issuer: 4 k-steps x 3 tcgen05.mma
-//               (M128 N128 K8, kind::tf32) per k-block into accumulator
-//               buffer g%4 (g counts this CTA's k-blocks); tcgen05.commit
-//               frees the smem stage (empty[]) and hands the buffer to the
-//               drain warps (acc_ready[]);
-//   warps 2-7   split each landed stage into hi (in place) and lo, fence the
-//               generic->async proxy, arrive on lo_ready[];
-//   warps 8-15  drain: one TMEM row per thread, 64 columns per warp, added
-//               into FP32 registers; release the buffer (acc_free[]); at the
-//               end of a unit, stage the 32x64 block through shared memory
-//               16 columns at a time so that each store instruction writes
-//               two 64-byte row segments (coalesced), applying the epilogue
-//               functor (or storing split-K partials); the epilogue's own
-//               global inputs for a chunk are loaded before any is used.
-// Operands may be K-major or MN-major (instruction-descriptor bits 15/16).
-// K-major tiles use the 128-byte swizzle; MN-major tiles arrive as four
-// 32-wide TMA boxes (LBO = 4 KB) in the 128-byte/32-byte-atom swizzle, the
-// only shared-memory layout the MMA takes for MN-major 32-bit operands.
+// Roles (22 warps):
+//   warp 0      TMA producer: the raw A tile (16 KB) and the B tile (32 KB)
+//               of each 32-deep k-block into a 2-stage ring (full[]);
+//   warp 1      TMEM owner and MMA issuer: 12 tcgen05.mma (M128 N256 K8,
+//               kind::tf32, A from TMEM) per k-block; tcgen05.commit frees
+//               the B stage (empty[]) and the A slot (a_free[]) and hands the
+//               accumulator to the drain warps (acc_ready);
+//   warps 2-5   converters.  A: thread = tile row (TMEM lane 32(w%4) +
+//               lane) reads its 32 values of the raw tile, frees the raw A
+//               stage, writes hi/lo into A slot g%3 with tcgen05.st, arrives
+//               on a_ready[].  B: split the stage's B tile into hi (in place)
+//               and lo, fence the generic->async proxy, arrive on b_ready[];
+//   warps 6-21  drain: one TMEM row per thread, 64 columns per warp, added
+//               into FP32 registers; at the end of a unit, stage the 32x64
+//               block through shared memory 16 columns at a time so that each
+//               store instruction writes two 64-byte row segments
+//               (coalesced), applying the epilogue functor (or storing split-K
+//               partials); the epilogue's own global inputs for a chunk are
+//               loaded before any is used.
+// Layouts: a K-major A tile arrives 128B-swizzled (row m's 16-byte chunk c
+// at ((c ^ (m & 7)) << 4)), an MN-major A tile unswizzled (K-row k at
+// 512 k bytes, so that lanes read consecutive words).  B is K-major with the
+// 128-byte swizzle, or MN-major as eight 32-wide boxes (LBO = 4 KB) in the
+// 128-byte/32-byte-atom swizzle, the only shared-memory layout the MMA takes
+// for MN-major 32-bit operands.
 // Every barrier wait is bounded (tc::kWaitCycles); on timeout the kernel
 // records an error code, drains its own MMAs and TMA loads (bounded), frees
 // TMEM and returns.
@@ -52,24 +65,27 @@
 
 namespace hx {
 
-constexpr int kTcBM = 128, kTcBN = 128, kTcBK = 32, kTcStages = 3;
-constexpr int kTcTileFloats = 128 * 32;   // one 128 x 32 fp32 tile = 16 KB
-constexpr int kTcConvWarps = 6, kTcDrainWarps = 8;
+constexpr int kTcBM = 128, kTcBN = 256, kTcBK = 32, kTcStages = 2;
+constexpr int kTcATileFloats = kTcBM * kTcBK;  // 16 KB
+constexpr int kTcBTileFloats = kTcBN * kTcBK;  // 32 KB
+constexpr int kTcConvWarps = 4, kTcDrainWarps = 16;
 constexpr int kTcConvThreads = 32 * kTcConvWarps;
 constexpr int kTcFirstDrainWarp = 2 + kTcConvWarps;
-constexpr int kTcThreads = 32 * (kTcFirstDrainWarp + kTcDrainWarps);  // 512
-constexpr int kTcAccBufs = 4;
-constexpr uint32_t kTcTmemCols = 128 * kTcAccBufs;  // 512: four 128-column accumulators
+constexpr int kTcThreads = 32 * (kTcFirstDrainWarp + kTcDrainWarps);  // 704
+constexpr int kTcASlots = 3;
+constexpr uint32_t kTcTmemCols = 512;
+constexpr uint32_t kTcColA = kTcBN;  // A slots after the accumulator: 64 columns each (hi 32, lo 32)
+static_assert(kTcColA + 64 * kTcASlots <= kTcTmemCols, "TMEM budget");
 constexpr int kTcStageLd = 17;  // epilogue staging row stride (floats): 16 columns + 1 pad
 
 struct TcSmem {
-    float a_hi[kTcStages][kTcTileFloats];
-    float b_hi[kTcStages][kTcTileFloats];
-    float a_lo[kTcStages][kTcTileFloats];
-    float b_lo[kTcStages][kTcTileFloats];
+    float a_raw[kTcStages][kTcATileFloats];
+    float b_hi[kTcStages][kTcBTileFloats];
+    float b_lo[kTcStages][kTcBTileFloats];
     float stage[kTcDrainWarps][32 * kTcStageLd];
-    uint64_t full[kTcStages], lo_ready[kTcStages], empty[kTcStages];
-    uint64_t acc_ready[kTcAccBufs], acc_free[kTcAccBufs], drain;
+    uint64_t full[kTcStages], b_ready[kTcStages], empty[kTcStages];
+    uint64_t a_ready[kTcASlots], a_free[kTcASlots];
+    uint64_t acc_ready, acc_free, drain;
     uint32_t tmem_addr;
     int abort;
 };
@@ -111,14 +127,16 @@ __device__ __forceinline__ void tc_fail(TcSmem& sm, int* err, int code) {
 __device__ __forceinline__ bool tc_aborted(TcSmem& sm) { return *reinterpret_cast<volatile int*>(&sm.abort) != 0; }
 
 // Nearest TF32 value (ties away from zero): add half a TF32 ulp to the
-// magnitude bits, clear the 13 low mantissa bits.  Rounding (rather than
-// truncating) leaves lo = x - hi with either sign, so the MMA's own
-// truncation of lo does not bias the products.  Values within a TF32 ulp of
-// the largest float are truncated instead, so hi stays finite.
+// magnitude bits, clear the 13 low mantissa bits -- two integer operations,
+// which matters: the split of a 128x32 A tile and a 128x32 B tile per
+// k-block would otherwise fill the SM's integer pipe for as long as the
+// k-block's MMAs take.  Rounding (rather than truncating) leaves lo = x - hi
+// with either sign, so the MMA's own truncation of lo does not bias the
+// products.  NaN and infinity pass through; finite |x| >= 0x1.fffffp+127
+// (within half a TF32 ulp of FLT_MAX) rounds to infinity, outside the range
+// the tensor-core paths accept.
 __device__ __forceinline__ float tf32_round(float x) {
-    const uint32_t u = __float_as_uint(x);
-    const uint32_t r = ((u & 0x7FFFFFFFu) >= 0x7F7FF000u) ? (u & 0xFFFFE000u) : ((u + 0x1000u) & 0xFFFFE000u);
-    return __uint_as_float(r);
+    return __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xFFFFE000u);
 }
 __device__ __forceinline__ float4 tf32_hi(float4 x) {
     return make_float4(tf32_round(x.x), tf32_round(x.y), tf32_round(x.z), tf32_round(x.w));
@@ -139,13 +157,15 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
     if (threadIdx.x == 0) {
         for (int s = 0; s < kTcStages; ++s) {
             tc::mbar_init(&sm.full[s], 1);
-            tc::mbar_init(&sm.lo_ready[s], kTcConvThreads);
-            tc::mbar_init(&sm.empty[s], 1);
+            tc::mbar_init(&sm.b_ready[s], kTcConvThreads);
+            tc::mbar_init(&sm.empty[s], 1 + kTcConvWarps);  // the MMA's commit (B) + the A warps (raw A)
         }
-        for (int b = 0; b < kTcAccBufs; ++b) {
-            tc::mbar_init(&sm.acc_ready[b], 1);
-            tc::mbar_init(&sm.acc_free[b], 32 * kTcDrainWarps);
+        for (int j = 0; j < kTcASlots; ++j) {
+            tc::mbar_init(&sm.a_ready[j], kTcConvWarps);
+            tc::mbar_init(&sm.a_free[j], 1);
         }
+        tc::mbar_init(&sm.acc_ready, 1);
+        tc::mbar_init(&sm.acc_free, kTcDrainWarps);
         tc::mbar_init(&sm.drain, 1);
         sm.abort = 0;
         tc::fence_mbar_init();
@@ -178,20 +198,17 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                     const uint32_t ph = (it / kTcStages) & 1;
                     if (!tc::mbar_wait(&sm.empty[s], ph ^ 1)) { tc_fail(sm, err, kTcErrProducer); stop = true; break; }
                     if (tc_aborted(sm)) { stop = true; break; }
-                    tc::mbar_arrive_expect_tx(&sm.full[s], 2 * kTcTileFloats * 4);
+                    tc::mbar_arrive_expect_tx(&sm.full[s], (kTcATileFloats + kTcBTileFloats) * 4);
                     const int k = t.kbeg + kb * kTcBK;
-                    if (!A_MN) {
-                        tc::tma_load_2d(sm.a_hi[s], &map_a, &sm.full[s], k, t.m0);
-                    } else {
-#pragma unroll
-                        for (int c = 0; c < 4; ++c)
-                            tc::tma_load_2d(sm.a_hi[s] + c * 1024, &map_a, &sm.full[s], t.m0 + 32 * c, k);
-                    }
+                    if (!A_MN)
+                        tc::tma_load_2d(sm.a_raw[s], &map_a, &sm.full[s], k, t.m0);   // box 32 (K) x 128 rows
+                    else
+                        tc::tma_load_2d(sm.a_raw[s], &map_a, &sm.full[s], t.m0, k);   // box 128 (M) x 32 K-rows
                     if (!B_MN) {
-                        tc::tma_load_2d(sm.b_hi[s], &map_b, &sm.full[s], k, t.n0);
+                        tc::tma_load_2d(sm.b_hi[s], &map_b, &sm.full[s], k, t.n0);    // box 32 (K) x 256 rows
                     } else {
 #pragma unroll
-                        for (int c = 0; c < 4; ++c)
+                        for (int c = 0; c < kTcBN / 32; ++c)
                             tc::tma_load_2d(sm.b_hi[s] + c * 1024, &map_b, &sm.full[s], t.n0 + 32 * c, k);
                     }
                     issued[s] = true;
@@ -207,15 +224,13 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
     } else if (warp == 1) {
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
-            constexpr uint32_t idesc = tc::idesc_tf32(kTcBM, kTcBN, A_MN, B_MN);
-            // K-major: SW128, SBO 1024, k-step = 32 bytes along the row.
-            // MN-major: SW128 with 32-byte atoms, SBO 512, LBO 4 KB between
+            constexpr uint32_t idesc = tc::idesc_tf32(kTcBM, kTcBN, false, B_MN);
+            // B K-major: SW128, SBO 1024, k-step = 32 bytes along the row.
+            // B MN-major: SW128 with 32-byte atoms, SBO 512, LBO 4 KB between
             // 32-wide chunks, k-step = 8 K-rows = 1024 bytes.
-            constexpr uint32_t a_lbo = A_MN ? 32 * 128 : 16, b_lbo = B_MN ? 32 * 128 : 16;
-            constexpr uint32_t a_sbo = A_MN ? 512 : 1024, b_sbo = B_MN ? 512 : 1024;
-            constexpr uint32_t a_lay = A_MN ? tc::kLayoutSw128Base32 : tc::kLayoutSw128;
+            constexpr uint32_t b_lbo = B_MN ? 32 * 128 : 16, b_sbo = B_MN ? 512 : 1024;
             constexpr uint32_t b_lay = B_MN ? tc::kLayoutSw128Base32 : tc::kLayoutSw128;
-            constexpr uint32_t a_step = A_MN ? 1024 : 32, b_step = B_MN ? 1024 : 32;
+            constexpr uint32_t b_step = B_MN ? 1024 : 32;
             uint32_t it = 0;
             bool stop = false;
             for (int u = blockIdx.x; u < g.units && !stop; u += gridDim.x) {
@@ -223,27 +238,30 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                 for (int kb = 0; kb < t.nk; ++kb, ++it) {
                     const int s = it % kTcStages;
                     const uint32_t ph = (it / kTcStages) & 1;
-                    const int b = it % kTcAccBufs;
-                    const uint32_t use = it / kTcAccBufs;
-                    if (!tc::mbar_wait(&sm.lo_ready[s], ph)) { tc_fail(sm, err, kTcErrMma); stop = true; break; }
-                    if (!tc::mbar_wait(&sm.acc_free[b], (use & 1) ^ 1)) { tc_fail(sm, err, kTcErrMma); stop = true; break; }
+                    const int j = it % kTcASlots;
+                    if (!tc::mbar_wait(&sm.a_ready[j], (it / kTcASlots) & 1)) { tc_fail(sm, err, kTcErrMma); stop = true; break; }
+                    if (!tc::mbar_wait(&sm.b_ready[s], ph)) { tc_fail(sm, err, kTcErrMma); stop = true; break; }
+                    if (!tc::mbar_wait(&sm.acc_free, (it & 1) ^ 1)) { tc_fail(sm, err, kTcErrMma); stop = true; break; }
                     if (tc_aborted(sm)) { stop = true; break; }
                     tc::tc_fence_after();
-                    const uint32_t acc = tmem + uint32_t(b * 128);
-                    const uint32_t ah = tc::smem_u32(sm.a_hi[s]), al = tc::smem_u32(sm.a_lo[s]);
+                    const uint32_t ah = tmem + kTcColA + 64 * j, al = ah + 32;
                     const uint32_t bh = tc::smem_u32(sm.b_hi[s]), bl = tc::smem_u32(sm.b_lo[s]);
+                    // hi*lo and lo*hi first, then hi*hi
 #pragma unroll
                     for (int k = 0; k < kTcBK / 8; ++k) {
-                        const uint64_t dah = tc::smem_desc(ah + k * a_step, a_lbo, a_sbo, a_lay);
-                        const uint64_t dal = tc::smem_desc(al + k * a_step, a_lbo, a_sbo, a_lay);
                         const uint64_t dbh = tc::smem_desc(bh + k * b_step, b_lbo, b_sbo, b_lay);
                         const uint64_t dbl = tc::smem_desc(bl + k * b_step, b_lbo, b_sbo, b_lay);
-                        tc::mma_tf32(acc, dah, dbh, idesc, k > 0 ? 1u : 0u);
-                        tc::mma_tf32(acc, dah, dbl, idesc, 1u);
-                        tc::mma_tf32(acc, dal, dbh, idesc, 1u);
+                        tc::mma_tf32_ts(tmem, ah + 8 * k, dbl, idesc, k > 0 ? 1u : 0u);
+                        tc::mma_tf32_ts(tmem, al + 8 * k, dbh, idesc, 1u);
+                    }
+#pragma unroll
+                    for (int k = 0; k < kTcBK / 8; ++k) {
+                        const uint64_t dbh = tc::smem_desc(bh + k * b_step, b_lbo, b_sbo, b_lay);
+                        tc::mma_tf32_ts(tmem, ah + 8 * k, dbh, idesc, 1u);
                     }
                     tc::mma_commit(&sm.empty[s]);
-                    tc::mma_commit(&sm.acc_ready[b]);
+                    tc::mma_commit(&sm.a_free[j]);
+                    tc::mma_commit(&sm.acc_ready);
                 }
             }
             // drain: every MMA issued above has completed before teardown
@@ -251,8 +269,11 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
             tc::mbar_wait(&sm.drain, 0);
         }
     } else if (warp < kTcFirstDrainWarp) {
-        // ---------------- converter ----------------
+        // ---------------- converters ----------------
         const int ct = threadIdx.x - 64;  // 0..kTcConvThreads-1
+        const int q = warp & 3;            // TMEM lane quarter
+        const int m = 32 * q + lane;       // the A tile row this thread splits
+        const uint32_t a_lane = tmem + (uint32_t(32 * q) << 16) + kTcColA;
         uint32_t it = 0;
         bool stop = false;
         for (int u = blockIdx.x; u < g.units && !stop; u += gridDim.x) {
@@ -262,31 +283,65 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                 const uint32_t ph = (it / kTcStages) & 1;
                 if (!tc::mbar_wait(&sm.full[s], ph)) { tc_fail(sm, err, kTcErrConverter); stop = true; break; }
                 if (tc_aborted(sm)) { stop = true; break; }
-                float4* ah = reinterpret_cast<float4*>(sm.a_hi[s]);
-                float4* al = reinterpret_cast<float4*>(sm.a_lo[s]);
+                {
+                    // row m's 32 K-values -> hi/lo in A slot it % 3, 16 at a time
+                    const int j = it % kTcASlots;
+                    if (!tc::mbar_wait(&sm.a_free[j], ((it / kTcASlots) & 1) ^ 1)) {
+                        tc_fail(sm, err, kTcErrConverter); stop = true; break;
+                    }
+                    tc::tc_fence_after();
+                    const float* raw = sm.a_raw[s];
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        float x[16];
+                        if (!A_MN) {
+#pragma unroll
+                            for (int c = 0; c < 4; ++c) {
+                                const int cc = 4 * h + c;
+                                const float4 v = *reinterpret_cast<const float4*>(raw + m * 32 + ((cc ^ (m & 7)) << 2));
+                                x[4 * c] = v.x; x[4 * c + 1] = v.y; x[4 * c + 2] = v.z; x[4 * c + 3] = v.w;
+                            }
+                        } else {
+#pragma unroll
+                            for (int k = 0; k < 16; ++k) x[k] = raw[(16 * h + k) * 128 + m];
+                        }
+                        uint32_t hi[16], lo[16];
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) {
+                            const float hv = tf32_round(x[i]);
+                            hi[i] = __float_as_uint(hv);
+                            lo[i] = __float_as_uint(x[i] - hv);
+                        }
+                        tc::tmem_st_32x32b_x16(a_lane + 64 * j + 16 * h, hi);
+                        tc::tmem_st_32x32b_x16(a_lane + 64 * j + 32 + 16 * h, lo);
+                    }
+                    __syncwarp();
+                    if (lane == 0) tc::mbar_arrive(&sm.empty[s]);  // raw A read
+                    tc::tmem_st_wait();
+                    tc::tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) tc::mbar_arrive(&sm.a_ready[j]);
+                }
                 float4* bh = reinterpret_cast<float4*>(sm.b_hi[s]);
                 float4* bl = reinterpret_cast<float4*>(sm.b_lo[s]);
-#pragma unroll 2
-                for (int i = ct; i < kTcTileFloats / 4; i += kTcConvThreads) {
-                    const float4 x = ah[i];
+#pragma unroll 4
+                for (int i = ct; i < kTcBTileFloats / 4; i += kTcConvThreads) {
                     const float4 y = bh[i];
-                    const float4 h = tf32_hi(x);
                     const float4 gg = tf32_hi(y);
-                    ah[i] = h;
-                    al[i] = make_float4(x.x - h.x, x.y - h.y, x.z - h.z, x.w - h.w);
                     bh[i] = gg;
                     bl[i] = make_float4(y.x - gg.x, y.y - gg.y, y.z - gg.z, y.w - gg.w);
                 }
                 tc::fence_proxy_async_smem();
-                tc::mbar_arrive(&sm.lo_ready[s]);
+                tc::mbar_arrive(&sm.b_ready[s]);
             }
         }
     } else {
         // ---------------- drain, then epilogue ----------------
-        const int dw = warp - kTcFirstDrainWarp;  // 0..7
+        const int dw = warp - kTcFirstDrainWarp;  // 0..15
         const int q = warp & 3;                   // TMEM lane quarter this warp may access
-        const int half = dw >> 2;                 // which 64 of the 128 columns
+        const int slice = dw >> 2;                // which 64 of the 256 columns
         float* stg = sm.stage[dw];
+        const uint32_t base = tmem + (uint32_t(32 * q) << 16) + uint32_t(64 * slice);
         uint32_t it = 0;
         bool stop = false;
         for (int u = blockIdx.x; u < g.units && !stop; u += gridDim.x) {
@@ -295,37 +350,39 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
 #pragma unroll
             for (int i = 0; i < 64; ++i) acc[i] = 0.f;
             for (int kb = 0; kb < t.nk; ++kb, ++it) {
-                const int b = it % kTcAccBufs;
-                const uint32_t use = it / kTcAccBufs;
-                if (!tc::mbar_wait(&sm.acc_ready[b], use & 1)) { tc_fail(sm, err, kTcErrEpilogue); stop = true; break; }
+                if (!tc::mbar_wait(&sm.acc_ready, it & 1)) { tc_fail(sm, err, kTcErrEpilogue); stop = true; break; }
                 if (tc_aborted(sm)) { stop = true; break; }
                 tc::tc_fence_after();
-                const uint32_t base = tmem + (uint32_t(32 * q) << 16) + uint32_t(b * 128 + 64 * half);
+                // 16 columns at a time (registers: 64 sums + 16 loaded); the
+                // accumulator is released once the last piece is in registers
 #pragma unroll
-                for (int h2 = 0; h2 < 2; ++h2) {  // two 32-column loads keep 32 temporaries live
-                    uint32_t r[32];
-                    tc::tmem_ld_32x32b_x32(base + 32 * h2, r);
+                for (int p = 0; p < 4; ++p) {
+                    uint32_t r[16];
+                    tc::tmem_ld_32x32b_x16(base + 16 * p, r);
                     tc::tmem_ld_wait();
+                    if (p == 3) {
+                        tc::tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) tc::mbar_arrive(&sm.acc_free);
+                    }
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) acc[32 * h2 + i] = __fadd_rn(acc[32 * h2 + i], __uint_as_float(r[i]));
+                    for (int i = 0; i < 16; ++i) acc[16 * p + i] = __fadd_rn(acc[16 * p + i], __uint_as_float(r[i]));
                 }
-                tc::tc_fence_before();
-                tc::mbar_arrive(&sm.acc_free[b]);
             }
             if (stop || tc_aborted(sm)) break;
             // Coalesced epilogue: this warp owns rows m0+32q .. +31 and
-            // columns n0+64*half .. +63.  Per 16-column chunk, lane = row
+            // columns n0+64*slice .. +63.  Per 16-column chunk, lane = row
             // writes its 16 values into the staging block (row stride 17:
             // conflict-free), then lanes 0-15 / 16-31 read rows 2i / 2i+1
             // column-wise and store 16 consecutive columns each.
             const int rbase = t.m0 + 32 * q;
-            const int cbase = t.n0 + 64 * half;
+            const int cbase = t.n0 + 64 * slice;
             const int rsub = lane >> 4, csub = lane & 15;
 #pragma unroll
             for (int c = 0; c < 4; ++c) {
                 __syncwarp();
 #pragma unroll
-                for (int j = 0; j < 16; ++j) stg[lane * kTcStageLd + j] = acc[c * 16 + j];
+                for (int jj = 0; jj < 16; ++jj) stg[lane * kTcStageLd + jj] = acc[c * 16 + jj];
                 __syncwarp();
                 const int n = cbase + c * 16 + csub;
                 if (partial) {
