@@ -92,19 +92,36 @@ inline bool tc_eligible(hx_runtime* rt, int M, int N, int K, const float* A, lon
     return M >= 64 && N >= 64 && 2.0 * M * N * K >= 6.4e7;
 }
 
+// B of a GEMM already split for the tensor cores: hi = B rounded to TF32,
+// lo = B - hi, both with B's leading dimension (weights are split once per
+// step, so their tiles are not split again in every CTA that loads them).
+struct BSplit {
+    const float* hi = nullptr;
+    const float* lo = nullptr;
+};
+
 template <bool AT, bool BT, class Epi>
-void launch_tc(hx_runtime* rt, int M, int N, int K, const float* A, long lda, const float* B, long ldb, Epi epi)
+void launch_tc(hx_runtime* rt, int M, int N, int K, const float* A, long lda, const float* B, long ldb, Epi epi,
+               BSplit bs)
 {
     // A(m,k): AT=false -> K-major rows [M][K];  AT=true -> MN-major [K][M].
     // B(k,n): BT=false -> MN-major [K][N];      BT=true -> K-major [N][K].
     constexpr bool A_MN = AT, B_MN = !BT;
     constexpr CUtensorMapSwizzle mn_swz = CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B;
+    auto map_b = [&](const float* base) {
+        return B_MN ? make_map(base, N, K, ldb, 32, 32, mn_swz) : make_map(base, K, N, ldb, 32, kTcBN);
+    };
     const CUtensorMap ma = A_MN ? make_map(A, M, K, lda, 128, 32, CU_TENSOR_MAP_SWIZZLE_NONE) : make_map(A, K, M, lda, 32, 128);
-    const CUtensorMap mb = B_MN ? make_map(B, N, K, ldb, 32, 32, mn_swz) : make_map(B, K, N, ldb, 32, kTcBN);
+    const bool split = bs.hi && bs.lo;
+    const CUtensorMap mb = map_b(split ? bs.hi : B);
+    const CUtensorMap mb_lo = split ? map_b(bs.lo) : mb;
     const TcGrid g = tc_grid(M, N, K, rt->sm_count, 64);
     int* err = rt->device_error();
     float* ws = g.splits > 1 ? rt->workspace(sizeof(float) * (size_t)g.splits * M * N) : nullptr;
-    HX_CUDA((launch_tc_kernel<A_MN, B_MN>(rt->stream, rt->sm_count, ma, mb, g, epi, ws, err)));
+    if (split)
+        HX_CUDA((launch_tc_kernel<A_MN, B_MN, true>(rt->stream, rt->sm_count, ma, mb, mb_lo, g, epi, ws, err)));
+    else
+        HX_CUDA((launch_tc_kernel<A_MN, B_MN, false>(rt->stream, rt->sm_count, ma, mb, mb_lo, g, epi, ws, err)));
     ++rt->metrics.kernel_launches;
     if (g.splits > 1) {
         const long total = (long)M * N;
@@ -115,14 +132,18 @@ void launch_tc(hx_runtime* rt, int M, int N, int K, const float* A, long lda, co
     }
 }
 
-// C = op(A) op(B) with the epilogue applied to every element.
+// C = op(A) op(B) with the epilogue applied to every element.  `bs`, when
+// given, is B's TF32 hi/lo split for the tensor-core path; the CUDA-core path
+// always reads B itself.
 template <bool AT, bool BT, class Epi>
-void gemm(hx_runtime* rt, int M, int N, int K, const float* A, long lda, const float* B, long ldb, Epi epi)
+void gemm(hx_runtime* rt, int M, int N, int K, const float* A, long lda, const float* B, long ldb, Epi epi,
+          BSplit bs = BSplit{})
 {
     require(M > 0 && N > 0 && K >= 0, HX_ERR_ARGUMENT, "gemm: bad shape");
     ProfScope prof(rt, kTagGemm, 2.0 * M * N * K, 4.0 * ((double)M * K + (double)K * N + (double)M * N));
-    if (tc_eligible(rt, M, N, K, A, lda, B, ldb)) {
-        launch_tc<AT, BT>(rt, M, N, K, A, lda, B, ldb, epi);
+    if (tc_eligible(rt, M, N, K, A, lda, B, ldb) &&
+        (!bs.hi || ((reinterpret_cast<uintptr_t>(bs.hi) | reinterpret_cast<uintptr_t>(bs.lo)) & 15) == 0)) {
+        launch_tc<AT, BT>(rt, M, N, K, A, lda, B, ldb, epi, bs);
         return;
     }
     const long mn = (long)M * N;

@@ -142,10 +142,11 @@ __device__ __forceinline__ float4 tf32_hi(float4 x) {
     return make_float4(tf32_round(x.x), tf32_round(x.y), tf32_round(x.z), tf32_round(x.w));
 }
 
-template <bool A_MN, bool B_MN, class Epi>
+template <bool A_MN, bool B_MN, bool B_SPLIT, class Epi>
 __global__ void __launch_bounds__(kTcThreads, 1)
-gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, TcGrid g, Epi epi,
-               float* __restrict__ partial, int* __restrict__ err)
+gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+               const __grid_constant__ CUtensorMap map_blo, TcGrid g, Epi epi, float* __restrict__ partial,
+               int* __restrict__ err)
 {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     // 128B-swizzled TMA tiles and UMMA descriptors need 1024-byte alignment
@@ -173,6 +174,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
     if (warp == 0 && lane == 0) {
         tc::prefetch_tensormap(&map_a);
         tc::prefetch_tensormap(&map_b);
+        if (B_SPLIT) tc::prefetch_tensormap(&map_blo);
     }
     if (warp == 1) {
         tc::tmem_alloc(&sm.tmem_addr, kTcTmemCols);
@@ -198,18 +200,23 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                     const uint32_t ph = (it / kTcStages) & 1;
                     if (!tc::mbar_wait(&sm.empty[s], ph ^ 1)) { tc_fail(sm, err, kTcErrProducer); stop = true; break; }
                     if (tc_aborted(sm)) { stop = true; break; }
-                    tc::mbar_arrive_expect_tx(&sm.full[s], (kTcATileFloats + kTcBTileFloats) * 4);
+                    tc::mbar_arrive_expect_tx(&sm.full[s], (kTcATileFloats + (B_SPLIT ? 2 : 1) * kTcBTileFloats) * 4);
                     const int k = t.kbeg + kb * kTcBK;
                     if (!A_MN)
                         tc::tma_load_2d(sm.a_raw[s], &map_a, &sm.full[s], k, t.m0);   // box 32 (K) x 128 rows
                     else
                         tc::tma_load_2d(sm.a_raw[s], &map_a, &sm.full[s], t.m0, k);   // box 128 (M) x 32 K-rows
-                    if (!B_MN) {
-                        tc::tma_load_2d(sm.b_hi[s], &map_b, &sm.full[s], k, t.n0);    // box 32 (K) x 256 rows
-                    } else {
 #pragma unroll
-                        for (int c = 0; c < kTcBN / 32; ++c)
-                            tc::tma_load_2d(sm.b_hi[s] + c * 1024, &map_b, &sm.full[s], t.n0 + 32 * c, k);
+                    for (int part = 0; part < (B_SPLIT ? 2 : 1); ++part) {
+                        float* dst = part ? sm.b_lo[s] : sm.b_hi[s];
+                        const CUtensorMap* mp = part ? &map_blo : &map_b;
+                        if (!B_MN) {
+                            tc::tma_load_2d(dst, mp, &sm.full[s], k, t.n0);    // box 32 (K) x 256 rows
+                        } else {
+#pragma unroll
+                            for (int c = 0; c < kTcBN / 32; ++c)
+                                tc::tma_load_2d(dst + c * 1024, mp, &sm.full[s], t.n0 + 32 * c, k);
+                        }
                     }
                     issued[s] = true;
                     issued_parity[s] = ph;
@@ -322,16 +329,18 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                     __syncwarp();
                     if (lane == 0) tc::mbar_arrive(&sm.a_ready[j]);
                 }
-                float4* bh = reinterpret_cast<float4*>(sm.b_hi[s]);
-                float4* bl = reinterpret_cast<float4*>(sm.b_lo[s]);
+                if (!B_SPLIT) {
+                    float4* bh = reinterpret_cast<float4*>(sm.b_hi[s]);
+                    float4* bl = reinterpret_cast<float4*>(sm.b_lo[s]);
 #pragma unroll 4
-                for (int i = ct; i < kTcBTileFloats / 4; i += kTcConvThreads) {
-                    const float4 y = bh[i];
-                    const float4 gg = tf32_hi(y);
-                    bh[i] = gg;
-                    bl[i] = make_float4(y.x - gg.x, y.y - gg.y, y.z - gg.z, y.w - gg.w);
+                    for (int i = ct; i < kTcBTileFloats / 4; i += kTcConvThreads) {
+                        const float4 y = bh[i];
+                        const float4 gg = tf32_hi(y);
+                        bh[i] = gg;
+                        bl[i] = make_float4(y.x - gg.x, y.y - gg.y, y.z - gg.z, y.w - gg.w);
+                    }
+                    tc::fence_proxy_async_smem();
                 }
-                tc::fence_proxy_async_smem();
                 tc::mbar_arrive(&sm.b_ready[s]);
             }
         }
@@ -448,16 +457,18 @@ inline TcGrid tc_grid(int M, int N, int K, int sm_count, int max_splits) {
     return g;
 }
 
-// Launches the persistent kernel: min(units, SMs) CTAs.
-template <bool A_MN, bool B_MN, class Epi>
+// Launches the persistent kernel: min(units, SMs) CTAs.  With B_SPLIT, B
+// arrives as two tensors, hi (already rounded to TF32) through mb and
+// lo = B - hi through mb_lo, and is not split on the device.
+template <bool A_MN, bool B_MN, bool B_SPLIT = false, class Epi>
 inline cudaError_t launch_tc_kernel(cudaStream_t stream, int sm_count, const CUtensorMap& ma, const CUtensorMap& mb,
-                                    const TcGrid& g, Epi epi, float* partial, int* err)
+                                    const CUtensorMap& mb_lo, const TcGrid& g, Epi epi, float* partial, int* err)
 {
-    const cudaError_t a = cudaFuncSetAttribute(gemm_tc_kernel<A_MN, B_MN, Epi>,
+    const cudaError_t a = cudaFuncSetAttribute(gemm_tc_kernel<A_MN, B_MN, B_SPLIT, Epi>,
                                                cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTcSmemBytes);
     if (a != cudaSuccess) return a;
     const int grid = std::max(1, std::min(g.units, sm_count));
-    gemm_tc_kernel<A_MN, B_MN, Epi><<<grid, kTcThreads, kTcSmemBytes, stream>>>(ma, mb, g, epi, partial, err);
+    gemm_tc_kernel<A_MN, B_MN, B_SPLIT, Epi><<<grid, kTcThreads, kTcSmemBytes, stream>>>(ma, mb, mb_lo, g, epi, partial, err);
     return cudaGetLastError();
 }
 

@@ -55,6 +55,7 @@ struct LmPlan {
     Arena arena;
     // arena offsets (bytes)
     size_t params, exec_params, grads, adam_m, adam_v, muon_buf, pos_fixed, wqkv;
+    size_t w_hi, w_lo, wqkv_hi, wqkv_lo;  // TF32 hi/lo splits of the GEMM weights, refreshed every forward
     size_t tokens, in_tok, tgt_tok, in_ids, tgt_ids, bad;
     std::vector<LayerActs> la;
     size_t xL, logits, probs, row_loss, row_correct, loss, acc, scalars;
@@ -255,6 +256,18 @@ struct DiagOut {
 // into logits [B][V] (what generation samples from).
 enum ForwardMode { kFullStep = 0, kForwardAllRows = 1, kForwardLastRow = 2 };
 
+// hi = w rounded to TF32, lo = w - hi: the tensor-core GEMMs' split of their
+// weight operands, done once per forward instead of in every CTA per tile.
+__global__ void split_tf32_kernel(long n, const float* __restrict__ w, float* __restrict__ hi, float* __restrict__ lo)
+{
+    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
+        const float x = w[i];
+        const float h = tf32_round(x);
+        hi[i] = h;
+        lo[i] = x - h;
+    }
+}
+
 void forward_backward(hx_runtime* rt, LmPlan& p, const float* W, float* G, float grad_scale, int mode = kFullStep)
 {
     const Arena& a = p.arena;
@@ -266,11 +279,24 @@ void forward_backward(hx_runtime* rt, LmPlan& p, const float* W, float* G, float
     float* wqkv = a.at<float>(p.wqkv);
     const int tpb = 256;
 
-    // pack W_qkv per layer
+    // pack W_qkv per layer; split the GEMM weights for the tensor cores
     for (uint32_t l = 0; l < p.L; ++l) {
         pack_qkv_kernel<<<grid_for(3L * D * D, tpb, rt->sm_count), tpb, 0, s>>>(D, W + p.lo[l].wq, wqkv + size_t(l) * 3 * D * D);
         HX_LAUNCHED(rt);
     }
+    float* whi = a.at<float>(p.w_hi);
+    float* wlo = a.at<float>(p.w_lo);
+    float* qhi = a.at<float>(p.wqkv_hi);
+    float* qlo = a.at<float>(p.wqkv_lo);
+    {
+        const long nq = long(p.L) * 3 * D * D;
+        split_tf32_kernel<<<grid_for(long(p.P), tpb, rt->sm_count), tpb, 0, s>>>(long(p.P), W, whi, wlo);
+        HX_LAUNCHED(rt);
+        split_tf32_kernel<<<grid_for(nq, tpb, rt->sm_count), tpb, 0, s>>>(nq, wqkv, qhi, qlo);
+        HX_LAUNCHED(rt);
+    }
+    auto wsplit = [&](size_t off) { return BSplit{whi + off, wlo + off}; };
+    auto qsplit = [&](uint32_t l) { return BSplit{qhi + size_t(l) * 3 * D * D, qlo + size_t(l) * 3 * D * D}; };
     // embedding
     float* x = a.at<float>(p.la[0].x);
     ProfScope pemb(rt, kTagEmbed, 1.0 * M * D, 4.0 * 3.0 * M * D);
@@ -292,29 +318,31 @@ void forward_backward(hx_runtime* rt, LmPlan& p, const float* W, float* G, float
         HX_LAUNCHED(rt);
         pln1.end();
         gemm<false, false>(rt, M, 3 * D, D, a.at<float>(A.n1), D, wqkv + size_t(l) * 3 * D * D, 3 * D,
-                           EpiStore{a.at<float>(A.qkv), 3L * D, 0, 0});
+                           EpiStore{a.at<float>(A.qkv), 3L * D, 0, 0}, qsplit(l));
         float* hp = p.diag ? a.at<float>(p.diag_hp) + size_t(l) * B * p.H * T * T : nullptr;
         HX_DH_DISPATCH(p.dh, attn_fwd_launch, rt, p, a.at<float>(A.qkv), a.at<float>(A.ctx), a.at<float>(A.rmax),
                        a.at<float>(A.rsum), hp);
-        gemm<false, false>(rt, M, D, D, a.at<float>(A.ctx), D, W + o.wo, D, EpiAddResidual{xin, a.at<float>(A.r1), D});
+        gemm<false, false>(rt, M, D, D, a.at<float>(A.ctx), D, W + o.wo, D, EpiAddResidual{xin, a.at<float>(A.r1), D},
+                           wsplit(o.wo));
         ProfScope pln2(rt, kTagLayerNorm, 8.0 * M * D, 4.0 * (2.0 * M * D + 2.0 * M));
         layernorm_fwd_kernel<<<row_grid, 32 * rows_per_block, 0, s>>>(M, D, p.cfg.eps, a.at<float>(A.r1), W + o.g2,
                                                                        W + o.b2, a.at<float>(A.n2),
                                                                        a.at<float>(A.mean2), a.at<float>(A.inv2));
         HX_LAUNCHED(rt);
         pln2.end();
-        gemm<false, false>(rt, M, F, D, a.at<float>(A.n2), D, W + o.w1, F, EpiRelu{a.at<float>(A.relu), nullptr, F});
+        gemm<false, false>(rt, M, F, D, a.at<float>(A.n2), D, W + o.w1, F, EpiRelu{a.at<float>(A.relu), nullptr, F},
+                           wsplit(o.w1));
         gemm<false, false>(rt, M, D, F, a.at<float>(A.relu), F, W + o.w2, D,
-                           EpiAddResidual{a.at<float>(A.r1), xout, D});
+                           EpiAddResidual{a.at<float>(A.r1), xout, D}, wsplit(o.w2));
     }
     const float* xL = a.at<float>(p.xL);
     float* logits = a.at<float>(p.logits);
     if (mode == kForwardLastRow) {
         gemm<false, false>(rt, B, V, D, xL + size_t(T - 1) * D, (long)T * D, W + p.off_out, V,
-                           EpiStore{logits, (long)V, 0, 0});
+                           EpiStore{logits, (long)V, 0, 0}, wsplit(p.off_out));
         return;
     }
-    gemm<false, false>(rt, M, V, D, xL, D, W + p.off_out, V, EpiStore{logits, (long)V, 0, 0});
+    gemm<false, false>(rt, M, V, D, xL, D, W + p.off_out, V, EpiStore{logits, (long)V, 0, 0}, wsplit(p.off_out));
     if (mode == kForwardAllRows) return;
     ProfScope pce(rt, kTagSoftmaxCe, 4.0 * M * V, 4.0 * 2.0 * M * V);
     softmax_ce_kernel<<<row_grid, 32 * rows_per_block, 0, s>>>(
@@ -332,7 +360,7 @@ void forward_backward(hx_runtime* rt, LmPlan& p, const float* W, float* G, float
     const float* dl = logits;  // dlogits, in place
     gemm<true, false>(rt, D, V, M, xL, D, dl, V, EpiStore{G + p.off_out, (long)V, 0, 0});
     float* dout = a.at<float>(p.dout);
-    gemm<false, true>(rt, M, D, V, dl, V, W + p.off_out, V, EpiStore{dout, (long)D, 0, 0});
+    gemm<false, true>(rt, M, D, V, dl, V, W + p.off_out, V, EpiStore{dout, (long)D, 0, 0}, wsplit(p.off_out));
     if (p.diag) copy_d2d(rt, a.at<float>(p.diag_dout), dout, sizeof(float) * size_t(M) * D);
     float* dr = a.at<float>(p.dr);
     float* dc = a.at<float>(p.dc);
@@ -349,9 +377,10 @@ void forward_backward(hx_runtime* rt, LmPlan& p, const float* W, float* G, float
         const LayerOffsets& o = p.lo[li];
         const float* xin = a.at<float>(A.x);
         gemm<true, false>(rt, F, D, M, a.at<float>(A.relu), F, dout, D, EpiStore{G + o.w2, (long)D, 0, 0});
-        gemm<false, true>(rt, M, F, D, dout, D, W + o.w2, D, EpiReluBackward{a.at<float>(A.relu), df1, nullptr, F});
+        gemm<false, true>(rt, M, F, D, dout, D, W + o.w2, D, EpiReluBackward{a.at<float>(A.relu), df1, nullptr, F},
+                          wsplit(o.w2));
         gemm<true, false>(rt, D, F, M, a.at<float>(A.n2), D, df1, F, EpiStore{G + o.w1, (long)F, 0, 0});
-        gemm<false, true>(rt, M, D, F, df1, F, W + o.w1, F, EpiStore{dn, (long)D, 0, 0});
+        gemm<false, true>(rt, M, D, F, df1, F, W + o.w1, F, EpiStore{dn, (long)D, 0, 0}, wsplit(o.w1));
         ProfScope plb2(rt, kTagLayerNorm, 12.0 * M * D, 4.0 * (4.0 * M * D + 2.0 * M));
         layernorm_bwd_kernel<<<p.ln_parts, 32 * lnw, ln_smem, s>>>(M, D, p.ln_rows, dn, a.at<float>(A.r1),
                                                                      a.at<float>(A.mean2), a.at<float>(A.inv2),
@@ -361,12 +390,13 @@ void forward_backward(hx_runtime* rt, LmPlan& p, const float* W, float* G, float
         column_reduce_kernel<<<grid_for(2L * D, tpb, rt->sm_count), tpb, 0, s>>>(p.ln_parts, D, part, G + o.g2, G + o.b2);
         HX_LAUNCHED(rt);
         gemm<true, false>(rt, D, D, M, a.at<float>(A.ctx), D, dr, D, EpiStore{G + o.wo, (long)D, 0, 0});
-        gemm<false, true>(rt, M, D, D, dr, D, W + o.wo, D, EpiStore{dc, (long)D, 0, 0});
+        gemm<false, true>(rt, M, D, D, dr, D, W + o.wo, D, EpiStore{dc, (long)D, 0, 0}, wsplit(o.wo));
         HX_DH_DISPATCH(p.dh, attn_bwd_launch, rt, p, a.at<float>(A.qkv), dc, a.at<float>(A.rmax), a.at<float>(A.rsum),
                        dqkv);
         gemm<true, false>(rt, D, 3 * D, M, a.at<float>(A.n1), D, dqkv, 3 * D,
                           EpiStore{G + o.wq, (long)D, (int)D, (long)D * D});
-        gemm<false, true>(rt, M, D, 3 * D, dqkv, 3 * D, wqkv + size_t(li) * 3 * D * D, 3 * D, EpiStore{dn, (long)D, 0, 0});
+        gemm<false, true>(rt, M, D, 3 * D, dqkv, 3 * D, wqkv + size_t(li) * 3 * D * D, 3 * D, EpiStore{dn, (long)D, 0, 0},
+                          qsplit(li));
         ProfScope plb1(rt, kTagLayerNorm, 12.0 * M * D, 4.0 * (4.0 * M * D + 2.0 * M));
         layernorm_bwd_kernel<<<p.ln_parts, 32 * lnw, ln_smem, s>>>(M, D, p.ln_rows, dn, xin, a.at<float>(A.mean1),
                                                                      a.at<float>(A.inv1), W + o.g1, dr, dout, part);
@@ -554,6 +584,10 @@ int hx_lm_prepare(hx_runtime* rt, const hx_lm_config* cfg, uint32_t batch, int d
         p.muon_buf = a.reserve(f * p.P);
         p.pos_fixed = a.reserve(f * T * D);
         p.wqkv = a.reserve(f * p.L * 3 * D * D);
+        p.w_hi = a.reserve(f * p.P);
+        p.w_lo = a.reserve(f * p.P);
+        p.wqkv_hi = a.reserve(f * p.L * 3 * D * D);
+        p.wqkv_lo = a.reserve(f * p.L * 3 * D * D);
         p.tokens = a.reserve(sizeof(uint32_t) * B * (T + 1));
         p.in_tok = a.reserve(sizeof(uint32_t) * M);
         p.tgt_tok = a.reserve(sizeof(uint32_t) * M);
