@@ -370,8 +370,22 @@ void forward_backward(hx_runtime* rt, LmPlan& p, const float* W, float* G, float
     float* part = a.at<float>(p.ln_part);
     const int lnw = 8;
     const size_t ln_smem = sizeof(float) * lnw * 2 * D;
-    if (ln_smem > 48 * 1024)
-        HX_CUDA(cudaFuncSetAttribute(layernorm_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ln_smem));
+    // LayerNorm backward with the residual add; the float4 path for D = 128, 256, 512
+    auto ln_bwd = [&](const float* dy, const float* xx, const float* mean, const float* inv, const float* gam,
+                      const float* res, float* dxo) {
+        const int C = (D % 128 == 0) ? D / 128 : 0;
+        if (C == 1 || C == 2 || C == 4) {
+            auto k = C == 1 ? layernorm_bwd_vec_kernel<1> : C == 2 ? layernorm_bwd_vec_kernel<2> : layernorm_bwd_vec_kernel<4>;
+            if (ln_smem > 48 * 1024) HX_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ln_smem));
+            k<<<p.ln_parts, 32 * lnw, ln_smem, s>>>(M, p.ln_rows, dy, xx, mean, inv, gam, res, dxo, part);
+        } else {
+            if (ln_smem > 48 * 1024)
+                HX_CUDA(cudaFuncSetAttribute(layernorm_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ln_smem));
+            layernorm_bwd_kernel<<<p.ln_parts, 32 * lnw, ln_smem, s>>>(M, D, p.ln_rows, dy, xx, mean, inv, gam, res, dxo,
+                                                                         part);
+        }
+        HX_LAUNCHED(rt);
+    };
     for (uint32_t li = p.L; li-- > 0;) {
         const LayerActs& A = p.la[li];
         const LayerOffsets& o = p.lo[li];
@@ -382,10 +396,7 @@ void forward_backward(hx_runtime* rt, LmPlan& p, const float* W, float* G, float
         gemm<true, false>(rt, D, F, M, a.at<float>(A.n2), D, df1, F, EpiStore{G + o.w1, (long)F, 0, 0});
         gemm<false, true>(rt, M, D, F, df1, F, W + o.w1, F, EpiStore{dn, (long)D, 0, 0}, wsplit(o.w1));
         ProfScope plb2(rt, kTagLayerNorm, 12.0 * M * D, 4.0 * (4.0 * M * D + 2.0 * M));
-        layernorm_bwd_kernel<<<p.ln_parts, 32 * lnw, ln_smem, s>>>(M, D, p.ln_rows, dn, a.at<float>(A.r1),
-                                                                     a.at<float>(A.mean2), a.at<float>(A.inv2),
-                                                                     W + o.g2, dout, dr, part);
-        HX_LAUNCHED(rt);
+        ln_bwd(dn, a.at<float>(A.r1), a.at<float>(A.mean2), a.at<float>(A.inv2), W + o.g2, dout, dr);
         plb2.end();
         column_reduce_kernel<<<grid_for(2L * D, tpb, rt->sm_count), tpb, 0, s>>>(p.ln_parts, D, part, G + o.g2, G + o.b2);
         HX_LAUNCHED(rt);
@@ -398,9 +409,7 @@ void forward_backward(hx_runtime* rt, LmPlan& p, const float* W, float* G, float
         gemm<false, true>(rt, M, D, 3 * D, dqkv, 3 * D, wqkv + size_t(li) * 3 * D * D, 3 * D, EpiStore{dn, (long)D, 0, 0},
                           qsplit(li));
         ProfScope plb1(rt, kTagLayerNorm, 12.0 * M * D, 4.0 * (4.0 * M * D + 2.0 * M));
-        layernorm_bwd_kernel<<<p.ln_parts, 32 * lnw, ln_smem, s>>>(M, D, p.ln_rows, dn, xin, a.at<float>(A.mean1),
-                                                                     a.at<float>(A.inv1), W + o.g1, dr, dout, part);
-        HX_LAUNCHED(rt);
+        ln_bwd(dn, xin, a.at<float>(A.mean1), a.at<float>(A.inv1), W + o.g1, dr, dout);
         plb1.end();
         column_reduce_kernel<<<grid_for(2L * D, tpb, rt->sm_count), tpb, 0, s>>>(p.ln_parts, D, part, G + o.g1, G + o.b1);
         HX_LAUNCHED(rt);
@@ -409,8 +418,13 @@ void forward_backward(hx_runtime* rt, LmPlan& p, const float* W, float* G, float
     // embedding gradients
     ProfScope pemb2(rt, kTagEmbed, 1.0 * M * D, 4.0 * (2.0 * M * D + (p.emb_chunks + 1.0) * V * D));
     {
-        dim3 grid(p.emb_chunks, (V + kEmbTokens - 1) / kEmbTokens, (D + 31) / 32);
-        embed_bwd_partial_kernel<<<grid, 128, 0, s>>>(M, V, D, p.emb_rows, in_ids, dout, a.at<float>(p.emb_part));
+        const int tb = std::max(1, std::min<int>(V, kEmbTableFloats / D));
+        const size_t esm = sizeof(float) * size_t(tb) * D;
+        if (esm > 48 * 1024)
+            HX_CUDA(cudaFuncSetAttribute(embed_bwd_partial_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)esm));
+        dim3 grid(p.emb_chunks, (V + tb - 1) / tb);
+        embed_bwd_partial_kernel<<<grid, 32 * kEmbWarps, esm, s>>>(M, V, D, p.emb_rows, tb, in_ids, dout,
+                                                                    a.at<float>(p.emb_part));
         HX_LAUNCHED(rt);
         embed_bwd_combine_kernel<<<grid_for(long(V) * D, tpb, rt->sm_count), tpb, 0, s>>>(
             p.emb_chunks, V, D, a.at<float>(p.emb_part), G + p.off_E);
@@ -630,7 +644,7 @@ int hx_lm_prepare(hx_runtime* rt, const hx_lm_config* cfg, uint32_t batch, int d
         p.ln_rows = (p.M + p.ln_parts - 1) / p.ln_parts;
         p.ln_parts = (p.M + p.ln_rows - 1) / p.ln_rows;
         p.ln_part = a.reserve(f * size_t(p.ln_parts) * 2 * D);
-        p.emb_rows = 8192;
+        p.emb_rows = 4096;
         p.emb_chunks = (p.M + p.emb_rows - 1) / p.emb_rows;
         p.emb_part = a.reserve(f * size_t(p.emb_chunks) * V * D);
         if (p.diag) {

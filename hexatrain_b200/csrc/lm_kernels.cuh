@@ -147,6 +147,96 @@ __global__ void layernorm_bwd_kernel(int M, int D, int rows_per_cta, const float
     }
 }
 
+// The same for D = 128 C: lane l owns columns 128k + 4l .. +3 (k < C), so a
+// row moves as C float4 loads per operand, the row stays in registers
+// between the two reductions, and each lane keeps its columns' dgamma /
+// dbeta partials in registers (rows of the warp in the same order as above,
+// so the partials, summed across warps in warp order, are identical).  The
+// row sums s and sx are double sums of the same terms in another order.
+template <int C>
+__global__ void layernorm_bwd_vec_kernel(int M, int rows_per_cta, const float* __restrict__ dy,
+                                         const float* __restrict__ x, const float* __restrict__ mean,
+                                         const float* __restrict__ inv, const float* __restrict__ g,
+                                         const float* __restrict__ res, float* __restrict__ dx,
+                                         float* __restrict__ part)
+{
+    constexpr int D = 128 * C;
+    extern __shared__ float acc[];  // [warps][2][D]
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    float gl[4 * C], ga[4 * C], ba[4 * C];
+#pragma unroll
+    for (int k = 0; k < C; ++k) {
+        const float4 v = *reinterpret_cast<const float4*>(g + 128 * k + 4 * lane);
+        gl[4 * k] = v.x; gl[4 * k + 1] = v.y; gl[4 * k + 2] = v.z; gl[4 * k + 3] = v.w;
+    }
+#pragma unroll
+    for (int i = 0; i < 4 * C; ++i) { ga[i] = 0.f; ba[i] = 0.f; }
+    const int r0 = blockIdx.x * rows_per_cta;
+    const int r1 = min(M, r0 + rows_per_cta);
+    const float ivd_scale = float(D);
+    for (int row = r0 + warp; row < r1; row += nw) {
+        const long base = (long)row * D;
+        float dyv[4 * C], xv[4 * C];
+#pragma unroll
+        for (int k = 0; k < C; ++k) {
+            const float4 a = *reinterpret_cast<const float4*>(dy + base + 128 * k + 4 * lane);
+            const float4 b = *reinterpret_cast<const float4*>(x + base + 128 * k + 4 * lane);
+            dyv[4 * k] = a.x; dyv[4 * k + 1] = a.y; dyv[4 * k + 2] = a.z; dyv[4 * k + 3] = a.w;
+            xv[4 * k] = b.x; xv[4 * k + 1] = b.y; xv[4 * k + 2] = b.z; xv[4 * k + 3] = b.w;
+        }
+        const float mf = mean[row], iv = inv[row];
+        double s = 0.0, sx = 0.0;
+#pragma unroll
+        for (int i = 0; i < 4 * C; ++i) {
+            const float xh = __fmul_rn(__fsub_rn(xv[i], mf), iv);
+            xv[i] = xh;
+            const double z = __fmul_rn(dyv[i], gl[i]);
+            s += z;
+            sx += z * xh;
+            ga[i] = __fadd_rn(ga[i], __fmul_rn(dyv[i], xh));
+            ba[i] = __fadd_rn(ba[i], dyv[i]);
+        }
+        s = warp_sum(s);
+        sx = warp_sum(sx);
+        const float ivd = __fdiv_rn(iv, ivd_scale);
+#pragma unroll
+        for (int k = 0; k < C; ++k) {
+            float o[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int i = 4 * k + e;
+                const double z = __fmul_rn(dyv[i], gl[i]);
+                o[e] = (float)((double)ivd * ((double)D * z - s - (double)xv[i] * sx));
+            }
+            const long off = base + 128 * k + 4 * lane;
+            if (res) {
+                const float4 r = *reinterpret_cast<const float4*>(res + off);
+                o[0] = __fadd_rn(r.x, o[0]); o[1] = __fadd_rn(r.y, o[1]);
+                o[2] = __fadd_rn(r.z, o[2]); o[3] = __fadd_rn(r.w, o[3]);
+            }
+            *reinterpret_cast<float4*>(dx + off) = make_float4(o[0], o[1], o[2], o[3]);
+        }
+    }
+    float* wa = acc + (size_t)warp * 2 * D;
+#pragma unroll
+    for (int k = 0; k < C; ++k)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            wa[128 * k + 4 * lane + e] = ga[4 * k + e];
+            wa[D + 128 * k + 4 * lane + e] = ba[4 * k + e];
+        }
+    __syncthreads();
+    for (int d = threadIdx.x; d < D; d += blockDim.x) {
+        float sg = 0.f, sb = 0.f;
+        for (int w = 0; w < nw; ++w) {
+            sg += acc[(size_t)w * 2 * D + d];
+            sb += acc[(size_t)w * 2 * D + D + d];
+        }
+        part[((size_t)blockIdx.x * 2) * D + d] = sg;
+        part[((size_t)blockIdx.x * 2 + 1) * D + d] = sb;
+    }
+}
+
 // out[c] = sum over parts p of part[p][which][c], in part order.
 __global__ void column_reduce_kernel(int parts, int D, const float* __restrict__ part, float* __restrict__ dgamma,
                                      float* __restrict__ dbeta)
@@ -410,32 +500,60 @@ __global__ void loss_reduce_kernel(int B, int T, const double* __restrict__ row_
 }
 
 // Token-embedding gradient gE[v,:] = sum over rows r with id[r] == v of
-// dX0[r,:] (one-hot^T * dX0, :82), deterministic: CTA (chunk c, token block,
-// 32-wide column block) walks the rows of chunk c; warp w takes rows
-// r = w, w+4, ... in increasing order and accumulates into its private
-// shared-memory table; the four warp tables are added in warp order and
-// written to part[c][v][d].  embed_bwd_combine sums the chunks in order.
-constexpr int kEmbTokens = 64;
-__global__ void embed_bwd_partial_kernel(int M, int V, int D, int chunk_rows, const int* __restrict__ ids,
-                                         const float* __restrict__ dx, float* __restrict__ part)
+// dX0[r,:] (one-hot^T * dX0, :82), deterministic.  CTA (chunk c, block of
+// `tb` tokens) keeps the block's rows of the gradient in shared memory
+// ([tb][D], tb * D <= 16384 floats); warp w owns columns 32w + lane (and
+// every 256th beyond) and walks the chunk's rows in increasing order: it
+// loads 32 ids at a time (the next batch's ids in flight), selects the rows
+// whose token falls in the block with a ballot, and adds them up to four at
+// a time (independent loads, then the adds in row order).  Each (token,
+// column) therefore sums its rows of the chunk in row order; the table goes
+// to part[c][v][d], and embed_bwd_combine sums the chunks in order.
+constexpr int kEmbWarps = 8;
+constexpr int kEmbTableFloats = 16384;  // 64 KB of shared memory
+__global__ void __launch_bounds__(32 * kEmbWarps)
+embed_bwd_partial_kernel(int M, int V, int D, int chunk_rows, int tb, const int* __restrict__ ids,
+                         const float* __restrict__ dx, float* __restrict__ part)
 {
-    __shared__ float acc[4][kEmbTokens][33];
+    extern __shared__ float tab[];  // [tb][D]
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int c = blockIdx.x, v0 = blockIdx.y * kEmbTokens, d0 = blockIdx.z * 32;
-    for (int i = 0; i < kEmbTokens; ++i) acc[warp][i][lane] = 0.f;
-    __syncwarp();
+    const int c = blockIdx.x, v0 = blockIdx.y * tb;
+    const int ntok = min(tb, V - v0);
+    for (int i = threadIdx.x; i < ntok * D; i += blockDim.x) tab[i] = 0.f;
+    __syncthreads();
     const int r0 = c * chunk_rows, r1 = min(M, r0 + chunk_rows);
-    const int d = d0 + lane;
-    for (int r = r0 + warp; r < r1; r += 4) {
-        const int v = ids[r] - v0;
-        if (v >= 0 && v < kEmbTokens && d < D) acc[warp][v][lane] += dx[(long)r * D + d];
+    for (int cb = 32 * warp; cb < D; cb += 32 * kEmbWarps) {
+        const int d = cb + lane;
+        const bool dok = d < D;
+        int vnext = (r0 + lane < r1) ? ids[r0 + lane] - v0 : -1;
+        for (int rb = r0; rb < r1; rb += 32) {
+            const int v = vnext;
+            vnext = (rb + 32 + lane < r1) ? ids[rb + 32 + lane] - v0 : -1;
+            unsigned mask = __ballot_sync(0xffffffffu, v >= 0 && v < ntok);
+            while (mask) {  // warp-uniform
+                int rr[4] = {0, 0, 0, 0}, vv[4] = {0, 0, 0, 0};
+                int n = 0;
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    if (mask) {
+                        const int i = __ffs(mask) - 1;
+                        mask &= mask - 1;
+                        rr[q] = rb + i;
+                        vv[q] = __shfl_sync(0xffffffffu, v, i);
+                        n = q + 1;
+                    }
+                }
+                float val[4];
+#pragma unroll
+                for (int q = 0; q < 4; ++q) val[q] = (q < n && dok) ? dx[(long)rr[q] * D + d] : 0.f;
+#pragma unroll
+                for (int q = 0; q < 4; ++q)
+                    if (q < n && dok) tab[vv[q] * D + d] += val[q];
+            }
+        }
     }
     __syncthreads();
-    for (int t = warp; t < kEmbTokens; t += 4) {
-        if (v0 + t >= V || d >= D) continue;
-        const float s = ((acc[0][t][lane] + acc[1][t][lane]) + acc[2][t][lane]) + acc[3][t][lane];
-        part[((long)c * V + v0 + t) * D + d] = s;
-    }
+    for (int i = threadIdx.x; i < ntok * D; i += blockDim.x) part[((long)c * V + v0) * D + i] = tab[i];
 }
 
 __global__ void embed_bwd_combine_kernel(int chunks, int V, int D, const float* __restrict__ part,
