@@ -83,6 +83,22 @@ inline CUtensorMap make_map(const float* base, uint64_t inner, uint64_t outer, u
     return m;
 }
 
+// Row-major FP32 [z][outer][inner] (strides ld and zstride elements), box
+// box_inner x box_outer x 1.
+inline CUtensorMap make_map3(const float* base, uint64_t inner, uint64_t outer, uint64_t depth, uint64_t ld,
+                             uint64_t zstride, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swz) {
+    CUtensorMap m;
+    const cuuint64_t dims[3] = {inner, outer, depth};
+    const cuuint64_t strides[2] = {ld * sizeof(float), zstride * sizeof(float)};
+    const cuuint32_t box[3] = {box_inner, box_outer, 1};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    const CUresult r = encode_tiled()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(base), dims, strides,
+                                      box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    require(r == CUDA_SUCCESS, HX_ERR_CUDA, "cuTensorMapEncodeTiled (3-D) failed (" + std::to_string(int(r)) + ")");
+    return m;
+}
+
 inline bool tc_eligible(hx_runtime* rt, int M, int N, int K, const float* A, long lda, const float* B, long ldb) {
     if (rt->gemm_backend == HX_GEMM_CUDA_CORES) return false;
     const bool aligned = ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(B)) & 15) == 0 && lda % 4 == 0 &&
@@ -118,10 +134,30 @@ void launch_tc(hx_runtime* rt, int M, int N, int K, const float* A, long lda, co
     const TcGrid g = tc_grid(M, N, K, rt->sm_count, 64);
     int* err = rt->device_error();
     float* ws = g.splits > 1 ? rt->workspace(sizeof(float) * (size_t)g.splits * M * N) : nullptr;
+    // bulk tensor stores for the epilogue when its single output (or the
+    // split-K workspace) meets TMA's 16-byte rules
+    bool c_tma;
+    CUtensorMap mc = mb;
+    if (ws) {
+        c_tma = N % 4 == 0;
+        if (c_tma)
+            mc = make_map3(ws, N, M, g.splits, N, (uint64_t)M * N, 16, 32, CU_TENSOR_MAP_SWIZZLE_64B);
+    } else {
+        const float* out = epi.tma_out();
+        const long ldc = epi.tma_ld();
+        const float* pre = epi.pre_ptr();
+        c_tma = epi.tma_ok() && out && ((reinterpret_cast<uintptr_t>(out) | reinterpret_cast<uintptr_t>(pre)) & 15) == 0 &&
+                ldc % 4 == 0;
+        if (c_tma) mc = make_map(out, N, M, ldc, 16, 32, CU_TENSOR_MAP_SWIZZLE_64B);
+    }
+    cudaError_t rc;
     if (split)
-        HX_CUDA((launch_tc_kernel<A_MN, B_MN, true>(rt->stream, rt->sm_count, ma, mb, mb_lo, g, epi, ws, err)));
+        rc = c_tma ? launch_tc_kernel<A_MN, B_MN, true, true>(rt->stream, rt->sm_count, ma, mb, mb_lo, mc, g, epi, ws, err)
+                   : launch_tc_kernel<A_MN, B_MN, true, false>(rt->stream, rt->sm_count, ma, mb, mb_lo, mc, g, epi, ws, err);
     else
-        HX_CUDA((launch_tc_kernel<A_MN, B_MN, false>(rt->stream, rt->sm_count, ma, mb, mb_lo, g, epi, ws, err)));
+        rc = c_tma ? launch_tc_kernel<A_MN, B_MN, false, true>(rt->stream, rt->sm_count, ma, mb, mb_lo, mc, g, epi, ws, err)
+                   : launch_tc_kernel<A_MN, B_MN, false, false>(rt->stream, rt->sm_count, ma, mb, mb_lo, mc, g, epi, ws, err);
+    HX_CUDA(rc);
     ++rt->metrics.kernel_launches;
     if (g.splits > 1) {
         const long total = (long)M * N;

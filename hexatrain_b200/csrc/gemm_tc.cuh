@@ -77,12 +77,18 @@ constexpr uint32_t kTcTmemCols = 512;
 constexpr uint32_t kTcColA = kTcBN;  // A slots after the accumulator: 64 columns each (hi 32, lo 32)
 static_assert(kTcColA + 64 * kTcASlots <= kTcTmemCols, "TMEM budget");
 constexpr int kTcStageLd = 17;  // epilogue staging row stride (floats): 16 columns + 1 pad
+// TMA-store epilogue: per drain warp two 32x16 fp32 chunks (2 KB each),
+// 64-byte swizzled as the output tensor map's box expects
+constexpr int kTcTmaStageFloats = 2 * 32 * 16;
 
 struct TcSmem {
     float a_raw[kTcStages][kTcATileFloats];
     float b_hi[kTcStages][kTcBTileFloats];
     float b_lo[kTcStages][kTcBTileFloats];
-    float stage[kTcDrainWarps][32 * kTcStageLd];
+    union {
+        float stage[kTcDrainWarps][32 * kTcStageLd];
+        float stage_tma[kTcDrainWarps][kTcTmaStageFloats];
+    };
     uint64_t full[kTcStages], b_ready[kTcStages], empty[kTcStages];
     uint64_t a_ready[kTcASlots], a_free[kTcASlots];
     uint64_t acc_ready, acc_free, drain;
@@ -142,11 +148,11 @@ __device__ __forceinline__ float4 tf32_hi(float4 x) {
     return make_float4(tf32_round(x.x), tf32_round(x.y), tf32_round(x.z), tf32_round(x.w));
 }
 
-template <bool A_MN, bool B_MN, bool B_SPLIT, class Epi>
+template <bool A_MN, bool B_MN, bool B_SPLIT, bool C_TMA, class Epi>
 __global__ void __launch_bounds__(kTcThreads, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
-               const __grid_constant__ CUtensorMap map_blo, TcGrid g, Epi epi, float* __restrict__ partial,
-               int* __restrict__ err)
+               const __grid_constant__ CUtensorMap map_blo, const __grid_constant__ CUtensorMap map_c, TcGrid g,
+               Epi epi, float* __restrict__ partial, int* __restrict__ err)
 {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     // 128B-swizzled TMA tiles and UMMA descriptors need 1024-byte alignment
@@ -175,6 +181,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
         tc::prefetch_tensormap(&map_a);
         tc::prefetch_tensormap(&map_b);
         if (B_SPLIT) tc::prefetch_tensormap(&map_blo);
+        if (C_TMA) tc::prefetch_tensormap(&map_c);
     }
     if (warp == 1) {
         tc::tmem_alloc(&sm.tmem_addr, kTcTmemCols);
@@ -379,52 +386,104 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                 }
             }
             if (stop || tc_aborted(sm)) break;
-            // Coalesced epilogue: this warp owns rows m0+32q .. +31 and
-            // columns n0+64*slice .. +63.  Per 16-column chunk, lane = row
-            // writes its 16 values into the staging block (row stride 17:
-            // conflict-free), then lanes 0-15 / 16-31 read rows 2i / 2i+1
-            // column-wise and store 16 consecutive columns each.
             const int rbase = t.m0 + 32 * q;
             const int cbase = t.n0 + 64 * slice;
-            const int rsub = lane >> 4, csub = lane & 15;
+            if constexpr (C_TMA) {
+                // TMA-store epilogue: per 16-column chunk, lane = row applies
+                // the functor, writes the chunk into one of two 64B-swizzled
+                // staging buffers, and lane 0 issues one bulk store (the
+                // split-K partials go to [split][M][N] through a 3-D map);
+                // rows and columns outside the output are clipped by TMA
+                const int row = rbase + lane;
 #pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                __syncwarp();
-#pragma unroll
-                for (int jj = 0; jj < 16; ++jj) stg[lane * kTcStageLd + jj] = acc[c * 16 + jj];
-                __syncwarp();
-                const int n = cbase + c * 16 + csub;
-                if (partial) {
-#pragma unroll 4
-                    for (int i = 0; i < 16; ++i) {
-                        const int row = rbase + 2 * i + rsub;
-                        if (row < g.M && n < g.N)
-                            partial[((long)t.z * g.M + row) * g.N + n] = stg[(2 * i + rsub) * kTcStageLd + csub];
-                    }
-                } else if constexpr (Epi::kReads) {
-                    // the chunk's global epilogue inputs, all loads in flight together
+                for (int c = 0; c < 4; ++c) {
+                    const int n = cbase + c * 16;
                     float pre[16];
 #pragma unroll
-                    for (int i = 0; i < 16; ++i) {
-                        const int row = rbase + 2 * i + rsub;
-                        pre[i] = (row < g.M && n < g.N) ? epi.prefetch(row, n) : 0.f;
-                    }
+                    for (int i = 0; i < 16; ++i) pre[i] = 0.f;
+                    if constexpr (Epi::kReads) {
+                        if (!partial && row < g.M) {
+                            const float* pp = epi.pre_ptr() + (long)row * epi.tma_ld() + n;
+                            if (n + 16 <= g.N) {
 #pragma unroll
-                    for (int i = 0; i < 16; ++i) {
-                        const int r = 2 * i + rsub;
-                        const int row = rbase + r;
-                        if (row < g.M && n < g.N) epi.finish(row, n, stg[r * kTcStageLd + csub], pre[i]);
+                                for (int v4 = 0; v4 < 4; ++v4) {
+                                    const float4 x4 = *reinterpret_cast<const float4*>(pp + 4 * v4);
+                                    pre[4 * v4] = x4.x; pre[4 * v4 + 1] = x4.y; pre[4 * v4 + 2] = x4.z; pre[4 * v4 + 3] = x4.w;
+                                }
+                            } else {
+                                for (int i = 0; i < 16 && n + i < g.N; ++i) pre[i] = pp[i];
+                            }
+                        }
                     }
-                } else {
+                    float* buf = sm.stage_tma[dw] + (c & 1) * 512;
+                    if (lane == 0) tc::bulk_wait_read<1>();  // the store that last read this buffer is done
+                    __syncwarp();
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        float o[4];
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            const float v = acc[16 * c + 4 * j + e];
+                            o[e] = partial ? v : epi.value(v, pre[4 * j + e]);
+                        }
+                        *reinterpret_cast<float4*>(buf + lane * 16 + ((j ^ ((lane >> 1) & 3)) << 2)) =
+                            make_float4(o[0], o[1], o[2], o[3]);
+                    }
+                    tc::fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) {
+                        if (partial) tc::tma_store_3d(&map_c, buf, n, rbase, t.z);
+                        else tc::tma_store_2d(&map_c, buf, n, rbase);
+                        tc::bulk_commit();
+                    }
+                }
+            } else {
+                // Coalesced epilogue: this warp owns rows m0+32q .. +31 and
+                // columns n0+64*slice .. +63.  Per 16-column chunk, lane = row
+                // writes its 16 values into the staging block (row stride 17:
+                // conflict-free), then lanes 0-15 / 16-31 read rows 2i / 2i+1
+                // column-wise and store 16 consecutive columns each.
+                const int rsub = lane >> 4, csub = lane & 15;
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    __syncwarp();
+#pragma unroll
+                    for (int jj = 0; jj < 16; ++jj) stg[lane * kTcStageLd + jj] = acc[c * 16 + jj];
+                    __syncwarp();
+                    const int n = cbase + c * 16 + csub;
+                    if (partial) {
 #pragma unroll 4
-                    for (int i = 0; i < 16; ++i) {
-                        const int r = 2 * i + rsub;
-                        const int row = rbase + r;
-                        if (row < g.M && n < g.N) epi.finish(row, n, stg[r * kTcStageLd + csub], 0.f);
+                        for (int i = 0; i < 16; ++i) {
+                            const int row = rbase + 2 * i + rsub;
+                            if (row < g.M && n < g.N)
+                                partial[((long)t.z * g.M + row) * g.N + n] = stg[(2 * i + rsub) * kTcStageLd + csub];
+                        }
+                    } else if constexpr (Epi::kReads) {
+                        // the chunk's global epilogue inputs, all loads in flight together
+                        float pre[16];
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) {
+                            const int row = rbase + 2 * i + rsub;
+                            pre[i] = (row < g.M && n < g.N) ? epi.prefetch(row, n) : 0.f;
+                        }
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) {
+                            const int r = 2 * i + rsub;
+                            const int row = rbase + r;
+                            if (row < g.M && n < g.N) epi.finish(row, n, stg[r * kTcStageLd + csub], pre[i]);
+                        }
+                    } else {
+#pragma unroll 4
+                        for (int i = 0; i < 16; ++i) {
+                            const int r = 2 * i + rsub;
+                            const int row = rbase + r;
+                            if (row < g.M && n < g.N) epi.finish(row, n, stg[r * kTcStageLd + csub], 0.f);
+                        }
                     }
                 }
             }
         }
+        if (C_TMA && lane == 0) tc::bulk_wait_all();  // stores complete before the CTA exits
     }
     tc::tc_fence_before();
     __syncthreads();
@@ -459,16 +518,20 @@ inline TcGrid tc_grid(int M, int N, int K, int sm_count, int max_splits) {
 
 // Launches the persistent kernel: min(units, SMs) CTAs.  With B_SPLIT, B
 // arrives as two tensors, hi (already rounded to TF32) through mb and
-// lo = B - hi through mb_lo, and is not split on the device.
-template <bool A_MN, bool B_MN, bool B_SPLIT = false, class Epi>
+// lo = B - hi through mb_lo, and is not split on the device.  With C_TMA the
+// epilogue writes through mc (box 16 x 32, 64-byte swizzle; for split-K
+// partials a 3-D map over [split][M][N]).
+template <bool A_MN, bool B_MN, bool B_SPLIT = false, bool C_TMA = false, class Epi>
 inline cudaError_t launch_tc_kernel(cudaStream_t stream, int sm_count, const CUtensorMap& ma, const CUtensorMap& mb,
-                                    const CUtensorMap& mb_lo, const TcGrid& g, Epi epi, float* partial, int* err)
+                                    const CUtensorMap& mb_lo, const CUtensorMap& mc, const TcGrid& g, Epi epi,
+                                    float* partial, int* err)
 {
-    const cudaError_t a = cudaFuncSetAttribute(gemm_tc_kernel<A_MN, B_MN, B_SPLIT, Epi>,
+    const cudaError_t a = cudaFuncSetAttribute(gemm_tc_kernel<A_MN, B_MN, B_SPLIT, C_TMA, Epi>,
                                                cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTcSmemBytes);
     if (a != cudaSuccess) return a;
     const int grid = std::max(1, std::min(g.units, sm_count));
-    gemm_tc_kernel<A_MN, B_MN, B_SPLIT, Epi><<<grid, kTcThreads, kTcSmemBytes, stream>>>(ma, mb, mb_lo, g, epi, partial, err);
+    gemm_tc_kernel<A_MN, B_MN, B_SPLIT, C_TMA, Epi>
+        <<<grid, kTcThreads, kTcSmemBytes, stream>>>(ma, mb, mb_lo, mc, g, epi, partial, err);
     return cudaGetLastError();
 }
 
