@@ -141,14 +141,14 @@ void launch_tc(hx_runtime* rt, int M, int N, int K, const float* A, long lda, co
     if (ws) {
         c_tma = N % 4 == 0;
         if (c_tma)
-            mc = make_map3(ws, N, M, g.splits, N, (uint64_t)M * N, 16, 32, CU_TENSOR_MAP_SWIZZLE_64B);
+            mc = make_map3(ws, N, M, g.splits, N, (uint64_t)M * N, 8, 32, CU_TENSOR_MAP_SWIZZLE_32B);
     } else {
         const float* out = epi.tma_out();
         const long ldc = epi.tma_ld();
         const float* pre = epi.pre_ptr();
         c_tma = epi.tma_ok() && out && ((reinterpret_cast<uintptr_t>(out) | reinterpret_cast<uintptr_t>(pre)) & 15) == 0 &&
                 ldc % 4 == 0;
-        if (c_tma) mc = make_map(out, N, M, ldc, 16, 32, CU_TENSOR_MAP_SWIZZLE_64B);
+        if (c_tma) mc = make_map(out, N, M, ldc, 8, 32, CU_TENSOR_MAP_SWIZZLE_32B);
     }
     cudaError_t rc;
     if (split)

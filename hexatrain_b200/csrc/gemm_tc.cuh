@@ -30,11 +30,14 @@
 // overlaps the next tile's first k-block.
 //
 // Roles (22 warps):
-//   warp 0      TMA producer: the raw A tile (16 KB) and the B tile (32 KB)
-//               of each 32-deep k-block into a 2-stage ring (full[]);
+//   warp 0      TMA producers: lane 0 loads the raw A tile (16 KB) of each
+//               32-deep k-block into a 4-slot ring (full_a[]), freed as soon
+//               as the converters hold the values; lane 1 the B tile (hi, or
+//               hi and lo when B comes pre-split; 32/64 KB) into a 2-slot
+//               ring (full_b[]), freed by the MMA's commit;
 //   warp 1      TMEM owner and MMA issuer: 12 tcgen05.mma (M128 N256 K8,
 //               kind::tf32, A from TMEM) per k-block; tcgen05.commit frees
-//               the B stage (empty[]) and the A slot (a_free[]) and hands the
+//               the B slot (empty_b[]) and the A slot (a_free[]) and hands the
 //               accumulator to the drain warps (acc_ready);
 //   warps 2-5   converters.  A: thread = tile row (TMEM lane 32(w%4) +
 //               lane) reads its 32 values of the raw tile, frees the raw A
@@ -42,12 +45,12 @@
 //               on a_ready[].  B: split the stage's B tile into hi (in place)
 //               and lo, fence the generic->async proxy, arrive on b_ready[];
 //   warps 6-21  drain: one TMEM row per thread, 64 columns per warp, added
-//               into FP32 registers; at the end of a unit, stage the 32x64
-//               block through shared memory 16 columns at a time so that each
-//               store instruction writes two 64-byte row segments
-//               (coalesced), applying the epilogue functor (or storing split-K
-//               partials); the epilogue's own global inputs for a chunk are
-//               loaded before any is used.
+//               into FP32 registers; at the end of a unit, apply the epilogue
+//               functor 8 columns at a time and hand each 32x8 chunk to a TMA
+//               bulk store (single-output epilogues), or stage it so that each
+//               store instruction writes four 32-byte row segments; the
+//               epilogue's own global inputs for a chunk are loaded before
+//               any is used.
 // Layouts: a K-major A tile arrives 128B-swizzled (row m's 16-byte chunk c
 // at ((c ^ (m & 7)) << 4)), an MN-major A tile unswizzled (K-row k at
 // 512 k bytes, so that lanes read consecutive words).  B is K-major with the
@@ -65,7 +68,10 @@
 
 namespace hx {
 
-constexpr int kTcBM = 128, kTcBN = 256, kTcBK = 32, kTcStages = 2;
+// A (16 KB per k-block, from HBM) and B (hi + lo, 64 KB per k-block) have
+// separate rings: a raw A slot is free as soon as the converters have read
+// it, so A loads run up to kTcAStages k-blocks ahead of the MMA.
+constexpr int kTcBM = 128, kTcBN = 256, kTcBK = 32, kTcAStages = 4, kTcBStages = 2;
 constexpr int kTcATileFloats = kTcBM * kTcBK;  // 16 KB
 constexpr int kTcBTileFloats = kTcBN * kTcBK;  // 32 KB
 constexpr int kTcConvWarps = 4, kTcDrainWarps = 16;
@@ -76,20 +82,21 @@ constexpr int kTcASlots = 3;
 constexpr uint32_t kTcTmemCols = 512;
 constexpr uint32_t kTcColA = kTcBN;  // A slots after the accumulator: 64 columns each (hi 32, lo 32)
 static_assert(kTcColA + 64 * kTcASlots <= kTcTmemCols, "TMEM budget");
-constexpr int kTcStageLd = 17;  // epilogue staging row stride (floats): 16 columns + 1 pad
-// TMA-store epilogue: per drain warp two 32x16 fp32 chunks (2 KB each),
-// 64-byte swizzled as the output tensor map's box expects
-constexpr int kTcTmaStageFloats = 2 * 32 * 16;
+constexpr int kTcStageLd = 9;  // epilogue staging row stride (floats): 8 columns + 1 pad
+// TMA-store epilogue: per drain warp two 32x8 fp32 chunks (1 KB each),
+// 32-byte swizzled as the output tensor map's box expects
+constexpr int kTcTmaStageFloats = 2 * 32 * 8;
 
 struct TcSmem {
-    float a_raw[kTcStages][kTcATileFloats];
-    float b_hi[kTcStages][kTcBTileFloats];
-    float b_lo[kTcStages][kTcBTileFloats];
+    float a_raw[kTcAStages][kTcATileFloats];
+    float b_hi[kTcBStages][kTcBTileFloats];
+    float b_lo[kTcBStages][kTcBTileFloats];
     union {
         float stage[kTcDrainWarps][32 * kTcStageLd];
         float stage_tma[kTcDrainWarps][kTcTmaStageFloats];
     };
-    uint64_t full[kTcStages], b_ready[kTcStages], empty[kTcStages];
+    uint64_t full_a[kTcAStages], empty_a[kTcAStages];
+    uint64_t full_b[kTcBStages], b_ready[kTcBStages], empty_b[kTcBStages];
     uint64_t a_ready[kTcASlots], a_free[kTcASlots];
     uint64_t acc_ready, acc_free, drain;
     uint32_t tmem_addr;
@@ -148,6 +155,14 @@ __device__ __forceinline__ float4 tf32_hi(float4 x) {
     return make_float4(tf32_round(x.x), tf32_round(x.y), tf32_round(x.z), tf32_round(x.w));
 }
 
+// acc[8 c + j] for a runtime chunk c, by selection (keeps acc in registers)
+__device__ __forceinline__ float chunk8(const float (&acc)[64], int c, int j) {
+    float v = acc[j];
+#pragma unroll
+    for (int k = 1; k < 8; ++k) v = (c == k) ? acc[8 * k + j] : v;
+    return v;
+}
+
 template <bool A_MN, bool B_MN, bool B_SPLIT, bool C_TMA, class Epi>
 __global__ void __launch_bounds__(kTcThreads, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
@@ -162,10 +177,14 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kTcStages; ++s) {
-            tc::mbar_init(&sm.full[s], 1);
+        for (int s = 0; s < kTcAStages; ++s) {
+            tc::mbar_init(&sm.full_a[s], 1);
+            tc::mbar_init(&sm.empty_a[s], kTcConvWarps);  // the A warps, once they hold the values
+        }
+        for (int s = 0; s < kTcBStages; ++s) {
+            tc::mbar_init(&sm.full_b[s], 1);
             tc::mbar_init(&sm.b_ready[s], kTcConvThreads);
-            tc::mbar_init(&sm.empty[s], 1 + kTcConvWarps);  // the MMA's commit (B) + the A warps (raw A)
+            tc::mbar_init(&sm.empty_b[s], 1);             // the MMA's commit
         }
         for (int j = 0; j < kTcASlots; ++j) {
             tc::mbar_init(&sm.a_ready[j], kTcConvWarps);
@@ -193,36 +212,45 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
     const uint32_t tmem = sm.tmem_addr;
 
     if (warp == 0) {
-        // ---------------- TMA producer ----------------
-        if (lane == 0) {
-            uint32_t issued_parity[kTcStages];
-            bool issued[kTcStages];
-            for (int s = 0; s < kTcStages; ++s) issued[s] = false;
+        // ---------------- TMA producers: lane 0 the A ring, lane 1 the B ring
+        if (lane < 2) {
+            const bool ring_a = lane == 0;
+            const int ns = ring_a ? kTcAStages : kTcBStages;
+            uint32_t issued_parity[kTcAStages];
+            bool issued[kTcAStages];
+            for (int s = 0; s < kTcAStages; ++s) issued[s] = false;
             uint32_t it = 0;  // k-blocks issued by this CTA
             bool stop = false;
             for (int u = blockIdx.x; u < g.units && !stop; u += gridDim.x) {
                 const TcUnit t = tc_unit(g, u);
                 for (int kb = 0; kb < t.nk; ++kb, ++it) {
-                    const int s = it % kTcStages;
-                    const uint32_t ph = (it / kTcStages) & 1;
-                    if (!tc::mbar_wait(&sm.empty[s], ph ^ 1)) { tc_fail(sm, err, kTcErrProducer); stop = true; break; }
+                    const int s = it % ns;
+                    const uint32_t ph = (it / ns) & 1;
+                    uint64_t* full = ring_a ? &sm.full_a[s] : &sm.full_b[s];
+                    if (!tc::mbar_wait(ring_a ? &sm.empty_a[s] : &sm.empty_b[s], ph ^ 1)) {
+                        tc_fail(sm, err, kTcErrProducer); stop = true; break;
+                    }
                     if (tc_aborted(sm)) { stop = true; break; }
-                    tc::mbar_arrive_expect_tx(&sm.full[s], (kTcATileFloats + (B_SPLIT ? 2 : 1) * kTcBTileFloats) * 4);
                     const int k = t.kbeg + kb * kTcBK;
-                    if (!A_MN)
-                        tc::tma_load_2d(sm.a_raw[s], &map_a, &sm.full[s], k, t.m0);   // box 32 (K) x 128 rows
-                    else
-                        tc::tma_load_2d(sm.a_raw[s], &map_a, &sm.full[s], t.m0, k);   // box 128 (M) x 32 K-rows
+                    if (ring_a) {
+                        tc::mbar_arrive_expect_tx(full, kTcATileFloats * 4);
+                        if (!A_MN)
+                            tc::tma_load_2d(sm.a_raw[s], &map_a, full, k, t.m0);   // box 32 (K) x 128 rows
+                        else
+                            tc::tma_load_2d(sm.a_raw[s], &map_a, full, t.m0, k);   // box 128 (M) x 32 K-rows
+                    } else {
+                        tc::mbar_arrive_expect_tx(full, (B_SPLIT ? 2 : 1) * kTcBTileFloats * 4);
 #pragma unroll
-                    for (int part = 0; part < (B_SPLIT ? 2 : 1); ++part) {
-                        float* dst = part ? sm.b_lo[s] : sm.b_hi[s];
-                        const CUtensorMap* mp = part ? &map_blo : &map_b;
-                        if (!B_MN) {
-                            tc::tma_load_2d(dst, mp, &sm.full[s], k, t.n0);    // box 32 (K) x 256 rows
-                        } else {
+                        for (int part = 0; part < (B_SPLIT ? 2 : 1); ++part) {
+                            float* dst = part ? sm.b_lo[s] : sm.b_hi[s];
+                            const CUtensorMap* mp = part ? &map_blo : &map_b;
+                            if (!B_MN) {
+                                tc::tma_load_2d(dst, mp, full, k, t.n0);    // box 32 (K) x 256 rows
+                            } else {
 #pragma unroll
-                            for (int c = 0; c < kTcBN / 32; ++c)
-                                tc::tma_load_2d(dst + c * 1024, mp, &sm.full[s], t.n0 + 32 * c, k);
+                                for (int c = 0; c < kTcBN / 32; ++c)
+                                    tc::tma_load_2d(dst + c * 1024, mp, full, t.n0 + 32 * c, k);
+                            }
                         }
                     }
                     issued[s] = true;
@@ -231,8 +259,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
             }
             if (tc_aborted(sm)) {
                 // let our own loads land before the CTA can exit
-                for (int s = 0; s < kTcStages; ++s)
-                    if (issued[s]) tc::mbar_wait(&sm.full[s], issued_parity[s]);
+                for (int s = 0; s < ns; ++s)
+                    if (issued[s]) tc::mbar_wait(ring_a ? &sm.full_a[s] : &sm.full_b[s], issued_parity[s]);
             }
         }
     } else if (warp == 1) {
@@ -250,11 +278,11 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
             for (int u = blockIdx.x; u < g.units && !stop; u += gridDim.x) {
                 const TcUnit t = tc_unit(g, u);
                 for (int kb = 0; kb < t.nk; ++kb, ++it) {
-                    const int s = it % kTcStages;
-                    const uint32_t ph = (it / kTcStages) & 1;
+                    const int s = it % kTcBStages;
+                    const uint32_t ph = (it / kTcBStages) & 1;
                     const int j = it % kTcASlots;
                     if (!tc::mbar_wait(&sm.a_ready[j], (it / kTcASlots) & 1)) { tc_fail(sm, err, kTcErrMma); stop = true; break; }
-                    if (!tc::mbar_wait(&sm.b_ready[s], ph)) { tc_fail(sm, err, kTcErrMma); stop = true; break; }
+                    if (!tc::mbar_wait(B_SPLIT ? &sm.full_b[s] : &sm.b_ready[s], ph)) { tc_fail(sm, err, kTcErrMma); stop = true; break; }
                     if (!tc::mbar_wait(&sm.acc_free, (it & 1) ^ 1)) { tc_fail(sm, err, kTcErrMma); stop = true; break; }
                     if (tc_aborted(sm)) { stop = true; break; }
                     tc::tc_fence_after();
@@ -273,7 +301,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                         const uint64_t dbh = tc::smem_desc(bh + k * b_step, b_lbo, b_sbo, b_lay);
                         tc::mma_tf32_ts(tmem, ah + 8 * k, dbh, idesc, 1u);
                     }
-                    tc::mma_commit(&sm.empty[s]);
+                    tc::mma_commit(&sm.empty_b[s]);
                     tc::mma_commit(&sm.a_free[j]);
                     tc::mma_commit(&sm.acc_ready);
                 }
@@ -293,9 +321,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
         for (int u = blockIdx.x; u < g.units && !stop; u += gridDim.x) {
             const TcUnit t = tc_unit(g, u);
             for (int kb = 0; kb < t.nk; ++kb, ++it) {
-                const int s = it % kTcStages;
-                const uint32_t ph = (it / kTcStages) & 1;
-                if (!tc::mbar_wait(&sm.full[s], ph)) { tc_fail(sm, err, kTcErrConverter); stop = true; break; }
+                const int sa = it % kTcAStages, s = it % kTcBStages;
+                if (!tc::mbar_wait(&sm.full_a[sa], (it / kTcAStages) & 1)) { tc_fail(sm, err, kTcErrConverter); stop = true; break; }
                 if (tc_aborted(sm)) { stop = true; break; }
                 {
                     // row m's 32 K-values -> hi/lo in A slot it % 3, 16 at a time
@@ -304,7 +331,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                         tc_fail(sm, err, kTcErrConverter); stop = true; break;
                     }
                     tc::tc_fence_after();
-                    const float* raw = sm.a_raw[s];
+                    const float* raw = sm.a_raw[sa];
 #pragma unroll
                     for (int h = 0; h < 2; ++h) {
                         float x[16];
@@ -330,13 +357,16 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                         tc::tmem_st_32x32b_x16(a_lane + 64 * j + 32 + 16 * h, lo);
                     }
                     __syncwarp();
-                    if (lane == 0) tc::mbar_arrive(&sm.empty[s]);  // raw A read
+                    if (lane == 0) tc::mbar_arrive(&sm.empty_a[sa]);  // raw A read
                     tc::tmem_st_wait();
                     tc::tc_fence_before();
                     __syncwarp();
                     if (lane == 0) tc::mbar_arrive(&sm.a_ready[j]);
                 }
-                if (!B_SPLIT) {
+                if (!B_SPLIT) {  // pre-split B goes from its TMA barrier straight to the MMA
+                    if (!tc::mbar_wait(&sm.full_b[s], (it / kTcBStages) & 1)) {
+                        tc_fail(sm, err, kTcErrConverter); stop = true; break;
+                    }
                     float4* bh = reinterpret_cast<float4*>(sm.b_hi[s]);
                     float4* bl = reinterpret_cast<float4*>(sm.b_lo[s]);
 #pragma unroll 4
@@ -347,8 +377,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                         bl[i] = make_float4(y.x - gg.x, y.y - gg.y, y.z - gg.z, y.w - gg.w);
                     }
                     tc::fence_proxy_async_smem();
+                    tc::mbar_arrive(&sm.b_ready[s]);
                 }
-                tc::mbar_arrive(&sm.b_ready[s]);
             }
         }
     } else {
@@ -389,44 +419,45 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
             const int rbase = t.m0 + 32 * q;
             const int cbase = t.n0 + 64 * slice;
             if constexpr (C_TMA) {
-                // TMA-store epilogue: per 16-column chunk, lane = row applies
-                // the functor, writes the chunk into one of two 64B-swizzled
-                // staging buffers, and lane 0 issues one bulk store (the
-                // split-K partials go to [split][M][N] through a 3-D map);
-                // rows and columns outside the output are clipped by TMA
+                // TMA-store epilogue: per 8-column chunk, lane = row applies
+                // the functor, writes the chunk into one of two 32B-swizzled
+                // staging buffers (row r's 16-byte half h at (h ^ ((r >> 2) & 1))),
+                // and lane 0 issues one bulk store (the split-K partials go to
+                // [split][M][N] through a 3-D map); rows and columns outside
+                // the output are clipped by TMA
                 const int row = rbase + lane;
 #pragma unroll
-                for (int c = 0; c < 4; ++c) {
-                    const int n = cbase + c * 16;
-                    float pre[16];
+                for (int c = 0; c < 8; ++c) {
+                    const int n = cbase + c * 8;
+                    float pre[8];
 #pragma unroll
-                    for (int i = 0; i < 16; ++i) pre[i] = 0.f;
+                    for (int i = 0; i < 8; ++i) pre[i] = 0.f;
                     if constexpr (Epi::kReads) {
                         if (!partial && row < g.M) {
                             const float* pp = epi.pre_ptr() + (long)row * epi.tma_ld() + n;
-                            if (n + 16 <= g.N) {
+                            if (n + 8 <= g.N) {
 #pragma unroll
-                                for (int v4 = 0; v4 < 4; ++v4) {
+                                for (int v4 = 0; v4 < 2; ++v4) {
                                     const float4 x4 = *reinterpret_cast<const float4*>(pp + 4 * v4);
                                     pre[4 * v4] = x4.x; pre[4 * v4 + 1] = x4.y; pre[4 * v4 + 2] = x4.z; pre[4 * v4 + 3] = x4.w;
                                 }
                             } else {
-                                for (int i = 0; i < 16 && n + i < g.N; ++i) pre[i] = pp[i];
+                                for (int i = 0; i < 8 && n + i < g.N; ++i) pre[i] = pp[i];
                             }
                         }
                     }
-                    float* buf = sm.stage_tma[dw] + (c & 1) * 512;
+                    float* buf = sm.stage_tma[dw] + (c & 1) * 256;
                     if (lane == 0) tc::bulk_wait_read<1>();  // the store that last read this buffer is done
                     __syncwarp();
 #pragma unroll
-                    for (int j = 0; j < 4; ++j) {
+                    for (int h = 0; h < 2; ++h) {
                         float o[4];
 #pragma unroll
                         for (int e = 0; e < 4; ++e) {
-                            const float v = acc[16 * c + 4 * j + e];
-                            o[e] = partial ? v : epi.value(v, pre[4 * j + e]);
+                            const float v = acc[8 * c + 4 * h + e];
+                            o[e] = partial ? v : epi.value(v, pre[4 * h + e]);
                         }
-                        *reinterpret_cast<float4*>(buf + lane * 16 + ((j ^ ((lane >> 1) & 3)) << 2)) =
+                        *reinterpret_cast<float4*>(buf + lane * 8 + ((h ^ ((lane >> 2) & 1)) << 2)) =
                             make_float4(o[0], o[1], o[2], o[3]);
                     }
                     tc::fence_proxy_async_smem();
@@ -439,43 +470,44 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                 }
             } else {
                 // Coalesced epilogue: this warp owns rows m0+32q .. +31 and
-                // columns n0+64*slice .. +63.  Per 16-column chunk, lane = row
-                // writes its 16 values into the staging block (row stride 17:
-                // conflict-free), then lanes 0-15 / 16-31 read rows 2i / 2i+1
-                // column-wise and store 16 consecutive columns each.
-                const int rsub = lane >> 4, csub = lane & 15;
-#pragma unroll
-                for (int c = 0; c < 4; ++c) {
+                // columns n0+64*slice .. +63.  Per 8-column chunk, lane = row
+                // writes its 8 values into the staging block (row stride 9:
+                // conflict-free), then lane (r, c) = (lane / 8, lane % 8) reads
+                // rows 4i + r column-wise, so that each store instruction
+                // writes four 32-byte row segments.
+                const int rsub = lane >> 3, csub = lane & 7;
+#pragma unroll 1
+                for (int c = 0; c < 8; ++c) {
                     __syncwarp();
 #pragma unroll
-                    for (int jj = 0; jj < 16; ++jj) stg[lane * kTcStageLd + jj] = acc[c * 16 + jj];
+                    for (int jj = 0; jj < 8; ++jj) stg[lane * kTcStageLd + jj] = chunk8(acc, c, jj);
                     __syncwarp();
-                    const int n = cbase + c * 16 + csub;
+                    const int n = cbase + c * 8 + csub;
                     if (partial) {
-#pragma unroll 4
-                        for (int i = 0; i < 16; ++i) {
-                            const int row = rbase + 2 * i + rsub;
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) {
+                            const int row = rbase + 4 * i + rsub;
                             if (row < g.M && n < g.N)
-                                partial[((long)t.z * g.M + row) * g.N + n] = stg[(2 * i + rsub) * kTcStageLd + csub];
+                                partial[((long)t.z * g.M + row) * g.N + n] = stg[(4 * i + rsub) * kTcStageLd + csub];
                         }
                     } else if constexpr (Epi::kReads) {
                         // the chunk's global epilogue inputs, all loads in flight together
-                        float pre[16];
+                        float pre[8];
 #pragma unroll
-                        for (int i = 0; i < 16; ++i) {
-                            const int row = rbase + 2 * i + rsub;
+                        for (int i = 0; i < 8; ++i) {
+                            const int row = rbase + 4 * i + rsub;
                             pre[i] = (row < g.M && n < g.N) ? epi.prefetch(row, n) : 0.f;
                         }
 #pragma unroll
-                        for (int i = 0; i < 16; ++i) {
-                            const int r = 2 * i + rsub;
+                        for (int i = 0; i < 8; ++i) {
+                            const int r = 4 * i + rsub;
                             const int row = rbase + r;
                             if (row < g.M && n < g.N) epi.finish(row, n, stg[r * kTcStageLd + csub], pre[i]);
                         }
                     } else {
-#pragma unroll 4
-                        for (int i = 0; i < 16; ++i) {
-                            const int r = 2 * i + rsub;
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) {
+                            const int r = 4 * i + rsub;
                             const int row = rbase + r;
                             if (row < g.M && n < g.N) epi.finish(row, n, stg[r * kTcStageLd + csub], 0.f);
                         }
