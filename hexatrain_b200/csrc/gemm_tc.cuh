@@ -12,51 +12,53 @@
 // hi*lo and lo*hi terms issued before hi*hi (four full-magnitude truncations
 // per k-block), and drained into FP32 registers with round-to-nearest adds.
 //
-// Tile shape.  A kind::tf32 MMA with M = 128, K = 8 costs about 120 cycles
-// whether N is 64 or 128, and about 140 at N = 256 with A read from TMEM
-// (measured on B200: 592 vs 1020 TFLOP/s of TF32 per GPU), so tiles are
-// 128 x 256.  A lives in TMEM: the A tile of each k-block is split by four
-// warps, one tile row per thread, straight from the landed raw tile into a
-// TMEM slot (hi 32 columns, lo 32 columns); the MMA reads only B (hi and lo)
-// from shared memory.  TMEM: the 256-column accumulator and three A slots.
-// The accumulator is single-buffered; the drain warps release it as soon as
-// their TMEM loads have landed, before adding.
+// Tile and orientation.  An output tile is 256 rows x 128 columns, computed
+// transposed: the MMA (kind::tf32, M = 128, N = 256, K = 8) takes op(B)^T --
+// 128 output columns -- as its A operand and op(A) -- 256 output rows -- as
+// its B operand, so TMEM lane l holds output column n0 + l and TMEM column c
+// output row m0 + c.  A warp that drains 32 lanes therefore holds 32
+// consecutive columns of each row, and the epilogue's global loads and stores
+// are whole 128-byte row segments straight from registers, with no staging.
+// A kind::tf32 MMA with M = 128 costs the same whether N is 64 or 256
+// (measured on B200), so N = 256 is the widest and cheapest per flop.
+//
+// The accumulator is double-buffered (two 256-column buffers fill the 512
+// TMEM columns): the MMAs of one k-block run while the drain warps read the
+// previous k-block's sums out of the other buffer, so the drain and the
+// epilogue overlap the tensor cores instead of stalling them.  Both operands
+// therefore live in shared memory, hi and lo side by side.
 //
 // Persistent: the grid is at most one CTA per SM, and each CTA walks work
-// units u = blockIdx.x, blockIdx.x + gridDim.x, ...  A unit is one 128x256
-// output tile of one K split; units are numbered with the N tile fastest so
-// that CTAs running together share A row blocks in L2.  The operand ring and
-// the A slots run on across unit boundaries, so the epilogue of one tile
-// overlaps the next tile's first k-block.
+// units u = blockIdx.x, blockIdx.x + gridDim.x, ...  A unit is one 256x128
+// output tile of one K split; units are numbered with the column tile
+// fastest so that CTAs running together share op(A) row blocks in L2.  The
+// rings run on across unit boundaries.
+//
+// Shared memory (224 KB): the op(B) stages ("W": 128 x 32, hi and lo, two
+// stages), the op(A) stages ("X": 256 x 32, hi and lo, two stages) and one
+// landing buffer for raw op(A) tiles.  W tiles arrive already split when B is
+// pre-split (weights), else raw into the hi half and are split in place.  X
+// tiles land raw in the landing buffer and are split from there into a free
+// X stage, so the next tile's load overlaps the current tile's split.
 //
 // Roles (22 warps):
-//   warp 0      TMA producers: lane 0 loads the raw A tile (16 KB) of each
-//               32-deep k-block into a 4-slot ring (full_a[]), freed as soon
-//               as the converters hold the values; lane 1 the B tile (hi, or
-//               hi and lo when B comes pre-split; 32/64 KB) into a 2-slot
-//               ring (full_b[]), freed by the MMA's commit;
-//   warp 1      TMEM owner and MMA issuer: 12 tcgen05.mma (M128 N256 K8,
-//               kind::tf32, A from TMEM) per k-block; tcgen05.commit frees
-//               the B slot (empty_b[]) and the A slot (a_free[]) and hands the
-//               accumulator to the drain warps (acc_ready);
-//   warps 2-5   converters.  A: thread = tile row (TMEM lane 32(w%4) +
-//               lane) reads its 32 values of the raw tile, frees the raw A
-//               stage, writes hi/lo into A slot g%3 with tcgen05.st, arrives
-//               on a_ready[].  B: split the stage's B tile into hi (in place)
-//               and lo, fence the generic->async proxy, arrive on b_ready[];
-//   warps 6-21  drain: one TMEM row per thread, 64 columns per warp, added
-//               into FP32 registers; at the end of a unit, apply the epilogue
-//               functor 8 columns at a time and hand each 32x8 chunk to a TMA
-//               bulk store (single-output epilogues), or stage it so that each
-//               store instruction writes four 32-byte row segments; the
-//               epilogue's own global inputs for a chunk are loaded before
-//               any is used.
-// Layouts: a K-major A tile arrives 128B-swizzled (row m's 16-byte chunk c
-// at ((c ^ (m & 7)) << 4)), an MN-major A tile unswizzled (K-row k at
-// 512 k bytes, so that lanes read consecutive words).  B is K-major with the
-// 128-byte swizzle, or MN-major as eight 32-wide boxes (LBO = 4 KB) in the
+//   warp 0      TMA producers: lane 0 the W tiles (16 or 32 KB per k-block),
+//               lane 1 the raw X tiles (32 KB) into the landing buffer;
+//   warp 1      TMEM owner and MMA issuer: 12 tcgen05.mma per k-block into
+//               accumulator buffer (k-block & 1); tcgen05.commit frees the W
+//               and X stages and hands the buffer to the drain warps;
+//   warps 2-5   converters: split a raw W stage in place (unless B came
+//               pre-split) and the landed X tile into a free X stage;
+//   warps 6-21  drain: warp (quarter q, slice s) adds TMEM lanes 32q..32q+31
+//               and columns 64s..64s+63 of each k-block's buffer into FP32
+//               registers, releasing the buffer once its loads have landed;
+//               at the end of a unit it applies the epilogue functor row by
+//               row (output columns on lanes).
+// Layouts: K-major tiles arrive 128B-swizzled (row r's 16-byte chunk c at
+// ((c ^ (r & 7)) << 4)); MN-major tiles as 32-wide boxes (4 KB apart) in the
 // 128-byte/32-byte-atom swizzle, the only shared-memory layout the MMA takes
-// for MN-major 32-bit operands.
+// for MN-major 32-bit operands.  The hi/lo split is elementwise, so split
+// tiles keep the layout TMA wrote.
 // Every barrier wait is bounded (tc::kWaitCycles); on timeout the kernel
 // records an error code, drains its own MMAs and TMA loads (bounded), frees
 // TMEM and returns.
@@ -68,37 +70,31 @@
 
 namespace hx {
 
-// A (16 KB per k-block, from HBM) and B (hi + lo, 64 KB per k-block) have
-// separate rings: a raw A slot is free as soon as the converters have read
-// it, so A loads run up to kTcAStages k-blocks ahead of the MMA.
-constexpr int kTcBM = 128, kTcBN = 256, kTcBK = 32, kTcAStages = 4, kTcBStages = 2;
-constexpr int kTcATileFloats = kTcBM * kTcBK;  // 16 KB
-constexpr int kTcBTileFloats = kTcBN * kTcBK;  // 32 KB
+constexpr int kTcBM = 256, kTcBN = 256, kTcBK = 32;  // pair tile: output rows, output columns; K per k-block
+constexpr int kTcHalf = 128;                         // rows of either operand one CTA of the pair holds
+constexpr int kTcStages = 3;                         // split W and X stages
+constexpr int kTcRawStages = 2;                      // landing buffers for raw X tiles
+constexpr int kTcTileFloats = kTcHalf * kTcBK;       // 16 KB
 constexpr int kTcConvWarps = 4, kTcDrainWarps = 16;
 constexpr int kTcConvThreads = 32 * kTcConvWarps;
 constexpr int kTcFirstDrainWarp = 2 + kTcConvWarps;
 constexpr int kTcThreads = 32 * (kTcFirstDrainWarp + kTcDrainWarps);  // 704
-constexpr int kTcASlots = 3;
-constexpr uint32_t kTcTmemCols = 512;
-constexpr uint32_t kTcColA = kTcBN;  // A slots after the accumulator: 64 columns each (hi 32, lo 32)
-static_assert(kTcColA + 64 * kTcASlots <= kTcTmemCols, "TMEM budget");
-constexpr int kTcStageLd = 9;  // epilogue staging row stride (floats): 8 columns + 1 pad
-// TMA-store epilogue: per drain warp two 32x8 fp32 chunks (1 KB each),
-// 32-byte swizzled as the output tensor map's box expects
-constexpr int kTcTmaStageFloats = 2 * 32 * 8;
+constexpr uint32_t kTcTmemCols = 512;                // two 256-column accumulators
+constexpr uint32_t kTcAccCols = kTcBM;
 
 struct TcSmem {
-    float a_raw[kTcAStages][kTcATileFloats];
-    float b_hi[kTcBStages][kTcBTileFloats];
-    float b_lo[kTcBStages][kTcBTileFloats];
-    union {
-        float stage[kTcDrainWarps][32 * kTcStageLd];
-        float stage_tma[kTcDrainWarps][kTcTmaStageFloats];
-    };
-    uint64_t full_a[kTcAStages], empty_a[kTcAStages];
-    uint64_t full_b[kTcBStages], b_ready[kTcBStages], empty_b[kTcBStages];
-    uint64_t a_ready[kTcASlots], a_free[kTcASlots];
-    uint64_t acc_ready, acc_free, drain;
+    float w_hi[kTcStages][kTcTileFloats];
+    float w_lo[kTcStages][kTcTileFloats];
+    float x_hi[kTcStages][kTcTileFloats];
+    float x_lo[kTcStages][kTcTileFloats];
+    float x_raw[kTcRawStages][kTcTileFloats];
+    // this CTA's own pipeline
+    uint64_t w_full[kTcStages], raw_full[kTcRawStages], raw_empty[kTcRawStages];
+    // arrived on by the pair MMA's commit, in both CTAs
+    uint64_t w_empty[kTcStages], x_empty[kTcStages], acc_ready[2];
+    // used in the even CTA only, arrived on by both CTAs
+    uint64_t w_ready[kTcStages], x_ready[kTcStages], acc_free[2];
+    uint64_t drain;
     uint32_t tmem_addr;
     int abort;
 };
@@ -107,7 +103,7 @@ static_assert(kTcSmemBytes <= 232448, "tcgen05 GEMM shared memory exceeds the 22
 
 enum TcError { kTcErrProducer = 1, kTcErrConverter = 2, kTcErrMma = 3, kTcErrEpilogue = 4 };
 
-// Work decomposition shared by every role.
+// Work decomposition shared by every role of both CTAs of a pair.
 struct TcGrid {
     int M, N, K;
     int tiles_m, tiles_n, splits;
@@ -141,8 +137,8 @@ __device__ __forceinline__ bool tc_aborted(TcSmem& sm) { return *reinterpret_cas
 
 // Nearest TF32 value (ties away from zero): add half a TF32 ulp to the
 // magnitude bits, clear the 13 low mantissa bits -- two integer operations,
-// which matters: the split of a 128x32 A tile and a 128x32 B tile per
-// k-block would otherwise fill the SM's integer pipe for as long as the
+// which matters: the split of the operand tiles of every k-block would
+// otherwise keep the SM's integer pipe busy for much of the time the
 // k-block's MMAs take.  Rounding (rather than truncating) leaves lo = x - hi
 // with either sign, so the MMA's own truncation of lo does not bias the
 // products.  NaN and infinity pass through; finite |x| >= 0x1.fffffp+127
@@ -155,103 +151,121 @@ __device__ __forceinline__ float4 tf32_hi(float4 x) {
     return make_float4(tf32_round(x.x), tf32_round(x.y), tf32_round(x.z), tf32_round(x.w));
 }
 
-// acc[8 c + j] for a runtime chunk c, by selection (keeps acc in registers)
-__device__ __forceinline__ float chunk8(const float (&acc)[64], int c, int j) {
-    float v = acc[j];
+// Splits one 16 KB tile `src` into hi (to `hi`, which may be `src`) and lo;
+// thread t of the converter warps takes every kTcConvThreads-th float4.
+__device__ __forceinline__ void tc_split_tile(const float* src, float* hi, float* lo, int t) {
+    const float4* s4 = reinterpret_cast<const float4*>(src);
+    float4* h4 = reinterpret_cast<float4*>(hi);
+    float4* l4 = reinterpret_cast<float4*>(lo);
 #pragma unroll
-    for (int k = 1; k < 8; ++k) v = (c == k) ? acc[8 * k + j] : v;
-    return v;
+    for (int i = t; i < kTcTileFloats / 4; i += kTcConvThreads) {
+        const float4 y = s4[i];
+        const float4 h = tf32_hi(y);
+        h4[i] = h;
+        l4[i] = make_float4(y.x - h.x, y.y - h.y, y.z - h.z, y.w - h.w);
+    }
 }
 
-template <bool A_MN, bool B_MN, bool B_SPLIT, bool C_TMA, class Epi>
+// TMA loads of one k-block's 128-row tile of a [rows][K] operand (K-major:
+// one box of 32 K x 128 rows) or a [K][rows] operand (MN-major: four boxes of
+// 32 x 32 K-rows, 4 KB apart).
+template <bool MN>
+__device__ __forceinline__ void tc_load_tile(float* dst, const CUtensorMap* map, uint64_t* bar, int k, int r0) {
+    if (!MN) {
+        tc::tma_load_2d(dst, map, bar, k, r0);
+    } else {
+#pragma unroll
+        for (int c = 0; c < kTcHalf / 32; ++c) tc::tma_load_2d(dst + c * 1024, map, bar, r0 + 32 * c, k);
+    }
+}
+
+// Shared-memory descriptor of k-step kk (8 K) of a split tile: K-major
+// 128B-swizzled rows of 128 bytes (SBO 1024, k-step 32 bytes), or MN-major
+// 32-wide boxes 4 KB apart (LBO), 4-K-row atoms 512 bytes apart (SBO),
+// k-step 8 K-rows = 1024 bytes.
+template <bool MN>
+__device__ __forceinline__ uint64_t tc_desc(const float* tile, int kk) {
+    return MN ? tc::smem_desc(tc::smem_u32(tile) + kk * 1024, 32 * 128, 512, tc::kLayoutSw128Base32)
+              : tc::smem_desc(tc::smem_u32(tile) + kk * 32, 16, 1024, tc::kLayoutSw128);
+}
+
+template <bool A_MN, bool B_MN, bool B_SPLIT, class Epi>
 __global__ void __launch_bounds__(kTcThreads, 1)
-gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
-               const __grid_constant__ CUtensorMap map_blo, const __grid_constant__ CUtensorMap map_c, TcGrid g,
-               Epi epi, float* __restrict__ partial, int* __restrict__ err)
+gemm_tc_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_w,
+               const __grid_constant__ CUtensorMap map_wlo, TcGrid g, Epi epi, float* __restrict__ partial,
+               int* __restrict__ err)
 {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     // 128B-swizzled TMA tiles and UMMA descriptors need 1024-byte alignment
-    // of the shared-memory address itself.
+    // of the shared-memory address itself (the same offset in both CTAs).
     const uint32_t pad = (1024u - (tc::smem_u32(smem_raw) & 1023u)) & 1023u;
     TcSmem& sm = *reinterpret_cast<TcSmem*>(smem_raw + pad);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = tc::cluster_ctarank();           // 0: issues the pair's MMAs
+    const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kTcAStages; ++s) {
-            tc::mbar_init(&sm.full_a[s], 1);
-            tc::mbar_init(&sm.empty_a[s], kTcConvWarps);  // the A warps, once they hold the values
+        for (int s = 0; s < kTcStages; ++s) {
+            tc::mbar_init(&sm.w_full[s], 1);
+            tc::mbar_init(&sm.w_empty[s], 1);
+            tc::mbar_init(&sm.x_empty[s], 1);
+            tc::mbar_init(&sm.w_ready[s], 2 * kTcConvWarps);
+            tc::mbar_init(&sm.x_ready[s], 2 * kTcConvWarps);
         }
-        for (int s = 0; s < kTcBStages; ++s) {
-            tc::mbar_init(&sm.full_b[s], 1);
-            tc::mbar_init(&sm.b_ready[s], kTcConvThreads);
-            tc::mbar_init(&sm.empty_b[s], 1);             // the MMA's commit
+        for (int r = 0; r < kTcRawStages; ++r) {
+            tc::mbar_init(&sm.raw_full[r], 1);
+            tc::mbar_init(&sm.raw_empty[r], kTcConvWarps);
         }
-        for (int j = 0; j < kTcASlots; ++j) {
-            tc::mbar_init(&sm.a_ready[j], kTcConvWarps);
-            tc::mbar_init(&sm.a_free[j], 1);
+        for (int b = 0; b < 2; ++b) {
+            tc::mbar_init(&sm.acc_ready[b], 1);
+            tc::mbar_init(&sm.acc_free[b], 2 * kTcDrainWarps);
         }
-        tc::mbar_init(&sm.acc_ready, 1);
-        tc::mbar_init(&sm.acc_free, kTcDrainWarps);
         tc::mbar_init(&sm.drain, 1);
         sm.abort = 0;
         tc::fence_mbar_init();
     }
     if (warp == 0 && lane == 0) {
-        tc::prefetch_tensormap(&map_a);
-        tc::prefetch_tensormap(&map_b);
-        if (B_SPLIT) tc::prefetch_tensormap(&map_blo);
-        if (C_TMA) tc::prefetch_tensormap(&map_c);
+        tc::prefetch_tensormap(&map_x);
+        tc::prefetch_tensormap(&map_w);
+        if (B_SPLIT) tc::prefetch_tensormap(&map_wlo);
     }
     if (warp == 1) {
-        tc::tmem_alloc(&sm.tmem_addr, kTcTmemCols);
-        tc::tmem_relinquish();
+        tc::tmem_alloc_pair(&sm.tmem_addr, kTcTmemCols);
+        tc::tmem_relinquish_pair();
     }
     tc::tc_fence_before();
     __syncthreads();
+    tc::cluster_sync();  // both CTAs' barriers exist before either arrives on the other's
     tc::tc_fence_after();
     const uint32_t tmem = sm.tmem_addr;
 
     if (warp == 0) {
-        // ---------------- TMA producers: lane 0 the A ring, lane 1 the B ring
+        // ---------------- TMA producers: lane 0 the W stages, lane 1 the X landing buffers
         if (lane < 2) {
-            const bool ring_a = lane == 0;
-            const int ns = ring_a ? kTcAStages : kTcBStages;
-            uint32_t issued_parity[kTcAStages];
-            bool issued[kTcAStages];
-            for (int s = 0; s < kTcAStages; ++s) issued[s] = false;
+            const bool ring_w = lane == 0;
+            const int ns = ring_w ? kTcStages : kTcRawStages;
+            uint32_t issued_parity[kTcStages];
+            bool issued[kTcStages];
+            for (int s = 0; s < kTcStages; ++s) issued[s] = false;
             uint32_t it = 0;  // k-blocks issued by this CTA
             bool stop = false;
-            for (int u = blockIdx.x; u < g.units && !stop; u += gridDim.x) {
+            for (int u = pair; u < g.units && !stop; u += npairs) {
                 const TcUnit t = tc_unit(g, u);
                 for (int kb = 0; kb < t.nk; ++kb, ++it) {
                     const int s = it % ns;
                     const uint32_t ph = (it / ns) & 1;
-                    uint64_t* full = ring_a ? &sm.full_a[s] : &sm.full_b[s];
-                    if (!tc::mbar_wait(ring_a ? &sm.empty_a[s] : &sm.empty_b[s], ph ^ 1)) {
-                        tc_fail(sm, err, kTcErrProducer); stop = true; break;
-                    }
+                    const bool ok = ring_w ? tc::mbar_wait(&sm.w_empty[s], ph ^ 1)
+                                           : tc::mbar_wait(&sm.raw_empty[s], ph ^ 1);
+                    if (!ok) { tc_fail(sm, err, kTcErrProducer); stop = true; break; }
                     if (tc_aborted(sm)) { stop = true; break; }
                     const int k = t.kbeg + kb * kTcBK;
-                    if (ring_a) {
-                        tc::mbar_arrive_expect_tx(full, kTcATileFloats * 4);
-                        if (!A_MN)
-                            tc::tma_load_2d(sm.a_raw[s], &map_a, full, k, t.m0);   // box 32 (K) x 128 rows
-                        else
-                            tc::tma_load_2d(sm.a_raw[s], &map_a, full, t.m0, k);   // box 128 (M) x 32 K-rows
+                    if (ring_w) {
+                        tc::mbar_arrive_expect_tx(&sm.w_full[s], (B_SPLIT ? 2 : 1) * kTcTileFloats * 4);
+                        tc_load_tile<B_MN>(sm.w_hi[s], &map_w, &sm.w_full[s], k, t.n0 + kTcHalf * rank);
+                        if (B_SPLIT) tc_load_tile<B_MN>(sm.w_lo[s], &map_wlo, &sm.w_full[s], k, t.n0 + kTcHalf * rank);
                     } else {
-                        tc::mbar_arrive_expect_tx(full, (B_SPLIT ? 2 : 1) * kTcBTileFloats * 4);
-#pragma unroll
-                        for (int part = 0; part < (B_SPLIT ? 2 : 1); ++part) {
-                            float* dst = part ? sm.b_lo[s] : sm.b_hi[s];
-                            const CUtensorMap* mp = part ? &map_blo : &map_b;
-                            if (!B_MN) {
-                                tc::tma_load_2d(dst, mp, full, k, t.n0);    // box 32 (K) x 256 rows
-                            } else {
-#pragma unroll
-                                for (int c = 0; c < kTcBN / 32; ++c)
-                                    tc::tma_load_2d(dst + c * 1024, mp, full, t.n0 + 32 * c, k);
-                            }
-                        }
+                        tc::mbar_arrive_expect_tx(&sm.raw_full[s], kTcTileFloats * 4);
+                        tc_load_tile<A_MN>(sm.x_raw[s], &map_x, &sm.raw_full[s], k, t.m0 + kTcHalf * rank);
                     }
                     issued[s] = true;
                     issued_parity[s] = ph;
@@ -260,124 +274,80 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
             if (tc_aborted(sm)) {
                 // let our own loads land before the CTA can exit
                 for (int s = 0; s < ns; ++s)
-                    if (issued[s]) tc::mbar_wait(ring_a ? &sm.full_a[s] : &sm.full_b[s], issued_parity[s]);
+                    if (issued[s]) tc::mbar_wait(ring_w ? &sm.w_full[s] : &sm.raw_full[s], issued_parity[s]);
             }
         }
     } else if (warp == 1) {
-        // ---------------- MMA issuer ----------------
-        if (lane == 0) {
-            constexpr uint32_t idesc = tc::idesc_tf32(kTcBM, kTcBN, false, B_MN);
-            // B K-major: SW128, SBO 1024, k-step = 32 bytes along the row.
-            // B MN-major: SW128 with 32-byte atoms, SBO 512, LBO 4 KB between
-            // 32-wide chunks, k-step = 8 K-rows = 1024 bytes.
-            constexpr uint32_t b_lbo = B_MN ? 32 * 128 : 16, b_sbo = B_MN ? 512 : 1024;
-            constexpr uint32_t b_lay = B_MN ? tc::kLayoutSw128Base32 : tc::kLayoutSw128;
-            constexpr uint32_t b_step = B_MN ? 1024 : 32;
+        // ---------------- MMA issuer (even CTA of the pair) ----------------
+        if (lane == 0 && rank == 0) {
+            // MMA A = op(B)^T (256 output columns, 128 per CTA),
+            // MMA B = op(A) (256 output rows, 128 per CTA)
+            constexpr uint32_t idesc = tc::idesc_tf32(2 * kTcHalf, kTcBM, B_MN, A_MN);
             uint32_t it = 0;
             bool stop = false;
-            for (int u = blockIdx.x; u < g.units && !stop; u += gridDim.x) {
+            for (int u = pair; u < g.units && !stop; u += npairs) {
                 const TcUnit t = tc_unit(g, u);
                 for (int kb = 0; kb < t.nk; ++kb, ++it) {
-                    const int s = it % kTcBStages;
-                    const uint32_t ph = (it / kTcBStages) & 1;
-                    const int j = it % kTcASlots;
-                    if (!tc::mbar_wait(&sm.a_ready[j], (it / kTcASlots) & 1)) { tc_fail(sm, err, kTcErrMma); stop = true; break; }
-                    if (!tc::mbar_wait(B_SPLIT ? &sm.full_b[s] : &sm.b_ready[s], ph)) { tc_fail(sm, err, kTcErrMma); stop = true; break; }
-                    if (!tc::mbar_wait(&sm.acc_free, (it & 1) ^ 1)) { tc_fail(sm, err, kTcErrMma); stop = true; break; }
+                    const int s = it % kTcStages;
+                    const uint32_t ph = (it / kTcStages) & 1;
+                    const int b = it & 1;
+                    if (!tc::mbar_wait(&sm.w_ready[s], ph)) { tc_fail(sm, err, kTcErrMma); stop = true; break; }
+                    if (!tc::mbar_wait(&sm.x_ready[s], ph)) { tc_fail(sm, err, kTcErrMma); stop = true; break; }
+                    if (!tc::mbar_wait(&sm.acc_free[b], ((it >> 1) & 1) ^ 1)) { tc_fail(sm, err, kTcErrMma); stop = true; break; }
                     if (tc_aborted(sm)) { stop = true; break; }
                     tc::tc_fence_after();
-                    const uint32_t ah = tmem + kTcColA + 64 * j, al = ah + 32;
-                    const uint32_t bh = tc::smem_u32(sm.b_hi[s]), bl = tc::smem_u32(sm.b_lo[s]);
+                    const uint32_t d = tmem + kTcAccCols * b;
                     // hi*lo and lo*hi first, then hi*hi
 #pragma unroll
                     for (int k = 0; k < kTcBK / 8; ++k) {
-                        const uint64_t dbh = tc::smem_desc(bh + k * b_step, b_lbo, b_sbo, b_lay);
-                        const uint64_t dbl = tc::smem_desc(bl + k * b_step, b_lbo, b_sbo, b_lay);
-                        tc::mma_tf32_ts(tmem, ah + 8 * k, dbl, idesc, k > 0 ? 1u : 0u);
-                        tc::mma_tf32_ts(tmem, al + 8 * k, dbh, idesc, 1u);
+                        const uint64_t wh = tc_desc<B_MN>(sm.w_hi[s], k), wl = tc_desc<B_MN>(sm.w_lo[s], k);
+                        const uint64_t xh = tc_desc<A_MN>(sm.x_hi[s], k), xl = tc_desc<A_MN>(sm.x_lo[s], k);
+                        tc::mma_tf32_pair(d, wh, xl, idesc, k > 0 ? 1u : 0u);
+                        tc::mma_tf32_pair(d, wl, xh, idesc, 1u);
                     }
 #pragma unroll
-                    for (int k = 0; k < kTcBK / 8; ++k) {
-                        const uint64_t dbh = tc::smem_desc(bh + k * b_step, b_lbo, b_sbo, b_lay);
-                        tc::mma_tf32_ts(tmem, ah + 8 * k, dbh, idesc, 1u);
-                    }
-                    tc::mma_commit(&sm.empty_b[s]);
-                    tc::mma_commit(&sm.a_free[j]);
-                    tc::mma_commit(&sm.acc_ready);
+                    for (int k = 0; k < kTcBK / 8; ++k)
+                        tc::mma_tf32_pair(d, tc_desc<B_MN>(sm.w_hi[s], k), tc_desc<A_MN>(sm.x_hi[s], k), idesc, 1u);
+                    tc::mma_commit_pair(&sm.w_empty[s], 0x3);
+                    tc::mma_commit_pair(&sm.x_empty[s], 0x3);
+                    tc::mma_commit_pair(&sm.acc_ready[b], 0x3);
                 }
             }
             // drain: every MMA issued above has completed before teardown
-            tc::mma_commit(&sm.drain);
+            tc::mma_commit_pair(&sm.drain, 0x1);
             tc::mbar_wait(&sm.drain, 0);
         }
     } else if (warp < kTcFirstDrainWarp) {
         // ---------------- converters ----------------
         const int ct = threadIdx.x - 64;  // 0..kTcConvThreads-1
-        const int q = warp & 3;            // TMEM lane quarter
-        const int m = 32 * q + lane;       // the A tile row this thread splits
-        const uint32_t a_lane = tmem + (uint32_t(32 * q) << 16) + kTcColA;
         uint32_t it = 0;
         bool stop = false;
-        for (int u = blockIdx.x; u < g.units && !stop; u += gridDim.x) {
+        for (int u = pair; u < g.units && !stop; u += npairs) {
             const TcUnit t = tc_unit(g, u);
             for (int kb = 0; kb < t.nk; ++kb, ++it) {
-                const int sa = it % kTcAStages, s = it % kTcBStages;
-                if (!tc::mbar_wait(&sm.full_a[sa], (it / kTcAStages) & 1)) { tc_fail(sm, err, kTcErrConverter); stop = true; break; }
+                const int s = it % kTcStages;
+                const uint32_t ph = (it / kTcStages) & 1;
+                // W stage: split in place unless B came pre-split; then
+                // report it to the pair's MMA
+                if (!tc::mbar_wait(&sm.w_full[s], ph)) { tc_fail(sm, err, kTcErrConverter); stop = true; break; }
                 if (tc_aborted(sm)) { stop = true; break; }
-                {
-                    // row m's 32 K-values -> hi/lo in A slot it % 3, 16 at a time
-                    const int j = it % kTcASlots;
-                    if (!tc::mbar_wait(&sm.a_free[j], ((it / kTcASlots) & 1) ^ 1)) {
-                        tc_fail(sm, err, kTcErrConverter); stop = true; break;
-                    }
-                    tc::tc_fence_after();
-                    const float* raw = sm.a_raw[sa];
-#pragma unroll
-                    for (int h = 0; h < 2; ++h) {
-                        float x[16];
-                        if (!A_MN) {
-#pragma unroll
-                            for (int c = 0; c < 4; ++c) {
-                                const int cc = 4 * h + c;
-                                const float4 v = *reinterpret_cast<const float4*>(raw + m * 32 + ((cc ^ (m & 7)) << 2));
-                                x[4 * c] = v.x; x[4 * c + 1] = v.y; x[4 * c + 2] = v.z; x[4 * c + 3] = v.w;
-                            }
-                        } else {
-#pragma unroll
-                            for (int k = 0; k < 16; ++k) x[k] = raw[(16 * h + k) * 128 + m];
-                        }
-                        uint32_t hi[16], lo[16];
-#pragma unroll
-                        for (int i = 0; i < 16; ++i) {
-                            const float hv = tf32_round(x[i]);
-                            hi[i] = __float_as_uint(hv);
-                            lo[i] = __float_as_uint(x[i] - hv);
-                        }
-                        tc::tmem_st_32x32b_x16(a_lane + 64 * j + 16 * h, hi);
-                        tc::tmem_st_32x32b_x16(a_lane + 64 * j + 32 + 16 * h, lo);
-                    }
-                    __syncwarp();
-                    if (lane == 0) tc::mbar_arrive(&sm.empty_a[sa]);  // raw A read
-                    tc::tmem_st_wait();
-                    tc::tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) tc::mbar_arrive(&sm.a_ready[j]);
-                }
-                if (!B_SPLIT) {  // pre-split B goes from its TMA barrier straight to the MMA
-                    if (!tc::mbar_wait(&sm.full_b[s], (it / kTcBStages) & 1)) {
-                        tc_fail(sm, err, kTcErrConverter); stop = true; break;
-                    }
-                    float4* bh = reinterpret_cast<float4*>(sm.b_hi[s]);
-                    float4* bl = reinterpret_cast<float4*>(sm.b_lo[s]);
-#pragma unroll 4
-                    for (int i = ct; i < kTcBTileFloats / 4; i += kTcConvThreads) {
-                        const float4 y = bh[i];
-                        const float4 gg = tf32_hi(y);
-                        bh[i] = gg;
-                        bl[i] = make_float4(y.x - gg.x, y.y - gg.y, y.z - gg.z, y.w - gg.w);
-                    }
+                if (!B_SPLIT) {
+                    tc_split_tile(sm.w_hi[s], sm.w_hi[s], sm.w_lo[s], ct);
                     tc::fence_proxy_async_smem();
-                    tc::mbar_arrive(&sm.b_ready[s]);
+                }
+                __syncwarp();
+                if (lane == 0) tc::mbar_arrive_cluster(tc::cluster_addr(&sm.w_ready[s], 0));
+                // landed X tile -> free X stage (hi and lo)
+                const int r = it % kTcRawStages;
+                if (!tc::mbar_wait(&sm.raw_full[r], (it / kTcRawStages) & 1)) { tc_fail(sm, err, kTcErrConverter); stop = true; break; }
+                if (!tc::mbar_wait(&sm.x_empty[s], ph ^ 1)) { tc_fail(sm, err, kTcErrConverter); stop = true; break; }
+                if (tc_aborted(sm)) { stop = true; break; }
+                tc_split_tile(sm.x_raw[r], sm.x_hi[s], sm.x_lo[s], ct);
+                tc::fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+                    tc::mbar_arrive(&sm.raw_empty[r]);
+                    tc::mbar_arrive_cluster(tc::cluster_addr(&sm.x_ready[s], 0));
                 }
             }
         }
@@ -385,158 +355,92 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
         // ---------------- drain, then epilogue ----------------
         const int dw = warp - kTcFirstDrainWarp;  // 0..15
         const int q = warp & 3;                   // TMEM lane quarter this warp may access
-        const int slice = dw >> 2;                // which 64 of the 256 columns
-        float* stg = sm.stage[dw];
+        const int slice = dw >> 2;                // which 64 of the 256 accumulator columns
         const uint32_t base = tmem + (uint32_t(32 * q) << 16) + uint32_t(64 * slice);
         uint32_t it = 0;
         bool stop = false;
-        for (int u = blockIdx.x; u < g.units && !stop; u += gridDim.x) {
+        for (int u = pair; u < g.units && !stop; u += npairs) {
             const TcUnit t = tc_unit(g, u);
             float acc[64];
 #pragma unroll
             for (int i = 0; i < 64; ++i) acc[i] = 0.f;
             for (int kb = 0; kb < t.nk; ++kb, ++it) {
-                if (!tc::mbar_wait(&sm.acc_ready, it & 1)) { tc_fail(sm, err, kTcErrEpilogue); stop = true; break; }
+                const int b = it & 1;
+                if (!tc::mbar_wait(&sm.acc_ready[b], (it >> 1) & 1)) { tc_fail(sm, err, kTcErrEpilogue); stop = true; break; }
                 if (tc_aborted(sm)) { stop = true; break; }
                 tc::tc_fence_after();
                 // 16 columns at a time (registers: 64 sums + 16 loaded); the
-                // accumulator is released once the last piece is in registers
+                // buffer is released once the last piece is in registers
 #pragma unroll
                 for (int p = 0; p < 4; ++p) {
-                    uint32_t r[16];
-                    tc::tmem_ld_32x32b_x16(base + 16 * p, r);
+                    uint32_t v[16];
+                    tc::tmem_ld_32x32b_x16(base + kTcAccCols * b + 16 * p, v);
                     tc::tmem_ld_wait();
                     if (p == 3) {
                         tc::tc_fence_before();
                         __syncwarp();
-                        if (lane == 0) tc::mbar_arrive(&sm.acc_free);
+                        if (lane == 0) tc::mbar_arrive_cluster(tc::cluster_addr(&sm.acc_free[b], 0));
                     }
 #pragma unroll
-                    for (int i = 0; i < 16; ++i) acc[16 * p + i] = __fadd_rn(acc[16 * p + i], __uint_as_float(r[i]));
+                    for (int i = 0; i < 16; ++i) acc[16 * p + i] = __fadd_rn(acc[16 * p + i], __uint_as_float(v[i]));
                 }
             }
             if (stop || tc_aborted(sm)) break;
-            const int rbase = t.m0 + 32 * q;
-            const int cbase = t.n0 + 64 * slice;
-            if constexpr (C_TMA) {
-                // TMA-store epilogue: per 8-column chunk, lane = row applies
-                // the functor, writes the chunk into one of two 32B-swizzled
-                // staging buffers (row r's 16-byte half h at (h ^ ((r >> 2) & 1))),
-                // and lane 0 issues one bulk store (the split-K partials go to
-                // [split][M][N] through a 3-D map); rows and columns outside
-                // the output are clipped by TMA
-                const int row = rbase + lane;
+            // Epilogue: this thread holds column n of rows row0 .. row0+63;
+            // each access below is a 128-byte row segment across the warp.
+            const int n = t.n0 + kTcHalf * (int)rank + 32 * q + lane;
+            const int row0 = t.m0 + 64 * slice;
+            if (n < g.N) {
+                if (partial) {
+                    float* pz = partial + ((long)t.z * g.M) * g.N + n;
 #pragma unroll
-                for (int c = 0; c < 8; ++c) {
-                    const int n = cbase + c * 8;
-                    float pre[8];
+                    for (int i = 0; i < 64; ++i)
+                        if (row0 + i < g.M) pz[(long)(row0 + i) * g.N] = acc[i];
+                } else {
 #pragma unroll
-                    for (int i = 0; i < 8; ++i) pre[i] = 0.f;
-                    if constexpr (Epi::kReads) {
-                        if (!partial && row < g.M) {
-                            const float* pp = epi.pre_ptr() + (long)row * epi.tma_ld() + n;
-                            if (n + 8 <= g.N) {
-#pragma unroll
-                                for (int v4 = 0; v4 < 2; ++v4) {
-                                    const float4 x4 = *reinterpret_cast<const float4*>(pp + 4 * v4);
-                                    pre[4 * v4] = x4.x; pre[4 * v4 + 1] = x4.y; pre[4 * v4 + 2] = x4.z; pre[4 * v4 + 3] = x4.w;
-                                }
-                            } else {
-                                for (int i = 0; i < 8 && n + i < g.N; ++i) pre[i] = pp[i];
-                            }
-                        }
-                    }
-                    float* buf = sm.stage_tma[dw] + (c & 1) * 256;
-                    if (lane == 0) tc::bulk_wait_read<1>();  // the store that last read this buffer is done
-                    __syncwarp();
-#pragma unroll
-                    for (int h = 0; h < 2; ++h) {
-                        float o[4];
-#pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            const float v = acc[8 * c + 4 * h + e];
-                            o[e] = partial ? v : epi.value(v, pre[4 * h + e]);
-                        }
-                        *reinterpret_cast<float4*>(buf + lane * 8 + ((h ^ ((lane >> 2) & 1)) << 2)) =
-                            make_float4(o[0], o[1], o[2], o[3]);
-                    }
-                    tc::fence_proxy_async_smem();
-                    __syncwarp();
-                    if (lane == 0) {
-                        if (partial) tc::tma_store_3d(&map_c, buf, n, rbase, t.z);
-                        else tc::tma_store_2d(&map_c, buf, n, rbase);
-                        tc::bulk_commit();
-                    }
-                }
-            } else {
-                // Coalesced epilogue: this warp owns rows m0+32q .. +31 and
-                // columns n0+64*slice .. +63.  Per 8-column chunk, lane = row
-                // writes its 8 values into the staging block (row stride 9:
-                // conflict-free), then lane (r, c) = (lane / 8, lane % 8) reads
-                // rows 4i + r column-wise, so that each store instruction
-                // writes four 32-byte row segments.
-                const int rsub = lane >> 3, csub = lane & 7;
-#pragma unroll 1
-                for (int c = 0; c < 8; ++c) {
-                    __syncwarp();
-#pragma unroll
-                    for (int jj = 0; jj < 8; ++jj) stg[lane * kTcStageLd + jj] = chunk8(acc, c, jj);
-                    __syncwarp();
-                    const int n = cbase + c * 8 + csub;
-                    if (partial) {
-#pragma unroll
-                        for (int i = 0; i < 8; ++i) {
-                            const int row = rbase + 4 * i + rsub;
-                            if (row < g.M && n < g.N)
-                                partial[((long)t.z * g.M + row) * g.N + n] = stg[(4 * i + rsub) * kTcStageLd + csub];
-                        }
-                    } else if constexpr (Epi::kReads) {
+                    for (int c = 0; c < 8; ++c) {
                         // the chunk's global epilogue inputs, all loads in flight together
                         float pre[8];
 #pragma unroll
-                        for (int i = 0; i < 8; ++i) {
-                            const int row = rbase + 4 * i + rsub;
-                            pre[i] = (row < g.M && n < g.N) ? epi.prefetch(row, n) : 0.f;
+                        for (int j = 0; j < 8; ++j) {
+                            const int row = row0 + 8 * c + j;
+                            pre[j] = (Epi::kReads && row < g.M) ? epi.prefetch(row, n) : 0.f;
                         }
 #pragma unroll
-                        for (int i = 0; i < 8; ++i) {
-                            const int r = 4 * i + rsub;
-                            const int row = rbase + r;
-                            if (row < g.M && n < g.N) epi.finish(row, n, stg[r * kTcStageLd + csub], pre[i]);
-                        }
-                    } else {
-#pragma unroll
-                        for (int i = 0; i < 8; ++i) {
-                            const int r = 4 * i + rsub;
-                            const int row = rbase + r;
-                            if (row < g.M && n < g.N) epi.finish(row, n, stg[r * kTcStageLd + csub], 0.f);
+                        for (int j = 0; j < 8; ++j) {
+                            const int row = row0 + 8 * c + j;
+                            if (row < g.M) epi.finish(row, n, acc[8 * c + j], pre[j]);
                         }
                     }
                 }
             }
         }
-        if (C_TMA && lane == 0) tc::bulk_wait_all();  // stores complete before the CTA exits
     }
+    // Neither CTA leaves while the pair's MMAs may still touch its shared
+    // memory or TMEM, or the other CTA may still arrive on its barriers.
     tc::tc_fence_before();
     __syncthreads();
+    tc::cluster_sync();
     if (warp == 1) {
         tc::tc_fence_after();
-        tc::tmem_dealloc(tmem, kTcTmemCols);
+        tc::tmem_dealloc_pair(tmem, kTcTmemCols);
     }
+    tc::cluster_sync();
 }
 
-// Work split for an M x N x K problem: with fewer output tiles than SMs and
-// a long K, split K so that tiles x splits fills the SMs in a single wave
-// (each split at least 256 deep).  `max_splits` = 1 forbids splitting.
-inline TcGrid tc_grid(int M, int N, int K, int sm_count, int max_splits) {
+// Work split for an M x N x K problem over `pairs` CTA pairs: with fewer
+// output tiles than pairs and a long K, split K so that tiles x splits fills
+// the pairs in a single wave (each split at least 256 deep).  `max_splits`
+// = 1 forbids splitting.
+inline TcGrid tc_grid(int M, int N, int K, int pairs, int max_splits) {
     TcGrid g{};
     g.M = M; g.N = N; g.K = K;
     g.tiles_m = (M + kTcBM - 1) / kTcBM;
     g.tiles_n = (N + kTcBN - 1) / kTcBN;
     const long tiles = (long)g.tiles_m * g.tiles_n;
     int splits = 1;
-    if (max_splits > 1 && tiles < sm_count && K >= 2 * 256) {
-        splits = (int)(sm_count / tiles);
+    if (max_splits > 1 && tiles < pairs && K >= 2 * 256) {
+        splits = (int)(pairs / tiles);
         splits = std::max(1, std::min({splits, K / 256, max_splits}));
     }
     int chunk = (K + splits - 1) / splits;
@@ -548,23 +452,58 @@ inline TcGrid tc_grid(int M, int N, int K, int sm_count, int max_splits) {
     return g;
 }
 
-// Launches the persistent kernel: min(units, SMs) CTAs.  With B_SPLIT, B
-// arrives as two tensors, hi (already rounded to TF32) through mb and
-// lo = B - hi through mb_lo, and is not split on the device.  With C_TMA the
-// epilogue writes through mc (box 16 x 32, 64-byte swizzle; for split-K
-// partials a 3-D map over [split][M][N]).
-template <bool A_MN, bool B_MN, bool B_SPLIT = false, bool C_TMA = false, class Epi>
-inline cudaError_t launch_tc_kernel(cudaStream_t stream, int sm_count, const CUtensorMap& ma, const CUtensorMap& mb,
-                                    const CUtensorMap& mb_lo, const CUtensorMap& mc, const TcGrid& g, Epi epi,
-                                    float* partial, int* err)
+inline cudaLaunchConfig_t tc_launch_config(int pairs, cudaStream_t stream, cudaLaunchAttribute* attr) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * std::max(1, pairs));
+    cfg.blockDim = dim3(kTcThreads);
+    cfg.dynamicSmemBytes = kTcSmemBytes;
+    cfg.stream = stream;
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cfg;
+}
+
+// CTA pairs of this kernel that can be resident at once: one CTA per SM (its
+// shared memory), two SMs per pair; queried once per instantiation.
+template <bool A_MN, bool B_MN, bool B_SPLIT, class Epi>
+inline int tc_pairs(int sm_count) {
+    static int pairs = 0;
+    if (pairs == 0) {
+        auto kern = gemm_tc_kernel<A_MN, B_MN, B_SPLIT, Epi>;
+        cudaLaunchAttribute attr[1];
+        const cudaLaunchConfig_t cfg = tc_launch_config(sm_count / 2, nullptr, attr);
+        int n = 0;
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTcSmemBytes) == cudaSuccess &&
+            cudaOccupancyMaxActiveClusters(&n, kern, &cfg) == cudaSuccess && n > 0)
+            pairs = n;
+        else
+            pairs = std::max(1, sm_count / 2);
+        (void)cudaGetLastError();
+    }
+    return pairs;
+}
+
+// Launches the persistent kernel as min(units, pairs) clusters of two CTAs.
+// mx maps op(A) (K-major [M][K]: box 32 x kTcHalf, 128B swizzle; MN-major
+// [K][M]: box 32 x 32, 128B swizzle with 32-byte atoms), mw op(B) likewise.
+// With B_SPLIT, B arrives as two tensors, hi (already rounded to TF32)
+// through mw and lo = B - hi through mw_lo, and is not split on the device.
+// With `partial`, unit z of the K split writes its sums to partial[z][M][N]
+// instead of applying the epilogue.
+template <bool A_MN, bool B_MN, bool B_SPLIT = false, class Epi>
+inline cudaError_t launch_tc_kernel(cudaStream_t stream, int pairs, const CUtensorMap& mx, const CUtensorMap& mw,
+                                    const CUtensorMap& mw_lo, const TcGrid& g, Epi epi, float* partial, int* err)
 {
-    const cudaError_t a = cudaFuncSetAttribute(gemm_tc_kernel<A_MN, B_MN, B_SPLIT, C_TMA, Epi>,
-                                               cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTcSmemBytes);
+    auto kern = gemm_tc_kernel<A_MN, B_MN, B_SPLIT, Epi>;
+    const cudaError_t a = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTcSmemBytes);
     if (a != cudaSuccess) return a;
-    const int grid = std::max(1, std::min(g.units, sm_count));
-    gemm_tc_kernel<A_MN, B_MN, B_SPLIT, C_TMA, Epi>
-        <<<grid, kTcThreads, kTcSmemBytes, stream>>>(ma, mb, mb_lo, mc, g, epi, partial, err);
-    return cudaGetLastError();
+    cudaLaunchAttribute attr[1];
+    const cudaLaunchConfig_t cfg = tc_launch_config(std::min(g.units, pairs), stream, attr);
+    return cudaLaunchKernelEx(&cfg, kern, mx, mw, mw_lo, g, epi, partial, err);
 }
 
 }  // namespace hx

@@ -87,10 +87,11 @@ void gemm_noalloc(hx_runtime* rt, int M, int N, int K, const float* A, long lda,
     if (tc_eligible(rt, M, N, K, A, lda, B, ldb)) {
         constexpr bool A_MN = AT, B_MN = !BT;
         constexpr CUtensorMapSwizzle mn_swz = CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B;
-        const CUtensorMap ma = A_MN ? make_map(A, M, K, lda, 128, 32, CU_TENSOR_MAP_SWIZZLE_NONE) : make_map(A, K, M, lda, 32, 128);
-        const CUtensorMap mb = B_MN ? make_map(B, N, K, ldb, 32, 32, mn_swz) : make_map(B, K, N, ldb, 32, kTcBN);
-        const TcGrid g = tc_grid(M, N, K, rt->sm_count, 1);
-        HX_CUDA((launch_tc_kernel<A_MN, B_MN, false, false>(rt->stream, rt->sm_count, ma, mb, mb, mb, g, epi, nullptr, err)));
+        const CUtensorMap mx = A_MN ? make_map(A, M, K, lda, 32, 32, mn_swz) : make_map(A, K, M, lda, 32, kTcHalf);
+        const CUtensorMap mw = B_MN ? make_map(B, N, K, ldb, 32, 32, mn_swz) : make_map(B, K, N, ldb, 32, kTcHalf);
+        const int pairs = tc_pairs<A_MN, B_MN, false, Epi>(rt->sm_count);
+        const TcGrid g = tc_grid(M, N, K, pairs, 1);
+        HX_CUDA((launch_tc_kernel<A_MN, B_MN, false>(rt->stream, pairs, mx, mw, mw, g, epi, nullptr, err)));
         ++rt->metrics.kernel_launches;
         return;
     }
