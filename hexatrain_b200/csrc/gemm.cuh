@@ -67,7 +67,8 @@ inline EncodeTiledFn encode_tiled() {
 // Row-major FP32 matrix [outer][inner] with leading dimension ld (elements),
 // boxes of box_inner x box_outer, zero fill out of bounds.  K-major operand
 // tiles use the 128B swizzle; MN-major tiles the 128B swizzle with 32-byte
-// atoms (the layout the MMA requires for MN-major 32-bit operands).
+// atoms (the layout the MMA requires for MN-major 32-bit operands); output
+// tiles written by TMA stores no swizzle.
 inline CUtensorMap make_map(const float* base, uint64_t inner, uint64_t outer, uint64_t ld, uint32_t box_inner,
                             uint32_t box_outer, CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B) {
     CUtensorMap m;
@@ -79,6 +80,22 @@ inline CUtensorMap make_map(const float* base, uint64_t inner, uint64_t outer, u
                                       box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
                                       CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     require(r == CUDA_SUCCESS, HX_ERR_CUDA, "cuTensorMapEncodeTiled failed (" + std::to_string(int(r)) + ")");
+    return m;
+}
+
+// Row-major FP32 [z][outer][inner] (strides ld and zstride elements), box
+// box_inner x box_outer x 1.
+inline CUtensorMap make_map3(const float* base, uint64_t inner, uint64_t outer, uint64_t depth, uint64_t ld,
+                             uint64_t zstride, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swz) {
+    CUtensorMap m;
+    const cuuint64_t dims[3] = {inner, outer, depth};
+    const cuuint64_t strides[2] = {ld * sizeof(float), zstride * sizeof(float)};
+    const cuuint32_t box[3] = {box_inner, box_outer, 1};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    const CUresult r = encode_tiled()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(base), dims, strides,
+                                      box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    require(r == CUDA_SUCCESS, HX_ERR_CUDA, "cuTensorMapEncodeTiled (3-D) failed (" + std::to_string(int(r)) + ")");
     return m;
 }
 
@@ -114,12 +131,30 @@ void launch_tc(hx_runtime* rt, int M, int N, int K, const float* A, long lda, co
     const bool split = bs.hi && bs.lo;
     const CUtensorMap mw = map_w(split ? bs.hi : B);
     const CUtensorMap mw_lo = split ? map_w(bs.lo) : mw;
-    const int pairs = split ? tc_pairs<A_MN, B_MN, true, Epi>(rt->sm_count) : tc_pairs<A_MN, B_MN, false, Epi>(rt->sm_count);
+    const int pairs = tc_pairs<A_MN, B_MN, false, false, Epi>(rt->sm_count);
     const TcGrid g = tc_grid(M, N, K, pairs, 64);
     int* err = rt->device_error();
     float* ws = g.splits > 1 ? rt->workspace(sizeof(float) * (size_t)g.splits * M * N) : nullptr;
-    const cudaError_t rc = split ? launch_tc_kernel<A_MN, B_MN, true>(rt->stream, pairs, mx, mw, mw_lo, g, epi, ws, err)
-                                 : launch_tc_kernel<A_MN, B_MN, false>(rt->stream, pairs, mx, mw, mw_lo, g, epi, ws, err);
+    // bulk tensor stores for the epilogue when its single output (or the
+    // split-K workspace) meets TMA's 16-byte rules
+    bool c_tma;
+    CUtensorMap mc = mw;
+    if (ws) {
+        c_tma = N % 4 == 0 && (reinterpret_cast<uintptr_t>(ws) & 15) == 0;
+        if (c_tma) mc = make_map3(ws, N, M, g.splits, N, (uint64_t)M * N, 32, kTcStoreRows, CU_TENSOR_MAP_SWIZZLE_NONE);
+    } else {
+        const float* out = epi.tma_out();
+        const long ldc = epi.tma_ld();
+        c_tma = epi.tma_ok() && out && (reinterpret_cast<uintptr_t>(out) & 15) == 0 && ldc % 4 == 0;
+        if (c_tma) mc = make_map(out, N, M, ldc, 32, kTcStoreRows, CU_TENSOR_MAP_SWIZZLE_NONE);
+    }
+    cudaError_t rc;
+    if (split)
+        rc = c_tma ? launch_tc_kernel<A_MN, B_MN, true, true>(rt->stream, pairs, mx, mw, mw_lo, mc, g, epi, ws, err)
+                   : launch_tc_kernel<A_MN, B_MN, true, false>(rt->stream, pairs, mx, mw, mw_lo, mc, g, epi, ws, err);
+    else
+        rc = c_tma ? launch_tc_kernel<A_MN, B_MN, false, true>(rt->stream, pairs, mx, mw, mw_lo, mc, g, epi, ws, err)
+                   : launch_tc_kernel<A_MN, B_MN, false, false>(rt->stream, pairs, mx, mw, mw_lo, mc, g, epi, ws, err);
     HX_CUDA(rc);
     ++rt->metrics.kernel_launches;
     if (g.splits > 1) {

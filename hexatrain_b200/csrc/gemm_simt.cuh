@@ -172,6 +172,10 @@ __global__ void splitk_reduce_kernel(int M, int N, int splits, const float* __re
 // for element (m, n), 0 if none -- and finish(m, n, v, pre).  The tensor-core
 // epilogue issues the prefetches of a whole chunk before finishing any of
 // them, so those loads are in flight together; operator() is the fused form.
+// An epilogue that writes one float array can also hand its results to TMA
+// bulk stores: tma_ok() (host) says so for this instance, tma_out()/tma_ld()
+// name the array, pre_ptr() the array prefetch() reads (same leading
+// dimension, or null), and value(v, pre) is the element written.
 
 struct EpiStore {  // C[m*ldc + n] = v, with an optional column split:
     static constexpr bool kReads = false;  // prefetch() loads from global memory
@@ -186,6 +190,11 @@ struct EpiStore {  // C[m*ldc + n] = v, with an optional column split:
         else c[(long)m * ldc + n] = v;
     }
     __device__ void operator()(int m, int n, float v) const { finish(m, n, v, 0.f); }
+    bool tma_ok() const { return split == 0; }
+    float* tma_out() const { return c; }
+    __host__ __device__ long tma_ld() const { return ldc; }
+    __host__ __device__ const float* pre_ptr() const { return nullptr; }
+    __device__ float value(float v, float) const { return v; }
 };
 
 struct EpiAddResidual {  // out = res + v   (r1 = x + ctx*Wo ; out = r1 + relu*W2)
@@ -196,6 +205,11 @@ struct EpiAddResidual {  // out = res + v   (r1 = x + ctx*Wo ; out = r1 + relu*W
     __device__ float prefetch(int m, int n) const { return res[(long)m * ld + n]; }
     __device__ void finish(int m, int n, float v, float r) const { out[(long)m * ld + n] = __fadd_rn(r, v); }
     __device__ void operator()(int m, int n, float v) const { finish(m, n, v, prefetch(m, n)); }
+    bool tma_ok() const { return true; }
+    float* tma_out() const { return out; }
+    __host__ __device__ long tma_ld() const { return ld; }
+    __host__ __device__ const float* pre_ptr() const { return res; }
+    __device__ float value(float v, float r) const { return __fadd_rn(r, v); }
 };
 
 struct EpiRelu {  // h = max(0, z) ; optional mask = h > 0
@@ -211,6 +225,11 @@ struct EpiRelu {  // h = max(0, z) ; optional mask = h > 0
         if (mask) mask[i] = r > 0.f ? 1 : 0;
     }
     __device__ void operator()(int m, int n, float v) const { finish(m, n, v, 0.f); }
+    bool tma_ok() const { return mask == nullptr; }
+    float* tma_out() const { return h; }
+    __host__ __device__ long tma_ld() const { return ld; }
+    __host__ __device__ const float* pre_ptr() const { return nullptr; }
+    __device__ float value(float v, float) const { return (0.f < v) ? v : 0.f; }
 };
 
 struct EpiReluBackward {  // dz = (act > 0) ? v : 0 ; optional raw store of v
@@ -226,6 +245,11 @@ struct EpiReluBackward {  // dz = (act > 0) ? v : 0 ; optional raw store of v
         dz[i] = a > 0.f ? v : 0.f;
     }
     __device__ void operator()(int m, int n, float v) const { finish(m, n, v, prefetch(m, n)); }
+    bool tma_ok() const { return raw == nullptr; }
+    float* tma_out() const { return dz; }
+    __host__ __device__ long tma_ld() const { return ld; }
+    __host__ __device__ const float* pre_ptr() const { return act; }
+    __device__ float value(float v, float a) const { return a > 0.f ? v : 0.f; }
 };
 
 struct EpiError {  // P = v ; E = P - Y ; dP = (P - Y) * s
@@ -245,6 +269,11 @@ struct EpiError {  // P = v ; E = P - Y ; dP = (P - Y) * s
         dp[i] = __fmul_rn(err, s);
     }
     __device__ void operator()(int m, int n, float v) const { finish(m, n, v, prefetch(m, n)); }
+    bool tma_ok() const { return false; }
+    float* tma_out() const { return dp; }
+    __host__ __device__ long tma_ld() const { return ld; }
+    __host__ __device__ const float* pre_ptr() const { return y; }
+    __device__ float value(float v, float) const { return v; }
 };
 
 struct EpiSgd {  // dW = v (optional) ; W_next = W - lr*dW (two roundings, as the reference)
@@ -261,6 +290,11 @@ struct EpiSgd {  // dW = v (optional) ; W_next = W - lr*dW (two roundings, as th
         w_next[i] = __fsub_rn(wv, __fmul_rn(lr, v));
     }
     __device__ void operator()(int m, int n, float v) const { finish(m, n, v, prefetch(m, n)); }
+    bool tma_ok() const { return false; }
+    float* tma_out() const { return w_next; }
+    __host__ __device__ long tma_ld() const { return ld; }
+    __host__ __device__ const float* pre_ptr() const { return w; }
+    __device__ float value(float v, float) const { return v; }
 };
 
 }  // namespace hx

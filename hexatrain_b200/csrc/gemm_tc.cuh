@@ -12,56 +12,62 @@
 // hi*lo and lo*hi terms issued before hi*hi (four full-magnitude truncations
 // per k-block), and drained into FP32 registers with round-to-nearest adds.
 //
-// Tile and orientation.  An output tile is 256 rows x 128 columns, computed
-// transposed: the MMA (kind::tf32, M = 128, N = 256, K = 8) takes op(B)^T --
-// 128 output columns -- as its A operand and op(A) -- 256 output rows -- as
-// its B operand, so TMEM lane l holds output column n0 + l and TMEM column c
-// output row m0 + c.  A warp that drains 32 lanes therefore holds 32
-// consecutive columns of each row, and the epilogue's global loads and stores
-// are whole 128-byte row segments straight from registers, with no staging.
-// A kind::tf32 MMA with M = 128 costs the same whether N is 64 or 256
-// (measured on B200), so N = 256 is the widest and cheapest per flop.
+// CTA pairs.  The kernel runs as clusters of two CTAs on two SMs, and the
+// even CTA issues tcgen05.mma with cta_group::2 (kind::tf32, M = 256,
+// N = 256, K = 8): CTA r holds rows [128 r, 128 r + 128) of either operand in
+// its shared memory and receives rows [128 r, ...) of the product in its own
+// TMEM.  Measured on B200 one such instruction costs what an M = 128, N = 256
+// one costs on a single SM (about 175 cycles), so per SM the rate is the same
+// while each SM stages and the MMA reads only half of the N-side operand.
+//
+// Orientation.  A pair tile is 256 output rows x 256 output columns,
+// computed transposed: the MMA's A operand is op(B)^T (the 256 output
+// columns; CTA r holds columns n0 + 128 r ...) and its B operand is op(A)
+// (the 256 output rows; CTA r holds rows m0 + 128 r ...).  TMEM lane l of
+// CTA r then holds output column n0 + 128 r + l, and TMEM column c output
+// row m0 + c: a warp that drains 32 lanes holds 32 consecutive columns of
+// each row, so the epilogue's global loads and stores are whole 128-byte row
+// segments straight from registers, with no staging.
 //
 // The accumulator is double-buffered (two 256-column buffers fill the 512
 // TMEM columns): the MMAs of one k-block run while the drain warps read the
-// previous k-block's sums out of the other buffer, so the drain and the
-// epilogue overlap the tensor cores instead of stalling them.  Both operands
-// therefore live in shared memory, hi and lo side by side.
+// previous k-block's sums out of the other buffer.
 //
-// Persistent: the grid is at most one CTA per SM, and each CTA walks work
-// units u = blockIdx.x, blockIdx.x + gridDim.x, ...  A unit is one 256x128
+// Persistent: the grid is at most the number of pairs that fit at once, and
+// pair p walks work units u = p, p + pairs, ...  A unit is one 256x256
 // output tile of one K split; units are numbered with the column tile
-// fastest so that CTAs running together share op(A) row blocks in L2.  The
+// fastest so that pairs running together share op(A) row blocks in L2.  The
 // rings run on across unit boundaries.
 //
-// Shared memory (224 KB): the op(B) stages ("W": 128 x 32, hi and lo, two
-// stages), the op(A) stages ("X": 256 x 32, hi and lo, two stages) and one
-// landing buffer for raw op(A) tiles.  W tiles arrive already split when B is
-// pre-split (weights), else raw into the hi half and are split in place.  X
-// tiles land raw in the landing buffer and are split from there into a free
-// X stage, so the next tile's load overlaps the current tile's split.
+// Shared memory per CTA (224 KB): three stages of this CTA's op(B) tile ("W",
+// 128 x 32, hi and lo) and op(A) tile ("X", 128 x 32, hi and lo), and two
+// landing buffers for raw X tiles.  W tiles arrive already split when B is
+// pre-split (weights), else raw into the hi half and are split in place; X
+// tiles land raw and are split from there into a free X stage, so the next
+// tile's load overlaps the current tile's split.
 //
-// Roles (22 warps):
-//   warp 0      TMA producers: lane 0 the W tiles (16 or 32 KB per k-block),
-//               lane 1 the raw X tiles (32 KB) into the landing buffer;
-//   warp 1      TMEM owner and MMA issuer: 12 tcgen05.mma per k-block into
-//               accumulator buffer (k-block & 1); tcgen05.commit frees the W
-//               and X stages and hands the buffer to the drain warps;
-//   warps 2-5   converters: split a raw W stage in place (unless B came
-//               pre-split) and the landed X tile into a free X stage;
+// Roles (22 warps per CTA):
+//   warp 0      TMA producers: lane 0 this CTA's W tiles, lane 1 its raw X
+//               tiles;
+//   warp 1      TMEM allocation for the pair; in the even CTA, lane 0 issues
+//               the 12 pair MMAs of each k-block into accumulator buffer
+//               (k-block & 1) and commits to both CTAs' barriers: the W and
+//               X stages are free, the buffer is ready;
+//   warps 2-5   converters: split the W stage (unless pre-split) and the
+//               landed X tile, then arrive on the even CTA's ready barriers;
 //   warps 6-21  drain: warp (quarter q, slice s) adds TMEM lanes 32q..32q+31
 //               and columns 64s..64s+63 of each k-block's buffer into FP32
-//               registers, releasing the buffer once its loads have landed;
-//               at the end of a unit it applies the epilogue functor row by
-//               row (output columns on lanes).
+//               registers and arrives on the even CTA's buffer-free barrier
+//               once its loads have landed; at the end of a unit it applies
+//               the epilogue functor row by row (output columns on lanes).
 // Layouts: K-major tiles arrive 128B-swizzled (row r's 16-byte chunk c at
 // ((c ^ (r & 7)) << 4)); MN-major tiles as 32-wide boxes (4 KB apart) in the
 // 128-byte/32-byte-atom swizzle, the only shared-memory layout the MMA takes
 // for MN-major 32-bit operands.  The hi/lo split is elementwise, so split
 // tiles keep the layout TMA wrote.
 // Every barrier wait is bounded (tc::kWaitCycles); on timeout the kernel
-// records an error code, drains its own MMAs and TMA loads (bounded), frees
-// TMEM and returns.
+// records an error code, drains its own MMAs and TMA loads (bounded), meets
+// the other CTA at the cluster barrier, frees TMEM and returns.
 #pragma once
 
 #include <algorithm>
@@ -72,13 +78,13 @@ namespace hx {
 
 constexpr int kTcBM = 256, kTcBN = 256, kTcBK = 32;  // pair tile: output rows, output columns; K per k-block
 constexpr int kTcHalf = 128;                         // rows of either operand one CTA of the pair holds
-constexpr int kTcStages = 3;                         // split W and X stages
-constexpr int kTcRawStages = 2;                      // landing buffers for raw X tiles
+constexpr int kTcStages = 3;                         // W and X stages (hi and lo)
 constexpr int kTcTileFloats = kTcHalf * kTcBK;       // 16 KB
-constexpr int kTcConvWarps = 4, kTcDrainWarps = 16;
+constexpr int kTcConvWarps = 6, kTcDrainWarps = 16;
+constexpr int kTcStoreRows = 16;                     // rows per TMA-store chunk of a drain warp (32 x 16, 2 KB)
 constexpr int kTcConvThreads = 32 * kTcConvWarps;
 constexpr int kTcFirstDrainWarp = 2 + kTcConvWarps;
-constexpr int kTcThreads = 32 * (kTcFirstDrainWarp + kTcDrainWarps);  // 704
+constexpr int kTcThreads = 32 * (kTcFirstDrainWarp + kTcDrainWarps);  // 768
 constexpr uint32_t kTcTmemCols = 512;                // two 256-column accumulators
 constexpr uint32_t kTcAccCols = kTcBM;
 
@@ -87,9 +93,9 @@ struct TcSmem {
     float w_lo[kTcStages][kTcTileFloats];
     float x_hi[kTcStages][kTcTileFloats];
     float x_lo[kTcStages][kTcTileFloats];
-    float x_raw[kTcRawStages][kTcTileFloats];
-    // this CTA's own pipeline
-    uint64_t w_full[kTcStages], raw_full[kTcRawStages], raw_empty[kTcRawStages];
+    float stage[kTcDrainWarps][kTcStoreRows * 32];   // TMA-store staging, one chunk per drain warp
+    // this CTA's own TMA loads
+    uint64_t w_full[kTcStages], x_full[kTcStages];
     // arrived on by the pair MMA's commit, in both CTAs
     uint64_t w_empty[kTcStages], x_empty[kTcStages], acc_ready[2];
     // used in the even CTA only, arrived on by both CTAs
@@ -189,11 +195,11 @@ __device__ __forceinline__ uint64_t tc_desc(const float* tile, int kk) {
               : tc::smem_desc(tc::smem_u32(tile) + kk * 32, 16, 1024, tc::kLayoutSw128);
 }
 
-template <bool A_MN, bool B_MN, bool B_SPLIT, class Epi>
+template <bool A_MN, bool B_MN, bool B_SPLIT, bool C_TMA, class Epi>
 __global__ void __launch_bounds__(kTcThreads, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_w,
-               const __grid_constant__ CUtensorMap map_wlo, TcGrid g, Epi epi, float* __restrict__ partial,
-               int* __restrict__ err)
+               const __grid_constant__ CUtensorMap map_wlo, const __grid_constant__ CUtensorMap map_c, TcGrid g,
+               Epi epi, float* __restrict__ partial, int* __restrict__ err)
 {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     // 128B-swizzled TMA tiles and UMMA descriptors need 1024-byte alignment
@@ -207,14 +213,11 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant_
     if (threadIdx.x == 0) {
         for (int s = 0; s < kTcStages; ++s) {
             tc::mbar_init(&sm.w_full[s], 1);
+            tc::mbar_init(&sm.x_full[s], 1);
             tc::mbar_init(&sm.w_empty[s], 1);
             tc::mbar_init(&sm.x_empty[s], 1);
             tc::mbar_init(&sm.w_ready[s], 2 * kTcConvWarps);
             tc::mbar_init(&sm.x_ready[s], 2 * kTcConvWarps);
-        }
-        for (int r = 0; r < kTcRawStages; ++r) {
-            tc::mbar_init(&sm.raw_full[r], 1);
-            tc::mbar_init(&sm.raw_empty[r], kTcConvWarps);
         }
         for (int b = 0; b < 2; ++b) {
             tc::mbar_init(&sm.acc_ready[b], 1);
@@ -228,6 +231,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant_
         tc::prefetch_tensormap(&map_x);
         tc::prefetch_tensormap(&map_w);
         if (B_SPLIT) tc::prefetch_tensormap(&map_wlo);
+        if (C_TMA) tc::prefetch_tensormap(&map_c);
     }
     if (warp == 1) {
         tc::tmem_alloc_pair(&sm.tmem_addr, kTcTmemCols);
@@ -240,10 +244,10 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant_
     const uint32_t tmem = sm.tmem_addr;
 
     if (warp == 0) {
-        // ---------------- TMA producers: lane 0 the W stages, lane 1 the X landing buffers
+        // ---------------- TMA producers: lane 0 the W tiles, lane 1 the X tiles
         if (lane < 2) {
             const bool ring_w = lane == 0;
-            const int ns = ring_w ? kTcStages : kTcRawStages;
+            const int ns = kTcStages;
             uint32_t issued_parity[kTcStages];
             bool issued[kTcStages];
             for (int s = 0; s < kTcStages; ++s) issued[s] = false;
@@ -254,9 +258,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant_
                 for (int kb = 0; kb < t.nk; ++kb, ++it) {
                     const int s = it % ns;
                     const uint32_t ph = (it / ns) & 1;
-                    const bool ok = ring_w ? tc::mbar_wait(&sm.w_empty[s], ph ^ 1)
-                                           : tc::mbar_wait(&sm.raw_empty[s], ph ^ 1);
-                    if (!ok) { tc_fail(sm, err, kTcErrProducer); stop = true; break; }
+                    if (!tc::mbar_wait(ring_w ? &sm.w_empty[s] : &sm.x_empty[s], ph ^ 1)) {
+                        tc_fail(sm, err, kTcErrProducer); stop = true; break;
+                    }
                     if (tc_aborted(sm)) { stop = true; break; }
                     const int k = t.kbeg + kb * kTcBK;
                     if (ring_w) {
@@ -264,8 +268,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant_
                         tc_load_tile<B_MN>(sm.w_hi[s], &map_w, &sm.w_full[s], k, t.n0 + kTcHalf * rank);
                         if (B_SPLIT) tc_load_tile<B_MN>(sm.w_lo[s], &map_wlo, &sm.w_full[s], k, t.n0 + kTcHalf * rank);
                     } else {
-                        tc::mbar_arrive_expect_tx(&sm.raw_full[s], kTcTileFloats * 4);
-                        tc_load_tile<A_MN>(sm.x_raw[s], &map_x, &sm.raw_full[s], k, t.m0 + kTcHalf * rank);
+                        tc::mbar_arrive_expect_tx(&sm.x_full[s], kTcTileFloats * 4);
+                        tc_load_tile<A_MN>(sm.x_hi[s], &map_x, &sm.x_full[s], k, t.m0 + kTcHalf * rank);
                     }
                     issued[s] = true;
                     issued_parity[s] = ph;
@@ -274,7 +278,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant_
             if (tc_aborted(sm)) {
                 // let our own loads land before the CTA can exit
                 for (int s = 0; s < ns; ++s)
-                    if (issued[s]) tc::mbar_wait(ring_w ? &sm.w_full[s] : &sm.raw_full[s], issued_parity[s]);
+                    if (issued[s]) tc::mbar_wait(ring_w ? &sm.w_full[s] : &sm.x_full[s], issued_parity[s]);
             }
         }
     } else if (warp == 1) {
@@ -337,18 +341,13 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant_
                 }
                 __syncwarp();
                 if (lane == 0) tc::mbar_arrive_cluster(tc::cluster_addr(&sm.w_ready[s], 0));
-                // landed X tile -> free X stage (hi and lo)
-                const int r = it % kTcRawStages;
-                if (!tc::mbar_wait(&sm.raw_full[r], (it / kTcRawStages) & 1)) { tc_fail(sm, err, kTcErrConverter); stop = true; break; }
-                if (!tc::mbar_wait(&sm.x_empty[s], ph ^ 1)) { tc_fail(sm, err, kTcErrConverter); stop = true; break; }
+                // X stage: split in place, then report it
+                if (!tc::mbar_wait(&sm.x_full[s], ph)) { tc_fail(sm, err, kTcErrConverter); stop = true; break; }
                 if (tc_aborted(sm)) { stop = true; break; }
-                tc_split_tile(sm.x_raw[r], sm.x_hi[s], sm.x_lo[s], ct);
+                tc_split_tile(sm.x_hi[s], sm.x_hi[s], sm.x_lo[s], ct);
                 tc::fence_proxy_async_smem();
                 __syncwarp();
-                if (lane == 0) {
-                    tc::mbar_arrive(&sm.raw_empty[r]);
-                    tc::mbar_arrive_cluster(tc::cluster_addr(&sm.x_ready[s], 0));
-                }
+                if (lane == 0) tc::mbar_arrive_cluster(tc::cluster_addr(&sm.x_ready[s], 0));
             }
         }
     } else {
@@ -386,11 +385,50 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant_
                 }
             }
             if (stop || tc_aborted(sm)) break;
-            // Epilogue: this thread holds column n of rows row0 .. row0+63;
-            // each access below is a 128-byte row segment across the warp.
             const int n = t.n0 + kTcHalf * (int)rank + 32 * q + lane;
             const int row0 = t.m0 + 64 * slice;
-            if (n < g.N) {
+            if constexpr (C_TMA) {
+                // TMA-store epilogue: per 16-row chunk, lane = column writes
+                // its 16 values into the warp's staging block (row-major
+                // 16 x 32, conflict-free) and lane 0 hands the block to one
+                // bulk tensor store (split-K partials go to [split][M][N]
+                // through a 3-D map); rows and columns outside the output
+                // are clipped by TMA.
+                float* buf = sm.stage[dw];
+                const int col0 = t.n0 + kTcHalf * (int)rank + 32 * q;
+#pragma unroll
+                for (int c = 0; c < 64 / kTcStoreRows; ++c) {
+                    const int r0 = row0 + kTcStoreRows * c;
+                    float pre[kTcStoreRows];
+#pragma unroll
+                    for (int j = 0; j < kTcStoreRows; ++j) pre[j] = 0.f;
+                    if constexpr (Epi::kReads) {
+                        // the chunk's global epilogue inputs, all loads in flight together
+                        if (!partial && n < g.N) {
+                            const float* pp = epi.pre_ptr() + n;
+#pragma unroll
+                            for (int j = 0; j < kTcStoreRows; ++j)
+                                if (r0 + j < g.M) pre[j] = pp[(long)(r0 + j) * epi.tma_ld()];
+                        }
+                    }
+                    if (lane == 0) tc::bulk_wait_read<0>();  // the last store has read the block
+                    __syncwarp();
+#pragma unroll
+                    for (int j = 0; j < kTcStoreRows; ++j) {
+                        const float v = acc[kTcStoreRows * c + j];
+                        buf[j * 32 + lane] = partial ? v : epi.value(v, pre[j]);
+                    }
+                    tc::fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0 && col0 < g.N && r0 < g.M) {
+                        if (partial) tc::tma_store_3d(&map_c, buf, col0, r0, t.z);
+                        else tc::tma_store_2d(&map_c, buf, col0, r0);
+                        tc::bulk_commit();
+                    }
+                }
+            } else if (n < g.N) {
+                // direct epilogue: each access is a 128-byte row segment
+                // across the warp
                 if (partial) {
                     float* pz = partial + ((long)t.z * g.M) * g.N + n;
 #pragma unroll
@@ -415,6 +453,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant_
                 }
             }
         }
+        if (C_TMA && lane == 0) tc::bulk_wait_all();  // stores complete before the CTA exits
     }
     // Neither CTA leaves while the pair's MMAs may still touch its shared
     // memory or TMEM, or the other CTA may still arrive on its barriers.
@@ -469,11 +508,11 @@ inline cudaLaunchConfig_t tc_launch_config(int pairs, cudaStream_t stream, cudaL
 
 // CTA pairs of this kernel that can be resident at once: one CTA per SM (its
 // shared memory), two SMs per pair; queried once per instantiation.
-template <bool A_MN, bool B_MN, bool B_SPLIT, class Epi>
+template <bool A_MN, bool B_MN, bool B_SPLIT, bool C_TMA, class Epi>
 inline int tc_pairs(int sm_count) {
     static int pairs = 0;
     if (pairs == 0) {
-        auto kern = gemm_tc_kernel<A_MN, B_MN, B_SPLIT, Epi>;
+        auto kern = gemm_tc_kernel<A_MN, B_MN, B_SPLIT, C_TMA, Epi>;
         cudaLaunchAttribute attr[1];
         const cudaLaunchConfig_t cfg = tc_launch_config(sm_count / 2, nullptr, attr);
         int n = 0;
@@ -493,17 +532,20 @@ inline int tc_pairs(int sm_count) {
 // With B_SPLIT, B arrives as two tensors, hi (already rounded to TF32)
 // through mw and lo = B - hi through mw_lo, and is not split on the device.
 // With `partial`, unit z of the K split writes its sums to partial[z][M][N]
-// instead of applying the epilogue.
-template <bool A_MN, bool B_MN, bool B_SPLIT = false, class Epi>
+// instead of applying the epilogue.  With C_TMA the epilogue writes through
+// mc: the output [M][N] (or, with `partial`, [split][M][N] as a 3-D map),
+// box 32 columns x kTcStoreRows rows, no swizzle.
+template <bool A_MN, bool B_MN, bool B_SPLIT = false, bool C_TMA = false, class Epi>
 inline cudaError_t launch_tc_kernel(cudaStream_t stream, int pairs, const CUtensorMap& mx, const CUtensorMap& mw,
-                                    const CUtensorMap& mw_lo, const TcGrid& g, Epi epi, float* partial, int* err)
+                                    const CUtensorMap& mw_lo, const CUtensorMap& mc, const TcGrid& g, Epi epi,
+                                    float* partial, int* err)
 {
-    auto kern = gemm_tc_kernel<A_MN, B_MN, B_SPLIT, Epi>;
+    auto kern = gemm_tc_kernel<A_MN, B_MN, B_SPLIT, C_TMA, Epi>;
     const cudaError_t a = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTcSmemBytes);
     if (a != cudaSuccess) return a;
     cudaLaunchAttribute attr[1];
     const cudaLaunchConfig_t cfg = tc_launch_config(std::min(g.units, pairs), stream, attr);
-    return cudaLaunchKernelEx(&cfg, kern, mx, mw, mw_lo, g, epi, partial, err);
+    return cudaLaunchKernelEx(&cfg, kern, mx, mw, mw_lo, mc, g, epi, partial, err);
 }
 
 }  // namespace hx

@@ -89,9 +89,9 @@ void gemm_noalloc(hx_runtime* rt, int M, int N, int K, const float* A, long lda,
         constexpr CUtensorMapSwizzle mn_swz = CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B;
         const CUtensorMap mx = A_MN ? make_map(A, M, K, lda, 32, 32, mn_swz) : make_map(A, K, M, lda, 32, kTcHalf);
         const CUtensorMap mw = B_MN ? make_map(B, N, K, ldb, 32, 32, mn_swz) : make_map(B, K, N, ldb, 32, kTcHalf);
-        const int pairs = tc_pairs<A_MN, B_MN, false, Epi>(rt->sm_count);
+        const int pairs = tc_pairs<A_MN, B_MN, false, false, Epi>(rt->sm_count);
         const TcGrid g = tc_grid(M, N, K, pairs, 1);
-        HX_CUDA((launch_tc_kernel<A_MN, B_MN, false>(rt->stream, pairs, mx, mw, mw, g, epi, nullptr, err)));
+        HX_CUDA((launch_tc_kernel<A_MN, B_MN, false, false>(rt->stream, pairs, mx, mw, mw, mw, g, epi, nullptr, err)));
         ++rt->metrics.kernel_launches;
         return;
     }
