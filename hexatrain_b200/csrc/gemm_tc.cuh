@@ -85,6 +85,14 @@ constexpr int kTcStoreRows = 16;                     // rows per TMA-store chunk
 constexpr int kTcConvThreads = 32 * kTcConvWarps;
 constexpr int kTcFirstDrainWarp = 2 + kTcConvWarps;
 constexpr int kTcThreads = 32 * (kTcFirstDrainWarp + kTcDrainWarps);  // 768
+// Registers: the kernel is built for 80 per thread (768 threads on one SM);
+// the producer/MMA/converter warpgroups give theirs down to 48 and the four
+// drain warpgroups, which hold 64 running sums per thread, take 96:
+// 256 x 48 + 512 x 96 = 768 x 80.
+constexpr int kTcRegsLaunch = 80, kTcRegsLow = 48, kTcRegsDrain = 96;
+static_assert(kTcFirstDrainWarp % 4 == 0, "warpgroups must not mix drain and other warps");
+static_assert(32 * kTcFirstDrainWarp * kTcRegsLow + 32 * kTcDrainWarps * kTcRegsDrain <= kTcThreads * kTcRegsLaunch,
+              "register split exceeds the registers the CTA is launched with");
 constexpr uint32_t kTcTmemCols = 512;                // two 256-column accumulators
 constexpr uint32_t kTcAccCols = kTcBM;
 
@@ -243,6 +251,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant_
     tc::tc_fence_after();
     const uint32_t tmem = sm.tmem_addr;
 
+    if (warp < kTcFirstDrainWarp) tc::setmaxnreg_dec<kTcRegsLow>();
     if (warp == 0) {
         // ---------------- TMA producers: lane 0 the W tiles, lane 1 the X tiles
         if (lane < 2) {
@@ -352,6 +361,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant_
         }
     } else {
         // ---------------- drain, then epilogue ----------------
+        tc::setmaxnreg_inc<kTcRegsDrain>();
         const int dw = warp - kTcFirstDrainWarp;  // 0..15
         const int q = warp & 3;                   // TMEM lane quarter this warp may access
         const int slice = dw >> 2;                // which 64 of the 256 accumulator columns
@@ -543,6 +553,15 @@ inline cudaError_t launch_tc_kernel(cudaStream_t stream, int pairs, const CUtens
     auto kern = gemm_tc_kernel<A_MN, B_MN, B_SPLIT, C_TMA, Epi>;
     const cudaError_t a = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTcSmemBytes);
     if (a != cudaSuccess) return a;
+    // the warpgroups' register split must fit what the CTA is launched with
+    static int regs = 0;
+    if (regs == 0) {
+        cudaFuncAttributes fa{};
+        const cudaError_t r = cudaFuncGetAttributes(&fa, kern);
+        if (r != cudaSuccess) return r;
+        regs = fa.numRegs;
+    }
+    if (regs != kTcRegsLaunch) return cudaErrorInvalidConfiguration;
     cudaLaunchAttribute attr[1];
     const cudaLaunchConfig_t cfg = tc_launch_config(std::min(g.units, pairs), stream, attr);
     return cudaLaunchKernelEx(&cfg, kern, mx, mw, mw_lo, mc, g, epi, partial, err);

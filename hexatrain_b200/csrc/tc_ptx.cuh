@@ -203,6 +203,20 @@ __device__ __forceinline__ float exp2_approx(float x) {
     return y;
 }
 
+// ---- register reallocation between warpgroups ------------------------------
+// Executed by every thread of a warpgroup (4 aligned warps).  An increase is
+// served from the registers the CTA was launched with, so the shares of all
+// warpgroups must add up to at most threads x registers at launch, or the
+// increase never completes: callers check that sum on the host.
+template <int N>
+__device__ __forceinline__ void setmaxnreg_dec() {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <int N>
+__device__ __forceinline__ void setmaxnreg_inc() {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+
 // ---- clusters and the CTA pair of a 2-SM MMA ------------------------------
 // A kernel launched with clusters of two CTAs can run tcgen05 with
 // cta_group::2: one MMA instruction, issued by the pair's even CTA, reads half
