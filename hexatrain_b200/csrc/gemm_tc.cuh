@@ -114,6 +114,7 @@ struct TcSmem {
 };
 constexpr size_t kTcSmemBytes = sizeof(TcSmem) + 1024;  // + alignment slack
 static_assert(kTcSmemBytes <= 232448, "tcgen05 GEMM shared memory exceeds the 227 KB per-CTA limit");
+static_assert((232448 >> 4) < (1 << 14), "shared addresses fit a descriptor's 14-bit start-address field");
 
 enum TcError { kTcErrProducer = 1, kTcErrConverter = 2, kTcErrMma = 3, kTcErrEpilogue = 4 };
 
@@ -257,9 +258,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant_
         if (lane < 2) {
             const bool ring_w = lane == 0;
             const int ns = kTcStages;
-            uint32_t issued_parity[kTcStages];
-            bool issued[kTcStages];
-            for (int s = 0; s < kTcStages; ++s) issued[s] = false;
+            uint32_t issued = 0, issued_parity = 0;  // per stage: a load was issued, and its phase parity
             uint32_t it = 0;  // k-blocks issued by this CTA
             bool stop = false;
             for (int u = pair; u < g.units && !stop; u += npairs) {
@@ -280,14 +279,14 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant_
                         tc::mbar_arrive_expect_tx(&sm.x_full[s], kTcTileFloats * 4);
                         tc_load_tile<A_MN>(sm.x_hi[s], &map_x, &sm.x_full[s], k, t.m0 + kTcHalf * rank);
                     }
-                    issued[s] = true;
-                    issued_parity[s] = ph;
+                    issued |= 1u << s;
+                    issued_parity = (issued_parity & ~(1u << s)) | (ph << s);
                 }
             }
             if (tc_aborted(sm)) {
                 // let our own loads land before the CTA can exit
                 for (int s = 0; s < ns; ++s)
-                    if (issued[s]) tc::mbar_wait(ring_w ? &sm.w_full[s] : &sm.x_full[s], issued_parity[s]);
+                    if ((issued >> s) & 1u) tc::mbar_wait(ring_w ? &sm.w_full[s] : &sm.x_full[s], (issued_parity >> s) & 1u);
             }
         }
     } else if (warp == 1) {
@@ -310,17 +309,20 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant_
                     if (tc_aborted(sm)) { stop = true; break; }
                     tc::tc_fence_after();
                     const uint32_t d = tmem + kTcAccCols * b;
+                    // k-step kk of a tile is its descriptor plus kk * step in
+                    // the start-address field (bits 0-13, address >> 4; shared
+                    // addresses stay below 2^18, so the field never carries)
+                    const uint64_t wh = tc_desc<B_MN>(sm.w_hi[s], 0), wl = tc_desc<B_MN>(sm.w_lo[s], 0);
+                    const uint64_t xh = tc_desc<A_MN>(sm.x_hi[s], 0), xl = tc_desc<A_MN>(sm.x_lo[s], 0);
+                    constexpr uint64_t ws = (B_MN ? 1024 : 32) >> 4, xs = (A_MN ? 1024 : 32) >> 4;
                     // hi*lo and lo*hi first, then hi*hi
 #pragma unroll
                     for (int k = 0; k < kTcBK / 8; ++k) {
-                        const uint64_t wh = tc_desc<B_MN>(sm.w_hi[s], k), wl = tc_desc<B_MN>(sm.w_lo[s], k);
-                        const uint64_t xh = tc_desc<A_MN>(sm.x_hi[s], k), xl = tc_desc<A_MN>(sm.x_lo[s], k);
-                        tc::mma_tf32_pair(d, wh, xl, idesc, k > 0 ? 1u : 0u);
-                        tc::mma_tf32_pair(d, wl, xh, idesc, 1u);
+                        tc::mma_tf32_pair(d, wh + k * ws, xl + k * xs, idesc, k > 0 ? 1u : 0u);
+                        tc::mma_tf32_pair(d, wl + k * ws, xh + k * xs, idesc, 1u);
                     }
 #pragma unroll
-                    for (int k = 0; k < kTcBK / 8; ++k)
-                        tc::mma_tf32_pair(d, tc_desc<B_MN>(sm.w_hi[s], k), tc_desc<A_MN>(sm.x_hi[s], k), idesc, 1u);
+                    for (int k = 0; k < kTcBK / 8; ++k) tc::mma_tf32_pair(d, wh + k * ws, xh + k * xs, idesc, 1u);
                     tc::mma_commit_pair(&sm.w_empty[s], 0x3);
                     tc::mma_commit_pair(&sm.x_empty[s], 0x3);
                     tc::mma_commit_pair(&sm.acc_ready[b], 0x3);
@@ -409,24 +411,28 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant_
 #pragma unroll
                 for (int c = 0; c < 64 / kTcStoreRows; ++c) {
                     const int r0 = row0 + kTcStoreRows * c;
-                    float pre[kTcStoreRows];
-#pragma unroll
-                    for (int j = 0; j < kTcStoreRows; ++j) pre[j] = 0.f;
-                    if constexpr (Epi::kReads) {
-                        // the chunk's global epilogue inputs, all loads in flight together
-                        if (!partial && n < g.N) {
-                            const float* pp = epi.pre_ptr() + n;
-#pragma unroll
-                            for (int j = 0; j < kTcStoreRows; ++j)
-                                if (r0 + j < g.M) pre[j] = pp[(long)(r0 + j) * epi.tma_ld()];
-                        }
-                    }
                     if (lane == 0) tc::bulk_wait_read<0>();  // the last store has read the block
                     __syncwarp();
 #pragma unroll
-                    for (int j = 0; j < kTcStoreRows; ++j) {
-                        const float v = acc[kTcStoreRows * c + j];
-                        buf[j * 32 + lane] = partial ? v : epi.value(v, pre[j]);
+                    for (int hh = 0; hh < kTcStoreRows / 8; ++hh) {
+                        // eight rows at a time: their global epilogue inputs
+                        // are loaded together, then the rows are staged
+                        float pre[8];
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) pre[j] = 0.f;
+                        if constexpr (Epi::kReads) {
+                            if (!partial && n < g.N) {
+                                const float* pp = epi.pre_ptr() + n;
+#pragma unroll
+                                for (int j = 0; j < 8; ++j)
+                                    if (r0 + 8 * hh + j < g.M) pre[j] = pp[(long)(r0 + 8 * hh + j) * epi.tma_ld()];
+                            }
+                        }
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) {
+                            const float v = acc[kTcStoreRows * c + 8 * hh + j];
+                            buf[(8 * hh + j) * 32 + lane] = partial ? v : epi.value(v, pre[j]);
+                        }
                     }
                     tc::fence_proxy_async_smem();
                     __syncwarp();
