@@ -398,7 +398,7 @@ void forward_backward(hx_runtime* rt, LmPlan& p, const float* W, float* G, float
         ProfScope plb2(rt, kTagLayerNorm, 12.0 * M * D, 4.0 * (4.0 * M * D + 2.0 * M));
         ln_bwd(dn, a.at<float>(A.r1), a.at<float>(A.mean2), a.at<float>(A.inv2), W + o.g2, dout, dr);
         plb2.end();
-        column_reduce_kernel<<<grid_for(2L * D, tpb, rt->sm_count), tpb, 0, s>>>(p.ln_parts, D, part, G + o.g2, G + o.b2);
+        column_reduce_kernel<<<(2 * D + 31) / 32, 32 * kColReduceWarps, 0, s>>>(p.ln_parts, D, part, G + o.g2, G + o.b2);
         HX_LAUNCHED(rt);
         gemm<true, false>(rt, D, D, M, a.at<float>(A.ctx), D, dr, D, EpiStore{G + o.wo, (long)D, 0, 0});
         gemm<false, true>(rt, M, D, D, dr, D, W + o.wo, D, EpiStore{dc, (long)D, 0, 0}, wsplit(o.wo));
@@ -411,7 +411,7 @@ void forward_backward(hx_runtime* rt, LmPlan& p, const float* W, float* G, float
         ProfScope plb1(rt, kTagLayerNorm, 12.0 * M * D, 4.0 * (4.0 * M * D + 2.0 * M));
         ln_bwd(dn, xin, a.at<float>(A.mean1), a.at<float>(A.inv1), W + o.g1, dr, dout);
         plb1.end();
-        column_reduce_kernel<<<grid_for(2L * D, tpb, rt->sm_count), tpb, 0, s>>>(p.ln_parts, D, part, G + o.g1, G + o.b1);
+        column_reduce_kernel<<<(2 * D + 31) / 32, 32 * kColReduceWarps, 0, s>>>(p.ln_parts, D, part, G + o.g1, G + o.b1);
         HX_LAUNCHED(rt);
         if (p.diag) copy_d2d(rt, a.at<float>(p.diag_lig) + size_t(li) * M * D, dout, sizeof(float) * size_t(M) * D);
     }
@@ -432,7 +432,7 @@ void forward_backward(hx_runtime* rt, LmPlan& p, const float* W, float* G, float
     }
     pemb2.end();
     if (p.learned) {
-        position_bwd_kernel<<<grid_for(long(T) * D, tpb, rt->sm_count), tpb, 0, s>>>(B, T, D, dout, G + p.off_pos);
+        position_bwd_kernel<<<(unsigned)((long(T) * D + 31) / 32), 32 * kPosWarps, 0, s>>>(B, T, D, dout, G + p.off_pos);
         HX_LAUNCHED(rt);
     }
 }
@@ -644,7 +644,7 @@ int hx_lm_prepare(hx_runtime* rt, const hx_lm_config* cfg, uint32_t batch, int d
         p.ln_rows = (p.M + p.ln_parts - 1) / p.ln_parts;
         p.ln_parts = (p.M + p.ln_rows - 1) / p.ln_rows;
         p.ln_part = a.reserve(f * size_t(p.ln_parts) * 2 * D);
-        p.emb_rows = 4096;
+        p.emb_rows = 1024;  // short chunks: the most frequent tokens' CTAs bound the kernel
         p.emb_chunks = (p.M + p.emb_rows - 1) / p.emb_rows;
         p.emb_part = a.reserve(f * size_t(p.emb_chunks) * V * D);
         if (p.diag) {

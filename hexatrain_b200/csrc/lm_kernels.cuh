@@ -237,15 +237,33 @@ __global__ void layernorm_bwd_vec_kernel(int M, int rows_per_cta, const float* _
     }
 }
 
-// out[c] = sum over parts p of part[p][which][c], in part order.
-__global__ void column_reduce_kernel(int parts, int D, const float* __restrict__ part, float* __restrict__ dgamma,
-                                     float* __restrict__ dbeta)
+// out[c] = sum over parts p of part[p][which][c].  A CTA takes 32 columns
+// (lane = column, so every load is a 128-byte segment); warp w sums parts
+// w, w + 8, w + 16, ... and the eight warp sums are added in warp order, so
+// the result does not depend on timing.
+constexpr int kColReduceWarps = 8;
+__global__ void __launch_bounds__(32 * kColReduceWarps)
+column_reduce_kernel(int parts, int D, const float* __restrict__ part, float* __restrict__ dgamma,
+                     float* __restrict__ dbeta)
 {
-    for (int c = blockIdx.x * blockDim.x + threadIdx.x; c < 2 * D; c += gridDim.x * blockDim.x) {
-        const int which = c / D, d = c % D;
-        float s = 0.f;
-        for (int p = 0; p < parts; ++p) s += part[((size_t)p * 2 + which) * D + d];
-        (which ? dbeta : dgamma)[d] = s;
+    __shared__ float red[kColReduceWarps][32];
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const int c = blockIdx.x * 32 + lane;
+    const bool ok = c < 2 * D;
+    const int which = ok ? c / D : 0, d = ok ? c % D : 0;
+    float s = 0.f;
+    if (ok) {
+        const float* src = part + (size_t)which * D + d;
+#pragma unroll 4
+        for (int p = w; p < parts; p += kColReduceWarps) s += src[(size_t)p * 2 * D];
+    }
+    red[w][lane] = s;
+    __syncthreads();
+    if (w == 0 && ok) {
+        float t = red[0][lane];
+#pragma unroll
+        for (int i = 1; i < kColReduceWarps; ++i) t += red[i][lane];
+        (which ? dbeta : dgamma)[d] = t;
     }
 }
 
@@ -505,11 +523,15 @@ __global__ void loss_reduce_kernel(int B, int T, const double* __restrict__ row_
 // ([tb][D], tb * D <= 16384 floats); warp w owns columns 32w + lane (and
 // every 256th beyond) and walks the chunk's rows in increasing order: it
 // loads 32 ids at a time (the next batch's ids in flight), selects the rows
-// whose token falls in the block with a ballot, and adds them up to four at
-// a time (independent loads, then the adds in row order).  Each (token,
+// whose token falls in the block with a ballot, and adds them up to
+// kEmbBatch at a time (independent loads, then the adds in row order).  With
+// skewed token frequencies most rows fall in one block, so that block's
+// CTAs carry the kernel: short chunks and many loads in flight per warp keep
+// them short.  Each (token,
 // column) therefore sums its rows of the chunk in row order; the table goes
 // to part[c][v][d], and embed_bwd_combine sums the chunks in order.
 constexpr int kEmbWarps = 8;
+constexpr int kEmbBatch = 16;   // selected rows loaded together per warp
 constexpr int kEmbTableFloats = 16384;  // 64 KB of shared memory
 __global__ void __launch_bounds__(32 * kEmbWarps)
 embed_bwd_partial_kernel(int M, int V, int D, int chunk_rows, int tb, const int* __restrict__ ids,
@@ -531,10 +553,12 @@ embed_bwd_partial_kernel(int M, int V, int D, int chunk_rows, int tb, const int*
             vnext = (rb + 32 + lane < r1) ? ids[rb + 32 + lane] - v0 : -1;
             unsigned mask = __ballot_sync(0xffffffffu, v >= 0 && v < ntok);
             while (mask) {  // warp-uniform
-                int rr[4] = {0, 0, 0, 0}, vv[4] = {0, 0, 0, 0};
+                int rr[kEmbBatch], vv[kEmbBatch];
                 int n = 0;
 #pragma unroll
-                for (int q = 0; q < 4; ++q) {
+                for (int q = 0; q < kEmbBatch; ++q) {
+                    rr[q] = 0;
+                    vv[q] = 0;
                     if (mask) {
                         const int i = __ffs(mask) - 1;
                         mask &= mask - 1;
@@ -543,11 +567,11 @@ embed_bwd_partial_kernel(int M, int V, int D, int chunk_rows, int tb, const int*
                         n = q + 1;
                     }
                 }
-                float val[4];
+                float val[kEmbBatch];
 #pragma unroll
-                for (int q = 0; q < 4; ++q) val[q] = (q < n && dok) ? dx[(long)rr[q] * D + d] : 0.f;
+                for (int q = 0; q < kEmbBatch; ++q) val[q] = (q < n && dok) ? dx[(long)rr[q] * D + d] : 0.f;
 #pragma unroll
-                for (int q = 0; q < 4; ++q)
+                for (int q = 0; q < kEmbBatch; ++q)
                     if (q < n && dok) tab[vv[q] * D + d] += val[q];
             }
         }
@@ -567,14 +591,30 @@ __global__ void embed_bwd_combine_kernel(int chunks, int V, int D, const float* 
     }
 }
 
-// Learned position table gradient: gP[t,:] = sum_b dx0[b*T+t,:] (batch order).
-__global__ void position_bwd_kernel(int B, int T, int D, const float* __restrict__ dx, float* __restrict__ gP)
+// Learned position table gradient: gP[t,:] = sum_b dx0[b*T+t,:].  A CTA takes
+// 32 consecutive elements of the [T][D] table (lane = element, 128-byte
+// loads); warp w sums sequences w, w + 8, ... and the eight warp sums are
+// added in warp order, so the result does not depend on timing.
+constexpr int kPosWarps = 8;
+__global__ void __launch_bounds__(32 * kPosWarps)
+position_bwd_kernel(int B, int T, int D, const float* __restrict__ dx, float* __restrict__ gP)
 {
+    __shared__ float red[kPosWarps][32];
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
     const long total = (long)T * D;
-    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
-        float s = 0.f;
-        for (int b = 0; b < B; ++b) s += dx[(long)b * T * D + i];
-        gP[i] = s;
+    const long i = (long)blockIdx.x * 32 + lane;
+    float s = 0.f;
+    if (i < total) {
+#pragma unroll 4
+        for (int b = w; b < B; b += kPosWarps) s += dx[(long)b * total + i];
+    }
+    red[w][lane] = s;
+    __syncthreads();
+    if (w == 0 && i < total) {
+        float t = red[0][lane];
+#pragma unroll
+        for (int k = 1; k < kPosWarps; ++k) t += red[k][lane];
+        gP[i] = t;
     }
 }
 
