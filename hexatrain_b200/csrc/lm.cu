@@ -305,6 +305,20 @@ void forward_backward(hx_runtime* rt, LmPlan& p, const float* W, float* G, float
         pemb.end();
     const int rows_per_block = 8;  // warps per block for row kernels
     const int row_grid = (M + rows_per_block - 1) / rows_per_block;
+    // LayerNorm forward: the row-in-registers kernel when D = 128, 256 or 512
+    // and every row pointer is 16-byte aligned, else the scalar kernel
+    auto ln_fwd = [&](const float* xx, const float* gam, const float* bet, float* yy, float* mo, float* io) {
+        const int C = (D % 128 == 0) ? D / 128 : 0;
+        const bool al = ((reinterpret_cast<uintptr_t>(xx) | reinterpret_cast<uintptr_t>(gam) |
+                          reinterpret_cast<uintptr_t>(bet) | reinterpret_cast<uintptr_t>(yy)) & 15) == 0;
+        if (al && (C == 1 || C == 2 || C == 4)) {
+            auto k = C == 1 ? layernorm_fwd_vec_kernel<1> : C == 2 ? layernorm_fwd_vec_kernel<2> : layernorm_fwd_vec_kernel<4>;
+            k<<<row_grid, 32 * rows_per_block, 0, s>>>(M, p.cfg.eps, xx, gam, bet, yy, mo, io);
+        } else {
+            layernorm_fwd_kernel<<<row_grid, 32 * rows_per_block, 0, s>>>(M, D, p.cfg.eps, xx, gam, bet, yy, mo, io);
+        }
+        HX_LAUNCHED(rt);
+    };
 
     for (uint32_t l = 0; l < p.L; ++l) {
         const LayerActs& A = p.la[l];
@@ -312,10 +326,7 @@ void forward_backward(hx_runtime* rt, LmPlan& p, const float* W, float* G, float
         const float* xin = a.at<float>(A.x);
         float* xout = (l + 1 < p.L) ? a.at<float>(p.la[l + 1].x) : a.at<float>(p.xL);
         ProfScope pln1(rt, kTagLayerNorm, 8.0 * M * D, 4.0 * (2.0 * M * D + 2.0 * M));
-        layernorm_fwd_kernel<<<row_grid, 32 * rows_per_block, 0, s>>>(M, D, p.cfg.eps, xin, W + o.g1, W + o.b1,
-                                                                       a.at<float>(A.n1), a.at<float>(A.mean1),
-                                                                       a.at<float>(A.inv1));
-        HX_LAUNCHED(rt);
+        ln_fwd(xin, W + o.g1, W + o.b1, a.at<float>(A.n1), a.at<float>(A.mean1), a.at<float>(A.inv1));
         pln1.end();
         gemm<false, false>(rt, M, 3 * D, D, a.at<float>(A.n1), D, wqkv + size_t(l) * 3 * D * D, 3 * D,
                            EpiStore{a.at<float>(A.qkv), 3L * D, 0, 0}, qsplit(l));
@@ -325,10 +336,7 @@ void forward_backward(hx_runtime* rt, LmPlan& p, const float* W, float* G, float
         gemm<false, false>(rt, M, D, D, a.at<float>(A.ctx), D, W + o.wo, D, EpiAddResidual{xin, a.at<float>(A.r1), D},
                            wsplit(o.wo));
         ProfScope pln2(rt, kTagLayerNorm, 8.0 * M * D, 4.0 * (2.0 * M * D + 2.0 * M));
-        layernorm_fwd_kernel<<<row_grid, 32 * rows_per_block, 0, s>>>(M, D, p.cfg.eps, a.at<float>(A.r1), W + o.g2,
-                                                                       W + o.b2, a.at<float>(A.n2),
-                                                                       a.at<float>(A.mean2), a.at<float>(A.inv2));
-        HX_LAUNCHED(rt);
+        ln_fwd(a.at<float>(A.r1), W + o.g2, W + o.b2, a.at<float>(A.n2), a.at<float>(A.mean2), a.at<float>(A.inv2));
         pln2.end();
         gemm<false, false>(rt, M, F, D, a.at<float>(A.n2), D, W + o.w1, F, EpiRelu{a.at<float>(A.relu), nullptr, F},
                            wsplit(o.w1));
@@ -345,9 +353,14 @@ void forward_backward(hx_runtime* rt, LmPlan& p, const float* W, float* G, float
     gemm<false, false>(rt, M, V, D, xL, D, W + p.off_out, V, EpiStore{logits, (long)V, 0, 0}, wsplit(p.off_out));
     if (mode == kForwardAllRows) return;
     ProfScope pce(rt, kTagSoftmaxCe, 4.0 * M * V, 4.0 * 2.0 * M * V);
-    softmax_ce_kernel<<<row_grid, 32 * rows_per_block, 0, s>>>(
-        M, V, T, grad_scale, logits, tgt_ids, p.diag ? a.at<float>(p.probs) : nullptr, logits,
-        a.at<double>(p.row_loss), a.at<int>(p.row_correct));
+    if (V == 1024)
+        softmax_ce_vec_kernel<32><<<row_grid, 32 * rows_per_block, 0, s>>>(
+            M, T, grad_scale, logits, tgt_ids, p.diag ? a.at<float>(p.probs) : nullptr, logits,
+            a.at<double>(p.row_loss), a.at<int>(p.row_correct));
+    else
+        softmax_ce_kernel<<<row_grid, 32 * rows_per_block, 0, s>>>(
+            M, V, T, grad_scale, logits, tgt_ids, p.diag ? a.at<float>(p.probs) : nullptr, logits,
+            a.at<double>(p.row_loss), a.at<int>(p.row_correct));
     HX_LAUNCHED(rt);
         pce.end();
     ProfScope plr(rt, kTagReduce, 1.0 * M, 12.0 * M);
@@ -640,7 +653,7 @@ int hx_lm_prepare(hx_runtime* rt, const hx_lm_config* cfg, uint32_t batch, int d
         p.df1 = a.reserve(f * M * F);
         p.dqkv = a.reserve(f * M * 3 * D);
         p.attn_bstat = a.reserve(f * 2 * B * H * T);
-        p.ln_parts = std::max(1, std::min<int>(p.M, 2 * rt->sm_count));
+        p.ln_parts = std::max(1, std::min<int>(p.M, 4 * rt->sm_count));  // 32 warps per SM of the LN backward
         p.ln_rows = (p.M + p.ln_parts - 1) / p.ln_parts;
         p.ln_parts = (p.M + p.ln_rows - 1) / p.ln_rows;
         p.ln_part = a.reserve(f * size_t(p.ln_parts) * 2 * D);

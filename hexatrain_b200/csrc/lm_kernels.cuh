@@ -93,6 +93,59 @@ __global__ void layernorm_fwd_kernel(int M, int D, float eps, const float* __res
     }
 }
 
+// The same for D = 128 C with the row in registers: lane l owns columns
+// 128k + 4l .. +3 (k < C), so the row is read once, as C float4 loads, and
+// written once.  The double sums are of the same terms as above, in another
+// order.
+template <int C>
+__global__ void layernorm_fwd_vec_kernel(int M, float eps, const float* __restrict__ x, const float* __restrict__ g,
+                                         const float* __restrict__ b, float* __restrict__ y,
+                                         float* __restrict__ mean_out, float* __restrict__ inv_out)
+{
+    constexpr int D = 128 * C;
+    const int lane = threadIdx.x & 31;
+    const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (row >= M) return;
+    const float* xr = x + (long)row * D;
+    float xv[4 * C];
+#pragma unroll
+    for (int k = 0; k < C; ++k) {
+        const float4 a = *reinterpret_cast<const float4*>(xr + 128 * k + 4 * lane);
+        xv[4 * k] = a.x; xv[4 * k + 1] = a.y; xv[4 * k + 2] = a.z; xv[4 * k + 3] = a.w;
+    }
+    double s = 0.0;
+#pragma unroll
+    for (int i = 0; i < 4 * C; ++i) s += xv[i];
+    const double m = warp_sum(s) / D;
+    double v = 0.0;
+#pragma unroll
+    for (int i = 0; i < 4 * C; ++i) {
+        const double z = xv[i] - m;
+        v += z * z;
+    }
+    v = warp_sum(v) / D;
+    const float inv = (float)(1.0 / sqrt(v + (double)eps));
+    const float mf = (float)m;
+    float* yr = y + (long)row * D;
+#pragma unroll
+    for (int k = 0; k < C; ++k) {
+        const float4 gg = *reinterpret_cast<const float4*>(g + 128 * k + 4 * lane);
+        const float4 bb = *reinterpret_cast<const float4*>(b + 128 * k + 4 * lane);
+        const float gv[4] = {gg.x, gg.y, gg.z, gg.w}, bv[4] = {bb.x, bb.y, bb.z, bb.w};
+        float o[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const float xh = __fmul_rn(__fsub_rn(xv[4 * k + e], mf), inv);
+            o[e] = __fadd_rn(__fmul_rn(xh, gv[e]), bv[e]);
+        }
+        *reinterpret_cast<float4*>(yr + 128 * k + 4 * lane) = make_float4(o[0], o[1], o[2], o[3]);
+    }
+    if (lane == 0) {
+        mean_out[row] = mf;
+        inv_out[row] = inv;
+    }
+}
+
 // LayerNorm backward fused with the residual add (nb, :37, and "dr = dout +
 // drn" of :79): dx = res + inv/D*(D*z - sum z - xhat*sum(z*xhat)), z=dy*g.
 // Also writes per-CTA partial column sums of dy*xhat (dgamma) and dy
@@ -176,13 +229,18 @@ __global__ void layernorm_bwd_vec_kernel(int M, int rows_per_cta, const float* _
     const float ivd_scale = float(D);
     for (int row = r0 + warp; row < r1; row += nw) {
         const long base = (long)row * D;
-        float dyv[4 * C], xv[4 * C];
+        // dy, x and the residual of the row are loaded together: one round
+        // trip to memory per row
+        float dyv[4 * C], xv[4 * C], rv[4 * C];
 #pragma unroll
         for (int k = 0; k < C; ++k) {
             const float4 a = *reinterpret_cast<const float4*>(dy + base + 128 * k + 4 * lane);
             const float4 b = *reinterpret_cast<const float4*>(x + base + 128 * k + 4 * lane);
+            const float4 r = res ? *reinterpret_cast<const float4*>(res + base + 128 * k + 4 * lane)
+                                 : make_float4(0.f, 0.f, 0.f, 0.f);
             dyv[4 * k] = a.x; dyv[4 * k + 1] = a.y; dyv[4 * k + 2] = a.z; dyv[4 * k + 3] = a.w;
             xv[4 * k] = b.x; xv[4 * k + 1] = b.y; xv[4 * k + 2] = b.z; xv[4 * k + 3] = b.w;
+            rv[4 * k] = r.x; rv[4 * k + 1] = r.y; rv[4 * k + 2] = r.z; rv[4 * k + 3] = r.w;
         }
         const float mf = mean[row], iv = inv[row];
         double s = 0.0, sx = 0.0;
@@ -210,9 +268,8 @@ __global__ void layernorm_bwd_vec_kernel(int M, int rows_per_cta, const float* _
             }
             const long off = base + 128 * k + 4 * lane;
             if (res) {
-                const float4 r = *reinterpret_cast<const float4*>(res + off);
-                o[0] = __fadd_rn(r.x, o[0]); o[1] = __fadd_rn(r.y, o[1]);
-                o[2] = __fadd_rn(r.z, o[2]); o[3] = __fadd_rn(r.w, o[3]);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) o[e] = __fadd_rn(rv[4 * k + e], o[e]);
             }
             *reinterpret_cast<float4*>(dx + off) = make_float4(o[0], o[1], o[2], o[3]);
         }
@@ -474,6 +531,63 @@ __global__ void softmax_ce_kernel(int M, int V, int T, float scale, float* logit
     float* pr = probs ? probs + (long)row * V : nullptr;
     for (int j = lane; j < V; j += 32) {
         const float p = __fdiv_rn(expf(l[j] - mx), sf);
+        if (pr) pr[j] = p;
+        float d = __fdiv_rn(__fsub_rn(p, j == y ? 1.0f : 0.0f), (float)T);
+        if (scale != 1.0f) d = __fmul_rn(d, scale);
+        out[j] = d;
+    }
+    if (lane == 0) {
+        row_loss[row] = (double)mx + log(s) - (double)ly;
+        row_correct[row] = arg == y;
+    }
+}
+
+// The same for V = 32 NR with the row in registers: lane l holds columns
+// l, l + 32, ... (the order in which the kernel above visits them), so the
+// row is read from memory once and exp is evaluated once per logit; every
+// result is bit-identical to the kernel above.
+template <int NR>
+__global__ void softmax_ce_vec_kernel(int M, int T, float scale, float* logits, const int* __restrict__ tgt,
+                                      float* __restrict__ probs, float* dlogits, double* __restrict__ row_loss,
+                                      int* __restrict__ row_correct)
+{
+    constexpr int V = 32 * NR;
+    const int lane = threadIdx.x & 31;
+    const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (row >= M) return;
+    const float* l = logits + (long)row * V;
+    float v[NR];
+#pragma unroll
+    for (int i = 0; i < NR; ++i) v[i] = l[lane + 32 * i];
+    const int y = tgt[row];
+    const float ly = l[y];
+    float mx = -INFINITY;
+    int arg = 0x7fffffff;
+#pragma unroll
+    for (int i = 0; i < NR; ++i) {
+        const int j = lane + 32 * i;
+        if (v[i] > mx || (v[i] == mx && j < arg)) { mx = v[i]; arg = j; }
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+        const float om = __shfl_xor_sync(0xffffffffu, mx, o);
+        const int oa = __shfl_xor_sync(0xffffffffu, arg, o);
+        if (om > mx || (om == mx && oa < arg)) { mx = om; arg = oa; }
+    }
+    double s = 0.0;
+#pragma unroll
+    for (int i = 0; i < NR; ++i) {
+        v[i] = expf(v[i] - mx);
+        s += (double)v[i];
+    }
+    s = warp_sum(s);
+    const float sf = (float)s;
+    __syncwarp();  // every lane has read its logits before any overwrites them
+    float* out = dlogits + (long)row * V;
+    float* pr = probs ? probs + (long)row * V : nullptr;
+#pragma unroll
+    for (int i = 0; i < NR; ++i) {
+        const int j = lane + 32 * i;
+        const float p = __fdiv_rn(v[i], sf);
         if (pr) pr[j] = p;
         float d = __fdiv_rn(__fsub_rn(p, j == y ? 1.0f : 0.0f), (float)T);
         if (scale != 1.0f) d = __fmul_rn(d, scale);
