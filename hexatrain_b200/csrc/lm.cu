@@ -58,7 +58,7 @@ struct LmPlan {
     size_t w_hi, w_lo, wqkv_hi, wqkv_lo;  // TF32 hi/lo splits of the GEMM weights, refreshed every forward
     size_t tokens, in_tok, tgt_tok, in_ids, tgt_ids, bad;
     std::vector<LayerActs> la;
-    size_t xL, logits, probs, row_loss, row_correct, loss, acc, scalars;
+    size_t xL, logits, probs, row_loss, row_correct, seq_loss, seq_correct, loss, acc, scalars;
     size_t dout, dr, dc, dn, df1, dqkv, ln_part;
     size_t attn_bstat;  // tensor-core attention backward: per (sequence, head, row) sum and D
     size_t diag_lig, diag_hp, diag_dout;
@@ -364,7 +364,10 @@ void forward_backward(hx_runtime* rt, LmPlan& p, const float* W, float* G, float
     HX_LAUNCHED(rt);
         pce.end();
     ProfScope plr(rt, kTagReduce, 1.0 * M, 12.0 * M);
-    loss_reduce_kernel<<<1, 256, 0, s>>>(B, T, a.at<double>(p.row_loss), a.at<int>(p.row_correct), grad_scale,
+    loss_seq_kernel<<<(B + 7) / 8, 256, 0, s>>>(B, T, a.at<double>(p.row_loss), a.at<int>(p.row_correct),
+                                               a.at<float>(p.seq_loss), a.at<int>(p.seq_correct));
+    HX_LAUNCHED(rt);
+    loss_reduce_kernel<<<1, 256, 0, s>>>(B, T, a.at<float>(p.seq_loss), a.at<int>(p.seq_correct), grad_scale,
                                          a.at<float>(p.loss), a.at<float>(p.acc), G + p.P);
     HX_LAUNCHED(rt);
         plr.end();
@@ -643,6 +646,8 @@ int hx_lm_prepare(hx_runtime* rt, const hx_lm_config* cfg, uint32_t batch, int d
         p.probs = p.diag ? a.reserve(f * M * V) : 0;
         p.row_loss = a.reserve(sizeof(double) * M);
         p.row_correct = a.reserve(sizeof(int) * M);
+        p.seq_loss = a.reserve(sizeof(float) * B);
+        p.seq_correct = a.reserve(sizeof(int) * B);
         p.loss = a.reserve(f * 4);
         p.acc = a.reserve(f * 4);
         p.scalars = a.reserve(f * 8);

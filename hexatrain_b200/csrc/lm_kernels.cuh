@@ -599,9 +599,34 @@ __global__ void softmax_ce_vec_kernel(int M, int T, float scale, float* logits, 
     }
 }
 
-// Per-sequence loss float(sum_t loss/T) (:77), batch mean in double, and the
+// Per-sequence loss float(sum_t loss/T) (:77): one warp per sequence loads
+// 32 positions at a time and every lane adds them in position order (a
+// double sum in the same order as a sequential loop over t).
+__global__ void loss_seq_kernel(int B, int T, const double* __restrict__ row_loss, const int* __restrict__ row_correct,
+                                float* __restrict__ seq_loss, int* __restrict__ seq_correct)
+{
+    const int lane = threadIdx.x & 31;
+    const int b = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (b >= B) return;
+    double s = 0.0;
+    int correct = 0;
+    for (int t0 = 0; t0 < T; t0 += 32) {
+        const bool ok = t0 + lane < T;
+        const double v = ok ? row_loss[(long)b * T + t0 + lane] : 0.0;
+        correct += ok ? row_correct[(long)b * T + t0 + lane] : 0;
+        const int n = min(32, T - t0);
+        for (int i = 0; i < n; ++i) s += __shfl_sync(0xffffffffu, v, i);
+    }
+    for (int o = 16; o > 0; o >>= 1) correct += __shfl_xor_sync(0xffffffffu, correct, o);
+    if (lane == 0) {
+        seq_loss[b] = (float)(s / T);
+        seq_correct[b] = correct;
+    }
+}
+
+// Batch mean of the per-sequence losses in double, the accuracy, and the
 // scaled loss term for the data-parallel gradient buffer.  One block.
-__global__ void loss_reduce_kernel(int B, int T, const double* __restrict__ row_loss, const int* __restrict__ row_correct,
+__global__ void loss_reduce_kernel(int B, int T, const float* __restrict__ seq_loss, const int* __restrict__ seq_correct,
                                    float grad_scale, float* __restrict__ loss_out, float* __restrict__ acc_out,
                                    float* __restrict__ scaled_loss_out)
 {
@@ -610,12 +635,8 @@ __global__ void loss_reduce_kernel(int B, int T, const double* __restrict__ row_
     double tot = 0.0;
     long correct = 0;
     for (int b = threadIdx.x; b < B; b += blockDim.x) {
-        double s = 0.0;
-        for (int t = 0; t < T; ++t) {
-            s += row_loss[(long)b * T + t];
-            correct += row_correct[(long)b * T + t];
-        }
-        tot += (double)(float)(s / T);
+        tot += (double)seq_loss[b];
+        correct += seq_correct[b];
     }
     tot = warp_sum(tot);
     for (int o = 16; o > 0; o >>= 1) correct += __shfl_xor_sync(0xffffffffu, correct, o);
