@@ -435,7 +435,7 @@ void forward_backward(hx_runtime* rt, LmPlan& p, const float* W, float* G, float
     ProfScope pemb2(rt, kTagEmbed, 1.0 * M * D, 4.0 * (2.0 * M * D + (p.emb_chunks + 1.0) * V * D));
     {
         const int tb = std::max(1, std::min<int>(V, kEmbTableFloats / D));
-        const size_t esm = sizeof(float) * size_t(tb) * D;
+        const size_t esm = embed_bwd_smem_bytes(tb, D, p.emb_rows);
         if (esm > 48 * 1024)
             HX_CUDA(cudaFuncSetAttribute(embed_bwd_partial_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)esm));
         dim3 grid(p.emb_chunks, (V + tb - 1) / tb);

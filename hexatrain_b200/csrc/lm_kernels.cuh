@@ -296,9 +296,9 @@ __global__ void layernorm_bwd_vec_kernel(int M, int rows_per_cta, const float* _
 
 // out[c] = sum over parts p of part[p][which][c].  A CTA takes 32 columns
 // (lane = column, so every load is a 128-byte segment); warp w sums parts
-// w, w + 8, w + 16, ... and the eight warp sums are added in warp order, so
+// w, w + 32, w + 64, ... and the 32 warp sums are added in warp order, so
 // the result does not depend on timing.
-constexpr int kColReduceWarps = 8;
+constexpr int kColReduceWarps = 32;
 __global__ void __launch_bounds__(32 * kColReduceWarps)
 column_reduce_kernel(int parts, int D, const float* __restrict__ part, float* __restrict__ dgamma,
                      float* __restrict__ dbeta)
@@ -653,62 +653,69 @@ __global__ void loss_reduce_kernel(int B, int T, const float* __restrict__ seq_l
 }
 
 // Token-embedding gradient gE[v,:] = sum over rows r with id[r] == v of
-// dX0[r,:] (one-hot^T * dX0, :82), deterministic.  CTA (chunk c, block of
-// `tb` tokens) keeps the block's rows of the gradient in shared memory
-// ([tb][D], tb * D <= 16384 floats); warp w owns columns 32w + lane (and
-// every 256th beyond) and walks the chunk's rows in increasing order: it
-// loads 32 ids at a time (the next batch's ids in flight), selects the rows
-// whose token falls in the block with a ballot, and adds them up to
-// kEmbBatch at a time (independent loads, then the adds in row order).  With
-// skewed token frequencies most rows fall in one block, so that block's
-// CTAs carry the kernel: short chunks and many loads in flight per warp keep
-// them short.  Each (token,
-// column) therefore sums its rows of the chunk in row order; the table goes
-// to part[c][v][d], and embed_bwd_combine sums the chunks in order.
+// dX0[r,:] (one-hot^T * dX0, :82), deterministic.  CTA (chunk c of
+// `chunk_rows` rows, block of `tb` tokens) keeps the block's rows of the
+// gradient in shared memory ([tb][D], tb * D <= 16384 floats).  The CTA
+// first loads the chunk's ids into shared memory in one pass; warp 0 then
+// lists, in row order, the rows whose token falls in the block; then warp w,
+// which owns columns 32w + lane (and every 256th beyond), walks that list
+// kEmbBatch rows at a time (independent loads, then the adds in row order).
+// Each (token, column) therefore sums its rows of the chunk in row order;
+// the table goes to part[c][v][d], and embed_bwd_combine sums the chunks in
+// order.  With skewed token frequencies most rows fall in one block, so that
+// block's CTAs carry the kernel: short chunks and many loads in flight keep
+// them short, and the other CTAs never wait on global memory for their ids.
 constexpr int kEmbWarps = 8;
-constexpr int kEmbBatch = 16;   // selected rows loaded together per warp
+constexpr int kEmbBatch = 16;   // listed rows loaded together per warp
 constexpr int kEmbTableFloats = 16384;  // 64 KB of shared memory
+// dynamic shared memory of embed_bwd_partial_kernel
+inline size_t embed_bwd_smem_bytes(int tb, int D, int chunk_rows) {
+    return sizeof(float) * size_t(tb) * D + sizeof(int) * 3 * size_t(chunk_rows) + 16;
+}
 __global__ void __launch_bounds__(32 * kEmbWarps)
 embed_bwd_partial_kernel(int M, int V, int D, int chunk_rows, int tb, const int* __restrict__ ids,
                          const float* __restrict__ dx, float* __restrict__ part)
 {
-    extern __shared__ float tab[];  // [tb][D]
+    extern __shared__ float tab[];  // [tb][D], then ids[chunk_rows], rows[chunk_rows], toks[chunk_rows], count
+    int* sid = reinterpret_cast<int*>(tab + (size_t)tb * D);
+    int* srow = sid + chunk_rows;
+    int* stok = srow + chunk_rows;
+    int* scount = stok + chunk_rows;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int c = blockIdx.x, v0 = blockIdx.y * tb;
     const int ntok = min(tb, V - v0);
+    const int r0 = c * chunk_rows, r1 = min(M, r0 + chunk_rows), nr = r1 - r0;
     for (int i = threadIdx.x; i < ntok * D; i += blockDim.x) tab[i] = 0.f;
+    for (int i = threadIdx.x; i < nr; i += blockDim.x) sid[i] = ids[r0 + i];
     __syncthreads();
-    const int r0 = c * chunk_rows, r1 = min(M, r0 + chunk_rows);
+    if (warp == 0) {
+        int n = 0;
+        for (int rb = 0; rb < nr; rb += 32) {
+            const int v = (rb + lane < nr) ? sid[rb + lane] - v0 : -1;
+            const bool in = v >= 0 && v < ntok;
+            const unsigned mask = __ballot_sync(0xffffffffu, in);
+            if (in) {
+                const int pos = n + __popc(mask & ((1u << lane) - 1u));
+                srow[pos] = r0 + rb + lane;
+                stok[pos] = v;
+            }
+            n += __popc(mask);
+        }
+        if (lane == 0) *scount = n;
+    }
+    __syncthreads();
+    const int nsel = *scount;
     for (int cb = 32 * warp; cb < D; cb += 32 * kEmbWarps) {
         const int d = cb + lane;
         const bool dok = d < D;
-        int vnext = (r0 + lane < r1) ? ids[r0 + lane] - v0 : -1;
-        for (int rb = r0; rb < r1; rb += 32) {
-            const int v = vnext;
-            vnext = (rb + 32 + lane < r1) ? ids[rb + 32 + lane] - v0 : -1;
-            unsigned mask = __ballot_sync(0xffffffffu, v >= 0 && v < ntok);
-            while (mask) {  // warp-uniform
-                int rr[kEmbBatch], vv[kEmbBatch];
-                int n = 0;
+        for (int b = 0; b < nsel; b += kEmbBatch) {
+            const int n = min(kEmbBatch, nsel - b);
+            float val[kEmbBatch];
 #pragma unroll
-                for (int q = 0; q < kEmbBatch; ++q) {
-                    rr[q] = 0;
-                    vv[q] = 0;
-                    if (mask) {
-                        const int i = __ffs(mask) - 1;
-                        mask &= mask - 1;
-                        rr[q] = rb + i;
-                        vv[q] = __shfl_sync(0xffffffffu, v, i);
-                        n = q + 1;
-                    }
-                }
-                float val[kEmbBatch];
+            for (int q = 0; q < kEmbBatch; ++q) val[q] = (q < n && dok) ? dx[(long)srow[b + q] * D + d] : 0.f;
 #pragma unroll
-                for (int q = 0; q < kEmbBatch; ++q) val[q] = (q < n && dok) ? dx[(long)rr[q] * D + d] : 0.f;
-#pragma unroll
-                for (int q = 0; q < kEmbBatch; ++q)
-                    if (q < n && dok) tab[vv[q] * D + d] += val[q];
-            }
+            for (int q = 0; q < kEmbBatch; ++q)
+                if (q < n && dok) tab[stok[b + q] * D + d] += val[q];
         }
     }
     __syncthreads();
