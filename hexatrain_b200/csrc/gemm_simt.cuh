@@ -174,8 +174,7 @@ __global__ void splitk_reduce_kernel(int M, int N, int splits, const float* __re
 // them, so those loads are in flight together; operator() is the fused form.
 // An epilogue that writes one float array can also hand its results to TMA
 // bulk stores: tma_ok() (host) says so for this instance, tma_out()/tma_ld()
-// name the array, pre_ptr() the array prefetch() reads (same leading
-// dimension, or null), and value(v, pre) is the element written.
+// name the array, and value(v, pre) is the element written.
 
 struct EpiStore {  // C[m*ldc + n] = v, with an optional column split:
     static constexpr bool kReads = false;  // prefetch() loads from global memory
@@ -193,7 +192,6 @@ struct EpiStore {  // C[m*ldc + n] = v, with an optional column split:
     bool tma_ok() const { return split == 0; }
     float* tma_out() const { return c; }
     __host__ __device__ long tma_ld() const { return ldc; }
-    __host__ __device__ const float* pre_ptr() const { return nullptr; }
     __device__ float value(float v, float) const { return v; }
 };
 
@@ -208,7 +206,6 @@ struct EpiAddResidual {  // out = res + v   (r1 = x + ctx*Wo ; out = r1 + relu*W
     bool tma_ok() const { return true; }
     float* tma_out() const { return out; }
     __host__ __device__ long tma_ld() const { return ld; }
-    __host__ __device__ const float* pre_ptr() const { return res; }
     __device__ float value(float v, float r) const { return __fadd_rn(r, v); }
 };
 
@@ -228,7 +225,6 @@ struct EpiRelu {  // h = max(0, z) ; optional mask = h > 0
     bool tma_ok() const { return mask == nullptr; }
     float* tma_out() const { return h; }
     __host__ __device__ long tma_ld() const { return ld; }
-    __host__ __device__ const float* pre_ptr() const { return nullptr; }
     __device__ float value(float v, float) const { return (0.f < v) ? v : 0.f; }
 };
 
@@ -248,7 +244,6 @@ struct EpiReluBackward {  // dz = (act > 0) ? v : 0 ; optional raw store of v
     bool tma_ok() const { return raw == nullptr; }
     float* tma_out() const { return dz; }
     __host__ __device__ long tma_ld() const { return ld; }
-    __host__ __device__ const float* pre_ptr() const { return act; }
     __device__ float value(float v, float a) const { return a > 0.f ? v : 0.f; }
 };
 
@@ -272,7 +267,6 @@ struct EpiError {  // P = v ; E = P - Y ; dP = (P - Y) * s
     bool tma_ok() const { return false; }
     float* tma_out() const { return dp; }
     __host__ __device__ long tma_ld() const { return ld; }
-    __host__ __device__ const float* pre_ptr() const { return y; }
     __device__ float value(float v, float) const { return v; }
 };
 
@@ -293,7 +287,6 @@ struct EpiSgd {  // dW = v (optional) ; W_next = W - lr*dW (two roundings, as th
     bool tma_ok() const { return false; }
     float* tma_out() const { return w_next; }
     __host__ __device__ long tma_ld() const { return ld; }
-    __host__ __device__ const float* pre_ptr() const { return w; }
     __device__ float value(float v, float) const { return v; }
 };
 

@@ -408,31 +408,41 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant_
                 // are clipped by TMA.
                 float* buf = sm.stage[dw];
                 const int col0 = t.n0 + kTcHalf * (int)rank + 32 * q;
+                // the epilogue's global inputs, eight rows at a time, one
+                // group ahead of the rows being staged, so that their load
+                // latency overlaps the staging and the store-buffer wait
+                constexpr int kGroups = 64 / 8;
+                float pre_cur[8], pre_nxt[8] = {};
+                auto load_group = [&](int grp8, float (&p)[8]) {
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) p[j] = 0.f;
+                    if constexpr (Epi::kReads) {
+                        if (!partial && n < g.N) {
+#pragma unroll
+                            for (int j = 0; j < 8; ++j)
+                                if (row0 + 8 * grp8 + j < g.M) p[j] = epi.prefetch(row0 + 8 * grp8 + j, n);
+                        }
+                    }
+                };
+                load_group(0, pre_cur);
 #pragma unroll
                 for (int c = 0; c < 64 / kTcStoreRows; ++c) {
                     const int r0 = row0 + kTcStoreRows * c;
-                    if (lane == 0) tc::bulk_wait_read<0>();  // the last store has read the block
-                    __syncwarp();
 #pragma unroll
                     for (int hh = 0; hh < kTcStoreRows / 8; ++hh) {
-                        // eight rows at a time: their global epilogue inputs
-                        // are loaded together, then the rows are staged
-                        float pre[8];
-#pragma unroll
-                        for (int j = 0; j < 8; ++j) pre[j] = 0.f;
-                        if constexpr (Epi::kReads) {
-                            if (!partial && n < g.N) {
-                                const float* pp = epi.pre_ptr() + n;
-#pragma unroll
-                                for (int j = 0; j < 8; ++j)
-                                    if (r0 + 8 * hh + j < g.M) pre[j] = pp[(long)(r0 + 8 * hh + j) * epi.tma_ld()];
-                            }
+                        const int grp8 = (kTcStoreRows / 8) * c + hh;
+                        if (grp8 + 1 < kGroups) load_group(grp8 + 1, pre_nxt);
+                        if (hh == 0) {
+                            if (lane == 0) tc::bulk_wait_read<0>();  // the last store has read the block
+                            __syncwarp();
                         }
 #pragma unroll
                         for (int j = 0; j < 8; ++j) {
                             const float v = acc[kTcStoreRows * c + 8 * hh + j];
-                            buf[(8 * hh + j) * 32 + lane] = partial ? v : epi.value(v, pre[j]);
+                            buf[(8 * hh + j) * 32 + lane] = partial ? v : epi.value(v, pre_cur[j]);
                         }
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) pre_cur[j] = pre_nxt[j];
                     }
                     tc::fence_proxy_async_smem();
                     __syncwarp();
