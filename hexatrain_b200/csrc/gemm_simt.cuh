@@ -174,7 +174,9 @@ __global__ void splitk_reduce_kernel(int M, int N, int splits, const float* __re
 // them, so those loads are in flight together; operator() is the fused form.
 // An epilogue that writes one float array can also hand its results to TMA
 // bulk stores: tma_ok() (host) says so for this instance, tma_out()/tma_ld()
-// name the array, and value(v, pre) is the element written.
+// name the array, and value(v, pre) is the element written.  An epilogue that
+// reads also names, by pre_addr(m, n), the address prefetch(m, n) reads, so
+// that the tensor-core epilogue can pull a tile's inputs into L2 early.
 
 struct EpiStore {  // C[m*ldc + n] = v, with an optional column split:
     static constexpr bool kReads = false;  // prefetch() loads from global memory
@@ -201,6 +203,7 @@ struct EpiAddResidual {  // out = res + v   (r1 = x + ctx*Wo ; out = r1 + relu*W
     float* out;
     long ld;
     __device__ float prefetch(int m, int n) const { return res[(long)m * ld + n]; }
+    __device__ const float* pre_addr(int m, int n) const { return res + (long)m * ld + n; }
     __device__ void finish(int m, int n, float v, float r) const { out[(long)m * ld + n] = __fadd_rn(r, v); }
     __device__ void operator()(int m, int n, float v) const { finish(m, n, v, prefetch(m, n)); }
     bool tma_ok() const { return true; }
@@ -235,6 +238,7 @@ struct EpiReluBackward {  // dz = (act > 0) ? v : 0 ; optional raw store of v
     float* raw;
     long ld;
     __device__ float prefetch(int m, int n) const { return act[(long)m * ld + n]; }
+    __device__ const float* pre_addr(int m, int n) const { return act + (long)m * ld + n; }
     __device__ void finish(int m, int n, float v, float a) const {
         const long i = (long)m * ld + n;
         if (raw) raw[i] = v;
@@ -256,6 +260,7 @@ struct EpiError {  // P = v ; E = P - Y ; dP = (P - Y) * s
     float s;
     long ld;
     __device__ float prefetch(int m, int n) const { return y[(long)m * ld + n]; }
+    __device__ const float* pre_addr(int m, int n) const { return y + (long)m * ld + n; }
     __device__ void finish(int m, int n, float v, float yv) const {
         const long i = (long)m * ld + n;
         const float err = __fsub_rn(v, yv);
@@ -278,6 +283,7 @@ struct EpiSgd {  // dW = v (optional) ; W_next = W - lr*dW (two roundings, as th
     float lr;
     long ld;
     __device__ float prefetch(int m, int n) const { return w[(long)m * ld + n]; }
+    __device__ const float* pre_addr(int m, int n) const { return w + (long)m * ld + n; }
     __device__ void finish(int m, int n, float v, float wv) const {
         const long i = (long)m * ld + n;
         if (dw) dw[i] = v;

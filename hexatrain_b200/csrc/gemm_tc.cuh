@@ -372,6 +372,18 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant_
         bool stop = false;
         for (int u = pair; u < g.units && !stop; u += npairs) {
             const TcUnit t = tc_unit(g, u);
+            if constexpr (C_TMA && Epi::kReads) {
+                // the tile's epilogue inputs into L2 now, read after the k-loop:
+                // lane l fetches the 128-byte lines of rows l and l + 32
+                const int pc = t.n0 + kTcHalf * (int)rank + 32 * q;
+                if (!partial && pc < g.N) {
+#pragma unroll
+                    for (int i = 0; i < 2; ++i) {
+                        const int row = t.m0 + 64 * slice + 32 * i + lane;
+                        if (row < g.M) tc::prefetch_l2(epi.pre_addr(row, pc));
+                    }
+                }
+            }
             float acc[64];
 #pragma unroll
             for (int i = 0; i < 64; ++i) acc[i] = 0.f;
