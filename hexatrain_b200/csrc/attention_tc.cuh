@@ -68,6 +68,22 @@ static_assert(kAtcFwdSmemBytes <= 232448, "attention forward shared memory excee
 
 enum AtcError { kAtcErrLoad = 11, kAtcErrMma = 12, kAtcErrSoftmax = 13, kAtcErrEpilogue = 14 };
 
+// L2 prefetch of the 128-byte lines at column `col` of rows [r0, r1) of a
+// row-major tensor with leading dimension ld (one head's 32 floats per row),
+// spread over threads tid = 0 .. nthreads-1.
+__device__ __forceinline__ void atc_prefetch_rows(const float* base, long ld, int col, int r0, int r1, int tid,
+                                                  int nthreads) {
+    for (int r = r0 + tid; r < r1; r += nthreads) tc::prefetch_l2(base + (long)r * ld + col);
+}
+// The CTA that starts on an SM one wave after this one (linear block id +
+// the number of SMs; one CTA per SM), or -1 past the grid.
+__device__ __forceinline__ int atc_next_wave_block() {
+    uint32_t nsm;
+    asm("mov.u32 %0, %%nsmid;" : "=r"(nsm));
+    const long id = blockIdx.x + (long)gridDim.x * (blockIdx.y + (long)gridDim.y * blockIdx.z) + nsm;
+    return id < (long)gridDim.x * gridDim.y * gridDim.z ? int(id) : -1;
+}
+
 // Bounded wait; after the first failure anywhere in the CTA it returns
 // false at once, so a broken CTA finishes in bounded time.
 __device__ __forceinline__ bool atc_wait(int& abort, int* err, int code, uint64_t* bar, uint32_t parity) {
@@ -96,8 +112,8 @@ __device__ __forceinline__ void atc_split(float* hi, float* lo, int n4, int t, i
 
 __global__ void __launch_bounds__(kAtcThreads, 1)
 attention_fwd_tc_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid_constant__ CUtensorMap map_v, int T,
-                        int D, int H, float scale, float* __restrict__ ctx, float* __restrict__ row_max,
-                        float* __restrict__ row_sum, int* __restrict__ err)
+                        int D, int H, float scale, const float* __restrict__ qkv, float* __restrict__ ctx,
+                        float* __restrict__ row_max, float* __restrict__ row_sum, int* __restrict__ err)
 {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     const uint32_t pad = (1024u - (tc::smem_u32(smem_raw) & 1023u)) & 1023u;
@@ -132,6 +148,15 @@ attention_fwd_tc_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid
     __syncthreads();
     tc::tc_fence_after();
     const uint32_t tmem = sm.tmem_addr;
+    if (warp < kAtcSoftWarps) {
+        // the next wave's CTA finds its Q, K and V rows in L2
+        const int nb = atc_next_wave_block();
+        if (nb >= 0) {
+            const int nh = nb % H, ny = (nb / H) * T;
+            for (int part = 0; part < 3; ++part)
+                atc_prefetch_rows(qkv, 3L * D, part * D + nh * kAtcDH, ny, ny + T, threadIdx.x, kAtcSoftThreads);
+        }
+    }
 
     if (warp == kAtcSoftWarps) {
         if (lane == 0) {

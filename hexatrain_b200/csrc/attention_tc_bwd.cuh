@@ -168,6 +168,18 @@ attention_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap map_qk, const __g
     tc::tc_fence_after();
     const uint32_t tmem = sm.tmem_addr;
 
+    if (warp < kAtcSoftWarps) {
+        // this CTA's Q and dO rows (read by the softmax threads after the
+        // K/V split) and the next wave's K and V rows, into L2
+        atc_prefetch_rows(qkv, 3L * D, h * kAtcDH, y0, y0 + T, threadIdx.x, kAtcSoftThreads);
+        atc_prefetch_rows(dctx, D, h * kAtcDH, y0, y0 + T, threadIdx.x, kAtcSoftThreads);
+        const int nb = atc_next_wave_block();
+        if (nb >= 0) {
+            const int nh = nb % H, ny = (nb / H) * T;
+            for (int part = 1; part < 3; ++part)
+                atc_prefetch_rows(qkv, 3L * D, part * D + nh * kAtcDH, ny, ny + T, threadIdx.x, kAtcSoftThreads);
+        }
+    }
     if (warp == kAtcSoftWarps) {
         if (lane == 0) {
             // ---------------- loads: K, V (K-major) and K (MN-major), all rows
@@ -402,7 +414,8 @@ __device__ __forceinline__ int atc_kv_chunk_vis(int kb, int q, int qb, int c, bo
 __global__ void __launch_bounds__(kAtcThreads, 1)
 attention_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid_constant__ CUtensorMap map_mn,
                              const __grid_constant__ CUtensorMap map_do, const __grid_constant__ CUtensorMap map_do_mn,
-                             int T, int D, int H, float scale, const float* __restrict__ row_max,
+                             int T, int D, int H, float scale, const float* __restrict__ qkv,
+                             const float* __restrict__ dctx, const float* __restrict__ row_max,
                              const float* __restrict__ bstat, float* __restrict__ dqkv, int* __restrict__ err)
 {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -440,6 +453,25 @@ attention_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap map_qk, const _
     tc::tc_fence_after();
     const uint32_t tmem = sm.tmem_addr;
 
+    if (warp < kAtcSoftWarps) {
+        // this CTA's later query blocks (their TMA loads wait for the
+        // previous block) and the next wave's first Q/dO block and K/V
+        // block, into L2
+        if (nqb > 1) {
+            atc_prefetch_rows(qkv, 3L * D, h * kAtcDH, y0 + kAtcTile * (kb + 1), min(y0 + T, y0 + kAtcTile * (kb + nqb)),
+                              threadIdx.x, kAtcSoftThreads);
+            atc_prefetch_rows(dctx, D, h * kAtcDH, y0 + kAtcTile * (kb + 1), min(y0 + T, y0 + kAtcTile * (kb + nqb)),
+                              threadIdx.x, kAtcSoftThreads);
+        }
+        const int nb = atc_next_wave_block();
+        if (nb >= 0) {
+            const int nh = nb % H, nbb = (nb / H) % gridDim.y, nkb = nb / (H * (int)gridDim.y);
+            const int r0 = nbb * T + kAtcTile * nkb, r1 = min(nbb * T + T, r0 + kAtcTile);
+            for (int part = 0; part < 3; ++part)
+                atc_prefetch_rows(qkv, 3L * D, part * D + nh * kAtcDH, r0, r1, threadIdx.x, kAtcSoftThreads);
+            atc_prefetch_rows(dctx, D, nh * kAtcDH, r0, r1, threadIdx.x, kAtcSoftThreads);
+        }
+    }
     if (warp == kAtcSoftWarps) {
         if (lane == 0) {
             tc::prefetch_tensormap(&map_qk);

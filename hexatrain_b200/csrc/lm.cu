@@ -144,7 +144,7 @@ void attn_fwd_tc_launch(hx_runtime* rt, const LmPlan& p, const float* qkv, float
     HX_CUDA(cudaFuncSetAttribute(attention_fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)kAtcFwdSmemBytes));
     attention_fwd_tc_kernel<<<dim3(p.H, p.B), kAtcThreads, kAtcFwdSmemBytes, rt->stream>>>(
-        mqk, mv, p.T, p.D, p.H, 1.0f / sqrtf((float)kAtcDH), ctx, rmax, rsum, rt->device_error());
+        mqk, mv, p.T, p.D, p.H, 1.0f / sqrtf((float)kAtcDH), qkv, ctx, rmax, rsum, rt->device_error());
     HX_LAUNCHED(rt);
 }
 
@@ -193,7 +193,7 @@ void attn_bwd_tc_launch(hx_runtime* rt, const LmPlan& p, const float* qkv, const
                                  (int)kAtcKvSmemBytes));
     const int ntile = p.T > uint32_t(kAtcTile) ? 2 : 1;
     attention_bwd_dkdv_tc_kernel<<<dim3(p.H, p.B, ntile), kAtcThreads, kAtcKvSmemBytes, rt->stream>>>(
-        mqk, mmn, mdo, mdo_mn, p.T, p.D, p.H, scale, rmax, bstat, dqkv, rt->device_error());
+        mqk, mmn, mdo, mdo_mn, p.T, p.D, p.H, scale, qkv, dctx, rmax, bstat, dqkv, rt->device_error());
     HX_LAUNCHED(rt);
 }
 
