@@ -132,7 +132,7 @@ void launch_tc(hx_runtime* rt, int M, int N, int K, const float* A, long lda, co
     const CUtensorMap mw = map_w(split ? bs.hi : B);
     const CUtensorMap mw_lo = split ? map_w(bs.lo) : mw;
     const int pairs = tc_pairs<A_MN, B_MN, false, false, Epi>(rt->sm_count);
-    const TcGrid g = tc_grid(M, N, K, pairs, 64);
+    const TcGrid g = tc_grid(M, N, K, pairs, 2 * pairs);
     int* err = rt->device_error();
     float* ws = g.splits > 1 ? rt->workspace(sizeof(float) * (size_t)g.splits * M * N) : nullptr;
     // bulk tensor stores for the epilogue when its single output (or the

@@ -505,27 +505,42 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant_
     tc::cluster_sync();
 }
 
-// Work split for an M x N x K problem over `pairs` CTA pairs: with fewer
-// output tiles than pairs and a long K, split K so that tiles x splits fills
-// the pairs in a single wave (each split at least 256 deep).  `max_splits`
-// = 1 forbids splitting.
+// Work split for an M x N x K problem over `pairs` CTA pairs.  With fewer
+// output tiles than pairs and a long K (each split at least 256 deep), K is
+// split so as to minimise the busiest pair's work: rounds of units per pair
+// times k-blocks per unit, plus the split-K reduction's extra reads of
+// splits x M x N floats (about 1.8 M floats per k-block time of a pair).  A
+// larger split count is taken only when it saves more than 1%.
+// `max_splits` = 1 forbids splitting.
 inline TcGrid tc_grid(int M, int N, int K, int pairs, int max_splits) {
     TcGrid g{};
     g.M = M; g.N = N; g.K = K;
     g.tiles_m = (M + kTcBM - 1) / kTcBM;
     g.tiles_n = (N + kTcBN - 1) / kTcBN;
     const long tiles = (long)g.tiles_m * g.tiles_n;
+    auto chunk_for = [&](int splits) {
+        const int chunk = (K + splits - 1) / splits;
+        return std::max(kTcBK, ((chunk + kTcBK - 1) / kTcBK) * kTcBK);
+    };
     int splits = 1;
     if (max_splits > 1 && tiles < pairs && K >= 2 * 256) {
-        splits = (int)(pairs / tiles);
-        splits = std::max(1, std::min({splits, K / 256, max_splits}));
+        double best = 0.0;
+        const int smax = std::max(1, std::min(max_splits, K / 256));
+        for (int s = 1; s <= smax; ++s) {
+            const int chunk = chunk_for(s);
+            const long units = tiles * ((K + chunk - 1) / chunk);
+            const double rounds = double((units + pairs - 1) / pairs);
+            const double cost = rounds * (chunk / kTcBK) + (s > 1 ? double(s) * M * N / 1.8e6 : 0.0);
+            if (s == 1 || cost < 0.99 * best) {
+                best = cost;
+                splits = s;
+            }
+        }
     }
-    int chunk = (K + splits - 1) / splits;
-    chunk = std::max(kTcBK, ((chunk + kTcBK - 1) / kTcBK) * kTcBK);
-    splits = std::max(1, (K + chunk - 1) / chunk);
-    g.splits = splits;
+    const int chunk = chunk_for(splits);
+    g.splits = std::max(1, (K + chunk - 1) / chunk);
     g.k_chunk = chunk;
-    g.units = (int)(tiles * splits);
+    g.units = (int)(tiles * g.splits);
     return g;
 }
 
