@@ -14,7 +14,9 @@
 //   128-key blocks:
 //     A: S and dP into TMEM; sum_r = sum_j e, dot_r = sum_j e dP (double);
 //        D_r = dot_r / sum_r.
-//     B: S and dP again; P = e * (1 / sum_r), dS = P (dP - D_r); dS hi is
+//     B: the key blocks in reverse order, S and dP again except for the
+//        first, which is pass A's last block still in TMEM;
+//        P = e * (1 / sum_r), dS = P (dP - D_r); dS hi is
 //        written over S and dS lo over dP, then each 32-key chunk gives
 //        dQ_c = dS_c K_c (A from TMEM) into a fresh accumulator that every
 //        thread drains into FP32 registers with round-to-nearest adds.
@@ -203,14 +205,20 @@ attention_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap map_qk, const __g
             for (int t = 0; t < ntile; ++t) {
                 atc_wait(sm.abort, err, kAtcErrMma, &sm.a_ready, t & 1);
                 for (int pass = 0; pass < 2; ++pass) {
-                    for (int kb = 0; kb <= t; ++kb) {
+                    for (int i = 0; i <= t; ++i) {
+                        // pass B walks the key blocks backwards: its first
+                        // block is pass A's last, whose S and dP are still in
+                        // TMEM (pass A only reads them), so it is not recomputed
+                        const int kb = pass ? t - i : i;
                         if (v > 0) atc_wait(sm.abort, err, kAtcErrMma, &sm.sd_free, (v - 1) & 1);
                         if (dq_pending) atc_wait(sm.abort, err, kAtcErrMma, &sm.dq_done, (u - 1) & 1);
                         dq_pending = false;
                         tc::tc_fence_after();
-                        const uint32_t ko = uint32_t(kb) * kAtcTileFloats * 4;
-                        atc_mma_ts_kmajor(tmem + kDqColS, tmem + kDqColQ, kh + ko, kl + ko, idesc_s);
-                        atc_mma_ts_kmajor(tmem + kDqColDp, tmem + kDqColDo, vh + ko, vl + ko, idesc_s);
+                        if (pass == 0 || i > 0) {
+                            const uint32_t ko = uint32_t(kb) * kAtcTileFloats * 4;
+                            atc_mma_ts_kmajor(tmem + kDqColS, tmem + kDqColQ, kh + ko, kl + ko, idesc_s);
+                            atc_mma_ts_kmajor(tmem + kDqColDp, tmem + kDqColDo, vh + ko, vl + ko, idesc_s);
+                        }
                         tc::mma_commit(&sm.sd_ready);
                         ++v;
                         if (pass == 0) continue;
@@ -312,7 +320,8 @@ attention_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap map_qk, const __g
             float dq[8];
 #pragma unroll
             for (int i = 0; i < 8; ++i) dq[i] = 0.f;
-            for (int kb = 0; kb <= t; ++kb, ++v, ++u) {
+            for (int i = 0; i <= t; ++i, ++v, ++u) {
+                const int kb = t - i;  // the MMA issuer's pass-B order
                 atc_wait(sm.abort, err, kAtcErrSoftmax, &sm.sd_ready, v & 1);
                 tc::tc_fence_after();
                 const int vis = atc_chunk_vis(t, q, kb, grp, rows_valid);
