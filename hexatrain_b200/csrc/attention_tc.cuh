@@ -23,16 +23,21 @@
 //        e is split into hi (written back over S) and lo (a 6-slot ring of
 //        32-column TMEM chunks); each finished chunk is handed to the MMA
 //        issuer, which computes E_c V_c into a fresh 32-column accumulator
-//        (one of two, alternating) with A read from TMEM (3 MMAs M128 N32
-//        K8 per 8 keys) and frees the slot; the softmax threads drain every
-//        chunk's accumulator into FP32 registers with round-to-nearest adds.
+//        with A read from TMEM (3 MMAs M128 N32 K8 per 8 keys) and frees
+//        the slot.  Chunks 0 and 1 accumulate in two dedicated slots, chunk
+//        c >= 2 over the S columns of chunk c - 2 once that chunk's MMAs
+//        are done, so no MMA waits for the softmax threads to drain.  When
+//        the tile's MMAs have completed, every softmax thread adds the
+//        chunks' accumulators, in chunk order, into FP32 registers with
+//        round-to-nearest adds.
 //   ctx[r] = (E V)[r] / sum;  row max m and float(sum) are saved for the
 //        backward.
 // Accuracy: the MMA's FP32 accumulation truncates, so no accumulator runs
 // longer than one 32-deep chunk, and within a chunk the small hi*lo and
 // lo*hi terms are issued before hi*hi: only four full-magnitude truncations
 // per chunk.  ctx matches an FP64 evaluation to a few 1e-7 of the row max.
-// TMEM: S [0,256), chunk accumulators [256,320), ring [320,512).
+// TMEM: S [0,256) (later chunk accumulators), chunk 0/1 accumulators
+// [256,320), ring [320,512).
 // Every mbarrier wait is bounded; after the first timeout the CTA records an
 // error code, stops waiting (later waits return at once), keeps the same
 // control flow through its named barriers, drains its MMAs and loads and
@@ -59,7 +64,7 @@ struct AtcFwdSmem {
     float red_max[kAtcGroups][kAtcTile];
     double red_sum[kAtcGroups][kAtcTile];
     uint64_t ld[2], conv[2], pv_done[2], s_ready, ring_full[kAtcRing], ring_empty[kAtcRing];
-    uint64_t acc_full[2], acc_empty[2], drain;
+    uint64_t pv_chunk[2], drained, drain;
     uint32_t tmem_addr;
     int abort;
 };
@@ -82,6 +87,13 @@ __device__ __forceinline__ int atc_next_wave_block() {
     asm("mov.u32 %0, %%nsmid;" : "=r"(nsm));
     const long id = blockIdx.x + (long)gridDim.x * (blockIdx.y + (long)gridDim.y * blockIdx.z) + nsm;
     return id < (long)gridDim.x * gridDim.y * gridDim.z ? int(id) : -1;
+}
+
+// TMEM address of the E_c V_c accumulator of a tile's chunk c: chunks 0 and
+// 1 in the two dedicated 32-column slots, chunk c >= 2 over the S columns of
+// chunk c - 2, whose MMAs have completed by then.
+__device__ __forceinline__ uint32_t atc_fwd_acc(uint32_t base, int c) {
+    return base + (c < 2 ? kAtcColO + 32u * c : kAtcColS + 32u * (c - 2));
 }
 
 // Bounded wait; after the first failure anywhere in the CTA it returns
@@ -128,14 +140,14 @@ attention_fwd_tc_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid
             tc::mbar_init(&sm.ld[i], 1);
             tc::mbar_init(&sm.conv[i], kAtcSoftThreads);
             tc::mbar_init(&sm.pv_done[i], 1);
-            tc::mbar_init(&sm.acc_full[i], 1);
-            tc::mbar_init(&sm.acc_empty[i], kAtcSoftWarps);
+            tc::mbar_init(&sm.pv_chunk[i], 1);
         }
         tc::mbar_init(&sm.s_ready, 1);
         for (int i = 0; i < kAtcRing; ++i) {
             tc::mbar_init(&sm.ring_full[i], 4);  // the four warps that own a chunk's 128 lanes
             tc::mbar_init(&sm.ring_empty[i], 1);
         }
+        tc::mbar_init(&sm.drained, kAtcSoftWarps);
         tc::mbar_init(&sm.drain, 1);
         sm.abort = 0;
         tc::fence_mbar_init();
@@ -178,7 +190,12 @@ attention_fwd_tc_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid
             uint32_t gch = 0;  // chunks handed over so far (ring position)
             for (int t = 0; t < ntile; ++t) {
                 atc_wait(sm.abort, err, kAtcErrMma, &sm.conv[t], 0);
-                if (t > 0) atc_wait(sm.abort, err, kAtcErrMma, &sm.pv_done[t - 1], 0);  // S columns free again
+                if (t > 0) {
+                    // S columns free again: no MMA reads them and every
+                    // accumulator of the previous tile has been drained
+                    atc_wait(sm.abort, err, kAtcErrMma, &sm.pv_done[t - 1], 0);
+                    atc_wait(sm.abort, err, kAtcErrMma, &sm.drained, 0);
+                }
                 tc::tc_fence_after();
                 const uint32_t idesc_s = tc::idesc_tf32(kAtcTile, kAtcTile * (t + 1), false, false);
                 const uint32_t qo = uint32_t(t) * kAtcTileFloats * 4;
@@ -202,11 +219,12 @@ attention_fwd_tc_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid
                 const int nch = 4 * (t + 1);
                 for (int c = 0; c < nch; ++c, ++gch) {
                     const int slot = gch % kAtcRing;
-                    const int buf = gch & 1;
                     atc_wait(sm.abort, err, kAtcErrMma, &sm.ring_full[slot], (gch / kAtcRing) & 1);
-                    atc_wait(sm.abort, err, kAtcErrMma, &sm.acc_empty[buf], ((gch >> 1) & 1) ^ 1);
+                    // chunk gch - 2's MMAs have completed, so the S columns
+                    // that chunk c - 2 read are free for chunk c's result
+                    if (gch >= 2) atc_wait(sm.abort, err, kAtcErrMma, &sm.pv_chunk[gch & 1], ((gch >> 1) & 1) ^ 1);
                     tc::tc_fence_after();
-                    const uint32_t acc = tmem + kAtcColO + 32 * buf;
+                    const uint32_t acc = atc_fwd_acc(tmem, c);
                     // V rows are 128-byte K-rows: 8 keys = 1024 bytes
 #pragma unroll
                     for (int k = 0; k < 4; ++k) {
@@ -223,7 +241,7 @@ attention_fwd_tc_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid
                         tc::mma_tf32_ts(acc, tmem + kAtcColS + key, bh, idesc_pv, 1u);
                     }
                     tc::mma_commit(&sm.ring_empty[slot]);
-                    tc::mma_commit(&sm.acc_full[buf]);
+                    tc::mma_commit(&sm.pv_chunk[gch & 1]);
                 }
                 tc::mma_commit(&sm.pv_done[t]);
             }
@@ -285,25 +303,6 @@ attention_fwd_tc_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid
             float oacc[8];
 #pragma unroll
             for (int i = 0; i < 8; ++i) oacc[i] = 0.f;
-            int drained = 0;  // chunks of this tile added into oacc
-            // adds chunk d's accumulator (this thread's row, 8 columns) into
-            // oacc and releases it; every softmax warp drains every chunk
-            auto drain_chunk = [&](int d) {
-                const uint32_t g = gch + d;
-                const int buf = g & 1;
-                atc_wait(sm.abort, err, kAtcErrEpilogue, &sm.acc_full[buf], (g >> 1) & 1);
-                tc::tc_fence_after();
-                if (d <= diag) {  // otherwise this warp's rows of the chunk are zero
-                    uint32_t o[8];
-                    tc::tmem_ld_32x32b_x8(lane_base + kAtcColO + 32 * buf + 8 * grp, o);
-                    tc::tmem_ld_wait();
-#pragma unroll
-                    for (int i = 0; i < 8; ++i) oacc[i] = __fadd_rn(oacc[i], __uint_as_float(o[i]));
-                }
-                tc::tc_fence_before();
-                __syncwarp();
-                if (lane == 0) tc::mbar_arrive(&sm.acc_empty[buf]);
-            };
             // pass 2: e, its hi/lo split, the hand-over to the MMA issuer
             for (int c = grp; c < nch; c += kAtcGroups) {
                 const uint32_t g = gch + c;
@@ -339,10 +338,23 @@ attention_fwd_tc_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid
                 tc::tc_fence_before();
                 __syncwarp();
                 if (lane == 0) tc::mbar_arrive(&sm.ring_full[slot]);
-                // chunks handed over a round ago are done or nearly
-                for (; drained <= c - kAtcGroups; ++drained) drain_chunk(drained);
             }
-            for (; drained < nch; ++drained) drain_chunk(drained);
+            // every chunk's E_c V_c is in TMEM once the tile's MMAs have
+            // completed: add them, in chunk order, into FP32 registers
+            // (this thread's row, 8 columns) with round-to-nearest adds;
+            // chunks past this warp's diagonal are zero in its rows
+            atc_wait(sm.abort, err, kAtcErrEpilogue, &sm.pv_done[t], 0);
+            tc::tc_fence_after();
+            for (int c = 0; c <= diag && c < nch; ++c) {
+                uint32_t o[8];
+                tc::tmem_ld_32x32b_x8(atc_fwd_acc(lane_base, c) + 8 * grp, o);
+                tc::tmem_ld_wait();
+#pragma unroll
+                for (int i = 0; i < 8; ++i) oacc[i] = __fadd_rn(oacc[i], __uint_as_float(o[i]));
+            }
+            tc::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(&sm.drained);
             gch += nch;
             sm.red_sum[grp][rl] = sum;
             atc_soft_sync();

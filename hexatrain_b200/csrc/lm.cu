@@ -244,6 +244,8 @@ int grid_for(long work, int threads, int sms) {
     return (int)std::max<long>(1, std::min<long>((work + threads - 1) / threads, long(sms) * 32));
 }
 
+bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15) == 0; }
+
 struct DiagOut {
     bool on = false;
 };
@@ -300,7 +302,14 @@ void forward_backward(hx_runtime* rt, LmPlan& p, const float* W, float* G, float
     // embedding
     float* x = a.at<float>(p.la[0].x);
     ProfScope pemb(rt, kTagEmbed, 1.0 * M * D, 4.0 * 3.0 * M * D);
-    embed_kernel<<<grid_for(long(M) * D, tpb, rt->sm_count), tpb, 0, s>>>(M, T, D, in_ids, W + p.off_E, pos, x);
+    if (D % 4 == 0 && long(M) * D / 4 < (1L << 31) && aligned16(W + p.off_E) && aligned16(pos) && aligned16(x)) {
+        const int D4 = D / 4;
+        embed_vec_kernel<<<grid_for(long(M) * D4, tpb, rt->sm_count), tpb, 0, s>>>(
+            M, T, D4, in_ids, reinterpret_cast<const float4*>(W + p.off_E), reinterpret_cast<const float4*>(pos),
+            reinterpret_cast<float4*>(x));
+    } else {
+        embed_kernel<<<grid_for(long(M) * D, tpb, rt->sm_count), tpb, 0, s>>>(M, T, D, in_ids, W + p.off_E, pos, x);
+    }
     HX_LAUNCHED(rt);
         pemb.end();
     const int rows_per_block = 8;  // warps per block for row kernels
