@@ -16,15 +16,16 @@
 //                  four threads: warp w reads lanes 32(w%4).. and the
 //                  32-key chunks c = w/4, w/4 + 4, ...
 // Per tile t (N = 128(t+1) keys):
-//   S  = Q_t K[0:N]^T          12 MMAs M128 N(N) K8 into TMEM columns [0, N)
+//   S  = Q_t K[0:N]^T          into TMEM columns [0, N), as two column halves
+//        of 12 MMAs M128 N(N/2) K8 each, issued interleaved
 //   m  = max_j<=r S[r][j] * scale        (pass 1 over the chunks)
 //   e  = exp(S * scale - m) (0 where j > r), sum = sum_j e   (pass 2),
 //        as 2^(S * scale * log2 e - m * log2 e) with the hardware ex2
 //        e is split into hi (written back over S) and lo (a 6-slot ring of
 //        32-column TMEM chunks); each finished chunk is handed to the MMA
 //        issuer, which computes E_c V_c into a fresh 32-column accumulator
-//        with A read from TMEM (3 MMAs M128 N32 K8 per 8 keys) and frees
-//        the slot.  Chunks 0 and 1 accumulate in two dedicated slots, chunk
+//        with A read from TMEM (3 MMAs M128 N32 K8 per 8 keys), two chunks
+//        at a time with their MMAs interleaved, and frees the slots.  Chunks 0 and 1 accumulate in two dedicated slots, chunk
 //        c >= 2 over the S columns of chunk c - 2 once that chunk's MMAs
 //        are done, so no MMA waits for the softmax threads to drain.  When
 //        the tile's MMAs have completed, every softmax thread adds the
@@ -94,6 +95,36 @@ __device__ __forceinline__ int atc_next_wave_block() {
 // chunk c - 2, whose MMAs have completed by then.
 __device__ __forceinline__ uint32_t atc_fwd_acc(uint32_t base, int c) {
     return base + (c < 2 ? kAtcColO + 32u * c : kAtcColS + 32u * (c - 2));
+}
+
+// NC independent products D_j (M128 x N32) = A_j B_j over K = 32: A_j in TMEM
+// (hi at a_hi[j], lo at a_lo[j]), B_j the 32 K-rows of an MN-major tile
+// (hi/lo at b_hi[j]/b_lo[j], 128-byte rows, 8 K-rows = 1024 bytes).  Each
+// accumulator gets the 3xTF32 terms in the same order (hi*lo and lo*hi per
+// k-step, then hi*hi); the chains are interleaved MMA by MMA, so that one
+// accumulator's MMA does not wait for the previous MMA on the same
+// accumulator to finish before the tensor pipe has other work.
+template <int NC>
+__device__ __forceinline__ void atc_mma_chunks_mn(const uint32_t (&d)[NC], const uint32_t (&a_hi)[NC],
+                                                  const uint32_t (&a_lo)[NC], const uint32_t (&b_hi)[NC],
+                                                  const uint32_t (&b_lo)[NC]) {
+    constexpr uint32_t idesc = tc::idesc_tf32(kAtcTile, kAtcDH, false, true);
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+#pragma unroll
+        for (int j = 0; j < NC; ++j) {
+            const uint64_t bh = tc::smem_desc(b_hi[j] + k * 1024, 4096, 512, tc::kLayoutSw128Base32);
+            const uint64_t bl = tc::smem_desc(b_lo[j] + k * 1024, 4096, 512, tc::kLayoutSw128Base32);
+            tc::mma_tf32_ts(d[j], a_hi[j] + 8 * k, bl, idesc, k > 0 ? 1u : 0u);
+            tc::mma_tf32_ts(d[j], a_lo[j] + 8 * k, bh, idesc, 1u);
+        }
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+#pragma unroll
+        for (int j = 0; j < NC; ++j) {
+            const uint64_t bh = tc::smem_desc(b_hi[j] + k * 1024, 4096, 512, tc::kLayoutSw128Base32);
+            tc::mma_tf32_ts(d[j], a_hi[j] + 8 * k, bh, idesc, 1u);
+        }
 }
 
 // Bounded wait; after the first failure anywhere in the CTA it returns
@@ -186,7 +217,6 @@ attention_fwd_tc_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid
             const uint32_t qh = tc::smem_u32(sm.qh), ql = tc::smem_u32(sm.ql);
             const uint32_t kh = tc::smem_u32(sm.kh), kl = tc::smem_u32(sm.kl);
             const uint32_t vh = tc::smem_u32(sm.vh), vl = tc::smem_u32(sm.vl);
-            constexpr uint32_t idesc_pv = tc::idesc_tf32(kAtcTile, kAtcDH, false, true);
             uint32_t gch = 0;  // chunks handed over so far (ring position)
             for (int t = 0; t < ntile; ++t) {
                 atc_wait(sm.abort, err, kAtcErrMma, &sm.conv[t], 0);
@@ -197,51 +227,59 @@ attention_fwd_tc_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid
                     atc_wait(sm.abort, err, kAtcErrMma, &sm.drained, 0);
                 }
                 tc::tc_fence_after();
-                const uint32_t idesc_s = tc::idesc_tf32(kAtcTile, kAtcTile * (t + 1), false, false);
+                // the key columns in two halves of nh keys each: independent
+                // accumulators whose MMAs interleave (B rows are 128 bytes)
+                const uint32_t nh = kAtcTile * (t + 1) / 2;
+                const uint32_t idesc_s = tc::idesc_tf32(kAtcTile, nh, false, false);
                 const uint32_t qo = uint32_t(t) * kAtcTileFloats * 4;
                 // corrections (hi*lo, lo*hi) first, then hi*hi
 #pragma unroll
                 for (int k = 0; k < kAtcDH / 8; ++k) {
                     const uint64_t ah = tc::smem_desc(qh + qo + 32 * k, 16, 1024, tc::kLayoutSw128);
                     const uint64_t al = tc::smem_desc(ql + qo + 32 * k, 16, 1024, tc::kLayoutSw128);
-                    const uint64_t bh = tc::smem_desc(kh + 32 * k, 16, 1024, tc::kLayoutSw128);
-                    const uint64_t bl = tc::smem_desc(kl + 32 * k, 16, 1024, tc::kLayoutSw128);
-                    tc::mma_tf32(tmem + kAtcColS, ah, bl, idesc_s, k > 0 ? 1u : 0u);
-                    tc::mma_tf32(tmem + kAtcColS, al, bh, idesc_s, 1u);
+#pragma unroll
+                    for (uint32_t j = 0; j < 2; ++j) {
+                        const uint64_t bh = tc::smem_desc(kh + j * nh * 128 + 32 * k, 16, 1024, tc::kLayoutSw128);
+                        const uint64_t bl = tc::smem_desc(kl + j * nh * 128 + 32 * k, 16, 1024, tc::kLayoutSw128);
+                        tc::mma_tf32(tmem + kAtcColS + j * nh, ah, bl, idesc_s, k > 0 ? 1u : 0u);
+                        tc::mma_tf32(tmem + kAtcColS + j * nh, al, bh, idesc_s, 1u);
+                    }
                 }
 #pragma unroll
                 for (int k = 0; k < kAtcDH / 8; ++k) {
                     const uint64_t ah = tc::smem_desc(qh + qo + 32 * k, 16, 1024, tc::kLayoutSw128);
-                    const uint64_t bh = tc::smem_desc(kh + 32 * k, 16, 1024, tc::kLayoutSw128);
-                    tc::mma_tf32(tmem + kAtcColS, ah, bh, idesc_s, 1u);
+#pragma unroll
+                    for (uint32_t j = 0; j < 2; ++j) {
+                        const uint64_t bh = tc::smem_desc(kh + j * nh * 128 + 32 * k, 16, 1024, tc::kLayoutSw128);
+                        tc::mma_tf32(tmem + kAtcColS + j * nh, ah, bh, idesc_s, 1u);
+                    }
                 }
                 tc::mma_commit(&sm.s_ready);
                 const int nch = 4 * (t + 1);
-                for (int c = 0; c < nch; ++c, ++gch) {
-                    const int slot = gch % kAtcRing;
-                    atc_wait(sm.abort, err, kAtcErrMma, &sm.ring_full[slot], (gch / kAtcRing) & 1);
-                    // chunk gch - 2's MMAs have completed, so the S columns
-                    // that chunk c - 2 read are free for chunk c's result
-                    if (gch >= 2) atc_wait(sm.abort, err, kAtcErrMma, &sm.pv_chunk[gch & 1], ((gch >> 1) & 1) ^ 1);
+                // chunks in pairs: the two accumulators' MMAs interleave
+                for (int c = 0; c < nch; c += 2, gch += 2) {
+                    uint32_t d[2], ahi[2], alo[2], bhi[2], blo[2];
+#pragma unroll
+                    for (int j = 0; j < 2; ++j) {
+                        const uint32_t g = gch + j;
+                        const uint32_t slot = g % kAtcRing;
+                        atc_wait(sm.abort, err, kAtcErrMma, &sm.ring_full[slot], (g / kAtcRing) & 1);
+                        // chunk g - 2's MMAs have completed, so the S columns
+                        // that chunk c + j - 2 read are free for this result
+                        if (g >= 2) atc_wait(sm.abort, err, kAtcErrMma, &sm.pv_chunk[g & 1], ((g >> 1) & 1) ^ 1);
+                        d[j] = atc_fwd_acc(tmem, c + j);
+                        ahi[j] = tmem + kAtcColS + 32 * (c + j);
+                        alo[j] = tmem + kAtcColRing + 32 * slot;
+                        bhi[j] = vh + 32 * (c + j) * 128;  // V rows are 128-byte K-rows
+                        blo[j] = vl + 32 * (c + j) * 128;
+                    }
                     tc::tc_fence_after();
-                    const uint32_t acc = atc_fwd_acc(tmem, c);
-                    // V rows are 128-byte K-rows: 8 keys = 1024 bytes
+                    atc_mma_chunks_mn<2>(d, ahi, alo, bhi, blo);
 #pragma unroll
-                    for (int k = 0; k < 4; ++k) {
-                        const uint32_t key = 32 * c + 8 * k;
-                        const uint64_t bh = tc::smem_desc(vh + key * 128, 4096, 512, tc::kLayoutSw128Base32);
-                        const uint64_t bl = tc::smem_desc(vl + key * 128, 4096, 512, tc::kLayoutSw128Base32);
-                        tc::mma_tf32_ts(acc, tmem + kAtcColS + key, bl, idesc_pv, k > 0 ? 1u : 0u);
-                        tc::mma_tf32_ts(acc, tmem + kAtcColRing + 32 * slot + 8 * k, bh, idesc_pv, 1u);
+                    for (int j = 0; j < 2; ++j) {
+                        tc::mma_commit(&sm.ring_empty[(gch + j) % kAtcRing]);
+                        tc::mma_commit(&sm.pv_chunk[(gch + j) & 1]);
                     }
-#pragma unroll
-                    for (int k = 0; k < 4; ++k) {
-                        const uint32_t key = 32 * c + 8 * k;
-                        const uint64_t bh = tc::smem_desc(vh + key * 128, 4096, 512, tc::kLayoutSw128Base32);
-                        tc::mma_tf32_ts(acc, tmem + kAtcColS + key, bh, idesc_pv, 1u);
-                    }
-                    tc::mma_commit(&sm.ring_empty[slot]);
-                    tc::mma_commit(&sm.pv_chunk[gch & 1]);
                 }
                 tc::mma_commit(&sm.pv_done[t]);
             }

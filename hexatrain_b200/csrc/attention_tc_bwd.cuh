@@ -85,42 +85,29 @@ __device__ __forceinline__ void atc_st_split8(uint32_t hi_addr, uint32_t lo_addr
                  : "memory");
 }
 
-// Issues D = A B^T over K = 32 in the forward's order, A hi/lo in TMEM
-// (columns a_col .. +31 hi, a_col + 32 .. lo), B hi/lo K-major in shared
-// memory (b_hi/b_lo: the block's first row).
-__device__ __forceinline__ void atc_mma_ts_kmajor(uint32_t d, uint32_t a_col, uint32_t b_hi, uint32_t b_lo,
-                                                  uint32_t idesc) {
+// Issues D_j = A_j B_j^T over K = 32 for two independent products j = 0, 1
+// in the forward's term order, their MMAs interleaved: A_j hi/lo in TMEM
+// (columns a_col[j] .. +31 hi, a_col[j] + 32 .. lo), B_j hi/lo K-major in
+// shared memory (b_hi/b_lo: the block's first row).
+__device__ __forceinline__ void atc_mma_ts_kmajor2(const uint32_t (&d)[2], const uint32_t (&a_col)[2],
+                                                   const uint32_t (&b_hi)[2], const uint32_t (&b_lo)[2],
+                                                   uint32_t idesc) {
 #pragma unroll
-    for (int k = 0; k < kAtcDH / 8; ++k) {
-        const uint64_t bh = tc::smem_desc(b_hi + 32 * k, 16, 1024, tc::kLayoutSw128);
-        const uint64_t bl = tc::smem_desc(b_lo + 32 * k, 16, 1024, tc::kLayoutSw128);
-        tc::mma_tf32_ts(d, a_col + 8 * k, bl, idesc, k > 0 ? 1u : 0u);
-        tc::mma_tf32_ts(d, a_col + 32 + 8 * k, bh, idesc, 1u);
-    }
+    for (int k = 0; k < kAtcDH / 8; ++k)
 #pragma unroll
-    for (int k = 0; k < kAtcDH / 8; ++k) {
-        const uint64_t bh = tc::smem_desc(b_hi + 32 * k, 16, 1024, tc::kLayoutSw128);
-        tc::mma_tf32_ts(d, a_col + 8 * k, bh, idesc, 1u);
-    }
-}
-
-// D (M128 x N32) = A (TMEM, hi at a_hi, lo at a_lo, 32 K columns) times the
-// 32 K-rows of an MN-major B tile (hi/lo at b_hi/b_lo); corrections first.
-__device__ __forceinline__ void atc_mma_chunk_mn(uint32_t d, uint32_t a_hi, uint32_t a_lo, uint32_t b_hi,
-                                                 uint32_t b_lo) {
-    constexpr uint32_t idesc = tc::idesc_tf32(kAtcTile, kAtcDH, false, true);
+        for (int j = 0; j < 2; ++j) {
+            const uint64_t bh = tc::smem_desc(b_hi[j] + 32 * k, 16, 1024, tc::kLayoutSw128);
+            const uint64_t bl = tc::smem_desc(b_lo[j] + 32 * k, 16, 1024, tc::kLayoutSw128);
+            tc::mma_tf32_ts(d[j], a_col[j] + 8 * k, bl, idesc, k > 0 ? 1u : 0u);
+            tc::mma_tf32_ts(d[j], a_col[j] + 32 + 8 * k, bh, idesc, 1u);
+        }
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-        const uint64_t bh = tc::smem_desc(b_hi + k * 1024, 4096, 512, tc::kLayoutSw128Base32);
-        const uint64_t bl = tc::smem_desc(b_lo + k * 1024, 4096, 512, tc::kLayoutSw128Base32);
-        tc::mma_tf32_ts(d, a_hi + 8 * k, bl, idesc, k > 0 ? 1u : 0u);
-        tc::mma_tf32_ts(d, a_lo + 8 * k, bh, idesc, 1u);
-    }
+    for (int k = 0; k < kAtcDH / 8; ++k)
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-        const uint64_t bh = tc::smem_desc(b_hi + k * 1024, 4096, 512, tc::kLayoutSw128Base32);
-        tc::mma_tf32_ts(d, a_hi + 8 * k, bh, idesc, 1u);
-    }
+        for (int j = 0; j < 2; ++j) {
+            const uint64_t bh = tc::smem_desc(b_hi[j] + 32 * k, 16, 1024, tc::kLayoutSw128);
+            tc::mma_tf32_ts(d[j], a_col[j] + 8 * k, bh, idesc, 1u);
+        }
 }
 
 // Visibility of a 32-key chunk (keys 128 kb + 32 c ..) to the 32 query rows
@@ -216,21 +203,31 @@ attention_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap map_qk, const __g
                         tc::tc_fence_after();
                         if (pass == 0 || i > 0) {
                             const uint32_t ko = uint32_t(kb) * kAtcTileFloats * 4;
-                            atc_mma_ts_kmajor(tmem + kDqColS, tmem + kDqColQ, kh + ko, kl + ko, idesc_s);
-                            atc_mma_ts_kmajor(tmem + kDqColDp, tmem + kDqColDo, vh + ko, vl + ko, idesc_s);
+                            const uint32_t d[2] = {tmem + kDqColS, tmem + kDqColDp};
+                            const uint32_t a[2] = {tmem + kDqColQ, tmem + kDqColDo};
+                            const uint32_t bh[2] = {kh + ko, vh + ko}, bl[2] = {kl + ko, vl + ko};
+                            atc_mma_ts_kmajor2(d, a, bh, bl, idesc_s);
                         }
                         tc::mma_commit(&sm.sd_ready);
                         ++v;
                         if (pass == 0) continue;
+                        // the four chunks' dQ products, their MMAs interleaved
+                        uint32_t d[4], ahi[4], alo[4], bhi[4], blo[4];
+#pragma unroll
                         for (int c = 0; c < 4; ++c) {
                             atc_wait(sm.abort, err, kAtcErrMma, &sm.ds_full[c], u & 1);
                             atc_wait(sm.abort, err, kAtcErrMma, &sm.acc_empty[c], (u & 1) ^ 1);
-                            tc::tc_fence_after();
                             const uint32_t row = uint32_t(kAtcTile * kb + 32 * c) * 128;
-                            atc_mma_chunk_mn(tmem + kDqColAcc + 32 * c, tmem + kDqColS + 32 * c, tmem + kDqColDp + 32 * c,
-                                             kmh + row, kml + row);
-                            tc::mma_commit(&sm.acc_full[c]);
+                            d[c] = tmem + kDqColAcc + 32 * c;
+                            ahi[c] = tmem + kDqColS + 32 * c;
+                            alo[c] = tmem + kDqColDp + 32 * c;
+                            bhi[c] = kmh + row;
+                            blo[c] = kml + row;
                         }
+                        tc::tc_fence_after();
+                        atc_mma_chunks_mn<4>(d, ahi, alo, bhi, blo);
+#pragma unroll
+                        for (int c = 0; c < 4; ++c) tc::mma_commit(&sm.acc_full[c]);
                         tc::mma_commit(&sm.dq_done);
                         ++u;
                         dq_pending = true;
@@ -512,14 +509,15 @@ attention_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap map_qk, const _
                 if (i == 0) atc_wait(sm.abort, err, kAtcErrMma, &sm.conv_kv, 0);
                 atc_wait(sm.abort, err, kAtcErrMma, &sm.conv_q, i & 1);
                 tc::tc_fence_after();
-                // S^T = K Q^T, dP^T = V dO^T (A from shared memory, same term order)
+                // S^T = K Q^T, dP^T = V dO^T (A from shared memory, same term
+                // order), the two products' MMAs interleaved
 #pragma unroll
-                for (int pass = 0; pass < 2; ++pass) {
-                    const uint32_t d = tmem + (pass ? kKvColDp : kKvColS);
-                    const uint32_t ah = pass ? vh : kh, al = pass ? vl : kl;
-                    const uint32_t bh = pass ? oh : qh, bl = pass ? ol : ql;
+                for (int k = 0; k < kAtcDH / 8; ++k)
 #pragma unroll
-                    for (int k = 0; k < kAtcDH / 8; ++k) {
+                    for (int pass = 0; pass < 2; ++pass) {
+                        const uint32_t d = tmem + (pass ? kKvColDp : kKvColS);
+                        const uint32_t ah = pass ? vh : kh, al = pass ? vl : kl;
+                        const uint32_t bh = pass ? oh : qh, bl = pass ? ol : ql;
                         const uint64_t dah = tc::smem_desc(ah + 32 * k, 16, 1024, tc::kLayoutSw128);
                         const uint64_t dal = tc::smem_desc(al + 32 * k, 16, 1024, tc::kLayoutSw128);
                         const uint64_t dbh = tc::smem_desc(bh + 32 * k, 16, 1024, tc::kLayoutSw128);
@@ -528,25 +526,47 @@ attention_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap map_qk, const _
                         tc::mma_tf32(d, dah, dbl, idesc_s, 1u);
                     }
 #pragma unroll
-                    for (int k = 0; k < kAtcDH / 8; ++k) {
+                for (int k = 0; k < kAtcDH / 8; ++k)
+#pragma unroll
+                    for (int pass = 0; pass < 2; ++pass) {
+                        const uint32_t d = tmem + (pass ? kKvColDp : kKvColS);
+                        const uint32_t ah = pass ? vh : kh, bh = pass ? oh : qh;
                         const uint64_t dah = tc::smem_desc(ah + 32 * k, 16, 1024, tc::kLayoutSw128);
                         const uint64_t dbh = tc::smem_desc(bh + 32 * k, 16, 1024, tc::kLayoutSw128);
                         tc::mma_tf32(d, dah, dbh, idesc_s, 1u);
                     }
-                }
                 tc::mma_commit(&sm.sd_ready);
                 // per 32-query chunk: dV_c = P^T_c dO_c, dK_c = dS^T_c Q_c
-                for (int c = 0; c < 4; ++c, ++g) {
-                    const int slot = g & 1;
-                    atc_wait(sm.abort, err, kAtcErrMma, &sm.ring_full[slot], (g >> 1) & 1);
-                    atc_wait(sm.abort, err, kAtcErrMma, &sm.acc_empty[slot], ((g >> 1) & 1) ^ 1);
+                // two chunks at a time (g is even here, so chunk c + j uses
+                // ring and accumulator slot j): four products whose MMAs
+                // interleave
+                for (int c = 0; c < 4; c += 2, g += 2) {
+                    uint32_t d[4], ahi[4], alo[4], bhi[4], blo[4];
+#pragma unroll
+                    for (int j = 0; j < 2; ++j) {
+                        const uint32_t gj = g + j;
+                        atc_wait(sm.abort, err, kAtcErrMma, &sm.ring_full[j], (gj >> 1) & 1);
+                        atc_wait(sm.abort, err, kAtcErrMma, &sm.acc_empty[j], ((gj >> 1) & 1) ^ 1);
+                        const uint32_t acc = tmem + kKvColAcc + 64 * j, ring = tmem + kKvColRing + 64 * j;
+                        const uint32_t row = uint32_t(32 * (c + j)) * 128;
+                        d[2 * j] = acc;
+                        ahi[2 * j] = tmem + kKvColS + 32 * (c + j);
+                        alo[2 * j] = ring;
+                        bhi[2 * j] = omh + row;
+                        blo[2 * j] = oml + row;
+                        d[2 * j + 1] = acc + 32;
+                        ahi[2 * j + 1] = tmem + kKvColDp + 32 * (c + j);
+                        alo[2 * j + 1] = ring + 32;
+                        bhi[2 * j + 1] = qmh + row;
+                        blo[2 * j + 1] = qml + row;
+                    }
                     tc::tc_fence_after();
-                    const uint32_t acc = tmem + kKvColAcc + 64 * slot, ring = tmem + kKvColRing + 64 * slot;
-                    const uint32_t row = uint32_t(32 * c) * 128;
-                    atc_mma_chunk_mn(acc, tmem + kKvColS + 32 * c, ring, omh + row, oml + row);
-                    atc_mma_chunk_mn(acc + 32, tmem + kKvColDp + 32 * c, ring + 32, qmh + row, qml + row);
-                    tc::mma_commit(&sm.ring_empty[slot]);
-                    tc::mma_commit(&sm.acc_full[slot]);
+                    atc_mma_chunks_mn<4>(d, ahi, alo, bhi, blo);
+#pragma unroll
+                    for (int j = 0; j < 2; ++j) {
+                        tc::mma_commit(&sm.ring_empty[j]);
+                        tc::mma_commit(&sm.acc_full[j]);
+                    }
                 }
                 tc::mma_commit(&sm.blk_done);
             }
