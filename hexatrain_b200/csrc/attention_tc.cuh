@@ -25,7 +25,8 @@
 //        32-column TMEM chunks); each finished chunk is handed to the MMA
 //        issuer, which computes E_c V_c into a fresh 32-column accumulator
 //        with A read from TMEM (3 MMAs M128 N32 K8 per 8 keys), two chunks
-//        at a time with their MMAs interleaved, and frees the slots.  Chunks 0 and 1 accumulate in two dedicated slots, chunk
+//        at a time with their MMAs interleaved, and frees the slots.
+//        Chunks 0 and 1 accumulate in two dedicated slots, chunk
 //        c >= 2 over the S columns of chunk c - 2 once that chunk's MMAs
 //        are done, so no MMA waits for the softmax threads to drain.  When
 //        the tile's MMAs have completed, every softmax thread adds the
@@ -101,30 +102,33 @@ __device__ __forceinline__ uint32_t atc_fwd_acc(uint32_t base, int c) {
 // (hi at a_hi[j], lo at a_lo[j]), B_j the 32 K-rows of an MN-major tile
 // (hi/lo at b_hi[j]/b_lo[j], 128-byte rows, 8 K-rows = 1024 bytes).  Each
 // accumulator gets the 3xTF32 terms in the same order (hi*lo and lo*hi per
-// k-step, then hi*hi); the chains are interleaved MMA by MMA, so that one
-// accumulator's MMA does not wait for the previous MMA on the same
-// accumulator to finish before the tensor pipe has other work.
+// k-step, then hi*hi); the chains are interleaved MMA by MMA.
 template <int NC>
 __device__ __forceinline__ void atc_mma_chunks_mn(const uint32_t (&d)[NC], const uint32_t (&a_hi)[NC],
                                                   const uint32_t (&a_lo)[NC], const uint32_t (&b_hi)[NC],
                                                   const uint32_t (&b_lo)[NC]) {
     constexpr uint32_t idesc = tc::idesc_tf32(kAtcTile, kAtcDH, false, true);
+    // descriptors built once; k-step k adds k * 1024 bytes to the start
+    // address field (address >> 4; shared addresses stay below 2^18, so the
+    // 14-bit field never carries), which keeps the issuing thread's work per
+    // MMA to a few instructions
+    uint64_t bh[NC], bl[NC];
+#pragma unroll
+    for (int j = 0; j < NC; ++j) {
+        bh[j] = tc::smem_desc(b_hi[j], 4096, 512, tc::kLayoutSw128Base32);
+        bl[j] = tc::smem_desc(b_lo[j], 4096, 512, tc::kLayoutSw128Base32);
+    }
 #pragma unroll
     for (int k = 0; k < 4; ++k)
 #pragma unroll
         for (int j = 0; j < NC; ++j) {
-            const uint64_t bh = tc::smem_desc(b_hi[j] + k * 1024, 4096, 512, tc::kLayoutSw128Base32);
-            const uint64_t bl = tc::smem_desc(b_lo[j] + k * 1024, 4096, 512, tc::kLayoutSw128Base32);
-            tc::mma_tf32_ts(d[j], a_hi[j] + 8 * k, bl, idesc, k > 0 ? 1u : 0u);
-            tc::mma_tf32_ts(d[j], a_lo[j] + 8 * k, bh, idesc, 1u);
+            tc::mma_tf32_ts(d[j], a_hi[j] + 8 * k, bl[j] + 64 * k, idesc, k > 0 ? 1u : 0u);
+            tc::mma_tf32_ts(d[j], a_lo[j] + 8 * k, bh[j] + 64 * k, idesc, 1u);
         }
 #pragma unroll
     for (int k = 0; k < 4; ++k)
 #pragma unroll
-        for (int j = 0; j < NC; ++j) {
-            const uint64_t bh = tc::smem_desc(b_hi[j] + k * 1024, 4096, 512, tc::kLayoutSw128Base32);
-            tc::mma_tf32_ts(d[j], a_hi[j] + 8 * k, bh, idesc, 1u);
-        }
+        for (int j = 0; j < NC; ++j) tc::mma_tf32_ts(d[j], a_hi[j] + 8 * k, bh[j] + 64 * k, idesc, 1u);
 }
 
 // Bounded wait; after the first failure anywhere in the CTA it returns
@@ -233,27 +237,28 @@ attention_fwd_tc_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid
                 const uint32_t idesc_s = tc::idesc_tf32(kAtcTile, nh, false, false);
                 const uint32_t qo = uint32_t(t) * kAtcTileFloats * 4;
                 // corrections (hi*lo, lo*hi) first, then hi*hi
+                // descriptors built once, k-step k at + 32 k bytes (+ 2 k in
+                // the start address field)
+                const uint64_t ah = tc::smem_desc(qh + qo, 16, 1024, tc::kLayoutSw128);
+                const uint64_t al = tc::smem_desc(ql + qo, 16, 1024, tc::kLayoutSw128);
+                uint64_t bh[2], bl[2];
 #pragma unroll
-                for (int k = 0; k < kAtcDH / 8; ++k) {
-                    const uint64_t ah = tc::smem_desc(qh + qo + 32 * k, 16, 1024, tc::kLayoutSw128);
-                    const uint64_t al = tc::smem_desc(ql + qo + 32 * k, 16, 1024, tc::kLayoutSw128);
-#pragma unroll
-                    for (uint32_t j = 0; j < 2; ++j) {
-                        const uint64_t bh = tc::smem_desc(kh + j * nh * 128 + 32 * k, 16, 1024, tc::kLayoutSw128);
-                        const uint64_t bl = tc::smem_desc(kl + j * nh * 128 + 32 * k, 16, 1024, tc::kLayoutSw128);
-                        tc::mma_tf32(tmem + kAtcColS + j * nh, ah, bl, idesc_s, k > 0 ? 1u : 0u);
-                        tc::mma_tf32(tmem + kAtcColS + j * nh, al, bh, idesc_s, 1u);
-                    }
+                for (uint32_t j = 0; j < 2; ++j) {
+                    bh[j] = tc::smem_desc(kh + j * nh * 128, 16, 1024, tc::kLayoutSw128);
+                    bl[j] = tc::smem_desc(kl + j * nh * 128, 16, 1024, tc::kLayoutSw128);
                 }
 #pragma unroll
-                for (int k = 0; k < kAtcDH / 8; ++k) {
-                    const uint64_t ah = tc::smem_desc(qh + qo + 32 * k, 16, 1024, tc::kLayoutSw128);
+                for (int k = 0; k < kAtcDH / 8; ++k)
 #pragma unroll
                     for (uint32_t j = 0; j < 2; ++j) {
-                        const uint64_t bh = tc::smem_desc(kh + j * nh * 128 + 32 * k, 16, 1024, tc::kLayoutSw128);
-                        tc::mma_tf32(tmem + kAtcColS + j * nh, ah, bh, idesc_s, 1u);
+                        tc::mma_tf32(tmem + kAtcColS + j * nh, ah + 2 * k, bl[j] + 2 * k, idesc_s, k > 0 ? 1u : 0u);
+                        tc::mma_tf32(tmem + kAtcColS + j * nh, al + 2 * k, bh[j] + 2 * k, idesc_s, 1u);
                     }
-                }
+#pragma unroll
+                for (int k = 0; k < kAtcDH / 8; ++k)
+#pragma unroll
+                    for (uint32_t j = 0; j < 2; ++j)
+                        tc::mma_tf32(tmem + kAtcColS + j * nh, ah + 2 * k, bh[j] + 2 * k, idesc_s, 1u);
                 tc::mma_commit(&sm.s_ready);
                 const int nch = 4 * (t + 1);
                 // chunks in pairs: the two accumulators' MMAs interleave

@@ -92,22 +92,25 @@ __device__ __forceinline__ void atc_st_split8(uint32_t hi_addr, uint32_t lo_addr
 __device__ __forceinline__ void atc_mma_ts_kmajor2(const uint32_t (&d)[2], const uint32_t (&a_col)[2],
                                                    const uint32_t (&b_hi)[2], const uint32_t (&b_lo)[2],
                                                    uint32_t idesc) {
+    // descriptors built once, k-step k at + 32 k bytes (+ 2 k in the start
+    // address field)
+    uint64_t bh[2], bl[2];
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+        bh[j] = tc::smem_desc(b_hi[j], 16, 1024, tc::kLayoutSw128);
+        bl[j] = tc::smem_desc(b_lo[j], 16, 1024, tc::kLayoutSw128);
+    }
 #pragma unroll
     for (int k = 0; k < kAtcDH / 8; ++k)
 #pragma unroll
         for (int j = 0; j < 2; ++j) {
-            const uint64_t bh = tc::smem_desc(b_hi[j] + 32 * k, 16, 1024, tc::kLayoutSw128);
-            const uint64_t bl = tc::smem_desc(b_lo[j] + 32 * k, 16, 1024, tc::kLayoutSw128);
-            tc::mma_tf32_ts(d[j], a_col[j] + 8 * k, bl, idesc, k > 0 ? 1u : 0u);
-            tc::mma_tf32_ts(d[j], a_col[j] + 32 + 8 * k, bh, idesc, 1u);
+            tc::mma_tf32_ts(d[j], a_col[j] + 8 * k, bl[j] + 2 * k, idesc, k > 0 ? 1u : 0u);
+            tc::mma_tf32_ts(d[j], a_col[j] + 32 + 8 * k, bh[j] + 2 * k, idesc, 1u);
         }
 #pragma unroll
     for (int k = 0; k < kAtcDH / 8; ++k)
 #pragma unroll
-        for (int j = 0; j < 2; ++j) {
-            const uint64_t bh = tc::smem_desc(b_hi[j] + 32 * k, 16, 1024, tc::kLayoutSw128);
-            tc::mma_tf32_ts(d[j], a_col[j] + 8 * k, bh, idesc, 1u);
-        }
+        for (int j = 0; j < 2; ++j) tc::mma_tf32_ts(d[j], a_col[j] + 8 * k, bh[j] + 2 * k, idesc, 1u);
 }
 
 // Visibility of a 32-key chunk (keys 128 kb + 32 c ..) to the 32 query rows
@@ -511,30 +514,29 @@ attention_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap map_qk, const _
                 tc::tc_fence_after();
                 // S^T = K Q^T, dP^T = V dO^T (A from shared memory, same term
                 // order), the two products' MMAs interleaved
+                // (descriptors built once, k-step k at + 2 k in the start
+                // address field)
+                const uint64_t dah[2] = {tc::smem_desc(kh, 16, 1024, tc::kLayoutSw128),
+                                         tc::smem_desc(vh, 16, 1024, tc::kLayoutSw128)};
+                const uint64_t dal[2] = {tc::smem_desc(kl, 16, 1024, tc::kLayoutSw128),
+                                         tc::smem_desc(vl, 16, 1024, tc::kLayoutSw128)};
+                const uint64_t dbh[2] = {tc::smem_desc(qh, 16, 1024, tc::kLayoutSw128),
+                                         tc::smem_desc(oh, 16, 1024, tc::kLayoutSw128)};
+                const uint64_t dbl[2] = {tc::smem_desc(ql, 16, 1024, tc::kLayoutSw128),
+                                         tc::smem_desc(ol, 16, 1024, tc::kLayoutSw128)};
 #pragma unroll
                 for (int k = 0; k < kAtcDH / 8; ++k)
 #pragma unroll
                     for (int pass = 0; pass < 2; ++pass) {
                         const uint32_t d = tmem + (pass ? kKvColDp : kKvColS);
-                        const uint32_t ah = pass ? vh : kh, al = pass ? vl : kl;
-                        const uint32_t bh = pass ? oh : qh, bl = pass ? ol : ql;
-                        const uint64_t dah = tc::smem_desc(ah + 32 * k, 16, 1024, tc::kLayoutSw128);
-                        const uint64_t dal = tc::smem_desc(al + 32 * k, 16, 1024, tc::kLayoutSw128);
-                        const uint64_t dbh = tc::smem_desc(bh + 32 * k, 16, 1024, tc::kLayoutSw128);
-                        const uint64_t dbl = tc::smem_desc(bl + 32 * k, 16, 1024, tc::kLayoutSw128);
-                        tc::mma_tf32(d, dal, dbh, idesc_s, k > 0 ? 1u : 0u);
-                        tc::mma_tf32(d, dah, dbl, idesc_s, 1u);
+                        tc::mma_tf32(d, dal[pass] + 2 * k, dbh[pass] + 2 * k, idesc_s, k > 0 ? 1u : 0u);
+                        tc::mma_tf32(d, dah[pass] + 2 * k, dbl[pass] + 2 * k, idesc_s, 1u);
                     }
 #pragma unroll
                 for (int k = 0; k < kAtcDH / 8; ++k)
 #pragma unroll
-                    for (int pass = 0; pass < 2; ++pass) {
-                        const uint32_t d = tmem + (pass ? kKvColDp : kKvColS);
-                        const uint32_t ah = pass ? vh : kh, bh = pass ? oh : qh;
-                        const uint64_t dah = tc::smem_desc(ah + 32 * k, 16, 1024, tc::kLayoutSw128);
-                        const uint64_t dbh = tc::smem_desc(bh + 32 * k, 16, 1024, tc::kLayoutSw128);
-                        tc::mma_tf32(d, dah, dbh, idesc_s, 1u);
-                    }
+                    for (int pass = 0; pass < 2; ++pass)
+                        tc::mma_tf32(tmem + (pass ? kKvColDp : kKvColS), dah[pass] + 2 * k, dbh[pass] + 2 * k, idesc_s, 1u);
                 tc::mma_commit(&sm.sd_ready);
                 // per 32-query chunk: dV_c = P^T_c dO_c, dK_c = dS^T_c Q_c
                 // two chunks at a time (g is even here, so chunk c + j uses
