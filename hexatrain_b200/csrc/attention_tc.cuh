@@ -21,14 +21,15 @@
 //   m  = max_j<=r S[r][j] * scale        (pass 1 over the chunks)
 //   e  = exp(S * scale - m) (0 where j > r), sum = sum_j e   (pass 2),
 //        as 2^(S * scale * log2 e - m * log2 e) with the hardware ex2
-//        e is split into hi (written back over S) and lo (a 6-slot ring of
+//        e is split into hi (written back over S) and lo (a 4-slot ring of
 //        32-column TMEM chunks); each finished chunk is handed to the MMA
 //        issuer, which computes E_c V_c into a fresh 32-column accumulator
 //        with A read from TMEM (3 MMAs M128 N32 K8 per 8 keys), two chunks
 //        at a time with their MMAs interleaved, and frees the slots.
-//        Chunks 0 and 1 accumulate in two dedicated slots, chunk
-//        c >= 2 over the S columns of chunk c - 2 once that chunk's MMAs
-//        are done, so no MMA waits for the softmax threads to drain.  When
+//        Chunks 0-3 accumulate in four dedicated slots, chunk c >= 4 over
+//        the S columns of chunk c - 4 once that chunk's MMAs are done, so no
+//        MMA waits for the softmax threads to drain and the issuer never
+//        waits for the pair just issued.  When
 //        the tile's MMAs have completed, every softmax thread adds the
 //        chunks' accumulators, in chunk order, into FP32 registers with
 //        round-to-nearest adds.
@@ -38,8 +39,8 @@
 // longer than one 32-deep chunk, and within a chunk the small hi*lo and
 // lo*hi terms are issued before hi*hi: only four full-magnitude truncations
 // per chunk.  ctx matches an FP64 evaluation to a few 1e-7 of the row max.
-// TMEM: S [0,256) (later chunk accumulators), chunk 0/1 accumulators
-// [256,320), ring [320,512).
+// TMEM: S [0,256) (later chunk accumulators), chunk 0-3 accumulators
+// [256,384), ring [384,512).
 // Every mbarrier wait is bounded; after the first timeout the CTA records an
 // error code, stops waiting (later waits return at once), keeps the same
 // control flow through its named barriers, drains its MMAs and loads and
@@ -54,8 +55,8 @@ constexpr int kAtcDH = 32, kAtcMaxT = 256, kAtcTile = 128;
 constexpr int kAtcSoftWarps = 16, kAtcGroups = 4;  // warps w, w+4, w+8, w+12 share lane quadrant w%4
 constexpr int kAtcSoftThreads = 32 * kAtcSoftWarps;
 constexpr int kAtcThreads = kAtcSoftThreads + 32;
-constexpr int kAtcRing = 6;
-constexpr uint32_t kAtcCols = 512, kAtcColS = 0, kAtcColO = 256, kAtcColRing = 320;
+constexpr int kAtcRing = 4;
+constexpr uint32_t kAtcCols = 512, kAtcColS = 0, kAtcColO = 256, kAtcColRing = 384;
 constexpr int kAtcTileFloats = kAtcTile * kAtcDH;  // 128 rows x 32 fp32 = 16 KB
 constexpr float kAtcLog2e = 1.4426950408889634f;
 
@@ -66,7 +67,7 @@ struct AtcFwdSmem {
     float red_max[kAtcGroups][kAtcTile];
     double red_sum[kAtcGroups][kAtcTile];
     uint64_t ld[2], conv[2], pv_done[2], s_ready, ring_full[kAtcRing], ring_empty[kAtcRing];
-    uint64_t pv_chunk[2], drained, drain;
+    uint64_t pv_chunk[4], drained, drain;
     uint32_t tmem_addr;
     int abort;
 };
@@ -91,11 +92,11 @@ __device__ __forceinline__ int atc_next_wave_block() {
     return id < (long)gridDim.x * gridDim.y * gridDim.z ? int(id) : -1;
 }
 
-// TMEM address of the E_c V_c accumulator of a tile's chunk c: chunks 0 and
-// 1 in the two dedicated 32-column slots, chunk c >= 2 over the S columns of
-// chunk c - 2, whose MMAs have completed by then.
+// TMEM address of the E_c V_c accumulator of a tile's chunk c: chunks 0-3
+// in the four dedicated 32-column slots, chunk c >= 4 over the S columns of
+// chunk c - 4, whose MMAs have completed by then.
 __device__ __forceinline__ uint32_t atc_fwd_acc(uint32_t base, int c) {
-    return base + (c < 2 ? kAtcColO + 32u * c : kAtcColS + 32u * (c - 2));
+    return base + (c < 4 ? kAtcColO + 32u * c : kAtcColS + 32u * (c - 4));
 }
 
 // NC independent products D_j (M128 x N32) = A_j B_j over K = 32: A_j in TMEM
@@ -175,9 +176,9 @@ attention_fwd_tc_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid
             tc::mbar_init(&sm.ld[i], 1);
             tc::mbar_init(&sm.conv[i], kAtcSoftThreads);
             tc::mbar_init(&sm.pv_done[i], 1);
-            tc::mbar_init(&sm.pv_chunk[i], 1);
         }
         tc::mbar_init(&sm.s_ready, 1);
+        for (int i = 0; i < 4; ++i) tc::mbar_init(&sm.pv_chunk[i], 1);
         for (int i = 0; i < kAtcRing; ++i) {
             tc::mbar_init(&sm.ring_full[i], 4);  // the four warps that own a chunk's 128 lanes
             tc::mbar_init(&sm.ring_empty[i], 1);
@@ -269,9 +270,10 @@ attention_fwd_tc_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid
                         const uint32_t g = gch + j;
                         const uint32_t slot = g % kAtcRing;
                         atc_wait(sm.abort, err, kAtcErrMma, &sm.ring_full[slot], (g / kAtcRing) & 1);
-                        // chunk g - 2's MMAs have completed, so the S columns
-                        // that chunk c + j - 2 read are free for this result
-                        if (g >= 2) atc_wait(sm.abort, err, kAtcErrMma, &sm.pv_chunk[g & 1], ((g >> 1) & 1) ^ 1);
+                        // chunk g - 4's MMAs (two pairs back) have completed,
+                        // so the S columns that chunk c + j - 4 read are free
+                        // for this result while the previous pair still runs
+                        if (g >= 4) atc_wait(sm.abort, err, kAtcErrMma, &sm.pv_chunk[g & 3], ((g >> 2) & 1) ^ 1);
                         d[j] = atc_fwd_acc(tmem, c + j);
                         ahi[j] = tmem + kAtcColS + 32 * (c + j);
                         alo[j] = tmem + kAtcColRing + 32 * slot;
@@ -283,7 +285,7 @@ attention_fwd_tc_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid
 #pragma unroll
                     for (int j = 0; j < 2; ++j) {
                         tc::mma_commit(&sm.ring_empty[(gch + j) % kAtcRing]);
-                        tc::mma_commit(&sm.pv_chunk[(gch + j) & 1]);
+                        tc::mma_commit(&sm.pv_chunk[(gch + j) & 3]);
                     }
                 }
                 tc::mma_commit(&sm.pv_done[t]);

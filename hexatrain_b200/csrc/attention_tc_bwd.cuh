@@ -30,7 +30,9 @@
 //   operands of dK and dV) layouts.  P^T and dS^T are formed from the
 //   statistics the dQ kernel stored, hi written over S^T / dP^T, lo into a
 //   2-slot ring; per 32-query chunk, dV_c = P^T_c dO_c and dK_c = dS^T_c Q_c
-//   go into fresh accumulators drained like dQ.
+//   go into fresh accumulators (chunks 0 and 1 in two dedicated slots,
+//   chunk c >= 2 over chunk c - 2's S^T / dP^T columns), which every
+//   thread adds into FP32 registers once the block's MMAs have completed.
 // Thread layout in both: 16 warps of four groups (warp w: TMEM lane quadrant
 // w % 4, group w / 4 owns 32-column chunk w / 4 of each 128-column block;
 // each thread drains 8 of the 32 output columns) plus one warp whose lane 0
@@ -404,13 +406,20 @@ struct AtcKvSmem {
     float qmh[kAtcTileFloats], qml[kAtcTileFloats];      // Q, MN-major
     float omh[kAtcTileFloats], oml[kAtcTileFloats];      // dO, MN-major
     float negml[kAtcTile], inv[kAtcTile], dr[kAtcTile];  // per-query statistics of the block
-    uint64_t ld_kv, ld_q, conv_kv, conv_q, sd_ready, blk_done, drain;
-    uint64_t ring_full[2], ring_empty[2], acc_full[2], acc_empty[2];
+    uint64_t ld_kv, ld_q, conv_kv, conv_q, sd_ready, blk_done, drained, drain;
+    uint64_t ring_full[2], ring_empty[2], kv_chunk[2];
     uint32_t tmem_addr;
     int abort;
 };
 constexpr size_t kAtcKvSmemBytes = sizeof(AtcKvSmem) + 1024;
 static_assert(kAtcKvSmemBytes <= 232448, "attention dK/dV kernel shared memory exceeds the 227 KB per-CTA limit");
+
+// TMEM column of chunk c's dV (dk = false) or dK accumulator: chunks 0 and 1
+// in the two dedicated 64-column slots, chunk c >= 2 over the S^T (dV) or
+// dP^T (dK) columns of chunk c - 2, whose MMAs have completed by then.
+__device__ __forceinline__ uint32_t atc_kv_acc(int c, bool dk) {
+    return c < 2 ? kKvColAcc + 64u * c + (dk ? 32u : 0u) : (dk ? kKvColDp : kKvColS) + 32u * (c - 2);
+}
 
 // Visibility of a 32-query chunk (queries 128 qb + 32 c ..) to the 32 keys
 // 128 kb + 32 q .. of a warp: 2 all visible, 1 diagonal or ragged, 0 none.
@@ -443,12 +452,12 @@ attention_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap map_qk, const _
         tc::mbar_init(&sm.conv_q, kAtcSoftThreads);
         tc::mbar_init(&sm.sd_ready, 1);
         tc::mbar_init(&sm.blk_done, 1);
+        tc::mbar_init(&sm.drained, kAtcSoftWarps);
         tc::mbar_init(&sm.drain, 1);
         for (int i = 0; i < 2; ++i) {
             tc::mbar_init(&sm.ring_full[i], 4);
             tc::mbar_init(&sm.ring_empty[i], 1);
-            tc::mbar_init(&sm.acc_full[i], 1);
-            tc::mbar_init(&sm.acc_empty[i], kAtcSoftWarps);
+            tc::mbar_init(&sm.kv_chunk[i], 1);
         }
         sm.abort = 0;
         tc::fence_mbar_init();
@@ -511,6 +520,8 @@ attention_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap map_qk, const _
                 tc::tma_load_2d(sm.omh, &map_do_mn, &sm.ld_q, h * kAtcDH, yq);
                 if (i == 0) atc_wait(sm.abort, err, kAtcErrMma, &sm.conv_kv, 0);
                 atc_wait(sm.abort, err, kAtcErrMma, &sm.conv_q, i & 1);
+                // the previous block's accumulators, over S^T / dP^T, are read
+                if (i > 0) atc_wait(sm.abort, err, kAtcErrMma, &sm.drained, (i - 1) & 1);
                 tc::tc_fence_after();
                 // S^T = K Q^T, dP^T = V dO^T (A from shared memory, same term
                 // order), the two products' MMAs interleaved
@@ -539,36 +550,25 @@ attention_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap map_qk, const _
                         tc::mma_tf32(tmem + (pass ? kKvColDp : kKvColS), dah[pass] + 2 * k, dbh[pass] + 2 * k, idesc_s, 1u);
                 tc::mma_commit(&sm.sd_ready);
                 // per 32-query chunk: dV_c = P^T_c dO_c, dK_c = dS^T_c Q_c
-                // two chunks at a time (g is even here, so chunk c + j uses
-                // ring and accumulator slot j): four products whose MMAs
-                // interleave
-                for (int c = 0; c < 4; c += 2, g += 2) {
-                    uint32_t d[4], ahi[4], alo[4], bhi[4], blo[4];
-#pragma unroll
-                    for (int j = 0; j < 2; ++j) {
-                        const uint32_t gj = g + j;
-                        atc_wait(sm.abort, err, kAtcErrMma, &sm.ring_full[j], (gj >> 1) & 1);
-                        atc_wait(sm.abort, err, kAtcErrMma, &sm.acc_empty[j], ((gj >> 1) & 1) ^ 1);
-                        const uint32_t acc = tmem + kKvColAcc + 64 * j, ring = tmem + kKvColRing + 64 * j;
-                        const uint32_t row = uint32_t(32 * (c + j)) * 128;
-                        d[2 * j] = acc;
-                        ahi[2 * j] = tmem + kKvColS + 32 * (c + j);
-                        alo[2 * j] = ring;
-                        bhi[2 * j] = omh + row;
-                        blo[2 * j] = oml + row;
-                        d[2 * j + 1] = acc + 32;
-                        ahi[2 * j + 1] = tmem + kKvColDp + 32 * (c + j);
-                        alo[2 * j + 1] = ring + 32;
-                        bhi[2 * j + 1] = qmh + row;
-                        blo[2 * j + 1] = qml + row;
-                    }
+                // per chunk, dV_c and dK_c with their MMAs interleaved;
+                // chunk c's slot in the 2-slot lo ring is g & 1
+                for (int c = 0; c < 4; ++c, ++g) {
+                    const int slot = g & 1;
+                    atc_wait(sm.abort, err, kAtcErrMma, &sm.ring_full[slot], (g >> 1) & 1);
+                    // chunk g - 2's MMAs have completed, so the S^T / dP^T
+                    // columns that chunk c - 2 read are free for chunk c's
+                    // results while chunk c - 1's MMAs still run
+                    if (g >= 2) atc_wait(sm.abort, err, kAtcErrMma, &sm.kv_chunk[g & 1], ((g >> 1) & 1) ^ 1);
                     tc::tc_fence_after();
-                    atc_mma_chunks_mn<4>(d, ahi, alo, bhi, blo);
-#pragma unroll
-                    for (int j = 0; j < 2; ++j) {
-                        tc::mma_commit(&sm.ring_empty[j]);
-                        tc::mma_commit(&sm.acc_full[j]);
-                    }
+                    const uint32_t ring = tmem + kKvColRing + 64 * slot;
+                    const uint32_t row = uint32_t(32 * c) * 128;
+                    const uint32_t d[2] = {tmem + atc_kv_acc(c, false), tmem + atc_kv_acc(c, true)};
+                    const uint32_t ahi[2] = {tmem + kKvColS + 32 * c, tmem + kKvColDp + 32 * c};
+                    const uint32_t alo[2] = {ring, ring + 32};
+                    const uint32_t bhi[2] = {omh + row, qmh + row}, blo[2] = {oml + row, qml + row};
+                    atc_mma_chunks_mn<2>(d, ahi, alo, bhi, blo);
+                    tc::mma_commit(&sm.ring_empty[slot]);
+                    tc::mma_commit(&sm.kv_chunk[g & 1]);
                 }
                 tc::mma_commit(&sm.blk_done);
             }
@@ -658,16 +658,14 @@ attention_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap map_qk, const _
             tc::tc_fence_before();
             __syncwarp();
             if (lane == 0) tc::mbar_arrive(&sm.ring_full[slot]);
-            // drain the block's four chunks
+            // the block's four chunks, once its MMAs have completed
+            atc_wait(sm.abort, err, kAtcErrEpilogue, &sm.blk_done, i & 1);
+            tc::tc_fence_after();
             for (int c = 0; c < 4; ++c) {
-                const uint32_t gd = g + c;
-                const int buf = gd & 1;
-                atc_wait(sm.abort, err, kAtcErrEpilogue, &sm.acc_full[buf], (gd >> 1) & 1);
-                tc::tc_fence_after();
                 if (atc_kv_chunk_vis(kb, q, qb, c, true)) {
                     uint32_t a[8], k8[8];
-                    tc::tmem_ld_32x32b_x8(lane_base + kKvColAcc + 64 * buf + 8 * grp, a);
-                    tc::tmem_ld_32x32b_x8(lane_base + kKvColAcc + 64 * buf + 32 + 8 * grp, k8);
+                    tc::tmem_ld_32x32b_x8(lane_base + atc_kv_acc(c, false) + 8 * grp, a);
+                    tc::tmem_ld_32x32b_x8(lane_base + atc_kv_acc(c, true) + 8 * grp, k8);
                     tc::tmem_ld_wait();
 #pragma unroll
                     for (int x = 0; x < 8; ++x) {
@@ -675,10 +673,10 @@ attention_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap map_qk, const _
                         dk[x] = __fadd_rn(dk[x], __uint_as_float(k8[x]));
                     }
                 }
-                tc::tc_fence_before();
-                __syncwarp();
-                if (lane == 0) tc::mbar_arrive(&sm.acc_empty[buf]);
             }
+            tc::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(&sm.drained);
             g += 4;
             atc_soft_sync();  // statistics of this block no longer read
         }
