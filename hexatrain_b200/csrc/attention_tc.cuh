@@ -362,16 +362,27 @@ attention_fwd_tc_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid
                     if (c <= diag) {
                         tc::tmem_ld_32x32b_x16(lane_base + kAtcColS + col, eh);
                         tc::tmem_ld_wait();
-                        float p0 = 0.f, p1 = 0.f;
+                        // two scores per paired FP32 instruction; pp holds the
+                        // even- and odd-column partial sums
+                        float2 pp = make_float2(0.f, 0.f);
 #pragma unroll
-                        for (int i = 0; i < 16; ++i) {
-                            float e = tc::exp2_approx(fmaf(__uint_as_float(eh[i]), c1, negml));
-                            if (!full && int(col) + i > lim) e = 0.f;
-                            if (i & 1) p1 += e; else p0 += e;
-                            eh[i] = tc::tf32_rna_bits(e);
-                            el[i] = __float_as_uint(e - __uint_as_float(eh[i]));
+                        for (int i = 0; i < 16; i += 2) {
+                            const float2 t = tc::fma2_rn(make_float2(__uint_as_float(eh[i]), __uint_as_float(eh[i + 1])),
+                                                         make_float2(c1, c1), make_float2(negml, negml));
+                            float e0 = tc::exp2_approx(t.x), e1 = tc::exp2_approx(t.y);
+                            if (!full) {
+                                if (int(col) + i > lim) e0 = 0.f;
+                                if (int(col) + i + 1 > lim) e1 = 0.f;
+                            }
+                            pp = tc::add2_rn(pp, make_float2(e0, e1));
+                            eh[i] = tc::tf32_rna_bits(e0);
+                            eh[i + 1] = tc::tf32_rna_bits(e1);
+                            const float2 l = tc::sub2_rn(make_float2(e0, e1),
+                                                         make_float2(__uint_as_float(eh[i]), __uint_as_float(eh[i + 1])));
+                            el[i] = __float_as_uint(l.x);
+                            el[i + 1] = __float_as_uint(l.y);
                         }
-                        sum += double(p0) + double(p1);
+                        sum += double(pp.x) + double(pp.y);
                     } else {
 #pragma unroll
                         for (int i = 0; i < 16; ++i) { eh[i] = 0u; el[i] = 0u; }

@@ -631,17 +631,42 @@ attention_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap map_qk, const _
                     tc::tmem_ld_32x32b_x16(lane_base + kKvColDp + col, pv);
                     tc::tmem_ld_wait();
                     uint32_t plo[16], dlo[16];
+                    // two queries per paired FP32 instruction; the statistics
+                    // of four queries per 16-byte shared-memory load
 #pragma unroll
-                    for (int x = 0; x < 16; ++x) {
-                        const int rloc = int(col) + x;  // query q0 + rloc
-                        float e = tc::exp2_approx(fmaf(__uint_as_float(sv[x]), c1, sm.negml[rloc]));
-                        if (vis == 1 && (j > q0 + rloc || q0 + rloc >= T)) e = 0.f;
-                        const float p = __fmul_rn(e, sm.inv[rloc]);
-                        const float ds = __fmul_rn(p, __fsub_rn(__uint_as_float(pv[x]), sm.dr[rloc]));
-                        sv[x] = tc::tf32_rna_bits(p);
-                        plo[x] = __float_as_uint(p - __uint_as_float(sv[x]));
-                        pv[x] = tc::tf32_rna_bits(ds);
-                        dlo[x] = __float_as_uint(ds - __uint_as_float(pv[x]));
+                    for (int x = 0; x < 16; x += 4) {
+                        const float4 nm = *reinterpret_cast<const float4*>(&sm.negml[col + x]);
+                        const float4 iv = *reinterpret_cast<const float4*>(&sm.inv[col + x]);
+                        const float4 d4 = *reinterpret_cast<const float4*>(&sm.dr[col + x]);
+#pragma unroll
+                        for (int y = 0; y < 4; y += 2) {
+                            const int rloc = int(col) + x + y;  // queries q0 + rloc, + 1
+                            const float2 t = tc::fma2_rn(
+                                make_float2(__uint_as_float(sv[x + y]), __uint_as_float(sv[x + y + 1])),
+                                make_float2(c1, c1), y ? make_float2(nm.z, nm.w) : make_float2(nm.x, nm.y));
+                            float e0 = tc::exp2_approx(t.x), e1 = tc::exp2_approx(t.y);
+                            if (vis == 1) {
+                                if (j > q0 + rloc || q0 + rloc >= T) e0 = 0.f;
+                                if (j > q0 + rloc + 1 || q0 + rloc + 1 >= T) e1 = 0.f;
+                            }
+                            const float2 p = tc::mul2_rn(make_float2(e0, e1), y ? make_float2(iv.z, iv.w)
+                                                                                 : make_float2(iv.x, iv.y));
+                            const float2 ds = tc::mul2_rn(
+                                p, tc::sub2_rn(make_float2(__uint_as_float(pv[x + y]), __uint_as_float(pv[x + y + 1])),
+                                               y ? make_float2(d4.z, d4.w) : make_float2(d4.x, d4.y)));
+                            sv[x + y] = tc::tf32_rna_bits(p.x);
+                            sv[x + y + 1] = tc::tf32_rna_bits(p.y);
+                            pv[x + y] = tc::tf32_rna_bits(ds.x);
+                            pv[x + y + 1] = tc::tf32_rna_bits(ds.y);
+                            const float2 pl = tc::sub2_rn(p, make_float2(__uint_as_float(sv[x + y]),
+                                                                         __uint_as_float(sv[x + y + 1])));
+                            const float2 dl = tc::sub2_rn(ds, make_float2(__uint_as_float(pv[x + y]),
+                                                                          __uint_as_float(pv[x + y + 1])));
+                            plo[x + y] = __float_as_uint(pl.x);
+                            plo[x + y + 1] = __float_as_uint(pl.y);
+                            dlo[x + y] = __float_as_uint(dl.x);
+                            dlo[x + y + 1] = __float_as_uint(dl.y);
+                        }
                     }
                     tc::tmem_st_32x32b_x16(lane_base + kKvColRing + 64 * slot + 16 * half, plo);
                     tc::tmem_st_32x32b_x16(lane_base + kKvColRing + 64 * slot + 32 + 16 * half, dlo);
