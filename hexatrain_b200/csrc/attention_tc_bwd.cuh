@@ -250,6 +250,11 @@ attention_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap map_qk, const __g
         const int rl = 32 * q + lane;
         const float c1 = scale * kAtcLog2e;
         const int ld3 = 3 * D;
+        // this thread's Q and dO values of tile 0 (columns 8 grp .. +7),
+        // loaded before the split so that their latency overlaps it
+        float xq[8], xo[8];
+        atc_row8(qkv + ((long)y0 + rl) * ld3 + h * kAtcDH + 8 * grp, rl < T, xq);
+        atc_row8(dctx + ((long)y0 + rl) * D + h * kAtcDH + 8 * grp, rl < T, xo);
         // ---------------- hi/lo split of K, V, K_mn ----------------
         atc_wait(sm.abort, err, kAtcErrLoad, &sm.ld, 0);
         const int n4 = ntile * kAtcTileFloats / 4;
@@ -258,19 +263,24 @@ attention_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap map_qk, const __g
         atc_split(sm.kmh, sm.kml, n4, st, kAtcSoftThreads);
         tc::fence_proxy_async_smem();
         tc::mbar_arrive(&sm.conv);
+        atc_st_split8(lane_base + kDqColQ + 8 * grp, lane_base + kDqColQ + 32 + 8 * grp, xq);
+        atc_st_split8(lane_base + kDqColDo + 8 * grp, lane_base + kDqColDo + 32 + 8 * grp, xo);
         uint32_t v = 0, u = 0;
         for (int t = 0; t < ntile; ++t) {
             const int r = kAtcTile * t + rl;
             const bool valid = r < T;
             const bool rows_valid = kAtcTile * t + 32 * q + 31 < T;
             const long grow = (long)y0 + r;
-            // ---- Q and dO of this row, columns 8 grp .. +7, into TMEM
+            // ---- Q and dO of this row, columns 8 grp .. +7, into TMEM (tile
+            // 0's went in after the split; both loads before the stores)
             {
-                float x[8];
-                atc_row8(qkv + grow * ld3 + h * kAtcDH + 8 * grp, valid, x);
-                atc_st_split8(lane_base + kDqColQ + 8 * grp, lane_base + kDqColQ + 32 + 8 * grp, x);
-                atc_row8(dctx + grow * D + h * kAtcDH + 8 * grp, valid, x);
-                atc_st_split8(lane_base + kDqColDo + 8 * grp, lane_base + kDqColDo + 32 + 8 * grp, x);
+                if (t > 0) {
+                    float x[8], y[8];
+                    atc_row8(qkv + grow * ld3 + h * kAtcDH + 8 * grp, valid, x);
+                    atc_row8(dctx + grow * D + h * kAtcDH + 8 * grp, valid, y);
+                    atc_st_split8(lane_base + kDqColQ + 8 * grp, lane_base + kDqColQ + 32 + 8 * grp, x);
+                    atc_st_split8(lane_base + kDqColDo + 8 * grp, lane_base + kDqColDo + 32 + 8 * grp, y);
+                }
                 tc::tmem_st_wait();
                 tc::tc_fence_before();
                 __syncwarp();
