@@ -11,8 +11,9 @@
 //                  tile t, Q/K in the 128-byte swizzle (K-major operands),
 //                  V in the 128-byte/32-byte-atom swizzle (MN-major B);
 //                  then the MMA issuer.
-//   warps 0-15     split each landed tile into hi (in place) and lo; then
-//                  the softmax of tile t, one TMEM lane (query row) per
+//   warps 0-15     split each landed tile into hi (in place) and lo (tile
+//                  1 after tile 0's pass 2); the softmax of tile t, one
+//                  TMEM lane (query row) per
 //                  four threads: warp w reads lanes 32(w%4).. and the
 //                  32-key chunks c = w/4, w/4 + 4, ...
 // Per tile t (N = 128(t+1) keys):
@@ -299,8 +300,11 @@ attention_fwd_tc_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid
     } else {
         const int st = threadIdx.x;
         const int q = warp & 3, grp = warp >> 2;
-        // ---------------- hi/lo split of the landed tiles ----------------
-        for (int t = 0; t < ntile; ++t) {
+        // ---------------- hi/lo split of a landed tile ----------------
+        // tile 0 here; tile 1 after tile 0's pass 2, while the MMA issuer
+        // runs tile 0's E V, so that it does not compete with the S MMAs of
+        // tile 0 for shared memory
+        auto split_tile = [&](int t) {
             atc_wait(sm.abort, err, kAtcErrLoad, &sm.ld[t], 0);
             const int o = t * kAtcTileFloats;
             atc_split(sm.qh + o, sm.ql + o, kAtcTileFloats / 4, st, kAtcSoftThreads);
@@ -308,7 +312,8 @@ attention_fwd_tc_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid
             atc_split(sm.vh + o, sm.vl + o, kAtcTileFloats / 4, st, kAtcSoftThreads);
             tc::fence_proxy_async_smem();
             tc::mbar_arrive(&sm.conv[t]);
-        }
+        };
+        split_tile(0);
         // ---------------- softmax and epilogue ----------------
         // e = 2^(s * scale * log2(e) - m * log2(e)): one FFMA and one ex2
         // per score; the per-row constant's rounding cancels in e / sum.
@@ -395,6 +400,7 @@ attention_fwd_tc_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid
                 __syncwarp();
                 if (lane == 0) tc::mbar_arrive(&sm.ring_full[slot]);
             }
+            if (t + 1 < ntile) split_tile(t + 1);
             // every chunk's E_c V_c is in TMEM once the tile's MMAs have
             // completed: add them, in chunk order, into FP32 registers
             // (this thread's row, 8 columns) with round-to-nearest adds;
