@@ -122,6 +122,7 @@ SIGNATURES = {
     "hx_runtime_synchronize": (C.c_int, [C.c_void_p]),
     "hx_runtime_metrics": (C.c_int, [C.c_void_p, C.POINTER(Metrics)]),
     "hx_runtime_inject_execute_failure": (C.c_int, [C.c_void_p, C.c_int64]),
+    "hx_runtime_check_wait_timeout": (C.c_int, [C.c_void_p, C.c_longlong]),
     "hx_runtime_set_gemm_backend": (C.c_int, [C.c_void_p, C.c_int]),
     "hx_runtime_set_attention_backend": (C.c_int, [C.c_void_p, C.c_int]),
     "hx_runtime_profile": (C.c_int, [C.c_void_p, C.c_int]),

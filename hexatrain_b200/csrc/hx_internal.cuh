@@ -118,6 +118,10 @@ struct Profiler {
     }
 };
 
+// Error-word codes of the bounded waits: GEMM roles 1-4, attention roles
+// 11-14, and the wait self-test (hx_runtime_check_wait_timeout).
+constexpr int kWaitProbeCode = 21;
+
 struct MlpPlan;
 struct LmPlan;
 struct AdamPlan;
@@ -149,9 +153,17 @@ struct hx_runtime {
 
     ~hx_runtime();
     void activate() const { hx::check_cuda(cudaSetDevice(device), "cudaSetDevice"); }
+    // Bumped by everything that changes what a captured CUDA graph would
+    // launch or where it reads: a workspace reallocation (graphs hold its
+    // address) and an engine switch.  Cached graphs of an older epoch are
+    // dropped before their next replay.
+    uint64_t graph_epoch = 0;
     // Grow-only device workspace for split-K partials and reductions.
     float* workspace(size_t bytes) {
-        if (scratch.bytes < bytes) scratch.allocate(bytes);
+        if (scratch.bytes < bytes) {
+            scratch.allocate(bytes);
+            ++graph_epoch;
+        }
         return scratch.as<float>();
     }
     int* device_error() {
@@ -164,15 +176,22 @@ struct hx_runtime {
     // Reads (and clears) the device error word; fails if a kernel reported
     // a timed-out pipeline wait.  Synchronises the stream.
     void check_device_error() {
-        hx::check_cuda(cudaStreamSynchronize(stream), "cudaStreamSynchronize");
-        if (!err_flag.ptr) return;
+        if (!err_flag.ptr) {
+            hx::check_cuda(cudaStreamSynchronize(stream), "cudaStreamSynchronize");
+            return;
+        }
         int code = 0;
-        hx::check_cuda(cudaMemcpy(&code, err_flag.ptr, sizeof(int), cudaMemcpyDeviceToHost), "cudaMemcpy");
+        hx::check_cuda(cudaMemcpyAsync(&code, err_flag.ptr, sizeof(int), cudaMemcpyDeviceToHost, stream),
+                       "cudaMemcpyAsync");
+        hx::check_cuda(cudaStreamSynchronize(stream), "cudaStreamSynchronize");
         if (code) {
-            hx::check_cuda(cudaMemset(err_flag.ptr, 0, sizeof(int)), "cudaMemset");
-            hx::fail(HX_ERR_CUDA, std::string("DEVICE_WAIT_TIMEOUT: a bounded pipeline wait in the tensor-core ") +
-                                      (code >= 10 ? "attention" : "GEMM") + " gave up (role " + std::to_string(code) +
-                                      "); results of this call are invalid");
+            hx::check_cuda(cudaMemsetAsync(err_flag.ptr, 0, sizeof(int), stream), "cudaMemsetAsync");
+            hx::check_cuda(cudaStreamSynchronize(stream), "cudaStreamSynchronize");
+            const char* where = code >= hx::kWaitProbeCode ? "wait self-test"
+                                : code >= 10               ? "tensor-core attention"
+                                                           : "tensor-core GEMM";
+            hx::fail(HX_ERR_CUDA, std::string("DEVICE_WAIT_TIMEOUT: a bounded pipeline wait in the ") + where +
+                                      " gave up (role " + std::to_string(code) + "); results of this call are invalid");
         }
     }
     // Record the outcome of an execute call (ApiTrace counters).

@@ -27,14 +27,15 @@ namespace hx {
 AdamScalars adam_scalars(float lr, float gradient_scale, float c1, float c2);
 void launch_adam(hx_runtime* rt, bool graph_order, size_t n, const float* w, const float* g, const float* m,
                  const float* v, float* wn, float* mn, float* vn, const AdamScalars& s, const AdamTaps& t,
-                 const float* scale_dev = nullptr);
+                 const float* scale_dev = nullptr, const AdamScalars* s_dev = nullptr);
 void launch_momentum(hx_runtime* rt, size_t n, const float* w, const float* g, const float* vel, float* wn,
-                     float* veln, float lr, float momentum);
+                     float* veln, float lr, float momentum, const float* lr_dev = nullptr);
 void launch_clip_scale(hx_runtime* rt, const float* g, const GradTensor* tensors, int count, double* sumsq,
                        float threshold, double* norm_out, float* scale_out);
 size_t muon_smem_bytes(int rows, int cols);
 void check_muon_shape(int rows, int cols);
-void launch_muon(hx_runtime* rt, const MuonMatrix* d_mats, int count, size_t smem, const MuonScalars& s);
+void launch_muon(hx_runtime* rt, const MuonMatrix* d_mats, int count, size_t smem, const MuonScalars& s,
+                 const float* lr_dev = nullptr);
 
 struct LayerOffsets {  // offsets (in floats) of one layer's tensors in the flat registry
     size_t g1, b1, wq, wk, wv, wo, g2, b2, w1, w2;
@@ -77,9 +78,22 @@ struct LmPlan {
     int norm_count = 0;                // tensors in the gradient-norm table
     size_t norm_table = 0, norm_sumsq = 0, norm_value = 0, clip_scale = 0;
     bool state_ready = false;
-    float* host_scalars = nullptr;  // pinned [c1, c2]
+    // Captured step graphs (train step, forward+backward, optimizer step).
+    GraphCache graphs;
+    // Per-step optimizer scalars: host values go through a ring of pinned
+    // slots into step_scalars (device), which the optimizer kernels read.  A
+    // slot is rewritten only after the copy that last read it has run.
+    static constexpr int kRing = 16;
+    size_t step_scalars = 0;
+    LmStepScalars* ring = nullptr;
+    cudaEvent_t ring_ev[kRing] = {};
+    bool ring_live[kRing] = {};
+    unsigned ring_next = 0;
     ~LmPlan() {
-        if (host_scalars) cudaFreeHost(host_scalars);
+        graphs.clear();
+        for (cudaEvent_t e : ring_ev)
+            if (e) cudaEventDestroy(e);
+        if (ring) cudaFreeHost(ring);
     }
 };
 
@@ -462,49 +476,92 @@ void forward_backward(hx_runtime* rt, LmPlan& p, const float* W, float* G, float
     }
 }
 
-void optimizer_step(hx_runtime* rt, LmPlan& p, uint32_t step)
+// Host part of the optimizer step: this step's scalars, exactly as the
+// reference driver forms them, copied to step_scalars on the stream.
+void upload_step_scalars(hx_runtime* rt, LmPlan& p, uint32_t step)
+{
+    // Bias corrections exactly as the reference driver computes them
+    // (qnn/qnn_transformer_training.cpp:1504-1507): double, then float.
+    const float c1 = float(1.0 / (1.0 - std::pow(double(p.opt.beta1), double(step))));
+    const float c2 = float(1.0 / (1.0 - std::pow(double(p.opt.beta2), double(step))));
+    // Scheduled learning rates (training_stability.h stabilityLearningRate).
+    const float adam_lr = hx_stability_learning_rate(p.stab_mode, p.opt.adam_lr, step, p.stab_total);
+    LmStepScalars v{};
+    v.adam = adam_scalars(adam_lr, 1.0f, c1, c2);
+    v.adam.beta1 = p.opt.beta1;
+    v.adam.beta2 = p.opt.beta2;
+    v.adam.one_minus_beta1 = 1.0f - p.opt.beta1;
+    v.adam.one_minus_beta2 = 1.0f - p.opt.beta2;
+    v.adam.eps = p.opt.adam_eps;
+    v.momentum_lr = hx_stability_learning_rate(p.stab_mode, p.opt.momentum_lr, step, p.stab_total);
+    v.muon_lr = hx_stability_learning_rate(p.stab_mode, p.opt.muon_lr, step, p.stab_total);
+    const int slot = int(p.ring_next++ % LmPlan::kRing);
+    if (p.ring_live[slot]) HX_CUDA(cudaEventSynchronize(p.ring_ev[slot]));
+    p.ring[slot] = v;
+    HX_CUDA(cudaMemcpyAsync(p.arena.at<LmStepScalars>(p.step_scalars), &p.ring[slot], sizeof(LmStepScalars),
+                            cudaMemcpyHostToDevice, rt->stream));
+    HX_CUDA(cudaEventRecord(p.ring_ev[slot], rt->stream));
+    p.ring_live[slot] = true;
+}
+
+// Device part of the optimizer step: every launch reads its per-step
+// scalars from step_scalars, so the same launches can be captured once and
+// replayed for every step.
+void optimizer_enqueue(hx_runtime* rt, LmPlan& p)
 {
     const Arena& a = p.arena;
     float* W = a.at<float>(p.params);
     const float* G = a.at<float>(p.grads);
     float* m = a.at<float>(p.adam_m);
     float* v = a.at<float>(p.adam_v);
-    // Bias corrections exactly as the reference driver computes them
-    // (qnn/qnn_transformer_training.cpp:1504-1507): double, then float.
-    const float c1 = float(1.0 / (1.0 - std::pow(double(p.opt.beta1), double(step))));
-    const float c2 = float(1.0 / (1.0 - std::pow(double(p.opt.beta2), double(step))));
-    // Scheduled learning rates (training_stability.h stabilityLearningRate)
-    // and the global-norm clip scale, which Adam reads from device memory.
-    const float adam_lr = hx_stability_learning_rate(p.stab_mode, p.opt.adam_lr, step, p.stab_total);
+    const LmStepScalars* dyn = a.at<LmStepScalars>(p.step_scalars);
+    // the global-norm clip scale, which Adam reads from device memory
     const float* scale_dev = nullptr;
     if (p.clip_threshold > 0.f) {
         launch_clip_scale(rt, G, a.at<GradTensor>(p.norm_table), p.norm_count, a.at<double>(p.norm_sumsq),
                           p.clip_threshold, a.at<double>(p.norm_value), a.at<float>(p.clip_scale));
         scale_dev = a.at<float>(p.clip_scale);
     }
-    AdamScalars sc = adam_scalars(adam_lr, 1.0f, c1, c2);
-    sc.beta1 = p.opt.beta1;
-    sc.beta2 = p.opt.beta2;
-    sc.one_minus_beta1 = 1.0f - p.opt.beta1;
-    sc.one_minus_beta2 = 1.0f - p.opt.beta2;
-    sc.eps = p.opt.adam_eps;
+    const AdamScalars host_unused = adam_scalars(0.f, 1.0f, 1.f, 1.f);  // replaced by dyn->adam on the device
     const AdamTaps none{};
     if (p.opt.kind == HX_OPT_MOMENTUM) {
         // velocity lives in the Muon buffer slot (zeroed on state upload)
         float* vel = a.at<float>(p.muon_buf);
-        launch_momentum(rt, p.P, W, G, vel, W, vel,
-                        hx_stability_learning_rate(p.stab_mode, p.opt.momentum_lr, step, p.stab_total),
-                        p.opt.momentum);
+        launch_momentum(rt, p.P, W, G, vel, W, vel, 0.f, p.opt.momentum, &dyn->momentum_lr);
     } else if (p.opt.kind == HX_OPT_MUON) {
-        MuonScalars ms{hx_stability_learning_rate(p.stab_mode, p.opt.muon_lr, step, p.stab_total), p.opt.muon_momentum, p.opt.ns_a, p.opt.ns_b, p.opt.ns_c,
+        MuonScalars ms{0.f, p.opt.muon_momentum, p.opt.ns_a, p.opt.ns_b, p.opt.ns_c,
                        (int)p.opt.muon_nesterov, (int)p.opt.muon_ns_steps, (int)p.opt.muon_bf16_inputs};
-        launch_muon(rt, a.at<MuonMatrix>(p.muon_table), p.muon_count, p.muon_smem, ms);
+        launch_muon(rt, a.at<MuonMatrix>(p.muon_table), p.muon_count, p.muon_smem, ms, &dyn->muon_lr);
         for (const auto& seg : p.adam_segments)
             launch_adam(rt, false, seg.second, W + seg.first, G + seg.first, m + seg.first, v + seg.first,
-                        W + seg.first, m + seg.first, v + seg.first, sc, none);
+                        W + seg.first, m + seg.first, v + seg.first, host_unused, none, nullptr, &dyn->adam);
     } else {
-        launch_adam(rt, false, p.P, W, G, m, v, W, m, v, sc, none, scale_dev);
+        launch_adam(rt, false, p.P, W, G, m, v, W, m, v, host_unused, none, scale_dev, &dyn->adam);
     }
+}
+
+// Runs `body` from the plan's graph cache under `key`, or eagerly while the
+// event profiler is on (its events need eager launches).
+template <class F>
+void lm_run(hx_runtime* rt, LmPlan& p, const GraphCache::Key& key, F&& body)
+{
+    if (rt->prof.on) {
+        body();
+        return;
+    }
+    run_cached(rt, p.graphs, key, body);
+}
+
+enum LmGraphKind : uintptr_t { kGraphTrainStep = 1, kGraphForwardBackward = 2, kGraphOptimizer = 3 };
+
+GraphCache::Key lm_key(LmGraphKind kind, const void* tokens, float grad_scale) {
+    GraphCache::Key k{};
+    k[0] = kind;
+    k[1] = reinterpret_cast<uintptr_t>(tokens);
+    uint32_t bits;
+    std::memcpy(&bits, &grad_scale, 4);
+    k[2] = bits;
+    return k;
 }
 
 LmPlan& need_lm(hx_runtime* rt) {
@@ -687,6 +744,7 @@ int hx_lm_prepare(hx_runtime* rt, const hx_lm_config* cfg, uint32_t batch, int d
         p.norm_sumsq = a.reserve(sizeof(double) * p.norm_count);
         p.norm_value = a.reserve(sizeof(double));
         p.clip_scale = a.reserve(sizeof(float));
+        p.step_scalars = a.reserve(sizeof(LmStepScalars));
         a.commit();
         HX_CUDA(cudaMemsetAsync(a.block.ptr, 0, a.used, rt->stream));
         std::vector<float> pos;
@@ -733,7 +791,9 @@ int hx_lm_prepare(hx_runtime* rt, const hx_lm_config* cfg, uint32_t batch, int d
         require(int(norm.size()) == p.norm_count, HX_ERR_STATE, "internal: gradient-norm table size");
         HX_CUDA(cudaMemcpyAsync(a.at<GradTensor>(p.norm_table), norm.data(), sizeof(GradTensor) * norm.size(),
                                 cudaMemcpyHostToDevice, rt->stream));
-        HX_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&p.host_scalars), 64, cudaHostAllocDefault));
+        HX_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&p.ring), sizeof(LmStepScalars) * LmPlan::kRing,
+                              cudaHostAllocDefault));
+        for (cudaEvent_t& e : p.ring_ev) HX_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
         HX_CUDA(cudaStreamSynchronize(rt->stream));
         rt->lm = std::move(pp);
         ++rt->metrics.graph_create_count;
@@ -978,6 +1038,7 @@ int hx_lm_set_optimizer(hx_runtime* rt, const hx_optimizer_config* opt) {
                     "optimizer: invalid Muon scalars");
         }
         p.opt = *opt;
+        p.graphs.clear();
     });
 }
 
@@ -995,6 +1056,7 @@ int hx_lm_set_stability(hx_runtime* rt, uint32_t mode, uint32_t total_steps, flo
         p.stab_mode = mode;
         p.stab_total = total_steps;
         p.clip_threshold = thr;
+        p.graphs.clear();
     });
 }
 
@@ -1021,12 +1083,16 @@ int hx_lm_train_step(hx_runtime* rt, const uint32_t* tokens, uint32_t step, floa
         HX_CUDA(cudaMemcpyAsync(a.at<uint32_t>(p.tokens), tokens, sizeof(uint32_t) * size_t(p.B) * (p.T + 1),
                                 cudaMemcpyHostToDevice, rt->stream));
         rt->metrics.last_input_bind_us = us_since(tb);
-        HX_CUDA(cudaMemsetAsync(a.at<int>(p.bad), 0, sizeof(int), rt->stream));
-        split_tokens_kernel<<<grid_for(p.M, 256, rt->sm_count), 256, 0, rt->stream>>>(
-            p.B, p.T, p.V, a.at<uint32_t>(p.tokens), a.at<int>(p.in_ids), a.at<int>(p.tgt_ids), a.at<int>(p.bad));
-        HX_LAUNCHED(rt);
-        forward_backward(rt, p, a.at<float>(p.params), a.at<float>(p.grads), 1.0f / float(p.B));
-        optimizer_step(rt, p, step);
+        upload_step_scalars(rt, p, step);
+        const float gs = 1.0f / float(p.B);
+        lm_run(rt, p, lm_key(kGraphTrainStep, a.at<uint32_t>(p.tokens), gs), [&] {
+            HX_CUDA(cudaMemsetAsync(a.at<int>(p.bad), 0, sizeof(int), rt->stream));
+            split_tokens_kernel<<<grid_for(p.M, 256, rt->sm_count), 256, 0, rt->stream>>>(
+                p.B, p.T, p.V, a.at<uint32_t>(p.tokens), a.at<int>(p.in_ids), a.at<int>(p.tgt_ids), a.at<int>(p.bad));
+            HX_LAUNCHED(rt);
+            forward_backward(rt, p, a.at<float>(p.params), a.at<float>(p.grads), gs);
+            optimizer_enqueue(rt, p);
+        });
         const auto to = Clock::now();
         int bad = 0;
         HX_CUDA(cudaMemcpyAsync(loss, a.at<float>(p.loss), sizeof(float), cudaMemcpyDeviceToHost, rt->stream));
@@ -1048,10 +1114,12 @@ int hx_lm_forward_backward_device(hx_runtime* rt, const uint32_t* tokens, float 
         require(std::isfinite(grad_scale) && grad_scale > 0.f, HX_ERR_ARGUMENT, "forward_backward: invalid grad_scale");
         require(p.state_ready, HX_ERR_STATE, "forward_backward before state upload");
         const Arena& a = p.arena;
-        split_tokens_kernel<<<grid_for(p.M, 256, rt->sm_count), 256, 0, rt->stream>>>(
-            p.B, p.T, p.V, tokens, a.at<int>(p.in_ids), a.at<int>(p.tgt_ids), a.at<int>(p.bad));
-        HX_LAUNCHED(rt);
-        forward_backward(rt, p, a.at<float>(p.params), a.at<float>(p.grads), grad_scale);
+        lm_run(rt, p, lm_key(kGraphForwardBackward, tokens, grad_scale), [&] {
+            split_tokens_kernel<<<grid_for(p.M, 256, rt->sm_count), 256, 0, rt->stream>>>(
+                p.B, p.T, p.V, tokens, a.at<int>(p.in_ids), a.at<int>(p.tgt_ids), a.at<int>(p.bad));
+            HX_LAUNCHED(rt);
+            forward_backward(rt, p, a.at<float>(p.params), a.at<float>(p.grads), grad_scale);
+        });
     });
 }
 
@@ -1068,7 +1136,8 @@ int hx_lm_optimizer_step_device(hx_runtime* rt, uint32_t step) {
     return hx_guard(rt, [&] {
         LmPlan& p = need_lm(rt);
         require(step >= 1, HX_ERR_ARGUMENT, "optimizer step is 1-based");
-        optimizer_step(rt, p, step);
+        upload_step_scalars(rt, p, step);
+        lm_run(rt, p, lm_key(kGraphOptimizer, nullptr, 0.f), [&] { optimizer_enqueue(rt, p); });
     });
 }
 

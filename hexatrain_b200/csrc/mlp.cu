@@ -5,7 +5,7 @@
 // elementwise node, plus one deterministic loss reduction:
 //   1. Z1 = X W1           epilogue: H = ReLU(Z1), mask = H > 0
 //   2. P  = H W2           epilogue: E = P - Y, dP = E * 2/(B*O)
-//   3. loss = mean(E^2)    one-block double-precision tree reduction
+//   3. loss = mean(E^2)    double-precision block sums, added in block order
 //   4. dW2 = H^T dP        epilogue: W2_next = W2 - lr*dW2
 //   5. dH = dP W2^T        epilogue: dZ1 = (H > 0) ? dH : 0   (pre-update W2)
 //   6. dW1 = X^T dZ1       epilogue: W1_next = W1 - lr*dW1
@@ -18,23 +18,61 @@
 
 namespace hx {
 
-__global__ void mse_reduce_kernel(const float* __restrict__ e, size_t n, float* __restrict__ loss)
+__global__ void mse_reduce_kernel(const float* __restrict__ e, size_t n, size_t chunk, double* __restrict__ part,
+                                  unsigned int* __restrict__ done, float* __restrict__ loss)
 {
-    __shared__ double part[32];
+    __shared__ double wsum[32];
+    __shared__ bool last;
+    const int w = threadIdx.x / 32, l = threadIdx.x % 32, nw = blockDim.x / 32;
+    // this block's contiguous chunk, strided over the block's threads
+    const size_t lo = size_t(blockIdx.x) * chunk, hi = lo + chunk < n ? lo + chunk : n;
     double s = 0.0;
-    for (size_t i = threadIdx.x; i < n; i += blockDim.x) {
+    for (size_t i = lo + threadIdx.x; i < hi; i += blockDim.x) {
         const double v = e[i];
         s += v * v;
     }
     for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-    const int w = threadIdx.x / 32, l = threadIdx.x % 32;
-    if (l == 0) part[w] = s;
+    if (l == 0) wsum[w] = s;
     __syncthreads();
     if (w == 0) {
-        s = (l < (int)(blockDim.x / 32)) ? part[l] : 0.0;
+        s = l < nw ? wsum[l] : 0.0;
         for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-        if (l == 0) *loss = (float)(s / (double)n);
+        if (l == 0) {
+            part[blockIdx.x] = s;
+            __threadfence();
+            last = atomicAdd(done, 1u) == gridDim.x - 1;
+        }
     }
+    __syncthreads();
+    if (!last) return;
+    // The last block to finish: the per-block sums in a fixed tree by index.
+    __threadfence();
+    s = 0.0;
+    for (unsigned int b = threadIdx.x; b < gridDim.x; b += blockDim.x) s += __ldcg(part + b);
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if (l == 0) wsum[w] = s;
+    __syncthreads();
+    if (w == 0) {
+        s = l < nw ? wsum[l] : 0.0;
+        for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+        if (l == 0) {
+            *loss = (float)(s / (double)n);
+            *done = 0u;  // ready for the next launch
+        }
+    }
+}
+
+void launch_mse_reduce(hx_runtime* rt, const float* e, size_t n, double* part, unsigned int* done, float* loss)
+{
+    // Chunks of at least 16K elements, at most two blocks per SM: the grid,
+    // and with it the summation order, depends only on n and the SM count.
+    const size_t min_chunk = 16384;
+    size_t blocks = (n + min_chunk - 1) / min_chunk;
+    blocks = std::max<size_t>(1, std::min<size_t>(blocks, std::min<size_t>(kMseMaxBlocks, 2 * size_t(rt->sm_count))));
+    const size_t chunk = (n + blocks - 1) / blocks;
+    blocks = std::max<size_t>(1, (n + chunk - 1) / chunk);
+    mse_reduce_kernel<<<(unsigned)blocks, 1024, 0, rt->stream>>>(e, n, chunk, part, done, loss);
+    HX_LAUNCHED(rt);
 }
 
 void copy_d2d(hx_runtime* rt, void* dst, const void* src, size_t bytes) {
@@ -59,8 +97,8 @@ void mlp_enqueue(hx_runtime* rt, const MlpPlan& pl, const MlpBinding& b)
     gemm<false, false>(rt, B, O, H, b.h, H, b.w2, O, EpiError{b.y, b.p, b.e, b.dp, s, O});
     {
         ProfScope prof(rt, kTagReduce, 2.0 * B * O, 4.0 * B * O);
-        mse_reduce_kernel<<<1, 1024, 0, rt->stream>>>(b.e, size_t(B) * O, b.loss);
-        HX_LAUNCHED(rt);
+        launch_mse_reduce(rt, b.e, size_t(B) * O, pl.arena.at<double>(pl.mse_part), pl.arena.at<unsigned int>(pl.mse_done),
+                          b.loss);
     }
     gemm<true, false>(rt, H, O, B, b.h, H, b.dp, O, EpiSgd{b.w2, b.dw2, b.w2n, b.lr, O});
     gemm<false, true>(rt, B, H, O, b.dp, O, b.w2, O, EpiReluBackward{b.h, b.dz1, b.dh, H});
@@ -87,30 +125,7 @@ void mlp_run(hx_runtime* rt, MlpPlan& pl, const MlpBinding& b)
         mlp_enqueue(rt, pl, b);
         return;
     }
-    const auto key = key_of(b);
-    auto it = pl.graphs.execs.find(key);
-    if (it == pl.graphs.execs.end()) {
-        mlp_enqueue(rt, pl, b);  // eager first run
-        if (pl.graphs.execs.size() >= 8) pl.graphs.clear();
-        cudaGraph_t g = nullptr;
-        HX_CUDA(cudaStreamBeginCapture(rt->stream, cudaStreamCaptureModeThreadLocal));
-        try {
-            mlp_enqueue(rt, pl, b);
-        } catch (...) {
-            cudaStreamEndCapture(rt->stream, &g);
-            if (g) cudaGraphDestroy(g);
-            throw;
-        }
-        HX_CUDA(cudaStreamEndCapture(rt->stream, &g));
-        cudaGraphExec_t exec = nullptr;
-        const cudaError_t e = cudaGraphInstantiate(&exec, g, 0);
-        cudaGraphDestroy(g);
-        check_cuda(e, "cudaGraphInstantiate");
-        pl.graphs.execs.emplace(key, exec);
-        ++rt->metrics.graph_finalize_count;
-        return;
-    }
-    HX_CUDA(cudaGraphLaunch(it->second, rt->stream));
+    run_cached(rt, pl.graphs, key_of(b), [&] { mlp_enqueue(rt, pl, b); });
 }
 
 MlpPlan& need_mlp(hx_runtime* rt) {
@@ -153,7 +168,11 @@ int hx_mlp_prepare(hx_runtime* rt, uint32_t B, uint32_t I, uint32_t H, uint32_t 
         pl->dz1 = a.reserve(f * B * H);
         pl->dw1 = a.reserve(f * I * H);
         pl->loss = a.reserve(f * 4);
+        pl->mse_part = a.reserve(sizeof(double) * kMseMaxBlocks);
+        pl->mse_done = a.reserve(sizeof(unsigned int));
         a.commit();
+        HX_CUDA(cudaMemsetAsync(a.at<unsigned int>(pl->mse_done), 0, sizeof(unsigned int), rt->stream));
+        HX_CUDA(cudaStreamSynchronize(rt->stream));
         rt->mlp = std::move(pl);
         ++rt->metrics.graph_create_count;
     });

@@ -14,27 +14,37 @@
 // library for as long as the process runs.
 //
 // The array (kNoallocScratchBytes = 4 MiB):
-//   [0, 256)        error word of the tensor-core pipeline waits; it must be
-//                   zero when the step starts, so every call clears it first
+//   [0, 4)          error word of the tensor-core pipeline waits
+//   [64, 68)        finished-block counter of the loss reduction
+//   [256, 4352)     per-block sums of the loss reduction (kMseMaxBlocks doubles)
 //   then, each 256-byte aligned:
 //                   H   = ReLU(X W1)           B x H floats
 //                   dZ1 = dH masked by H > 0   B x H floats
 //                   E   = P - Y                B x O floats
 //                   dP  = E * 2/(B*O)          B x O floats
-// Every element of H, dZ1, E and dP is written before it is read within a
+// The error word and the counter must be zero when the step starts, so every
+// call clears the first 256 bytes before its first launch.  Every element of
+// the block sums, H, dZ1, E and dP is written before it is read within a
 // call, so their stale contents from the previous call do not matter.  The
-// step needs 2*B*H + 2*B*O floats; shapes beyond the array are rejected with
-// HX_ERR_UNSUPPORTED.  GEMMs here never split K (split-K would need a
-// partial-sum workspace), so a shape that the allocating step splits sums
-// its K products in another order and may differ from it in the last bits.
+// step needs 4352 bytes plus 2*B*H + 2*B*O floats (each tensor rounded up to
+// 256 bytes); shapes beyond the array are rejected with HX_ERR_UNSUPPORTED.
+// GEMMs here never split K (split-K would need a partial-sum workspace), so a
+// shape that the allocating step splits sums its K products in another order
+// and may differ from it in the last bits.
 //
 // Set-up: the first call on a device looks up the array's device address
 // with cudaGetSymbolAddress (with that device current; this also loads the
-// library's device code on that device if nothing has yet) and caches it.
+// library's device code on that device if nothing has yet) and caches it
+// together with the identity of the device's current CUDA context.  A call
+// that finds another context current (the old one was destroyed, for
+// example by cudaDeviceReset, and the module was loaded again) repeats the
+// set-up.  Make the first call on a device before capturing any stream.
 //
 // All calls on a device share the one array: two calls whose work overlaps
 // on the GPU (different streams, or different runtimes on the same device)
-// race on it.  Calls on one stream are ordered and safe.
+// race on it.  Calls on one stream are ordered and safe.  The call waits
+// for its own stream only (not for the caller's other streams) before it
+// returns, so that a timed-out pipeline wait is reported by this call.
 #include <cmath>
 #include <mutex>
 
@@ -45,27 +55,59 @@ namespace hx {
 namespace {
 
 constexpr size_t kNoallocScratchBytes = size_t(4) << 20;
-constexpr size_t kNoallocHeaderBytes = 256;
+constexpr size_t kNoallocCounterOffset = 64;
+constexpr size_t kNoallocPartOffset = 256;
+constexpr size_t kNoallocHeaderBytes = kNoallocPartOffset + sizeof(double) * kMseMaxBlocks;
+static_assert(kNoallocHeaderBytes % 256 == 0, "tensors after the header start 256-byte aligned");
 
 static __device__ __align__(256) unsigned char g_mlp_noalloc_scratch[kNoallocScratchBytes];
 
 constexpr int kMaxDevices = 64;
 std::mutex g_scratch_mu;
-void* g_scratch_ptr[kMaxDevices] = {};
+struct ScratchSetup {
+    void* ptr = nullptr;
+    unsigned long long context = 0;  // cuCtxGetId of the context the address belongs to
+};
+ScratchSetup g_scratch[kMaxDevices];
+
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+using CtxGetIdFn = CUresult (*)(CUcontext, unsigned long long*);
+
+template <class Fn>
+Fn driver_fn(const char* name) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    check_cuda(cudaGetDriverEntryPoint(name, &p, cudaEnableDefault, &q), name);
+    require(q == cudaDriverEntryPointSuccess && p, HX_ERR_CUDA, std::string(name) + " unavailable");
+    return reinterpret_cast<Fn>(p);
+}
+
+// Identity of the current context (unique for the life of the process).
+unsigned long long current_context_id() {
+    static const CtxGetCurrentFn get_current = driver_fn<CtxGetCurrentFn>("cuCtxGetCurrent");
+    static const CtxGetIdFn get_id = driver_fn<CtxGetIdFn>("cuCtxGetId");
+    CUcontext ctx = nullptr;
+    require(get_current(&ctx) == CUDA_SUCCESS && ctx != nullptr, HX_ERR_CUDA, "no-alloc step: no current CUDA context");
+    unsigned long long id = 0;
+    require(get_id(ctx, &id) == CUDA_SUCCESS, HX_ERR_CUDA, "no-alloc step: cuCtxGetId failed");
+    return id;
+}
 
 // Device address of the array on rt's device; the caller has made that
-// device current (hx_guard does).
+// device current (hx_guard does).  Looked up once per device and context.
 unsigned char* scratch_on(hx_runtime* rt) {
     require(rt->device >= 0 && rt->device < kMaxDevices, HX_ERR_ARGUMENT, "no-alloc step: device index out of range");
+    const unsigned long long ctx = current_context_id();
     std::lock_guard<std::mutex> lock(g_scratch_mu);
-    void*& p = g_scratch_ptr[rt->device];
-    if (!p) {
+    ScratchSetup& s = g_scratch[rt->device];
+    if (!s.ptr || s.context != ctx) {
         void* addr = nullptr;
         check_cuda(cudaGetSymbolAddress(&addr, g_mlp_noalloc_scratch), "cudaGetSymbolAddress(no-alloc scratch)");
         require(addr != nullptr, HX_ERR_CUDA, "no-alloc step: scratch symbol has no device address");
-        p = addr;
+        s.ptr = addr;
+        s.context = ctx;
     }
-    return static_cast<unsigned char*>(p);
+    return static_cast<unsigned char*>(s.ptr);
 }
 
 size_t round256(size_t b) { return (b + 255) & ~size_t(255); }
@@ -84,6 +126,7 @@ template <bool AT, bool BT, class Epi>
 void gemm_noalloc(hx_runtime* rt, int M, int N, int K, const float* A, long lda, const float* B, long ldb, Epi epi,
                   int* err)
 {
+    ProfScope prof(rt, kTagGemm, 2.0 * M * N * K, 4.0 * ((double)M * K + (double)K * N + (double)M * N));
     if (tc_eligible(rt, M, N, K, A, lda, B, ldb)) {
         constexpr bool A_MN = AT, B_MN = !BT;
         constexpr CUtensorMapSwizzle mn_swz = CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B;
@@ -138,31 +181,36 @@ int hx_mlp_execute_device_noalloc(hx_runtime* rt, uint32_t B, uint32_t I, uint32
         const size_t need = kNoallocHeaderBytes + 2 * bh + 2 * bo;
         require(need <= kNoallocScratchBytes, HX_ERR_UNSUPPORTED,
                 "no-alloc step: B=" + std::to_string(B) + " H=" + std::to_string(H) + " O=" + std::to_string(O) +
-                    " needs " + std::to_string(need) + " bytes of scratch (2*B*H + 2*B*O floats), above the fixed " +
+                    " needs " + std::to_string(need) + " bytes of scratch (4352 + 2*B*H + 2*B*O floats), above the fixed " +
                     std::to_string(kNoallocScratchBytes) + "-byte array; use hx_mlp_prepare/hx_mlp_execute_device");
         unsigned char* s = scratch_on(rt);
         int* err = reinterpret_cast<int*>(s);
+        unsigned int* done = reinterpret_cast<unsigned int*>(s + kNoallocCounterOffset);
+        double* part = reinterpret_cast<double*>(s + kNoallocPartOffset);
         float* h = reinterpret_cast<float*>(s + kNoallocHeaderBytes);
         float* dz1 = reinterpret_cast<float*>(s + kNoallocHeaderBytes + bh);
         float* e = reinterpret_cast<float*>(s + kNoallocHeaderBytes + 2 * bh);
         float* dp = reinterpret_cast<float*>(s + kNoallocHeaderBytes + 2 * bh + bo);
-        HX_CUDA(cudaMemsetAsync(err, 0, sizeof(int), rt->stream));
+        HX_CUDA(cudaMemsetAsync(s, 0, kNoallocPartOffset, rt->stream));  // error word and block counter
 
         const int b = (int)B, i = (int)I, hd = (int)H, o = (int)O;
         const float scale = 2.0f / float(b * o);
         gemm_noalloc<false, false>(rt, b, hd, i, x, i, w1, hd, EpiRelu{h, nullptr, hd}, err);
         gemm_noalloc<false, false>(rt, b, o, hd, h, hd, w2, o, EpiError{y, nullptr, e, dp, scale, o}, err);
-        mse_reduce_kernel<<<1, 1024, 0, rt->stream>>>(e, size_t(b) * o, loss);
-        HX_LAUNCHED(rt);
+        {
+            ProfScope prof(rt, kTagReduce, 2.0 * b * o, 4.0 * b * o);
+            launch_mse_reduce(rt, e, size_t(b) * o, part, done, loss);
+        }
         gemm_noalloc<true, false>(rt, hd, o, b, h, hd, dp, o, EpiSgd{w2, nullptr, w2_next, lr, o}, err);
         gemm_noalloc<false, true>(rt, b, hd, o, dp, o, w2, o, EpiReluBackward{h, dz1, nullptr, hd}, err);
         gemm_noalloc<true, false>(rt, i, hd, b, x, i, dz1, hd, EpiSgd{w1, nullptr, w1_next, lr, hd}, err);
 
         // Finish here so that a timed-out pipeline wait is reported by this
-        // call rather than left in the shared array for the next one.
-        HX_CUDA(cudaStreamSynchronize(rt->stream));
+        // call rather than left in the shared array for the next one.  The
+        // read-back is ordered on this runtime's stream only.
         int code = 0;
-        HX_CUDA(cudaMemcpy(&code, err, sizeof(int), cudaMemcpyDeviceToHost));
+        HX_CUDA(cudaMemcpyAsync(&code, err, sizeof(int), cudaMemcpyDeviceToHost, rt->stream));
+        HX_CUDA(cudaStreamSynchronize(rt->stream));
         if (code)
             fail(HX_ERR_CUDA, "DEVICE_WAIT_TIMEOUT: a bounded pipeline wait in the tensor-core GEMM gave up (role " +
                                   std::to_string(code) + "); results of this call are invalid");

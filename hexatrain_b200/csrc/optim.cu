@@ -10,8 +10,9 @@ namespace hx {
 
 // One CTA per matrix.  Shared memory: X [R][C] (R <= C, the shorter side
 // first), A [R][R], Bm [R][R].  Limits: R <= 128, R*C <= 16384.
-__global__ void muon_kernel(const MuonMatrix* __restrict__ mats, MuonScalars s)
+__global__ void muon_kernel(const MuonMatrix* __restrict__ mats, MuonScalars s, const float* __restrict__ lr_dev)
 {
+    if (lr_dev) s.lr = *lr_dev;
     extern __shared__ float sm[];
     const MuonMatrix mt = mats[blockIdx.x];
     const int rows = mt.rows, cols = mt.cols;
@@ -103,7 +104,7 @@ AdamScalars adam_scalars(float lr, float gradient_scale, float c1, float c2) {
 
 void launch_adam(hx_runtime* rt, bool graph_order, size_t n, const float* w, const float* g, const float* m,
                  const float* v, float* wn, float* mn, float* vn, const AdamScalars& s, const AdamTaps& t,
-                 const float* scale_dev = nullptr)
+                 const float* scale_dev = nullptr, const AdamScalars* s_dev = nullptr)
 {
     if (n == 0) return;
     ProfScope prof(rt, kTagOptimizer, 12.0 * n, 28.0 * n);
@@ -111,15 +112,17 @@ void launch_adam(hx_runtime* rt, bool graph_order, size_t n, const float* w, con
     const size_t work = graph_order ? n : (n + 3) / 4;
     const int blocks = (int)std::min<size_t>((work + threads - 1) / threads, size_t(rt->sm_count) * 16);
     if (graph_order)
-        adam_kernel<true><<<blocks, threads, 0, rt->stream>>>(n, w, g, m, v, wn, mn, vn, s, t, scale_dev);
+        adam_kernel<true><<<blocks, threads, 0, rt->stream>>>(n, w, g, m, v, wn, mn, vn, s, t, scale_dev, s_dev);
     else
-        adam_kernel<false><<<blocks, threads, 0, rt->stream>>>(n, w, g, m, v, wn, mn, vn, s, t, scale_dev);
+        adam_kernel<false><<<blocks, threads, 0, rt->stream>>>(n, w, g, m, v, wn, mn, vn, s, t, scale_dev, s_dev);
     HX_LAUNCHED(rt);
 }
 
 __global__ void momentum_kernel(size_t n, const float* w, const float* __restrict__ g, const float* vel,
-                                float* w_next, float* vel_next, float lr, float momentum)
+                                float* w_next, float* vel_next, float lr, float momentum,
+                                const float* __restrict__ lr_dev)
 {
+    if (lr_dev) lr = *lr_dev;
     const size_t stride = (size_t)gridDim.x * blockDim.x;
     const size_t tid = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
     auto one = [&](float wi, float gi, float vi, float& wo, float& vo) {
@@ -155,13 +158,13 @@ __global__ void momentum_kernel(size_t n, const float* w, const float* __restric
 }
 
 void launch_momentum(hx_runtime* rt, size_t n, const float* w, const float* g, const float* vel, float* wn,
-                     float* veln, float lr, float momentum)
+                     float* veln, float lr, float momentum, const float* lr_dev = nullptr)
 {
     if (n == 0) return;
     ProfScope prof(rt, kTagOptimizer, 3.0 * n, 20.0 * n);
     const int threads = 256;
     const int blocks = (int)std::min<size_t>(((n + 3) / 4 + threads - 1) / threads, size_t(rt->sm_count) * 16);
-    momentum_kernel<<<blocks, threads, 0, rt->stream>>>(n, w, g, vel, wn, veln, lr, momentum);
+    momentum_kernel<<<blocks, threads, 0, rt->stream>>>(n, w, g, vel, wn, veln, lr, momentum, lr_dev);
     HX_LAUNCHED(rt);
 }
 
@@ -228,11 +231,12 @@ void check_muon_shape(int rows, int cols) {
                 " exceeds the single-CTA Newton-Schulz limit (shorter side <= 128, <= 16384 elements)");
 }
 
-void launch_muon(hx_runtime* rt, const MuonMatrix* d_mats, int count, size_t smem, const MuonScalars& s) {
+void launch_muon(hx_runtime* rt, const MuonMatrix* d_mats, int count, size_t smem, const MuonScalars& s,
+                 const float* lr_dev = nullptr) {
     if (count == 0) return;
     ProfScope prof(rt, kTagOptimizer, 0.0, 0.0);
     HX_CUDA(cudaFuncSetAttribute(muon_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    muon_kernel<<<count, 1024, smem, rt->stream>>>(d_mats, s);
+    muon_kernel<<<count, 1024, smem, rt->stream>>>(d_mats, s, lr_dev);
     HX_LAUNCHED(rt);
 }
 

@@ -56,10 +56,13 @@ __device__ __forceinline__ float adam_element(float w, float g, float& m, float&
 template <bool kGraphOrder>
 __global__ void adam_kernel(size_t n, const float* w, const float* __restrict__ g, const float* m,
                             const float* v, float* w_next, float* m_next, float* v_next, AdamScalars s,
-                            AdamTaps t, const float* __restrict__ scale_dev)
+                            AdamTaps t, const float* __restrict__ scale_dev, const AdamScalars* __restrict__ s_dev)
 {
-    // A gradient scale computed on the device (the global-norm clip) replaces
-    // the host scalar when given.
+    // Scalars in device memory (a captured training step, whose learning
+    // rate and bias corrections change every step) replace the by-value
+    // ones; a gradient scale computed on the device (the global-norm clip)
+    // replaces the host scalar when given.
+    if (s_dev) s = *s_dev;
     if (scale_dev) s.gradient_scale = *scale_dev;
     const size_t stride = (size_t)gridDim.x * blockDim.x;
     const size_t tid = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -101,7 +104,16 @@ __global__ void adam_kernel(size_t n, const float* w, const float* __restrict__ 
 // (tiny_lm::momentumUpdate, tiny_language_model_cpu.cpp:123, rounds the
 // same products).  In place is allowed.
 __global__ void momentum_kernel(size_t n, const float* w, const float* __restrict__ g, const float* vel,
-                                float* w_next, float* vel_next, float lr, float momentum);
+                                float* w_next, float* vel_next, float lr, float momentum,
+                                const float* __restrict__ lr_dev);
+
+// Per-step scalars of the LM optimizer step, read from device memory so that
+// a captured step graph replays with each step's values: Adam's learning
+// rate and bias corrections, and the scheduled momentum and Muon rates.
+struct LmStepScalars {
+    AdamScalars adam;
+    float momentum_lr, muon_lr;
+};
 
 // ---- global gradient norm and clip scale ----------------------------------
 // gradientNorm (qnn/qnn_transformer_training.cpp:888-938): per tensor the
@@ -137,6 +149,7 @@ __device__ __forceinline__ float muon_operand(float x, int bf16) {
 }
 
 // Momentum + Newton-Schulz for a batch of matrices, one CTA each (optim.cu).
-__global__ void muon_kernel(const MuonMatrix* __restrict__ mats, MuonScalars s);
+// lr_dev, when given, replaces s.lr.
+__global__ void muon_kernel(const MuonMatrix* __restrict__ mats, MuonScalars s, const float* __restrict__ lr_dev);
 
 }  // namespace hx

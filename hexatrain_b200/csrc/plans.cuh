@@ -16,13 +16,72 @@ namespace hx {
 // (qnn/qnn_mlp_training.cpp:748-749) produces two keys that alternate.
 struct GraphCache {
     using Key = std::array<uintptr_t, 24>;
-    std::map<Key, cudaGraphExec_t> execs;
+    struct Entry {
+        cudaGraphExec_t exec;
+        uint64_t kernels;  // kernel launches the graph replays
+    };
+    std::map<Key, Entry> execs;
+    uint64_t epoch = 0;          // the runtime's graph_epoch when the cached graphs were captured
+    bool capture_failed = false; // a capture failed once: run eagerly from then on
     ~GraphCache() { clear(); }
     void clear() {
-        for (auto& kv : execs) cudaGraphExecDestroy(kv.second);
+        for (auto& kv : execs) cudaGraphExecDestroy(kv.second.exec);
         execs.clear();
     }
 };
+
+// Runs the work `enqueue` puts on the runtime stream: eagerly the first time
+// `key` is seen (this also sizes the runtime workspace), from a CUDA graph
+// captured right after that eager run on every later call.  Graphs of an
+// older runtime graph epoch are dropped.  A stream that cannot be captured
+// (the legacy default stream), or a capture that fails, leaves the work to
+// run eagerly; the eager run has already done this call's work.
+template <class F>
+void run_cached(hx_runtime* rt, GraphCache& c, const GraphCache::Key& key, F&& enqueue)
+{
+    if (c.epoch != rt->graph_epoch) {
+        c.clear();
+        c.epoch = rt->graph_epoch;
+    }
+    auto it = c.execs.find(key);
+    if (it != c.execs.end()) {
+        check_cuda(cudaGraphLaunch(it->second.exec, rt->stream), "cudaGraphLaunch");
+        rt->metrics.kernel_launches += it->second.kernels;
+        return;
+    }
+    enqueue();  // eager first run
+    if (c.capture_failed) return;
+    if (c.epoch != rt->graph_epoch) {
+        c.clear();
+        c.epoch = rt->graph_epoch;
+    }
+    if (c.execs.size() >= 8) c.clear();
+    if (cudaStreamBeginCapture(rt->stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
+        (void)cudaGetLastError();
+        c.capture_failed = true;
+        return;
+    }
+    cudaGraph_t g = nullptr;
+    const uint64_t launches = rt->metrics.kernel_launches;
+    bool ok = true;
+    try {
+        enqueue();
+    } catch (...) {
+        ok = false;
+    }
+    const uint64_t kernels = rt->metrics.kernel_launches - launches;
+    rt->metrics.kernel_launches = launches;  // captured, not launched
+    const cudaError_t ec = cudaStreamEndCapture(rt->stream, &g);
+    cudaGraphExec_t exec = nullptr;
+    if (ok && ec == cudaSuccess && g && cudaGraphInstantiate(&exec, g, 0) == cudaSuccess) {
+        c.execs.emplace(key, GraphCache::Entry{exec, kernels});
+        ++rt->metrics.graph_finalize_count;
+    } else {
+        c.capture_failed = true;
+    }
+    if (g) cudaGraphDestroy(g);
+    (void)cudaGetLastError();
+}
 
 struct MlpPlan {
     uint32_t B = 0, I = 0, H = 0, O = 0;
@@ -30,6 +89,7 @@ struct MlpPlan {
     Arena arena;
     // arena offsets
     size_t x, y, w1, w2, w1n, w2n, h, p, e, dp, dw2, dh, mask, dz1, dw1, loss;
+    size_t mse_part, mse_done;  // per-block loss sums and the finished-block counter
     GraphCache graphs;
     bool use_graphs = true;
 };
@@ -65,8 +125,14 @@ inline size_t plan_device_bytes(const hx_runtime* rt) {
 
 // Sum of squares in double over n floats, divided by n, rounded to float:
 // the reference's meanSquaredError (cpu_reference_training.cpp:163-170)
-// with a fixed-shape tree instead of a sequential sum.  One block.
-__global__ void mse_reduce_kernel(const float* __restrict__ e, size_t n, float* __restrict__ loss);
+// with fixed-shape trees instead of a sequential sum.  Each block sums one
+// contiguous chunk into part[block]; the last block to finish adds the
+// block sums in index order and re-zeroes *done, which must be zero when the
+// kernel starts.  part holds at least kMseMaxBlocks doubles.
+constexpr size_t kMseMaxBlocks = 512;
+__global__ void mse_reduce_kernel(const float* __restrict__ e, size_t n, size_t chunk, double* __restrict__ part,
+                                  unsigned int* __restrict__ done, float* __restrict__ loss);
+void launch_mse_reduce(hx_runtime* rt, const float* e, size_t n, double* part, unsigned int* done, float* loss);
 
 // Copies `count` floats, used for D2D staging inside captured graphs.
 void copy_d2d(hx_runtime* rt, void* dst, const void* src, size_t bytes);

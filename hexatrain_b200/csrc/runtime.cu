@@ -8,6 +8,7 @@
 #include <cstdio>
 
 #include "plans.cuh"
+#include "tc_ptx.cuh"
 
 hx_runtime::~hx_runtime() {
     cudaSetDevice(device);
@@ -20,6 +21,20 @@ hx_runtime::~hx_runtime() {
 }
 
 namespace {
+// One thread waits, with the bounded wait of the tensor-core kernels, on an
+// mbarrier that nothing arrives at; when the wait gives up it records the
+// self-test code in the error word the way those kernels record theirs.
+// Nothing else is in flight in this block (no TMA copy, no MMA, no TMEM).
+__global__ void wait_timeout_probe_kernel(long long limit, int* err)
+{
+    __shared__ __align__(8) uint64_t bar;
+    if (threadIdx.x == 0) {
+        hx::tc::mbar_init(&bar, 1);
+        hx::tc::fence_mbar_init();
+        if (!hx::tc::mbar_wait(&bar, 0, limit)) atomicCAS(err, 0, hx::kWaitProbeCode);
+    }
+}
+
 void write_err(char* err, size_t len, const std::string& msg) {
     if (err && len) {
         std::snprintf(err, len, "%s", msg.c_str());
@@ -91,6 +106,7 @@ int hx_runtime_set_gemm_backend(hx_runtime* rt, int backend) {
     return hx_guard(rt, [&] {
         hx::require(backend == HX_GEMM_AUTO || backend == HX_GEMM_CUDA_CORES || backend == HX_GEMM_TENSOR_CORES,
                     HX_ERR_ARGUMENT, "unknown GEMM backend");
+        if (rt->gemm_backend != backend) ++rt->graph_epoch;
         rt->gemm_backend = backend;
     });
 }
@@ -99,6 +115,7 @@ int hx_runtime_set_attention_backend(hx_runtime* rt, int backend) {
     return hx_guard(rt, [&] {
         hx::require(backend == HX_ATTN_AUTO || backend == HX_ATTN_CUDA_CORES, HX_ERR_ARGUMENT,
                     "unknown attention backend");
+        if (rt->attention_backend != backend) ++rt->graph_epoch;
         rt->attention_backend = backend;
     });
 }
@@ -140,6 +157,16 @@ int hx_runtime_profile_read(hx_runtime* rt, hx_profile_entry* entries, int capac
         for (int t = 0; t < hx::kTagCount && n < capacity; ++t)
             if (agg[t].launches) entries[n++] = agg[t];
         *count = n;
+    });
+}
+
+int hx_runtime_check_wait_timeout(hx_runtime* rt, long long cycles) {
+    return hx_guard(rt, [&] {
+        hx::require(cycles > 0 && cycles <= 4000000000LL, HX_ERR_ARGUMENT,
+                    "wait self-test: cycles must be in (0, 4e9]");
+        wait_timeout_probe_kernel<<<1, 32, 0, rt->stream>>>(cycles, rt->device_error());
+        HX_LAUNCHED(rt);
+        rt->check_device_error();
     });
 }
 

@@ -315,6 +315,12 @@ class Runtime:
             self._lib.hx_runtime_metrics(self._rt, C.byref(m))
         return RuntimeMetrics(**{f: getattr(m, f) for f, _ in _lib.Metrics._fields_})
 
+    def check_wait_timeout(self, cycles: int) -> bool:
+        """Failure-path self-test of the kernels' bounded waits: one thread
+        waits `cycles` clock cycles on an mbarrier nothing arrives at.  Returns
+        False with a DEVICE_WAIT_TIMEOUT message in last_error (expected)."""
+        return self._need() and self._ok(self._lib.hx_runtime_check_wait_timeout(self._rt, int(cycles)))
+
     def set_gemm_backend(self, backend: int) -> bool:
         """0 = auto (tensor cores for large aligned GEMMs), 1 = CUDA cores, 2 = tensor cores when aligned."""
         return self._need() and self._ok(self._lib.hx_runtime_set_gemm_backend(self._rt, int(backend)))

@@ -81,6 +81,18 @@ int hx_runtime_metrics(const hx_runtime* rt, hx_metrics* out);
  * work finished.  -1 disables.  No device fault is involved. */
 int hx_runtime_inject_execute_failure(hx_runtime* rt, int64_t call_index);
 
+/* Failure-path self-test of the device-side bounded waits (no counterpart in
+ * the reference).  Every pipeline wait of the tensor-core GEMM and attention
+ * kernels gives up after a bounded number of clock cycles, records a code in
+ * the runtime's device error word, tears down and returns; the next
+ * synchronising call then fails with a "DEVICE_WAIT_TIMEOUT: ..." message.
+ * This call runs that path on purpose without any fault: one thread waits,
+ * with the same bounded wait, on an mbarrier that nothing arrives at, for
+ * `cycles` SM clock cycles (0 < cycles <= 4e9).  It returns HX_ERR_CUDA with
+ * the DEVICE_WAIT_TIMEOUT message; the error word is cleared, so the
+ * runtime's next call proceeds normally.  Synchronous. */
+int hx_runtime_check_wait_timeout(hx_runtime* rt, long long cycles);
+
 /* GEMM engine selection.  AUTO (default) runs large FP32 GEMMs on the
  * tensor cores as 3xTF32 (tcgen05, TMEM accumulators, TMA-fed) and small or
  * unaligned ones on the CUDA cores; the other values force one engine where
@@ -163,15 +175,16 @@ int hx_mlp_execute_device(hx_runtime* rt, const float* x, const float* y, const 
  * own allocator (a host framework's caching pool), or a step path on which
  * cudaMalloc/cudaFree are not allowed because they synchronise the device.
  * It has no counterpart in the reference.  No hx_mlp_prepare is needed and
- * nothing is allocated: the intermediates (2*B*H + 2*B*O floats) live in one
- * fixed 4 MiB array of device memory that every GPU loading this library
- * holds until the process exits; larger shapes fail with
- * HX_ERR_UNSUPPORTED.  The first call on a device looks up that array's
- * address (and may load the library's device code); make it before any
- * stream capture.  All calls on a device share the array, so calls whose
- * work overlaps on the GPU (other streams or other runtimes on the same
- * device) race; calls on one stream are safe.  Returns after the step has
- * finished on the runtime stream.  K is never split, so shapes that the
+ * nothing is allocated: the intermediates (2*B*H + 2*B*O floats, after a
+ * 4352-byte header) live in one fixed 4 MiB array of device memory that every
+ * GPU loading this library holds until the process exits; larger shapes fail
+ * with HX_ERR_UNSUPPORTED.  The first call on a device (and the first after
+ * that device's context was recreated) looks up that array's address (and
+ * may load the library's device code); make it before any stream capture.
+ * All calls on a device share the array, so calls whose work overlaps on the
+ * GPU (other streams or other runtimes on the same device) race; calls on
+ * one stream are safe.  Returns after the step has finished on the runtime
+ * stream; it waits for that stream only.  K is never split, so shapes that the
  * allocating step splits may differ from it in the last bits. */
 int hx_mlp_execute_device_noalloc(hx_runtime* rt, uint32_t batch, uint32_t input_dim,
                                   uint32_t hidden_dim, uint32_t output_dim, const float* x,
