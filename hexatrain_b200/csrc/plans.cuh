@@ -36,6 +36,10 @@ struct GraphCache {
 // older runtime graph epoch are dropped.  A stream that cannot be captured
 // (the legacy default stream), or a capture that fails, leaves the work to
 // run eagerly; the eager run has already done this call's work.
+// A plan keeps at most this many captured graphs (the MLP driver's cyclic
+// batches over 512 samples at B = 8 bind 64 distinct input slices).
+constexpr size_t kGraphCacheMax = 256;
+
 template <class F>
 void run_cached(hx_runtime* rt, GraphCache& c, const GraphCache::Key& key, F&& enqueue)
 {
@@ -55,7 +59,7 @@ void run_cached(hx_runtime* rt, GraphCache& c, const GraphCache::Key& key, F&& e
         c.clear();
         c.epoch = rt->graph_epoch;
     }
-    if (c.execs.size() >= 8) c.clear();
+    if (c.execs.size() >= kGraphCacheMax) c.clear();
     if (cudaStreamBeginCapture(rt->stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
         (void)cudaGetLastError();
         c.capture_failed = true;
