@@ -115,5 +115,6 @@ def _device_view(ptr: int, count: int):
 
 def replica_seeds(first_seed: int, world: int) -> list[int]:
     """Independent-seed replica sweep: rank r trains its own model with seed
-    first_seed + r and never communicates (seeds 20260710..20260717 at 8 GPUs)."""
+    first_seed + r and never communicates (seeds 20260710..20260717 at 8
+    GPUs); hexatrain_b200/replicas.py runs the sweep."""
     return [first_seed + r for r in range(world)]
