@@ -119,7 +119,8 @@ struct Profiler {
 };
 
 // Error-word codes of the bounded waits: GEMM roles 1-4, attention roles
-// 11-14, and the wait self-test (hx_runtime_check_wait_timeout).
+// 11-14, the Muon kernel 16, and the wait self-test
+// (hx_runtime_check_wait_timeout).
 constexpr int kWaitProbeCode = 21;
 
 struct MlpPlan;
@@ -188,6 +189,7 @@ struct hx_runtime {
             hx::check_cuda(cudaMemsetAsync(err_flag.ptr, 0, sizeof(int), stream), "cudaMemsetAsync");
             hx::check_cuda(cudaStreamSynchronize(stream), "cudaStreamSynchronize");
             const char* where = code >= hx::kWaitProbeCode ? "wait self-test"
+                                : code >= 16               ? "tensor-core Muon"
                                 : code >= 10               ? "tensor-core attention"
                                                            : "tensor-core GEMM";
             hx::fail(HX_ERR_CUDA, std::string("DEVICE_WAIT_TIMEOUT: a bounded pipeline wait in the ") + where +

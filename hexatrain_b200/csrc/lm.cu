@@ -35,7 +35,8 @@ void launch_clip_scale(hx_runtime* rt, const float* g, const GradTensor* tensors
 size_t muon_smem_bytes(int rows, int cols);
 void check_muon_shape(int rows, int cols);
 void launch_muon(hx_runtime* rt, const MuonMatrix* d_mats, int count, size_t smem, const MuonScalars& s,
-                 const float* lr_dev = nullptr);
+                 const float* lr_dev = nullptr, bool tc_shapes = false);
+bool muon_tc_shape(int rows, int cols);
 
 struct LayerOffsets {  // offsets (in floats) of one layer's tensors in the flat registry
     size_t g1, b1, wq, wk, wv, wo, g2, b2, w1, w2;
@@ -531,7 +532,8 @@ void optimizer_enqueue(hx_runtime* rt, LmPlan& p)
     } else if (p.opt.kind == HX_OPT_MUON) {
         MuonScalars ms{0.f, p.opt.muon_momentum, p.opt.ns_a, p.opt.ns_b, p.opt.ns_c,
                        (int)p.opt.muon_nesterov, (int)p.opt.muon_ns_steps, (int)p.opt.muon_bf16_inputs};
-        launch_muon(rt, a.at<MuonMatrix>(p.muon_table), p.muon_count, p.muon_smem, ms, &dyn->muon_lr);
+        launch_muon(rt, a.at<MuonMatrix>(p.muon_table), p.muon_count, p.muon_smem, ms, &dyn->muon_lr,
+                    muon_tc_shape(int(p.D), int(p.D)) && muon_tc_shape(int(p.D), int(p.F)));
         for (const auto& seg : p.adam_segments)
             launch_adam(rt, false, seg.second, W + seg.first, G + seg.first, m + seg.first, v + seg.first,
                         W + seg.first, m + seg.first, v + seg.first, host_unused, none, nullptr, &dyn->adam);

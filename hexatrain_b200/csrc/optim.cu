@@ -3,6 +3,7 @@
 // and Muon (no reference counterpart).
 #include <cmath>
 
+#include "muon_tc.cuh"
 #include "optim.cuh"
 #include "plans.cuh"
 
@@ -231,10 +232,28 @@ void check_muon_shape(int rows, int cols) {
                 " exceeds the single-CTA Newton-Schulz limit (shorter side <= 128, <= 16384 elements)");
 }
 
+// Whether every Muon matrix of a launch fits the tensor-core kernel (bf16
+// operands, shorter side and longer side at most 128).
+bool muon_tc_shape(int rows, int cols) {
+    return std::max(rows, cols) <= kMuonTcMaxDim;
+}
+
+// Muon for `count` matrices: the tcgen05 kernel when the operands are bf16,
+// every matrix fits it (`tc_shapes`) and the GEMM engine is not forced to
+// the CUDA cores; the CUDA-core kernel otherwise (FP32 operands, larger
+// matrices).
 void launch_muon(hx_runtime* rt, const MuonMatrix* d_mats, int count, size_t smem, const MuonScalars& s,
-                 const float* lr_dev = nullptr) {
+                 const float* lr_dev = nullptr, bool tc_shapes = false) {
     if (count == 0) return;
     ProfScope prof(rt, kTagOptimizer, 0.0, 0.0);
+    if (s.bf16 && tc_shapes && rt->gemm_backend != HX_GEMM_CUDA_CORES) {
+        HX_CUDA(cudaFuncSetAttribute(muon_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)kMuonTcSmemBytes));
+        muon_tc_kernel<<<count, kMuonTcThreads, kMuonTcSmemBytes, rt->stream>>>(d_mats, s, lr_dev,
+                                                                               rt->device_error());
+        HX_LAUNCHED(rt);
+        return;
+    }
     HX_CUDA(cudaFuncSetAttribute(muon_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     muon_kernel<<<count, 1024, smem, rt->stream>>>(d_mats, s, lr_dev);
     HX_LAUNCHED(rt);
@@ -387,10 +406,11 @@ int hx_muon_execute(hx_runtime* rt, uint32_t rows, uint32_t cols, const float* w
         MuonMatrix mm{arena.at<float>(ow), arena.at<float>(og), arena.at<float>(ob), (int)rows, (int)cols};
         HX_CUDA(cudaMemcpyAsync(arena.at<MuonMatrix>(om), &mm, sizeof(mm), cudaMemcpyHostToDevice, rt->stream));
         MuonScalars s{lr, momentum, a, b, c, nesterov ? 1 : 0, (int)ns_steps, bf16 ? 1 : 0};
-        launch_muon(rt, arena.at<MuonMatrix>(om), 1, muon_smem_bytes((int)rows, (int)cols), s);
+        launch_muon(rt, arena.at<MuonMatrix>(om), 1, muon_smem_bytes((int)rows, (int)cols), s, nullptr,
+                    muon_tc_shape((int)rows, (int)cols));
         HX_CUDA(cudaMemcpyAsync(weight_next, arena.at<float>(ow), bytes, cudaMemcpyDeviceToHost, rt->stream));
         HX_CUDA(cudaMemcpyAsync(buffer_next, arena.at<float>(ob), bytes, cudaMemcpyDeviceToHost, rt->stream));
-        HX_CUDA(cudaStreamSynchronize(rt->stream));
+        rt->check_device_error();
     });
 }
 

@@ -69,3 +69,31 @@ def test_muon_rejects_oversized(gpu_runtime):
     w = np.zeros((256, 256), np.float32)
     ok, _, _ = gpu_runtime.execute_muon(w, w, w, 0.02)
     assert not ok and "Newton-Schulz limit" in gpu_runtime.last_error
+
+
+@pytest.mark.parametrize("shape", [(48, 48), (96, 48), (48, 96), (17, 33), (128, 128), (128, 64)])
+def test_muon_tensor_cores_match_cuda_cores_and_oracle(oracle, shape):
+    """bf16 Muon: the tcgen05 Newton-Schulz kernel (kind::f16, FP32 TMEM
+    accumulators; the default for matrices up to 128 x 128) against the
+    CUDA-core kernel (forced through the GEMM engine switch) and the oracle.
+    Both engines round the same operands to bf16 and accumulate in FP32, in
+    different orders, so they agree far more closely than the bf16 bound."""
+    rng = np.random.default_rng(shape[0] * 31 + shape[1])
+    w = rng.normal(0, 0.02, shape).astype(np.float32)
+    g = rng.normal(0, 1e-3, shape).astype(np.float32)
+    buf = rng.normal(0, 1e-3, shape).astype(np.float32)
+    outs = {}
+    for backend in (0, 1):
+        rt = hx.Runtime()
+        assert rt.initialize(0) and rt.set_gemm_backend(backend)
+        ok, wn, bn = rt.execute_muon(w, g, buf, 0.02, bf16_inputs=True)
+        assert ok, rt.last_error
+        outs[backend] = (wn, bn)
+        rt.close()
+    rw, rb = oracle.muon(w, g, buf, 0.02, bf16_inputs=True)
+    upd = {k: (w - v[0]).astype(np.float64) for k, v in outs.items()}
+    rupd = (w - rw).astype(np.float64)
+    assert np.array_equal(outs[0][1], rb) and np.array_equal(outs[1][1], rb)
+    assert rel_err(upd[0], rupd) <= 2e-2, rel_err(upd[0], rupd)
+    assert rel_err(upd[0], upd[1]) <= 2e-2, rel_err(upd[0], upd[1])
+    assert np.max(np.abs(outs[0][0] - rw)) <= 1e-2
