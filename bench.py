@@ -329,8 +329,16 @@ def run_lm(name, K, W, world=1, rank=0, local=0, global_batch=None, profile_step
     def ids(step):
         return trainer.shard(data.lm_tokens(SEED, GB, T, V, step=step))
 
+    # Each step's ids are staged (device to device) into one static buffer
+    # that the captured step graph reads, as a graph-replaying training loop
+    # does.
     dev_tokens = [torch.from_numpy(ids(s).astype(np.int32)).cuda() for s in range(W + K)]
+    tok_static = torch.empty_like(dev_tokens[0])
     torch.cuda.synchronize()
+
+    def device_step(i):
+        tok_static.copy_(dev_tokens[i], non_blocking=True)
+        return trainer.step(tok_static)
 
     def barrier():
         if world > 1:
@@ -344,7 +352,7 @@ def run_lm(name, K, W, world=1, rank=0, local=0, global_batch=None, profile_step
         return float(t.item())
 
     for s in range(W):
-        trainer.step(dev_tokens[s])
+        device_step(s)
     barrier()
     sampler = ClockSampler(physical_gpu(local)) if (clocks and rank == 0) else None
     launches0 = rt.metrics().kernel_launches
@@ -352,7 +360,7 @@ def run_lm(name, K, W, world=1, rank=0, local=0, global_batch=None, profile_step
     barrier()
     e0.record(stream)
     for s in range(K):
-        trainer.step(dev_tokens[W + s])
+        device_step(W + s)
     e1.record(stream)
     barrier()
     t_ms = tmax(e0.elapsed_time(e1))
@@ -367,7 +375,7 @@ def run_lm(name, K, W, world=1, rank=0, local=0, global_batch=None, profile_step
         p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         p0.record(stream)
         for s in range(profile_steps):
-            trainer.step(dev_tokens[s % (W + K)])
+            device_step(s % (W + K))
         p1.record(stream)
         barrier()
         p_ms = p0.elapsed_time(p1)

@@ -21,19 +21,23 @@ struct GraphCache {
         uint64_t kernels;  // kernel launches the graph replays
     };
     std::map<Key, Entry> execs;
+    std::map<Key, int> seen;     // keys run eagerly once, not yet captured
     uint64_t epoch = 0;          // the runtime's graph_epoch when the cached graphs were captured
     bool capture_failed = false; // a capture failed once: run eagerly from then on
     ~GraphCache() { clear(); }
     void clear() {
         for (auto& kv : execs) cudaGraphExecDestroy(kv.second.exec);
         execs.clear();
+        seen.clear();
     }
 };
 
-// Runs the work `enqueue` puts on the runtime stream: eagerly the first time
-// `key` is seen (this also sizes the runtime workspace), from a CUDA graph
-// captured right after that eager run on every later call.  Graphs of an
-// older runtime graph epoch are dropped.  A stream that cannot be captured
+// Runs the work `enqueue` puts on the runtime stream: eagerly the first two
+// times `key` is seen (the first run also sizes the runtime workspace), with
+// a CUDA graph captured right after the second eager run and replayed on
+// every later call.  A caller whose pointers change on every call therefore
+// never pays for a capture.  Graphs of an older runtime graph epoch are
+// dropped.  A stream that cannot be captured
 // (the legacy default stream), or a capture that fails, leaves the work to
 // run eagerly; the eager run has already done this call's work.
 // A plan keeps at most this many captured graphs (the MLP driver's cyclic
@@ -53,8 +57,11 @@ void run_cached(hx_runtime* rt, GraphCache& c, const GraphCache::Key& key, F&& e
         rt->metrics.kernel_launches += it->second.kernels;
         return;
     }
-    enqueue();  // eager first run
+    enqueue();  // eager run
     if (c.capture_failed) return;
+    if (c.seen.size() >= 4 * kGraphCacheMax) c.seen.clear();
+    if (c.seen.emplace(key, 1).second) return;  // first sighting: no capture yet
+    c.seen.erase(key);
     if (c.epoch != rt->graph_epoch) {
         c.clear();
         c.epoch = rt->graph_epoch;
