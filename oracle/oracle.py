@@ -15,6 +15,7 @@ from __future__ import annotations
 import ctypes as C
 import os
 import subprocess
+from typing import Optional
 from dataclasses import dataclass
 
 import numpy as np
@@ -47,10 +48,12 @@ class LmConfig(C.Structure):
         return LmConfig(V, T, D, F, L, H, eps, int(bool(learned_position)))
 
 
-def build(quiet: bool = True) -> None:
-    """Build the checker libraries with oracle/Makefile (reference part only
-    when the HexaTrain tree is present)."""
-    out = subprocess.run(["make", "-s", "-C", HERE, "all"], capture_output=True, text=True)
+def build(quiet: bool = True, reference_tree: Optional[str] = None) -> None:
+    """Build the checker libraries with oracle/Makefile (the reference part
+    only when the HexaTrain tree is given, here or by the environment
+    variable HEXATRAIN_REFERENCE)."""
+    ref = reference_tree or os.environ.get("HEXATRAIN_REFERENCE", "")
+    out = subprocess.run(["make", "-s", "-C", HERE, "all", f"REF={ref}"], capture_output=True, text=True)
     if out.returncode != 0:
         raise RuntimeError("oracle build failed:\n" + out.stdout + out.stderr)
     if not quiet:
@@ -519,3 +522,46 @@ def reference_checkpoint_available() -> bool:
 
 def reference_available() -> bool:
     return os.path.exists(REF_SO)
+
+
+REF_DRIVER_SO = os.path.join(HERE, "_ref", "libhexaref_driver.so")
+
+
+class ReferenceDriver:
+    """The reference's own experiment drivers (trainFullStep for the MLP
+    modes, languageModelAdam for the LM modes), compiled with the product's
+    Runtime adapter in place of the stub/QAIRT runtime
+    (oracle/_ref/libhexaref_driver.so).  run_mode returns the driver's
+    KEY=VALUE report as a dict plus the raw text."""
+
+    def __init__(self, path: str = REF_DRIVER_SO):
+        if not os.path.exists(path):
+            raise FileNotFoundError(path)
+        self.lib = C.CDLL(path)
+        self.lib.hxd_run_mode.restype = C.c_long
+        self.lib.hxd_run_mode.argtypes = [C.c_int] * 10 + [C.c_float, C.c_ulonglong, C.c_int, C.c_int,
+                                                           C.c_char_p, C.c_size_t]
+
+    def run_mode(self, mode, batch=8, dimension=128, hidden=128, output=64, steps=100, epochs=0,
+                 sample_count=512, measured_steps=0, correctness_interval=0, learning_rate=0.1,
+                 seed=20260710, benchmark=False, feed_forward=32):
+        cap = 1 << 16
+        while True:
+            buf = C.create_string_buffer(cap)
+            n = self.lib.hxd_run_mode(mode, batch, dimension, hidden, output, steps, epochs, sample_count,
+                                      measured_steps, correctness_interval, learning_rate, seed, int(benchmark),
+                                      feed_forward, buf, cap)
+            if n < cap:
+                break
+            cap = int(n) + 1
+        text = buf.value.decode(errors="replace")
+        kv = {}
+        for line in text.splitlines():
+            if "=" in line:
+                k, v = line.split("=", 1)
+                kv.setdefault(k, v)
+        return kv, text
+
+
+def reference_driver_available() -> bool:
+    return os.path.exists(REF_DRIVER_SO)
