@@ -10,10 +10,13 @@
 //   5. dH = dP W2^T        epilogue: dZ1 = (H > 0) ? dH : 0   (pre-update W2)
 //   6. dW1 = X^T dZ1       epilogue: W1_next = W1 - lr*dW1
 // The whole sequence is captured once per distinct set of bound pointers into
-// a CUDA graph and replayed, so a step costs one graph launch.
+// a CUDA graph and replayed, so a step costs one graph launch.  Small shapes
+// (the reference's 8/128/128/64 and 32/256/256/128) run instead as one
+// kernel on one cluster of CTAs (mlp_fused.cuh).
 #include <cmath>
 
 #include "gemm.cuh"
+#include "mlp_fused.cuh"
 #include "plans.cuh"
 
 namespace hx {
@@ -89,9 +92,51 @@ struct MlpBinding {
     float lr;
 };
 
+// Whether the fused MLP step can run as a 16-CTA cluster on this device (a
+// non-portable cluster size: opted in per kernel, then checked by the
+// occupancy query); sets the kernels' shared-memory limits either way.
+bool mlp_fused_cluster16(hx_runtime* rt)
+{
+    static int answer[64] = {};  // per device: 0 unknown, 1 yes, 2 no
+    int& a = answer[rt->device & 63];
+    if (a == 0) {
+        HX_CUDA(cudaFuncSetAttribute(mlp_fused_step_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)kMlpFusedSmemBytes));
+        a = 2;
+        if (cudaFuncSetAttribute(mlp_fused_step_kernel<16>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) ==
+                cudaSuccess &&
+            cudaFuncSetAttribute(mlp_fused_step_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)kMlpFusedSmemBytes) == cudaSuccess) {
+            cudaLaunchConfig_t cfg = {};
+            cfg.gridDim = dim3(16);
+            cfg.blockDim = dim3(kMlpFusedThreads);
+            cfg.dynamicSmemBytes = kMlpFusedSmemBytes;
+            int clusters = 0;
+            if (cudaOccupancyMaxActiveClusters(&clusters, mlp_fused_step_kernel<16>, &cfg) == cudaSuccess &&
+                clusters >= 1)
+                a = 1;
+        }
+        (void)cudaGetLastError();
+    }
+    return a == 1;
+}
+
 void mlp_enqueue(hx_runtime* rt, const MlpPlan& pl, const MlpBinding& b)
 {
     const int B = pl.B, I = pl.I, H = pl.H, O = pl.O;
+    if (rt->gemm_backend == HX_GEMM_AUTO && mlp_fused_eligible(pl.B, pl.I, pl.H, pl.O)) {
+        // the whole step in one cluster launch (small shapes)
+        ProfScope prof(rt, kTagGemm, 2.0 * B * (2.0 * I * H + 3.0 * H * O),
+                       4.0 * (2.0 * (double(I) * H + double(H) * O) + double(B) * I + double(B) * O));
+        const MlpFusedArgs fa{b.x, b.y, b.w1, b.w2, b.loss, b.w1n, b.w2n, b.h, b.p, b.e, b.dp, b.dw2, b.dh, b.dz1,
+                              b.dw1, b.mask, pl.arena.at<double>(pl.mse_part), b.lr, B, I, H, O};
+        if (mlp_fused_cluster16(rt))
+            mlp_fused_step_kernel<16><<<16, kMlpFusedThreads, kMlpFusedSmemBytes, rt->stream>>>(fa);
+        else
+            mlp_fused_step_kernel<8><<<8, kMlpFusedThreads, kMlpFusedSmemBytes, rt->stream>>>(fa);
+        HX_LAUNCHED(rt);
+        return;
+    }
     const float s = 2.0f / float(B * O);
     gemm<false, false>(rt, B, H, I, b.x, I, b.w1, H, EpiRelu{b.h, b.mask, H});
     gemm<false, false>(rt, B, O, H, b.h, H, b.w2, O, EpiError{b.y, b.p, b.e, b.dp, s, O});
