@@ -8,6 +8,23 @@
 
 namespace hx {
 
+// Sums the split-K partials in split order and applies the epilogue: four
+// elements per thread with 16-byte loads when the rows allow it.
+template <class Epi>
+void launch_splitk_reduce(hx_runtime* rt, int M, int N, int splits, const float* ws, Epi epi)
+{
+    const long total = (long)M * N;
+    const int threads = 256;
+    if (N % 4 == 0 && (reinterpret_cast<uintptr_t>(ws) & 15) == 0) {
+        const int blocks = (int)std::min<long>((total / 4 + threads - 1) / threads, 4L * rt->sm_count * 8);
+        splitk_reduce4_kernel<Epi><<<blocks, threads, 0, rt->stream>>>(M, N, splits, ws, epi);
+    } else {
+        const int blocks = (int)std::min<long>((total + threads - 1) / threads, 4L * rt->sm_count * 8);
+        splitk_reduce_kernel<Epi><<<blocks, threads, 0, rt->stream>>>(M, N, splits, ws, epi);
+    }
+    HX_LAUNCHED(rt);
+}
+
 template <int BM, int BN, int BK, int TX, int TY, bool AT, bool BT, class Epi>
 void launch_simt(hx_runtime* rt, int M, int N, int K, const float* A, long lda, const float* B, long ldb,
                  Epi epi)
@@ -37,11 +54,7 @@ void launch_simt(hx_runtime* rt, int M, int N, int K, const float* A, long lda, 
         gemm_simt_kernel<S, BM, BN, BK, TX, TY, AT, BT, Epi>
             <<<grid, S::kThreads, 0, rt->stream>>>(M, N, K, A, lda, B, ldb, chunk, epi, ws);
         HX_LAUNCHED(rt);
-        const long total = (long)M * N;
-        const int threads = 256;
-        const int blocks = (int)std::min<long>((total + threads - 1) / threads, 4L * rt->sm_count * 8);
-        splitk_reduce_kernel<Epi><<<blocks, threads, 0, rt->stream>>>(M, N, splits, ws, epi);
-        HX_LAUNCHED(rt);
+        launch_splitk_reduce(rt, M, N, splits, ws, epi);
     }
 }
 
@@ -157,13 +170,7 @@ void launch_tc(hx_runtime* rt, int M, int N, int K, const float* A, long lda, co
                    : launch_tc_kernel<A_MN, B_MN, false, false>(rt->stream, pairs, mx, mw, mw_lo, mc, g, epi, ws, err);
     HX_CUDA(rc);
     ++rt->metrics.kernel_launches;
-    if (g.splits > 1) {
-        const long total = (long)M * N;
-        const int threads = 256;
-        const int blocks = (int)std::min<long>((total + threads - 1) / threads, 4L * rt->sm_count * 8);
-        splitk_reduce_kernel<Epi><<<blocks, threads, 0, rt->stream>>>(M, N, g.splits, ws, epi);
-        HX_LAUNCHED(rt);
-    }
+    if (g.splits > 1) launch_splitk_reduce(rt, M, N, g.splits, ws, epi);
 }
 
 // C = op(A) op(B) with the epilogue applied to every element.  `bs`, when

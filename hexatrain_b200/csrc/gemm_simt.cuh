@@ -167,6 +167,29 @@ __global__ void splitk_reduce_kernel(int M, int N, int splits, const float* __re
     }
 }
 
+// The same for N % 4 == 0 with 16-byte aligned partials: each thread sums
+// four consecutive elements of a row with 16-byte loads, in the same split
+// order, so the results are bit-identical to splitk_reduce_kernel's.
+template <class Epi>
+__global__ void splitk_reduce4_kernel(int M, int N, int splits, const float* __restrict__ partial, Epi epi)
+{
+    const long total4 = (long)M * N / 4, stride4 = (long)M * N / 4;
+    const float4* p4 = reinterpret_cast<const float4*>(partial);
+    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total4; i += (long)gridDim.x * blockDim.x) {
+        float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int z = 0; z < splits; ++z) {
+            const float4 v = __ldcs(p4 + (long)z * stride4 + i);
+            s.x += v.x; s.y += v.y; s.z += v.z; s.w += v.w;
+        }
+        const long e = 4 * i;
+        const int m = int(e / N), n = int(e % N);
+        epi(m, n, s.x);
+        epi(m, n + 1, s.y);
+        epi(m, n + 2, s.z);
+        epi(m, n + 3, s.w);
+    }
+}
+
 // ---- epilogues -----------------------------------------------------------
 // Each epilogue is split into prefetch(m, n) -- the one global value it reads
 // for element (m, n), 0 if none -- and finish(m, n, v, pre).  The tensor-core

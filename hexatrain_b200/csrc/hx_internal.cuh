@@ -147,6 +147,10 @@ struct hx_runtime {
     std::unique_ptr<hx::AdamPlan> adam;
     std::unique_ptr<hx::MomentumPlan> momentum;
     hx::DeviceBuffer scratch;  // generic device workspace (grows on demand)
+    // Second stream for work that runs beside the main stream's (the weight
+    // gradients of the LM backward) and its own workspace.
+    cudaStream_t side_stream = nullptr;
+    hx::DeviceBuffer side_scratch;
     hx::DeviceBuffer err_flag; // device-side error word of bounded waits
     hx::Profiler prof;
     int gemm_backend = 0;      // HX_GEMM_AUTO / HX_GEMM_CUDA_CORES / HX_GEMM_TENSOR_CORES
@@ -159,13 +163,15 @@ struct hx_runtime {
     // address) and an engine switch.  Cached graphs of an older epoch are
     // dropped before their next replay.
     uint64_t graph_epoch = 0;
-    // Grow-only device workspace for split-K partials and reductions.
+    // Grow-only device workspace for split-K partials and reductions, one
+    // per stream so that launches on the two streams never share one.
     float* workspace(size_t bytes) {
-        if (scratch.bytes < bytes) {
-            scratch.allocate(bytes);
+        hx::DeviceBuffer& b = (side_stream && stream == side_stream) ? side_scratch : scratch;
+        if (b.bytes < bytes) {
+            b.allocate(bytes);
             ++graph_epoch;
         }
-        return scratch.as<float>();
+        return b.as<float>();
     }
     int* device_error() {
         if (!err_flag.ptr) {

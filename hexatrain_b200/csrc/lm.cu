@@ -81,6 +81,9 @@ struct LmPlan {
     bool state_ready = false;
     // Captured step graphs (train step, forward+backward, optimizer step).
     GraphCache graphs;
+    // Fork/join events of the backward's second stream (weight gradients).
+    static constexpr int kForkEvents = 64;
+    cudaEvent_t fork_ev[kForkEvents] = {};
     // Per-step optimizer scalars: host values go through a ring of pinned
     // slots into step_scalars (device), which the optimizer kernels read.  A
     // slot is rewritten only after the copy that last read it has run.
@@ -92,6 +95,8 @@ struct LmPlan {
     unsigned ring_next = 0;
     ~LmPlan() {
         graphs.clear();
+        for (cudaEvent_t e : fork_ev)
+            if (e) cudaEventDestroy(e);
         for (cudaEvent_t e : ring_ev)
             if (e) cudaEventDestroy(e);
         if (ring) cudaFreeHost(ring);
@@ -285,6 +290,53 @@ __global__ void split_tf32_kernel(long n, const float* __restrict__ w, float* __
     }
 }
 
+// The backward's weight-gradient GEMMs run on the runtime's second stream,
+// beside the main stream's input-gradient GEMMs and attention: both kinds
+// are persistent or many-CTA kernels that fill the GPU, so each fills the
+// other's last, partial wave.  fork() lets the side stream start after the
+// main stream's work so far; join() makes the main stream wait for all side
+// work so far.  With the event profiler on, everything stays on the main
+// stream (the profile then times each launch alone).
+struct SideStream {
+    hx_runtime* rt;
+    LmPlan& p;
+    bool on;
+    int k = 0;
+    SideStream(hx_runtime* r, LmPlan& plan) : rt(r), p(plan), on(!r->prof.on && r->side_stream != nullptr) {}
+    // Events are reused cyclically: a wait takes the event's state when it is
+    // enqueued, so a later record of the same event does not affect it.
+    cudaEvent_t next() { return p.fork_ev[k++ % LmPlan::kForkEvents]; }
+    void fork() {
+        if (!on) return;
+        cudaEvent_t e = next();
+        HX_CUDA(cudaEventRecord(e, rt->stream));
+        HX_CUDA(cudaStreamWaitEvent(rt->side_stream, e, 0));
+    }
+    void join() {
+        if (!on) return;
+        cudaEvent_t e = next();
+        HX_CUDA(cudaEventRecord(e, rt->side_stream));
+        HX_CUDA(cudaStreamWaitEvent(rt->stream, e, 0));
+    }
+    // Runs f's launches on the side stream (on the main one when off).
+    template <class F>
+    void run(F&& f) {
+        if (!on) {
+            f();
+            return;
+        }
+        cudaStream_t main = rt->stream;
+        rt->stream = rt->side_stream;
+        try {
+            f();
+        } catch (...) {
+            rt->stream = main;
+            throw;
+        }
+        rt->stream = main;
+    }
+};
+
 void forward_backward(hx_runtime* rt, LmPlan& p, const float* W, float* G, float grad_scale, int mode = kFullStep)
 {
     const Arena& a = p.arena;
@@ -398,7 +450,9 @@ void forward_backward(hx_runtime* rt, LmPlan& p, const float* W, float* G, float
 
     // ---- backward ----
     const float* dl = logits;  // dlogits, in place
-    gemm<true, false>(rt, D, V, M, xL, D, dl, V, EpiStore{G + p.off_out, (long)V, 0, 0});
+    SideStream side(rt, p);
+    side.fork();
+    side.run([&] { gemm<true, false>(rt, D, V, M, xL, D, dl, V, EpiStore{G + p.off_out, (long)V, 0, 0}); });
     float* dout = a.at<float>(p.dout);
     gemm<false, true>(rt, M, D, V, dl, V, W + p.off_out, V, EpiStore{dout, (long)D, 0, 0}, wsplit(p.off_out));
     if (p.diag) copy_d2d(rt, a.at<float>(p.diag_dout), dout, sizeof(float) * size_t(M) * D);
@@ -430,24 +484,40 @@ void forward_backward(hx_runtime* rt, LmPlan& p, const float* W, float* G, float
         const LayerActs& A = p.la[li];
         const LayerOffsets& o = p.lo[li];
         const float* xin = a.at<float>(A.x);
-        gemm<true, false>(rt, F, D, M, a.at<float>(A.relu), F, dout, D, EpiStore{G + o.w2, (long)D, 0, 0});
+        side.fork();  // dout is ready
+        side.run([&] {
+            gemm<true, false>(rt, F, D, M, a.at<float>(A.relu), F, dout, D, EpiStore{G + o.w2, (long)D, 0, 0});
+        });
         gemm<false, true>(rt, M, F, D, dout, D, W + o.w2, D, EpiReluBackward{a.at<float>(A.relu), df1, nullptr, F},
                           wsplit(o.w2));
-        gemm<true, false>(rt, D, F, M, a.at<float>(A.n2), D, df1, F, EpiStore{G + o.w1, (long)F, 0, 0});
+        side.fork();  // df1 is ready
+        side.run([&] {
+            gemm<true, false>(rt, D, F, M, a.at<float>(A.n2), D, df1, F, EpiStore{G + o.w1, (long)F, 0, 0});
+        });
         gemm<false, true>(rt, M, D, F, df1, F, W + o.w1, F, EpiStore{dn, (long)D, 0, 0}, wsplit(o.w1));
         ProfScope plb2(rt, kTagLayerNorm, 12.0 * M * D, 4.0 * (4.0 * M * D + 2.0 * M));
         ln_bwd(dn, a.at<float>(A.r1), a.at<float>(A.mean2), a.at<float>(A.inv2), W + o.g2, dout, dr);
         plb2.end();
         column_reduce_kernel<<<(2 * D + 31) / 32, 32 * kColReduceWarps, 0, s>>>(p.ln_parts, D, part, G + o.g2, G + o.b2);
         HX_LAUNCHED(rt);
-        gemm<true, false>(rt, D, D, M, a.at<float>(A.ctx), D, dr, D, EpiStore{G + o.wo, (long)D, 0, 0});
+        side.fork();  // dr is ready
+        side.run([&] {
+            gemm<true, false>(rt, D, D, M, a.at<float>(A.ctx), D, dr, D, EpiStore{G + o.wo, (long)D, 0, 0});
+        });
         gemm<false, true>(rt, M, D, D, dr, D, W + o.wo, D, EpiStore{dc, (long)D, 0, 0}, wsplit(o.wo));
         HX_DH_DISPATCH(p.dh, attn_bwd_launch, rt, p, a.at<float>(A.qkv), dc, a.at<float>(A.rmax), a.at<float>(A.rsum),
                        dqkv);
-        gemm<true, false>(rt, D, 3 * D, M, a.at<float>(A.n1), D, dqkv, 3 * D,
-                          EpiStore{G + o.wq, (long)D, (int)D, (long)D * D});
+        side.fork();  // dqkv is ready
+        side.run([&] {
+            gemm<true, false>(rt, D, 3 * D, M, a.at<float>(A.n1), D, dqkv, 3 * D,
+                              EpiStore{G + o.wq, (long)D, (int)D, (long)D * D});
+        });
         gemm<false, true>(rt, M, D, 3 * D, dqkv, 3 * D, wqkv + size_t(li) * 3 * D * D, 3 * D, EpiStore{dn, (long)D, 0, 0},
                           qsplit(li));
+        // The side stream has read this layer's dout, df1, dr and dqkv before
+        // the main stream overwrites them (dout next, the rest in the layer
+        // below).
+        side.join();
         ProfScope plb1(rt, kTagLayerNorm, 12.0 * M * D, 4.0 * (4.0 * M * D + 2.0 * M));
         ln_bwd(dn, xin, a.at<float>(A.mean1), a.at<float>(A.inv1), W + o.g1, dr, dout);
         plb1.end();
@@ -475,6 +545,7 @@ void forward_backward(hx_runtime* rt, LmPlan& p, const float* W, float* G, float
         position_bwd_kernel<<<(unsigned)((long(T) * D + 31) / 32), 32 * kPosWarps, 0, s>>>(B, T, D, dout, G + p.off_pos);
         HX_LAUNCHED(rt);
     }
+    side.join();  // the output projection's gradient, when L = 0
 }
 
 // Host part of the optimizer step: this step's scalars, exactly as the
@@ -730,7 +801,10 @@ int hx_lm_prepare(hx_runtime* rt, const hx_lm_config* cfg, uint32_t batch, int d
         p.ln_rows = (p.M + p.ln_parts - 1) / p.ln_parts;
         p.ln_parts = (p.M + p.ln_rows - 1) / p.ln_rows;
         p.ln_part = a.reserve(f * size_t(p.ln_parts) * 2 * D);
-        p.emb_rows = 1024;  // short chunks: the most frequent tokens' CTAs bound the kernel
+        // Short chunks: the CTAs of the most frequent tokens bound the kernel
+        // (under Zipf ids most rows fall in the first token block), so the
+        // chunk shrinks with the row count, down to 64 rows.
+        p.emb_rows = std::max(64, std::min(1024, p.M / 64));
         p.emb_chunks = (p.M + p.emb_rows - 1) / p.emb_rows;
         p.emb_part = a.reserve(f * size_t(p.emb_chunks) * V * D);
         if (p.diag) {
@@ -795,6 +869,8 @@ int hx_lm_prepare(hx_runtime* rt, const hx_lm_config* cfg, uint32_t batch, int d
                                 cudaMemcpyHostToDevice, rt->stream));
         HX_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&p.ring), sizeof(LmStepScalars) * LmPlan::kRing,
                               cudaHostAllocDefault));
+        for (cudaEvent_t& e : p.fork_ev) HX_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+        if (!rt->side_stream) HX_CUDA(cudaStreamCreateWithFlags(&rt->side_stream, cudaStreamNonBlocking));
         for (cudaEvent_t& e : p.ring_ev) HX_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
         HX_CUDA(cudaStreamSynchronize(rt->stream));
         rt->lm = std::move(pp);

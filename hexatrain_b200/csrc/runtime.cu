@@ -17,6 +17,8 @@ hx_runtime::~hx_runtime() {
     adam.reset();
     momentum.reset();
     scratch.release();
+    side_scratch.release();
+    if (side_stream) cudaStreamDestroy(side_stream);
     if (own_stream) cudaStreamDestroy(own_stream);
 }
 
@@ -123,7 +125,7 @@ int hx_runtime_set_attention_backend(hx_runtime* rt, int backend) {
 int hx_runtime_metrics(const hx_runtime* rt, hx_metrics* out) {
     if (!rt || !out) return HX_ERR_ARGUMENT;
     *out = rt->metrics;
-    out->device_bytes = rt->scratch.bytes + hx::plan_device_bytes(rt);
+    out->device_bytes = rt->scratch.bytes + rt->side_scratch.bytes + hx::plan_device_bytes(rt);
     return HX_OK;
 }
 
