@@ -152,6 +152,10 @@ SIGNATURES = {
     "hx_lm_grad_buffer": (C.c_int, [C.c_void_p, C.POINTER(C.c_void_p), C.POINTER(C.c_size_t)]),
     "hx_lm_optimizer_step_device": (C.c_int, [C.c_void_p, C.c_uint32]),
     "hx_lm_loss_device": (C.c_int, [C.c_void_p, C.POINTER(C.c_void_p)]),
+    "hx_lm_grad_buckets": (C.c_int, [C.c_void_p, C.POINTER(C.c_size_t), C.POINTER(C.c_size_t), C.c_int,
+                                     C.POINTER(C.c_int)]),
+    "hx_lm_enable_bucket_events": (C.c_int, [C.c_void_p, C.c_int]),
+    "hx_lm_bucket_wait": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p]),
     "hx_adam_prepare": (C.c_int, [C.c_void_p, C.c_uint32]),
     "hx_adam_execute": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_float,
                                   C.c_float, C.c_float, C.c_float, C.POINTER(AdamOutputsC)]),

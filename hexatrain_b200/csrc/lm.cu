@@ -84,6 +84,10 @@ struct LmPlan {
     // Fork/join events of the backward's second stream (weight gradients).
     static constexpr int kForkEvents = 64;
     cudaEvent_t fork_ev[kForkEvents] = {};
+    // Gradient buckets in completion order and their events.
+    std::vector<std::pair<size_t, size_t>> buckets;  // [offset, count) in floats
+    std::vector<cudaEvent_t> bucket_ev;
+    bool bucket_events = false;
     // Per-step optimizer scalars: host values go through a ring of pinned
     // slots into step_scalars (device), which the optimizer kernels read.  A
     // slot is rewritten only after the copy that last read it has run.
@@ -96,6 +100,8 @@ struct LmPlan {
     ~LmPlan() {
         graphs.clear();
         for (cudaEvent_t e : fork_ev)
+            if (e) cudaEventDestroy(e);
+        for (cudaEvent_t e : bucket_ev)
             if (e) cudaEventDestroy(e);
         for (cudaEvent_t e : ring_ev)
             if (e) cudaEventDestroy(e);
@@ -337,6 +343,15 @@ struct SideStream {
     }
 };
 
+// Records bucket i's event on `stream` when bucket events are on; an external
+// event node when the stream is being captured, so that waits outside the
+// graph see each replay's record.
+void record_bucket(hx_runtime* rt, LmPlan& p, int i, cudaStream_t stream)
+{
+    if (!p.bucket_events) return;
+    HX_CUDA(cudaEventRecordWithFlags(p.bucket_ev[size_t(i)], stream, cudaEventRecordExternal));
+}
+
 void forward_backward(hx_runtime* rt, LmPlan& p, const float* W, float* G, float grad_scale, int mode = kFullStep)
 {
     const Arena& a = p.arena;
@@ -452,7 +467,10 @@ void forward_backward(hx_runtime* rt, LmPlan& p, const float* W, float* G, float
     const float* dl = logits;  // dlogits, in place
     SideStream side(rt, p);
     side.fork();
-    side.run([&] { gemm<true, false>(rt, D, V, M, xL, D, dl, V, EpiStore{G + p.off_out, (long)V, 0, 0}); });
+    side.run([&] {
+        gemm<true, false>(rt, D, V, M, xL, D, dl, V, EpiStore{G + p.off_out, (long)V, 0, 0});
+        record_bucket(rt, p, 0, rt->stream);  // the output projection and the loss slot
+    });
     float* dout = a.at<float>(p.dout);
     gemm<false, true>(rt, M, D, V, dl, V, W + p.off_out, V, EpiStore{dout, (long)D, 0, 0}, wsplit(p.off_out));
     if (p.diag) copy_d2d(rt, a.at<float>(p.diag_dout), dout, sizeof(float) * size_t(M) * D);
@@ -523,6 +541,7 @@ void forward_backward(hx_runtime* rt, LmPlan& p, const float* W, float* G, float
         plb1.end();
         column_reduce_kernel<<<(2 * D + 31) / 32, 32 * kColReduceWarps, 0, s>>>(p.ln_parts, D, part, G + o.g1, G + o.b1);
         HX_LAUNCHED(rt);
+        record_bucket(rt, p, int(p.L - li), s);  // this layer's ten tensors (its side work was joined above)
         if (p.diag) copy_d2d(rt, a.at<float>(p.diag_lig) + size_t(li) * M * D, dout, sizeof(float) * size_t(M) * D);
     }
     // embedding gradients
@@ -546,6 +565,7 @@ void forward_backward(hx_runtime* rt, LmPlan& p, const float* W, float* G, float
         HX_LAUNCHED(rt);
     }
     side.join();  // the output projection's gradient, when L = 0
+    record_bucket(rt, p, int(p.L + 1), s);  // token (and position) embedding
 }
 
 // Host part of the optimizer step: this step's scalars, exactly as the
@@ -870,6 +890,11 @@ int hx_lm_prepare(hx_runtime* rt, const hx_lm_config* cfg, uint32_t batch, int d
         HX_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&p.ring), sizeof(LmStepScalars) * LmPlan::kRing,
                               cudaHostAllocDefault));
         for (cudaEvent_t& e : p.fork_ev) HX_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+        p.buckets.push_back({p.off_out, D * V + 1});  // output projection + the scaled loss slot G[P]
+        for (uint32_t l = p.L; l-- > 0;) p.buckets.push_back({p.lo[l].g1, 4 * D * D + 4 * D + 2 * D * F});
+        p.buckets.push_back({0, p.L ? p.lo[0].g1 : p.off_out});
+        p.bucket_ev.resize(p.buckets.size());
+        for (cudaEvent_t& e : p.bucket_ev) HX_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
         if (!rt->side_stream) HX_CUDA(cudaStreamCreateWithFlags(&rt->side_stream, cudaStreamNonBlocking));
         for (cudaEvent_t& e : p.ring_ev) HX_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
         HX_CUDA(cudaStreamSynchronize(rt->stream));
@@ -1216,6 +1241,36 @@ int hx_lm_optimizer_step_device(hx_runtime* rt, uint32_t step) {
         require(step >= 1, HX_ERR_ARGUMENT, "optimizer step is 1-based");
         upload_step_scalars(rt, p, step);
         lm_run(rt, p, lm_key(kGraphOptimizer, nullptr, 0.f), [&] { optimizer_enqueue(rt, p); });
+    });
+}
+
+int hx_lm_grad_buckets(hx_runtime* rt, size_t* offsets, size_t* counts, int capacity, int* count) {
+    return hx_guard(rt, [&] {
+        LmPlan& p = need_lm(rt);
+        require(count && capacity >= 0 && (capacity == 0 || (offsets && counts)), HX_ERR_ARGUMENT,
+                "grad_buckets: null output");
+        *count = int(p.buckets.size());
+        for (int i = 0; i < capacity && i < int(p.buckets.size()); ++i) {
+            offsets[i] = p.buckets[size_t(i)].first;
+            counts[i] = p.buckets[size_t(i)].second;
+        }
+    });
+}
+
+int hx_lm_enable_bucket_events(hx_runtime* rt, int enable) {
+    return hx_guard(rt, [&] {
+        LmPlan& p = need_lm(rt);
+        if (p.bucket_events != (enable != 0)) p.graphs.clear();
+        p.bucket_events = enable != 0;
+    });
+}
+
+int hx_lm_bucket_wait(hx_runtime* rt, int bucket, void* stream) {
+    return hx_guard(rt, [&] {
+        LmPlan& p = need_lm(rt);
+        require(p.bucket_events, HX_ERR_STATE, "bucket_wait: bucket events are not enabled");
+        require(bucket >= 0 && bucket < int(p.buckets.size()), HX_ERR_ARGUMENT, "bucket_wait: bucket out of range");
+        HX_CUDA(cudaStreamWaitEvent(static_cast<cudaStream_t>(stream), p.bucket_ev[size_t(bucket)], 0));
     });
 }
 

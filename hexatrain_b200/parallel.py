@@ -12,11 +12,19 @@ bit-identical.
 
 The backend is injectable: ``GpuLmBackend`` drives libhexatrain_b200.so on
 one device (torch tensors are only views of its buffers, so NCCL reduces
-them in place on the runtime's stream); tests use a CPU stand-in with the
-same three methods.
+them in place); tests use a CPU stand-in with the same methods.
+
+Overlap: a backend that exposes gradient buckets (``buckets()``, the
+[P+1] buffer's contiguous pieces in the order the backward finishes them)
+has each bucket all-reduced as soon as it is final, on a communication
+stream that waits for that bucket's event (``comm(i)``), while the backward
+continues on the compute streams; ``join_comm()`` then makes the compute
+stream wait for every reduction before the optimizer step.  The buckets'
+all-reduces run in the same order on every rank.
 """
 from __future__ import annotations
 
+import contextlib
 from typing import Optional, Protocol
 
 import numpy as np
@@ -39,12 +47,17 @@ def shard_bounds(global_batch: int, rank: int, world: int) -> tuple[int, int]:
 
 
 class DataParallelLmTrainer:
-    def __init__(self, backend: LmBackend, global_batch: int, rank: int = 0, world: int = 1, group=None):
+    def __init__(self, backend: LmBackend, global_batch: int, rank: int = 0, world: int = 1, group=None,
+                 overlap: bool = True):
         self.backend = backend
         self.global_batch = global_batch
         self.rank, self.world, self.group = rank, world, group
         self.lo, self.hi = shard_bounds(global_batch, rank, world)
         self.step_count = 0
+        # bucketed all-reduce overlapped with the backward, when the backend can
+        self.overlap = bool(overlap and world > 1 and hasattr(backend, "buckets"))
+        if self.overlap and hasattr(backend, "enable_buckets"):
+            backend.enable_buckets()
 
     def shard(self, global_tokens: np.ndarray) -> np.ndarray:
         """This rank's rows of a [global_batch, T+1] token array."""
@@ -60,7 +73,13 @@ class DataParallelLmTrainer:
         grads = self.backend.grad_buffer()
         if self.world > 1:
             import torch.distributed as dist
-            dist.all_reduce(grads, op=dist.ReduceOp.SUM, group=self.group)
+            if self.overlap:
+                for i, (off, cnt) in enumerate(self.backend.buckets()):
+                    with self.backend.comm(i):
+                        dist.all_reduce(grads[off:off + cnt], op=dist.ReduceOp.SUM, group=self.group)
+                self.backend.join_comm()
+            else:
+                dist.all_reduce(grads, op=dist.ReduceOp.SUM, group=self.group)
         self.backend.optimizer_step(self.step_count)
         return grads
 
@@ -100,6 +119,27 @@ class GpuLmBackend:
 
     def local_mean_loss(self):
         return self._loss
+
+    # ---- gradient buckets (overlapped all-reduce) ----
+    def enable_buckets(self) -> None:
+        if not self.rt.lm_enable_bucket_events(True):
+            raise RuntimeError(self.rt.last_error)
+        self._buckets = self.rt.lm_grad_buckets()
+        self._comm = self._torch.cuda.Stream()
+
+    def buckets(self):
+        return self._buckets
+
+    @contextlib.contextmanager
+    def comm(self, i: int):
+        """The communication stream, after bucket i's gradients are final."""
+        if not self.rt.lm_bucket_wait(i, self._comm.cuda_stream):
+            raise RuntimeError(self.rt.last_error)
+        with self._torch.cuda.stream(self._comm):
+            yield
+
+    def join_comm(self) -> None:
+        self._torch.cuda.current_stream().wait_stream(self._comm)
 
 
 def _device_view(ptr: int, count: int):

@@ -604,6 +604,27 @@ class Runtime:
             raise RuntimeError(self.last_error)
         return int(p.value), int(n.value)
 
+    def lm_grad_buckets(self):
+        """[(offset, count)] of the gradient buffer's buckets, in the order
+        the backward finishes them (hx_lm_grad_buckets)."""
+        n = C.c_int()
+        if not self._ok(self._lib.hx_lm_grad_buckets(self._rt, None, None, 0, C.byref(n))):
+            raise RuntimeError(self.last_error)
+        off = (C.c_size_t * n.value)()
+        cnt = (C.c_size_t * n.value)()
+        if not self._ok(self._lib.hx_lm_grad_buckets(self._rt, off, cnt, n.value, C.byref(n))):
+            raise RuntimeError(self.last_error)
+        return [(int(off[i]), int(cnt[i])) for i in range(n.value)]
+
+    def lm_enable_bucket_events(self, enable: bool) -> bool:
+        return self._need() and self._ok(self._lib.hx_lm_enable_bucket_events(self._rt, int(bool(enable))))
+
+    def lm_bucket_wait(self, bucket: int, stream_handle: int) -> bool:
+        """Make cudaStream_t `stream_handle` wait for bucket `bucket` of the
+        most recent forward_backward (hx_lm_bucket_wait)."""
+        return self._need() and self._ok(self._lib.hx_lm_bucket_wait(self._rt, int(bucket),
+                                                                     C.c_void_p(stream_handle or None)))
+
     def lm_optimizer_step_device(self, step: int) -> bool:
         return self._need() and self._ok(self._lib.hx_lm_optimizer_step_device(self._rt, step))
 

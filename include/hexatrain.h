@@ -345,6 +345,25 @@ int hx_lm_optimizer_step_device(hx_runtime* rt, uint32_t step);
 /* Device pointer to the mean loss of the last step (1 float). */
 int hx_lm_loss_device(hx_runtime* rt, float** loss);
 
+/* Gradient buckets for overlapping the data-parallel all-reduce with the
+ * backward pass (no counterpart in the reference, which averages on the
+ * host, qnn/qnn_transformer_training.cpp:7322-7330).  The [P+1] gradient
+ * buffer splits into contiguous buckets in the order the backward finishes
+ * them: the output projection with the loss slot, each layer's ten tensors
+ * from the last layer down, then the token (and position) embedding.
+ * hx_lm_grad_buckets writes up to `capacity` (offset, count) pairs in that
+ * order and their number.  With bucket events enabled, every
+ * hx_lm_forward_backward_device records one CUDA event per bucket when the
+ * bucket's gradients are final (inside a captured step graph too), and
+ * hx_lm_bucket_wait(rt, i, stream) makes `stream` (a cudaStream_t) wait for
+ * bucket i of the most recent forward_backward: a communication stream can
+ * then reduce bucket i while the backward continues.  The caller must make
+ * the runtime's stream wait for that communication stream before
+ * hx_lm_optimizer_step_device. */
+int hx_lm_grad_buckets(hx_runtime* rt, size_t* offsets, size_t* counts, int capacity, int* count);
+int hx_lm_enable_bucket_events(hx_runtime* rt, int enable);
+int hx_lm_bucket_wait(hx_runtime* rt, int bucket, void* stream);
+
 /* ---- elementwise Adam ----------------------------------------------------- */
 /* Graph phonelm_adam_optimizer (qnn/qnn_runtime_transformer.inc:926-1109):
  *   g'=g*gradient_scale; m'=b1*m+(1-b1)*g'; v'=b2*v+(1-b2)*g'^2;

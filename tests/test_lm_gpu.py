@@ -250,3 +250,49 @@ def test_lm_gemm_engines_agree_with_oracle(oracle, backend):
     assert abs(out.loss - loss) <= TOL * abs(loss)
     check_grads(cfg, out.gradients, g)
     rt.close()
+
+
+def test_gradient_buckets_and_their_events(gpu_runtime):
+    """hx_lm_grad_buckets tiles the [P+1] buffer in completion order; with
+    bucket events on, a stream that waited for every bucket sees the same
+    gradients as the plain device step, also on graph replays (the events
+    are external nodes of the captured backward)."""
+    import torch
+    V, T, D, F, L, H, B = 64, 16, 32, 64, 2, 4, 4
+    cfg = hx.LmConfig(V, T, D, F, L, H, learned_position=True)
+    p0 = cfg.init_normal(12, 0.02)
+    P = cfg.parameter_count()
+    ref = hx.Runtime()
+    assert ref.initialize(0) and ref.prepare_lm(cfg, B) and ref.lm_state_upload(p0)
+    rt = gpu_runtime
+    assert rt.prepare_lm(cfg, B) and rt.lm_state_upload(p0), rt.last_error
+    buckets = rt.lm_grad_buckets()
+    assert len(buckets) == L + 2
+    reg = {n: (o, int(np.prod(sh))) for n, o, sh in cfg.registry()}
+    assert buckets[0] == (reg["output_projection"][0], D * V + 1)
+    assert buckets[1][0] == reg["layer_001.norm1_gamma"][0] and buckets[-1] == (0, reg["layer_000.norm1_gamma"][0])
+    assert sum(n for _, n in buckets) == P + 1
+    assert not rt.lm_bucket_wait(0, 0) and "not enabled" in rt.last_error
+    assert rt.lm_enable_bucket_events(True), rt.last_error
+    comm = torch.cuda.Stream()
+    tok = torch.empty((B, T + 1), dtype=torch.int32, device="cuda")
+    for step in range(3):
+        toks = data.lm_tokens(12, B, T, V, step=step)
+        tok.copy_(torch.from_numpy(toks.astype(np.int32)))
+        torch.cuda.synchronize()
+        for r in (rt, ref):
+            assert r.lm_forward_backward_device(tok.data_ptr(), 1.0 / B), r.last_error
+        gp, n = rt.lm_grad_buffer()
+        for i in range(len(buckets)):
+            assert rt.lm_bucket_wait(i, comm.cuda_stream), rt.last_error
+        comm.synchronize()  # returns once every bucket's event has fired
+        assert rt.synchronize() and ref.synchronize()
+        from hexatrain_b200.parallel import _device_view
+        got = _device_view(gp, n).cpu().numpy()
+        rp, rn = ref.lm_grad_buffer()
+        want = _device_view(rp, rn).cpu().numpy()
+        assert np.array_equal(got, want), step
+        for r in (rt, ref):
+            assert r.lm_optimizer_step_device(step + 1), r.last_error
+    assert rt.lm_enable_bucket_events(False)
+    ref.close()

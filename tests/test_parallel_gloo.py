@@ -56,20 +56,47 @@ class OracleBackend:
         self.m, self.v, _, _, self.params = self.o.adam(self.params, g, self.m, self.v, LR, c1, c2)
 
 
+class BucketedOracleBackend(OracleBackend):
+    """The same, exposing the gradient buckets the GPU backend reduces one by
+    one (output projection + loss slot, layers from the last, embeddings);
+    on CPU the communication stream is the current thread."""
+
+    def buckets(self):
+        import hexatrain_b200 as hx
+        reg = {n: (o, int(np.prod(sh))) for n, o, sh in
+               hx.LmConfig(V, T, D, F, L, H, learned_position=True).registry()}
+        out_off = reg["output_projection"][0]
+        b = [(out_off, self.P + 1 - out_off)]
+        for l in reversed(range(L)):
+            first = reg[f"layer_{l:03d}.norm1_gamma"][0]
+            last_off, last_n = reg[f"layer_{l:03d}.ffn_w2"]
+            b.append((first, last_off + last_n - first))
+        b.append((0, reg["layer_000.norm1_gamma"][0]))
+        return b
+
+    def comm(self, i):
+        import contextlib
+        return contextlib.nullcontext()
+
+    def join_comm(self):
+        pass
+
+
 def _params0():
     import hexatrain_b200 as hx
     return hx.LmConfig(V, T, D, F, L, H, learned_position=True).init_normal(3, 0.02)
 
 
-def _run(rank, world, port, out, steps=2, die_before_step=None):
+def _run(rank, world, port, out, steps=2, die_before_step=None, bucketed=False):
     import torch.distributed as dist
     from datetime import timedelta
     if world > 1:
         os.environ["MASTER_ADDR"] = "127.0.0.1"
         os.environ["MASTER_PORT"] = str(port)
         dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=8))
-    be = OracleBackend(_params0())
+    be = (BucketedOracleBackend if bucketed else OracleBackend)(_params0())
     tr = DataParallelLmTrainer(be, GLOBAL_B, rank, world)
+    assert tr.overlap == (bucketed and world > 1)
     losses = []
     try:
         for s in range(steps):
@@ -135,3 +162,32 @@ def test_rank_failure_is_detected_by_the_survivor():
     for p in procs:
         p.join(timeout=30)
     assert procs[1].exitcode == 3
+
+
+def test_bucketed_all_reduce_equals_single_all_reduce():
+    """The per-bucket all-reduces cover the whole [P+1] buffer exactly once,
+    in the same order on every rank: the bucketed run equals the unbucketed
+    one bit for bit (two gloo ranks sum exactly in any grouping)."""
+    ctx = mp.get_context("spawn")
+    results = {}
+    for bucketed in (False, True):
+        q = ctx.Queue()
+        port = _free_port()
+        procs = [ctx.Process(target=_run, args=(r, 2, port, q, 2, None, bucketed)) for r in range(2)]
+        for p in procs:
+            p.start()
+        res = {}
+        for _ in range(2):
+            rank, status, params, losses = q.get(timeout=120)
+            assert status == "ok", params
+            res[rank] = (params, losses)
+        for p in procs:
+            p.join(timeout=30)
+        assert np.array_equal(res[0][0], res[1][0])
+        results[bucketed] = res[0]
+    assert np.array_equal(results[False][0], results[True][0])
+    assert results[False][1] == results[True][1]
+    b = BucketedOracleBackend(_params0()).buckets()
+    covered = sorted((o, o + n) for o, n in b)
+    assert covered[0][0] == 0 and all(x[1] == y[0] for x, y in zip(covered, covered[1:]))
+    assert covered[-1][1] == _params0().size + 1
