@@ -349,7 +349,12 @@ struct SideStream {
 void record_bucket(hx_runtime* rt, LmPlan& p, int i, cudaStream_t stream)
 {
     if (!p.bucket_events) return;
-    HX_CUDA(cudaEventRecordWithFlags(p.bucket_ev[size_t(i)], stream, cudaEventRecordExternal));
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    HX_CUDA(cudaStreamIsCapturing(stream, &cs));
+    if (cs == cudaStreamCaptureStatusActive)
+        HX_CUDA(cudaEventRecordWithFlags(p.bucket_ev[size_t(i)], stream, cudaEventRecordExternal));
+    else
+        HX_CUDA(cudaEventRecord(p.bucket_ev[size_t(i)], stream));
 }
 
 void forward_backward(hx_runtime* rt, LmPlan& p, const float* W, float* G, float grad_scale, int mode = kFullStep)
