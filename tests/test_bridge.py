@@ -174,8 +174,18 @@ def _mlp_replay(seed, N, B, I, H, O, steps, lr):
     return first, last
 
 
+def _mlp_oracle_replay(oracle, seed, N, B, I, H, O, steps, lr):
+    """The same run on the oracle (the reference's pass() + sgdUpdate)."""
+    x, y, w1, w2 = data.mlp_data(seed, N, I, H, O)
+    first = oracle.mlp_step(x, y, w1, w2, 0.0).loss
+    for s in range(steps):
+        r = oracle.mlp_step(data.batch(x, s * B, B), data.batch(y, s * B, B), w1, w2, lr)
+        w1, w2 = r.w1_next.reshape(w1.shape), r.w2_next.reshape(w2.shape)
+    return first, oracle.mlp_step(x, y, w1, w2, 0.0).loss
+
+
 @pytest.mark.gpu
-def test_mlp_full_step_mode_matches_runtime_replay(jni):
+def test_mlp_full_step_mode_matches_runtime_replay(jni, oracle):
     N, B, I, H, O, seed, lr = 64, 8, 128, 128, 64, 20260710, 0.5
     fake = FakeJni()
     h = getattr(jni, JNI_PREFIX + "nativeRunExecutionMode")(C.byref(fake.env), None, 32, B, I, H, O, 0, 0, lr, seed,
@@ -187,6 +197,10 @@ def test_mlp_full_step_mode_matches_runtime_replay(jni):
     first, last = _mlp_replay(seed, N, B, I, H, O, 16, lr)
     assert float(rep["initial_loss"]) == pytest.approx(first, rel=1e-6)
     assert float(rep["final_loss"]) == pytest.approx(last, rel=1e-6)
+    # and the oracle's run of the same 16 steps
+    ofirst, olast = _mlp_oracle_replay(oracle, seed, N, B, I, H, O, 16, lr)
+    assert float(rep["initial_loss"]) == pytest.approx(ofirst, rel=1e-4)
+    assert float(rep["final_loss"]) == pytest.approx(olast, rel=1e-4)
 
 
 @pytest.mark.gpu
@@ -198,7 +212,7 @@ def test_mlp_fail_execute_mode_reports_the_injected_failure():
 
 
 @pytest.mark.gpu
-def test_generic_lm_mode_trains_checkpoints_and_resumes(tmp_path):
+def test_generic_lm_mode_trains_checkpoints_and_resumes(tmp_path, oracle):
     V, T, D, F, L, H, B, seed = 64, 16, 32, 64, 2, 4, 4, 5
     common = dict(execution_mode=99, batch_size=B, dimension=D, hidden_dimension=F, output_dimension=V,
                   learning_rate=1e-3, seed=seed, sample_count=T, epochs=L, measured_steps=H,
@@ -219,3 +233,16 @@ def test_generic_lm_mode_trains_checkpoints_and_resumes(tmp_path):
     assert float(straight["first_loss"]) == pytest.approx(losses[0], rel=1e-7)
     assert float(straight["final_loss"]) == pytest.approx(losses[-1], rel=1e-7)
     assert len(straight["_progress"]) == 5
+    # and the oracle's trajectory: batch gradients at its own weights, then Adam
+    from oracle.oracle import LmConfig as OC
+    oc = OC.make(V, T, D, F, L, H)
+    w = cfg.init_reference(seed)
+    m, v = np.zeros_like(w), np.zeros_like(w)
+    olosses = []
+    for step in range(1, 6):
+        g, lo = oracle.lm_batch_gradients(oc, data.lm_tokens(seed, B, T, V, step=step - 1), w, threads=4)
+        olosses.append(lo)
+        c1, c2 = oracle.adam_correction(0.9, step), oracle.adam_correction(0.999, step)
+        m, v, _, _, w = oracle.adam(w, g, m, v, 1e-3, c1, c2)
+    assert float(straight["first_loss"]) == pytest.approx(olosses[0], rel=1e-4)
+    assert float(straight["final_loss"]) == pytest.approx(olosses[-1], rel=1e-4)
