@@ -48,6 +48,8 @@
 // frees TMEM.
 #pragma once
 
+#include "pdl.cuh"
+
 #include "gemm_tc.cuh"
 
 namespace hx {
@@ -164,6 +166,7 @@ attention_fwd_tc_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid
                         int D, int H, float scale, const float* __restrict__ qkv, float* __restrict__ ctx,
                         float* __restrict__ row_max, float* __restrict__ row_sum, int* __restrict__ err)
 {
+    HX_PDL_PROLOGUE();
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     const uint32_t pad = (1024u - (tc::smem_u32(smem_raw) & 1023u)) & 1023u;
     AtcFwdSmem& sm = *reinterpret_cast<AtcFwdSmem*>(smem_raw + pad);

@@ -39,6 +39,8 @@
 // issues the TMA loads and the MMAs.  Waits are bounded as in the forward.
 #pragma once
 
+#include "pdl.cuh"
+
 #include "attention_tc.cuh"
 
 namespace hx {
@@ -129,6 +131,7 @@ attention_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap map_qk, const __g
                            const float* __restrict__ row_max, float* __restrict__ bstat, float* __restrict__ dqkv,
                            int* __restrict__ err)
 {
+    HX_PDL_PROLOGUE();
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     const uint32_t pad = (1024u - (tc::smem_u32(smem_raw) & 1023u)) & 1023u;
     AtcDqSmem& sm = *reinterpret_cast<AtcDqSmem*>(smem_raw + pad);
@@ -446,6 +449,7 @@ attention_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap map_qk, const _
                              const float* __restrict__ dctx, const float* __restrict__ row_max,
                              const float* __restrict__ bstat, float* __restrict__ dqkv, int* __restrict__ err)
 {
+    HX_PDL_PROLOGUE();
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     const uint32_t pad = (1024u - (tc::smem_u32(smem_raw) & 1023u)) & 1023u;
     AtcKvSmem& sm = *reinterpret_cast<AtcKvSmem*>(smem_raw + pad);

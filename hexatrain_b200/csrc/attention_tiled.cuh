@@ -35,6 +35,8 @@
 // Limits: T <= 256, DH in {8, 16, 32}.
 #pragma once
 
+#include "pdl.cuh"
+
 #include <cuda_runtime.h>
 #include <cstdint>
 
@@ -219,6 +221,7 @@ __global__ void __launch_bounds__(kAttnTiledThreads, 1)
 attention_fwd_tiled_kernel(int T, int D, int H, float scale, const float* __restrict__ qkv, float* __restrict__ ctx,
                            float* __restrict__ row_max, float* __restrict__ row_sum, float* __restrict__ probs)
 {
+    HX_PDL_PROLOGUE();
     using Lay = AttnTiledLayout<DH>;
     constexpr int LD = Lay::LD, CW = DH / 4;
     extern __shared__ float4 sm4[];
@@ -316,6 +319,7 @@ attention_bwd_tiled_kernel(int T, int D, int H, float scale, const float* __rest
                            const float* __restrict__ dctx,
                            const float* __restrict__ row_max, float* __restrict__ dqkv)
 {
+    HX_PDL_PROLOGUE();
     using Lay = AttnTiledLayout<DH>;
     constexpr int LD = Lay::LD, CW = DH / 4;
     extern __shared__ float4 sm4[];

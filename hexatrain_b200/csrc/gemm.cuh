@@ -17,10 +17,10 @@ void launch_splitk_reduce(hx_runtime* rt, int M, int N, int splits, const float*
     const int threads = 256;
     if (N % 4 == 0 && (reinterpret_cast<uintptr_t>(ws) & 15) == 0) {
         const int blocks = (int)std::min<long>((total / 4 + threads - 1) / threads, 4L * rt->sm_count * 8);
-        splitk_reduce4_kernel<Epi><<<blocks, threads, 0, rt->stream>>>(M, N, splits, ws, epi);
+        ::hx::pdl_launch(splitk_reduce4_kernel<Epi>, blocks, threads, 0, rt->stream, M, N, splits, ws, epi);
     } else {
         const int blocks = (int)std::min<long>((total + threads - 1) / threads, 4L * rt->sm_count * 8);
-        splitk_reduce_kernel<Epi><<<blocks, threads, 0, rt->stream>>>(M, N, splits, ws, epi);
+        ::hx::pdl_launch(splitk_reduce_kernel<Epi>, blocks, threads, 0, rt->stream, M, N, splits, ws, epi);
     }
     HX_LAUNCHED(rt);
 }
@@ -46,13 +46,11 @@ void launch_simt(hx_runtime* rt, int M, int N, int K, const float* A, long lda, 
     if (K == 0) { splits = 1; chunk = BK; }
     dim3 grid(tiles_n, tiles_m, splits);
     if (splits == 1) {
-        gemm_simt_kernel<S, BM, BN, BK, TX, TY, AT, BT, Epi>
-            <<<grid, S::kThreads, 0, rt->stream>>>(M, N, K, A, lda, B, ldb, chunk, epi, nullptr);
+        ::hx::pdl_launch(gemm_simt_kernel<S, BM, BN, BK, TX, TY, AT, BT, Epi>, grid, S::kThreads, 0, rt->stream, M, N, K, A, lda, B, ldb, chunk, epi, nullptr);
         HX_LAUNCHED(rt);
     } else {
         float* ws = rt->workspace(sizeof(float) * (size_t)splits * M * N);
-        gemm_simt_kernel<S, BM, BN, BK, TX, TY, AT, BT, Epi>
-            <<<grid, S::kThreads, 0, rt->stream>>>(M, N, K, A, lda, B, ldb, chunk, epi, ws);
+        ::hx::pdl_launch(gemm_simt_kernel<S, BM, BN, BK, TX, TY, AT, BT, Epi>, grid, S::kThreads, 0, rt->stream, M, N, K, A, lda, B, ldb, chunk, epi, ws);
         HX_LAUNCHED(rt);
         launch_splitk_reduce(rt, M, N, splits, ws, epi);
     }

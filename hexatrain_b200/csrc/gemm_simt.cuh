@@ -14,6 +14,8 @@
 // CPU path.
 #pragma once
 
+#include "pdl.cuh"
+
 #include <cuda_runtime.h>
 #include <cstdint>
 
@@ -35,6 +37,7 @@ gemm_simt_kernel(int M, int N, int K, const float* __restrict__ A, long lda,
                  const float* __restrict__ B, long ldb, int k_chunk, Epi epi,
                  float* __restrict__ partial)
 {
+    HX_PDL_PROLOGUE();
     constexpr int NT = S::kThreads;
     __shared__ __align__(16) float As[2][BK][BM];
     __shared__ __align__(16) float Bs[2][BK][BN];
@@ -159,6 +162,7 @@ gemm_simt_kernel(int M, int N, int K, const float* __restrict__ A, long lda,
 template <class Epi>
 __global__ void splitk_reduce_kernel(int M, int N, int splits, const float* __restrict__ partial, Epi epi)
 {
+    HX_PDL_PROLOGUE();
     const long total = (long)M * N;
     for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
         float s = 0.f;
@@ -173,6 +177,7 @@ __global__ void splitk_reduce_kernel(int M, int N, int splits, const float* __re
 template <class Epi>
 __global__ void splitk_reduce4_kernel(int M, int N, int splits, const float* __restrict__ partial, Epi epi)
 {
+    HX_PDL_PROLOGUE();
     const long total4 = (long)M * N / 4, stride4 = (long)M * N / 4;
     const float4* p4 = reinterpret_cast<const float4*>(partial);
     for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total4; i += (long)gridDim.x * blockDim.x) {

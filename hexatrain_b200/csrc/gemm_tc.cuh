@@ -70,6 +70,8 @@
 // the other CTA at the cluster barrier, frees TMEM and returns.
 #pragma once
 
+#include "pdl.cuh"
+
 #include <algorithm>
 
 #include "tc_ptx.cuh"
@@ -210,6 +212,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant_
                const __grid_constant__ CUtensorMap map_wlo, const __grid_constant__ CUtensorMap map_c, TcGrid g,
                Epi epi, float* __restrict__ partial, int* __restrict__ err)
 {
+    HX_PDL_PROLOGUE();
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     // 128B-swizzled TMA tiles and UMMA descriptors need 1024-byte alignment
     // of the shared-memory address itself (the same offset in both CTAs).
@@ -554,8 +557,10 @@ inline cudaLaunchConfig_t tc_launch_config(int pairs, cudaStream_t stream, cudaL
     attr[0].val.clusterDim.x = 2;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = 2;
     return cfg;
 }
 
@@ -566,7 +571,7 @@ inline int tc_pairs(int sm_count) {
     static int pairs = 0;
     if (pairs == 0) {
         auto kern = gemm_tc_kernel<A_MN, B_MN, B_SPLIT, C_TMA, Epi>;
-        cudaLaunchAttribute attr[1];
+        cudaLaunchAttribute attr[2];
         const cudaLaunchConfig_t cfg = tc_launch_config(sm_count / 2, nullptr, attr);
         int n = 0;
         if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTcSmemBytes) == cudaSuccess &&
@@ -605,7 +610,7 @@ inline cudaError_t launch_tc_kernel(cudaStream_t stream, int pairs, const CUtens
         regs = fa.numRegs;
     }
     if (regs != kTcRegsLaunch) return cudaErrorInvalidConfiguration;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     const cudaLaunchConfig_t cfg = tc_launch_config(std::min(g.units, pairs), stream, attr);
     return cudaLaunchKernelEx(&cfg, kern, mx, mw, mw_lo, mc, g, epi, partial, err);
 }

@@ -6,6 +6,8 @@
 // reference's bool + std::string& error convention (qnn/qnn_runtime.h:250-451).
 #pragma once
 
+#include "pdl.cuh"
+
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -14,6 +16,7 @@
 #include <cstring>
 #include <memory>
 #include <string>
+#include <utility>
 #include <vector>
 
 #include "../../include/hexatrain.h"
@@ -33,6 +36,26 @@ inline void check_cuda(cudaError_t e, const char* what) {
 #define HX_CUDA(call) ::hx::check_cuda((call), #call)
 // After a kernel launch: catches launch-configuration errors immediately.
 #define HX_LAUNCHED(rt) do { ::hx::check_cuda(cudaGetLastError(), "kernel launch"); ++(rt)->metrics.kernel_launches; } while (0)
+
+// Launches `kernel` on `stream` with programmatic stream serialisation: the
+// kernel may be launched as the previous kernel of the stream drains,
+// and its HX_PDL_PROLOGUE() holds it until that kernel has completed.
+// Arguments are converted to the kernel's parameter types.
+template <class... KArgs, class... Args>
+inline void pdl_launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                       Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    check_cuda(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...), "kernel launch");
+}
 
 inline void require(bool ok, int code, const std::string& msg) {
     if (!ok) fail(code, msg);

@@ -169,7 +169,7 @@ void attn_fwd_tc_launch(hx_runtime* rt, const LmPlan& p, const float* qkv, float
     const CUtensorMap mv = make_map(qkv, w, rows, w, 32, kAtcTile, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
     HX_CUDA(cudaFuncSetAttribute(attention_fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)kAtcFwdSmemBytes));
-    attention_fwd_tc_kernel<<<dim3(p.H, p.B), kAtcThreads, kAtcFwdSmemBytes, rt->stream>>>(
+    ::hx::pdl_launch(attention_fwd_tc_kernel, dim3(p.H, p.B), kAtcThreads, kAtcFwdSmemBytes, rt->stream, 
         mqk, mv, p.T, p.D, p.H, 1.0f / sqrtf((float)kAtcDH), qkv, ctx, rmax, rsum, rt->device_error());
     HX_LAUNCHED(rt);
 }
@@ -186,7 +186,7 @@ void attn_fwd_launch(hx_runtime* rt, const LmPlan& p, const float* qkv, float* c
         if (attn_tiled(p.T, DH)) {
             const size_t smem = AttnTiledLayout<DH>::fwd_bytes(p.T);
             HX_CUDA(cudaFuncSetAttribute(attention_fwd_tiled_kernel<DH>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-            attention_fwd_tiled_kernel<DH><<<dim3(p.H, p.B), kAttnTiledThreads, smem, rt->stream>>>(
+            ::hx::pdl_launch(attention_fwd_tiled_kernel<DH>, dim3(p.H, p.B), kAttnTiledThreads, smem, rt->stream, 
                 p.T, p.D, p.H, 1.0f / sqrtf((float)DH), qkv, ctx, rmax, rsum, probs);
             HX_LAUNCHED(rt);
             return;
@@ -194,7 +194,7 @@ void attn_fwd_launch(hx_runtime* rt, const LmPlan& p, const float* qkv, float* c
     }
     const size_t smem = attn_fwd_smem(p.T, DH, kAttnThreads / 32);
     HX_CUDA(cudaFuncSetAttribute(attention_fwd_kernel<DH>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    attention_fwd_kernel<DH><<<dim3(p.H, p.B), kAttnThreads, smem, rt->stream>>>(
+    ::hx::pdl_launch(attention_fwd_kernel<DH>, dim3(p.H, p.B), kAttnThreads, smem, rt->stream, 
         p.T, p.D, p.H, 1.0f / sqrtf((float)DH), qkv, ctx, rmax, rsum, probs);
     HX_LAUNCHED(rt);
 }
@@ -212,13 +212,13 @@ void attn_bwd_tc_launch(hx_runtime* rt, const LmPlan& p, const float* qkv, const
     const float scale = 1.0f / sqrtf((float)kAtcDH);
     HX_CUDA(cudaFuncSetAttribute(attention_bwd_dq_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)kAtcDqSmemBytes));
-    attention_bwd_dq_tc_kernel<<<dim3(p.H, p.B), kAtcThreads, kAtcDqSmemBytes, rt->stream>>>(
+    ::hx::pdl_launch(attention_bwd_dq_tc_kernel, dim3(p.H, p.B), kAtcThreads, kAtcDqSmemBytes, rt->stream, 
         mqk, mmn, p.T, p.D, p.H, scale, qkv, dctx, rmax, bstat, dqkv, rt->device_error());
     HX_LAUNCHED(rt);
     HX_CUDA(cudaFuncSetAttribute(attention_bwd_dkdv_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)kAtcKvSmemBytes));
     const int ntile = p.T > uint32_t(kAtcTile) ? 2 : 1;
-    attention_bwd_dkdv_tc_kernel<<<dim3(p.H, p.B, ntile), kAtcThreads, kAtcKvSmemBytes, rt->stream>>>(
+    ::hx::pdl_launch(attention_bwd_dkdv_tc_kernel, dim3(p.H, p.B, ntile), kAtcThreads, kAtcKvSmemBytes, rt->stream, 
         mqk, mmn, mdo, mdo_mn, p.T, p.D, p.H, scale, qkv, dctx, rmax, bstat, dqkv, rt->device_error());
     HX_LAUNCHED(rt);
 }
@@ -236,7 +236,7 @@ void attn_bwd_launch(hx_runtime* rt, const LmPlan& p, const float* qkv, const fl
         if (attn_tiled(p.T, DH)) {
             const size_t smem = AttnTiledLayout<DH>::bwd_bytes(p.T);
             HX_CUDA(cudaFuncSetAttribute(attention_bwd_tiled_kernel<DH>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-            attention_bwd_tiled_kernel<DH><<<dim3(p.H, p.B), kAttnTiledThreads, smem, rt->stream>>>(
+            ::hx::pdl_launch(attention_bwd_tiled_kernel<DH>, dim3(p.H, p.B), kAttnTiledThreads, smem, rt->stream, 
                 p.T, p.D, p.H, 1.0f / sqrtf((float)DH), qkv, dctx, rmax, dqkv);
             HX_LAUNCHED(rt);
             return;
@@ -244,7 +244,7 @@ void attn_bwd_launch(hx_runtime* rt, const LmPlan& p, const float* qkv, const fl
     }
     const size_t smem = attn_bwd_smem(p.T, DH, kAttnThreads / 32);
     HX_CUDA(cudaFuncSetAttribute(attention_bwd_kernel<DH>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    attention_bwd_kernel<DH><<<dim3(p.H, p.B), kAttnThreads, smem, rt->stream>>>(
+    ::hx::pdl_launch(attention_bwd_kernel<DH>, dim3(p.H, p.B), kAttnThreads, smem, rt->stream, 
         p.T, p.D, p.H, 1.0f / sqrtf((float)DH), qkv, dctx, rmax, rsum, dqkv);
     HX_LAUNCHED(rt);
 }
@@ -288,6 +288,7 @@ enum ForwardMode { kFullStep = 0, kForwardAllRows = 1, kForwardLastRow = 2 };
 // weight operands, done once per forward instead of in every CTA per tile.
 __global__ void split_tf32_kernel(long n, const float* __restrict__ w, float* __restrict__ hi, float* __restrict__ lo)
 {
+    HX_PDL_PROLOGUE();
     for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
         const float x = w[i];
         const float h = tf32_round(x);
@@ -370,7 +371,7 @@ void forward_backward(hx_runtime* rt, LmPlan& p, const float* W, float* G, float
 
     // pack W_qkv per layer; split the GEMM weights for the tensor cores
     for (uint32_t l = 0; l < p.L; ++l) {
-        pack_qkv_kernel<<<grid_for(3L * D * D, tpb, rt->sm_count), tpb, 0, s>>>(D, W + p.lo[l].wq, wqkv + size_t(l) * 3 * D * D);
+        ::hx::pdl_launch(pack_qkv_kernel, grid_for(3L * D * D, tpb, rt->sm_count), tpb, 0, s, D, W + p.lo[l].wq, wqkv + size_t(l) * 3 * D * D);
         HX_LAUNCHED(rt);
     }
     float* whi = a.at<float>(p.w_hi);
@@ -379,9 +380,9 @@ void forward_backward(hx_runtime* rt, LmPlan& p, const float* W, float* G, float
     float* qlo = a.at<float>(p.wqkv_lo);
     {
         const long nq = long(p.L) * 3 * D * D;
-        split_tf32_kernel<<<grid_for(long(p.P), tpb, rt->sm_count), tpb, 0, s>>>(long(p.P), W, whi, wlo);
+        ::hx::pdl_launch(split_tf32_kernel, grid_for(long(p.P), tpb, rt->sm_count), tpb, 0, s, long(p.P), W, whi, wlo);
         HX_LAUNCHED(rt);
-        split_tf32_kernel<<<grid_for(nq, tpb, rt->sm_count), tpb, 0, s>>>(nq, wqkv, qhi, qlo);
+        ::hx::pdl_launch(split_tf32_kernel, grid_for(nq, tpb, rt->sm_count), tpb, 0, s, nq, wqkv, qhi, qlo);
         HX_LAUNCHED(rt);
     }
     auto wsplit = [&](size_t off) { return BSplit{whi + off, wlo + off}; };
@@ -391,11 +392,11 @@ void forward_backward(hx_runtime* rt, LmPlan& p, const float* W, float* G, float
     ProfScope pemb(rt, kTagEmbed, 1.0 * M * D, 4.0 * 3.0 * M * D);
     if (D % 4 == 0 && long(M) * D / 4 < (1L << 31) && aligned16(W + p.off_E) && aligned16(pos) && aligned16(x)) {
         const int D4 = D / 4;
-        embed_vec_kernel<<<grid_for(long(M) * D4, tpb, rt->sm_count), tpb, 0, s>>>(
+        ::hx::pdl_launch(embed_vec_kernel, grid_for(long(M) * D4, tpb, rt->sm_count), tpb, 0, s, 
             M, T, D4, in_ids, reinterpret_cast<const float4*>(W + p.off_E), reinterpret_cast<const float4*>(pos),
             reinterpret_cast<float4*>(x));
     } else {
-        embed_kernel<<<grid_for(long(M) * D, tpb, rt->sm_count), tpb, 0, s>>>(M, T, D, in_ids, W + p.off_E, pos, x);
+        ::hx::pdl_launch(embed_kernel, grid_for(long(M) * D, tpb, rt->sm_count), tpb, 0, s, M, T, D, in_ids, W + p.off_E, pos, x);
     }
     HX_LAUNCHED(rt);
         pemb.end();
@@ -409,9 +410,9 @@ void forward_backward(hx_runtime* rt, LmPlan& p, const float* W, float* G, float
                           reinterpret_cast<uintptr_t>(bet) | reinterpret_cast<uintptr_t>(yy)) & 15) == 0;
         if (al && (C == 1 || C == 2 || C == 4)) {
             auto k = C == 1 ? layernorm_fwd_vec_kernel<1> : C == 2 ? layernorm_fwd_vec_kernel<2> : layernorm_fwd_vec_kernel<4>;
-            k<<<row_grid, 32 * rows_per_block, 0, s>>>(M, p.cfg.eps, xx, gam, bet, yy, mo, io);
+            ::hx::pdl_launch(k, row_grid, 32 * rows_per_block, 0, s, M, p.cfg.eps, xx, gam, bet, yy, mo, io);
         } else {
-            layernorm_fwd_kernel<<<row_grid, 32 * rows_per_block, 0, s>>>(M, D, p.cfg.eps, xx, gam, bet, yy, mo, io);
+            ::hx::pdl_launch(layernorm_fwd_kernel, row_grid, 32 * rows_per_block, 0, s, M, D, p.cfg.eps, xx, gam, bet, yy, mo, io);
         }
         HX_LAUNCHED(rt);
     };
@@ -450,20 +451,20 @@ void forward_backward(hx_runtime* rt, LmPlan& p, const float* W, float* G, float
     if (mode == kForwardAllRows) return;
     ProfScope pce(rt, kTagSoftmaxCe, 4.0 * M * V, 4.0 * 2.0 * M * V);
     if (V == 1024)
-        softmax_ce_vec_kernel<32><<<row_grid, 32 * rows_per_block, 0, s>>>(
+        ::hx::pdl_launch(softmax_ce_vec_kernel<32>, row_grid, 32 * rows_per_block, 0, s, 
             M, T, grad_scale, logits, tgt_ids, p.diag ? a.at<float>(p.probs) : nullptr, logits,
             a.at<double>(p.row_loss), a.at<int>(p.row_correct));
     else
-        softmax_ce_kernel<<<row_grid, 32 * rows_per_block, 0, s>>>(
+        ::hx::pdl_launch(softmax_ce_kernel, row_grid, 32 * rows_per_block, 0, s, 
             M, V, T, grad_scale, logits, tgt_ids, p.diag ? a.at<float>(p.probs) : nullptr, logits,
             a.at<double>(p.row_loss), a.at<int>(p.row_correct));
     HX_LAUNCHED(rt);
         pce.end();
     ProfScope plr(rt, kTagReduce, 1.0 * M, 12.0 * M);
-    loss_seq_kernel<<<(B + 7) / 8, 256, 0, s>>>(B, T, a.at<double>(p.row_loss), a.at<int>(p.row_correct),
+    ::hx::pdl_launch(loss_seq_kernel, (B + 7) / 8, 256, 0, s, B, T, a.at<double>(p.row_loss), a.at<int>(p.row_correct),
                                                a.at<float>(p.seq_loss), a.at<int>(p.seq_correct));
     HX_LAUNCHED(rt);
-    loss_reduce_kernel<<<1, 256, 0, s>>>(B, T, a.at<float>(p.seq_loss), a.at<int>(p.seq_correct), grad_scale,
+    ::hx::pdl_launch(loss_reduce_kernel, 1, 256, 0, s, B, T, a.at<float>(p.seq_loss), a.at<int>(p.seq_correct), grad_scale,
                                          a.at<float>(p.loss), a.at<float>(p.acc), G + p.P);
     HX_LAUNCHED(rt);
         plr.end();
@@ -494,11 +495,11 @@ void forward_backward(hx_runtime* rt, LmPlan& p, const float* W, float* G, float
         if (C == 1 || C == 2 || C == 4) {
             auto k = C == 1 ? layernorm_bwd_vec_kernel<1> : C == 2 ? layernorm_bwd_vec_kernel<2> : layernorm_bwd_vec_kernel<4>;
             if (ln_smem > 48 * 1024) HX_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ln_smem));
-            k<<<p.ln_parts, 32 * lnw, ln_smem, s>>>(M, p.ln_rows, dy, xx, mean, inv, gam, res, dxo, part);
+            ::hx::pdl_launch(k, p.ln_parts, 32 * lnw, ln_smem, s, M, p.ln_rows, dy, xx, mean, inv, gam, res, dxo, part);
         } else {
             if (ln_smem > 48 * 1024)
                 HX_CUDA(cudaFuncSetAttribute(layernorm_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ln_smem));
-            layernorm_bwd_kernel<<<p.ln_parts, 32 * lnw, ln_smem, s>>>(M, D, p.ln_rows, dy, xx, mean, inv, gam, res, dxo,
+            ::hx::pdl_launch(layernorm_bwd_kernel, p.ln_parts, 32 * lnw, ln_smem, s, M, D, p.ln_rows, dy, xx, mean, inv, gam, res, dxo,
                                                                          part);
         }
         HX_LAUNCHED(rt);
@@ -521,7 +522,7 @@ void forward_backward(hx_runtime* rt, LmPlan& p, const float* W, float* G, float
         ProfScope plb2(rt, kTagLayerNorm, 12.0 * M * D, 4.0 * (4.0 * M * D + 2.0 * M));
         ln_bwd(dn, a.at<float>(A.r1), a.at<float>(A.mean2), a.at<float>(A.inv2), W + o.g2, dout, dr);
         plb2.end();
-        column_reduce_kernel<<<(2 * D + 31) / 32, 32 * kColReduceWarps, 0, s>>>(p.ln_parts, D, part, G + o.g2, G + o.b2);
+        ::hx::pdl_launch(column_reduce_kernel, (2 * D + 31) / 32, 32 * kColReduceWarps, 0, s, p.ln_parts, D, part, G + o.g2, G + o.b2);
         HX_LAUNCHED(rt);
         side.fork();  // dr is ready
         side.run([&] {
@@ -544,7 +545,7 @@ void forward_backward(hx_runtime* rt, LmPlan& p, const float* W, float* G, float
         ProfScope plb1(rt, kTagLayerNorm, 12.0 * M * D, 4.0 * (4.0 * M * D + 2.0 * M));
         ln_bwd(dn, xin, a.at<float>(A.mean1), a.at<float>(A.inv1), W + o.g1, dr, dout);
         plb1.end();
-        column_reduce_kernel<<<(2 * D + 31) / 32, 32 * kColReduceWarps, 0, s>>>(p.ln_parts, D, part, G + o.g1, G + o.b1);
+        ::hx::pdl_launch(column_reduce_kernel, (2 * D + 31) / 32, 32 * kColReduceWarps, 0, s, p.ln_parts, D, part, G + o.g1, G + o.b1);
         HX_LAUNCHED(rt);
         record_bucket(rt, p, int(p.L - li), s);  // this layer's ten tensors (its side work was joined above)
         if (p.diag) copy_d2d(rt, a.at<float>(p.diag_lig) + size_t(li) * M * D, dout, sizeof(float) * size_t(M) * D);
@@ -557,16 +558,16 @@ void forward_backward(hx_runtime* rt, LmPlan& p, const float* W, float* G, float
         if (esm > 48 * 1024)
             HX_CUDA(cudaFuncSetAttribute(embed_bwd_partial_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)esm));
         dim3 grid(p.emb_chunks, (V + tb - 1) / tb);
-        embed_bwd_partial_kernel<<<grid, 32 * kEmbWarps, esm, s>>>(M, V, D, p.emb_rows, tb, in_ids, dout,
+        ::hx::pdl_launch(embed_bwd_partial_kernel, grid, 32 * kEmbWarps, esm, s, M, V, D, p.emb_rows, tb, in_ids, dout,
                                                                     a.at<float>(p.emb_part));
         HX_LAUNCHED(rt);
-        embed_bwd_combine_kernel<<<grid_for(long(V) * D, tpb, rt->sm_count), tpb, 0, s>>>(
+        ::hx::pdl_launch(embed_bwd_combine_kernel, grid_for(long(V) * D, tpb, rt->sm_count), tpb, 0, s, 
             p.emb_chunks, V, D, a.at<float>(p.emb_part), G + p.off_E);
         HX_LAUNCHED(rt);
     }
     pemb2.end();
     if (p.learned) {
-        position_bwd_kernel<<<(unsigned)((long(T) * D + 31) / 32), 32 * kPosWarps, 0, s>>>(B, T, D, dout, G + p.off_pos);
+        ::hx::pdl_launch(position_bwd_kernel, (unsigned)((long(T) * D + 31) / 32), 32 * kPosWarps, 0, s, B, T, D, dout, G + p.off_pos);
         HX_LAUNCHED(rt);
     }
     side.join();  // the output projection's gradient, when L = 0
@@ -965,12 +966,12 @@ int hx_lm_execute(hx_runtime* rt, const float* input_one_hot, const float* targe
         HX_CUDA(cudaMemcpyAsync(dev + n, target_one_hot, n * sizeof(float), cudaMemcpyHostToDevice, rt->stream));
         const Arena& a = p.arena;
         HX_CUDA(cudaMemsetAsync(a.at<int>(p.bad), 0, sizeof(int), rt->stream));
-        one_hot_decode_kernel<<<(p.M + 7) / 8, 256, 0, rt->stream>>>(p.M, p.V, dev, a.at<uint32_t>(p.in_tok), a.at<int>(p.bad));
+        ::hx::pdl_launch(one_hot_decode_kernel, (p.M + 7) / 8, 256, 0, rt->stream, p.M, p.V, dev, a.at<uint32_t>(p.in_tok), a.at<int>(p.bad));
         HX_LAUNCHED(rt);
-        one_hot_decode_kernel<<<(p.M + 7) / 8, 256, 0, rt->stream>>>(p.M, p.V, dev + n, a.at<uint32_t>(p.tgt_tok), a.at<int>(p.bad));
+        ::hx::pdl_launch(one_hot_decode_kernel, (p.M + 7) / 8, 256, 0, rt->stream, p.M, p.V, dev + n, a.at<uint32_t>(p.tgt_tok), a.at<int>(p.bad));
         HX_LAUNCHED(rt);
         check_bad(rt, p, "INVALID_TINY_LM_ONE_HOT: every input/target row must hold exactly one 1.0 and zeros elsewhere");
-        copy_ids_kernel<<<grid_for(p.M, 256, rt->sm_count), 256, 0, rt->stream>>>(
+        ::hx::pdl_launch(copy_ids_kernel, grid_for(p.M, 256, rt->sm_count), 256, 0, rt->stream, 
             p.M, p.V, a.at<uint32_t>(p.in_tok), a.at<uint32_t>(p.tgt_tok), a.at<int>(p.in_ids), a.at<int>(p.tgt_ids), a.at<int>(p.bad));
         HX_LAUNCHED(rt);
         lm_execute_common(rt, p, params, pc, lr, out);
@@ -990,7 +991,7 @@ int hx_lm_execute_tokens(hx_runtime* rt, const uint32_t* in, const uint32_t* tgt
         HX_CUDA(cudaMemcpyAsync(a.at<uint32_t>(p.in_tok), in, sizeof(uint32_t) * p.M, cudaMemcpyHostToDevice, rt->stream));
         HX_CUDA(cudaMemcpyAsync(a.at<uint32_t>(p.tgt_tok), tgt, sizeof(uint32_t) * p.M, cudaMemcpyHostToDevice, rt->stream));
         HX_CUDA(cudaMemsetAsync(a.at<int>(p.bad), 0, sizeof(int), rt->stream));
-        copy_ids_kernel<<<grid_for(p.M, 256, rt->sm_count), 256, 0, rt->stream>>>(
+        ::hx::pdl_launch(copy_ids_kernel, grid_for(p.M, 256, rt->sm_count), 256, 0, rt->stream, 
             p.M, p.V, a.at<uint32_t>(p.in_tok), a.at<uint32_t>(p.tgt_tok), a.at<int>(p.in_ids), a.at<int>(p.tgt_ids), a.at<int>(p.bad));
         HX_LAUNCHED(rt);
         check_bad(rt, p, "INVALID_TINY_LM_TOKEN: token id >= vocabulary size");
@@ -1021,7 +1022,7 @@ int hx_lm_forward_tokens(hx_runtime* rt, const uint32_t* tokens, const float* pa
         HX_CUDA(cudaMemcpyAsync(a.at<uint32_t>(p.in_tok), tokens, sizeof(uint32_t) * p.M, cudaMemcpyHostToDevice,
                                 rt->stream));
         HX_CUDA(cudaMemsetAsync(a.at<int>(p.bad), 0, sizeof(int), rt->stream));
-        copy_ids_kernel<<<grid_for(p.M, 256, rt->sm_count), 256, 0, rt->stream>>>(
+        ::hx::pdl_launch(copy_ids_kernel, grid_for(p.M, 256, rt->sm_count), 256, 0, rt->stream, 
             p.M, p.V, a.at<uint32_t>(p.in_tok), a.at<uint32_t>(p.in_tok), a.at<int>(p.in_ids), a.at<int>(p.tgt_ids),
             a.at<int>(p.bad));
         HX_LAUNCHED(rt);
@@ -1067,7 +1068,7 @@ int hx_lm_generate(hx_runtime* rt, const uint32_t* prompts, uint32_t prompt_len,
             }
             HX_CUDA(cudaMemcpyAsync(a.at<uint32_t>(p.in_tok), window.data(), sizeof(uint32_t) * p.M,
                                     cudaMemcpyHostToDevice, rt->stream));
-            copy_ids_kernel<<<grid_for(p.M, 256, rt->sm_count), 256, 0, rt->stream>>>(
+            ::hx::pdl_launch(copy_ids_kernel, grid_for(p.M, 256, rt->sm_count), 256, 0, rt->stream, 
                 p.M, p.V, a.at<uint32_t>(p.in_tok), a.at<uint32_t>(p.in_tok), a.at<int>(p.in_ids),
                 a.at<int>(p.tgt_ids), a.at<int>(p.bad));
             HX_LAUNCHED(rt);
@@ -1195,7 +1196,7 @@ int hx_lm_train_step(hx_runtime* rt, const uint32_t* tokens, uint32_t step, floa
         const float gs = 1.0f / float(p.B);
         lm_run(rt, p, lm_key(kGraphTrainStep, a.at<uint32_t>(p.tokens), gs), [&] {
             HX_CUDA(cudaMemsetAsync(a.at<int>(p.bad), 0, sizeof(int), rt->stream));
-            split_tokens_kernel<<<grid_for(p.M, 256, rt->sm_count), 256, 0, rt->stream>>>(
+            ::hx::pdl_launch(split_tokens_kernel, grid_for(p.M, 256, rt->sm_count), 256, 0, rt->stream, 
                 p.B, p.T, p.V, a.at<uint32_t>(p.tokens), a.at<int>(p.in_ids), a.at<int>(p.tgt_ids), a.at<int>(p.bad));
             HX_LAUNCHED(rt);
             forward_backward(rt, p, a.at<float>(p.params), a.at<float>(p.grads), gs);
@@ -1223,7 +1224,7 @@ int hx_lm_forward_backward_device(hx_runtime* rt, const uint32_t* tokens, float 
         require(p.state_ready, HX_ERR_STATE, "forward_backward before state upload");
         const Arena& a = p.arena;
         lm_run(rt, p, lm_key(kGraphForwardBackward, tokens, grad_scale), [&] {
-            split_tokens_kernel<<<grid_for(p.M, 256, rt->sm_count), 256, 0, rt->stream>>>(
+            ::hx::pdl_launch(split_tokens_kernel, grid_for(p.M, 256, rt->sm_count), 256, 0, rt->stream, 
                 p.B, p.T, p.V, tokens, a.at<int>(p.in_ids), a.at<int>(p.tgt_ids), a.at<int>(p.bad));
             HX_LAUNCHED(rt);
             forward_backward(rt, p, a.at<float>(p.params), a.at<float>(p.grads), grad_scale);

@@ -6,6 +6,8 @@
 // (tiny_language_model_cpu.cpp unless noted).
 #pragma once
 
+#include "pdl.cuh"
+
 #include <cuda_runtime.h>
 #include <cstdint>
 
@@ -28,6 +30,7 @@ __device__ __forceinline__ float warp_sumf(float v) {
 __global__ void split_tokens_kernel(int B, int T, int V, const uint32_t* __restrict__ tokens,
                                     int* __restrict__ in_ids, int* __restrict__ tgt_ids, int* bad)
 {
+    HX_PDL_PROLOGUE();
     const int M = B * T;
     for (int r = blockIdx.x * blockDim.x + threadIdx.x; r < M; r += gridDim.x * blockDim.x) {
         const int b = r / T, t = r % T;
@@ -42,6 +45,7 @@ __global__ void split_tokens_kernel(int B, int T, int V, const uint32_t* __restr
 __global__ void copy_ids_kernel(int M, int V, const uint32_t* __restrict__ a, const uint32_t* __restrict__ y,
                                 int* __restrict__ in_ids, int* __restrict__ tgt_ids, int* bad)
 {
+    HX_PDL_PROLOGUE();
     for (int r = blockIdx.x * blockDim.x + threadIdx.x; r < M; r += gridDim.x * blockDim.x) {
         if (a[r] >= (uint32_t)V || y[r] >= (uint32_t)V) atomicExch(bad, 1);
         in_ids[r] = a[r] < (uint32_t)V ? (int)a[r] : 0;
@@ -53,6 +57,7 @@ __global__ void copy_ids_kernel(int M, int V, const uint32_t* __restrict__ a, co
 __global__ void embed_kernel(int M, int T, int D, const int* __restrict__ ids, const float* __restrict__ E,
                              const float* __restrict__ pos, float* __restrict__ x)
 {
+    HX_PDL_PROLOGUE();
     const long total = (long)M * D;
     for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
         const int r = (int)(i / D), d = (int)(i % D);
@@ -68,6 +73,7 @@ __global__ void embed_vec_kernel(int M, int T, int D4, const int* __restrict__ i
                                  const float4* __restrict__ E, const float4* __restrict__ pos,
                                  float4* __restrict__ x)
 {
+    HX_PDL_PROLOGUE();
     const int total = M * D4;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
         const int r = i / D4, d = i - r * D4;
@@ -84,6 +90,7 @@ __global__ void layernorm_fwd_kernel(int M, int D, float eps, const float* __res
                                      const float* __restrict__ g, const float* __restrict__ b,
                                      float* __restrict__ y, float* __restrict__ mean_out, float* __restrict__ inv_out)
 {
+    HX_PDL_PROLOGUE();
     const int lane = threadIdx.x & 31;
     const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (row >= M) return;
@@ -119,6 +126,7 @@ __global__ void layernorm_fwd_vec_kernel(int M, float eps, const float* __restri
                                          const float* __restrict__ b, float* __restrict__ y,
                                          float* __restrict__ mean_out, float* __restrict__ inv_out)
 {
+    HX_PDL_PROLOGUE();
     constexpr int D = 128 * C;
     const int lane = threadIdx.x & 31;
     const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -174,6 +182,7 @@ __global__ void layernorm_bwd_kernel(int M, int D, int rows_per_cta, const float
                                      const float* __restrict__ res, float* __restrict__ dx,
                                      float* __restrict__ part)
 {
+    HX_PDL_PROLOGUE();
     extern __shared__ float acc[];  // [warps][2][D]
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
     float* ga = acc + (size_t)warp * 2 * D;
@@ -230,6 +239,7 @@ __global__ void layernorm_bwd_vec_kernel(int M, int rows_per_cta, const float* _
                                          const float* __restrict__ res, float* __restrict__ dx,
                                          float* __restrict__ part)
 {
+    HX_PDL_PROLOGUE();
     constexpr int D = 128 * C;
     extern __shared__ float acc[];  // [warps][2][D]
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
@@ -320,6 +330,7 @@ __global__ void __launch_bounds__(32 * kColReduceWarps)
 column_reduce_kernel(int parts, int D, const float* __restrict__ part, float* __restrict__ dgamma,
                      float* __restrict__ dbeta)
 {
+    HX_PDL_PROLOGUE();
     __shared__ float red[kColReduceWarps][32];
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
     const int c = blockIdx.x * 32 + lane;
@@ -362,6 +373,7 @@ __global__ void attention_fwd_kernel(int T, int D, int H, float scale, const flo
                                      float* __restrict__ ctx, float* __restrict__ row_max, float* __restrict__ row_sum,
                                      float* __restrict__ probs)
 {
+    HX_PDL_PROLOGUE();
     extern __shared__ float sm[];
     const int h = blockIdx.x, b = blockIdx.y;
     const int nw = blockDim.x >> 5, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -429,6 +441,7 @@ __global__ void attention_bwd_kernel(int T, int D, int H, float scale, const flo
                                      const float* __restrict__ dctx, const float* __restrict__ row_max,
                                      const float* __restrict__ row_sum, float* __restrict__ dqkv)
 {
+    HX_PDL_PROLOGUE();
     extern __shared__ float sm[];
     const int h = blockIdx.x, b = blockIdx.y;
     const int nw = blockDim.x >> 5, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -522,6 +535,7 @@ __global__ void softmax_ce_kernel(int M, int V, int T, float scale, float* logit
                                   float* __restrict__ probs, float* dlogits, double* __restrict__ row_loss,
                                   int* __restrict__ row_correct)
 {
+    HX_PDL_PROLOGUE();
     const int lane = threadIdx.x & 31;
     const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (row >= M) return;
@@ -568,6 +582,7 @@ __global__ void softmax_ce_vec_kernel(int M, int T, float scale, float* logits, 
                                       float* __restrict__ probs, float* dlogits, double* __restrict__ row_loss,
                                       int* __restrict__ row_correct)
 {
+    HX_PDL_PROLOGUE();
     constexpr int V = 32 * NR;
     const int lane = threadIdx.x & 31;
     const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -622,6 +637,7 @@ __global__ void softmax_ce_vec_kernel(int M, int T, float scale, float* logits, 
 __global__ void loss_seq_kernel(int B, int T, const double* __restrict__ row_loss, const int* __restrict__ row_correct,
                                 float* __restrict__ seq_loss, int* __restrict__ seq_correct)
 {
+    HX_PDL_PROLOGUE();
     const int lane = threadIdx.x & 31;
     const int b = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (b >= B) return;
@@ -647,6 +663,7 @@ __global__ void loss_reduce_kernel(int B, int T, const float* __restrict__ seq_l
                                    float grad_scale, float* __restrict__ loss_out, float* __restrict__ acc_out,
                                    float* __restrict__ scaled_loss_out)
 {
+    HX_PDL_PROLOGUE();
     __shared__ double red[32];
     __shared__ long cred[32];
     double tot = 0.0;
@@ -693,6 +710,7 @@ __global__ void __launch_bounds__(32 * kEmbWarps)
 embed_bwd_partial_kernel(int M, int V, int D, int chunk_rows, int tb, const int* __restrict__ ids,
                          const float* __restrict__ dx, float* __restrict__ part)
 {
+    HX_PDL_PROLOGUE();
     extern __shared__ float tab[];  // [tb][D], then ids[chunk_rows], rows[chunk_rows], toks[chunk_rows], count
     int* sid = reinterpret_cast<int*>(tab + (size_t)tb * D);
     int* srow = sid + chunk_rows;
@@ -742,6 +760,7 @@ embed_bwd_partial_kernel(int M, int V, int D, int chunk_rows, int tb, const int*
 __global__ void embed_bwd_combine_kernel(int chunks, int V, int D, const float* __restrict__ part,
                                          float* __restrict__ gE)
 {
+    HX_PDL_PROLOGUE();
     const long total = (long)V * D;
     for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
         float s = 0.f;
@@ -758,6 +777,7 @@ constexpr int kPosWarps = 8;
 __global__ void __launch_bounds__(32 * kPosWarps)
 position_bwd_kernel(int B, int T, int D, const float* __restrict__ dx, float* __restrict__ gP)
 {
+    HX_PDL_PROLOGUE();
     __shared__ float red[kPosWarps][32];
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
     const long total = (long)T * D;
@@ -780,6 +800,7 @@ position_bwd_kernel(int B, int T, int D, const float* __restrict__ dx, float* __
 // Packs wq, wk, wv [D,D] (consecutive in the registry) into W_qkv [D,3D].
 __global__ void pack_qkv_kernel(int D, const float* __restrict__ wq, float* __restrict__ packed)
 {
+    HX_PDL_PROLOGUE();
     const long total = 3L * D * D;
     for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
         const int k = (int)(i / (3 * D)), n = (int)(i % (3 * D));
@@ -792,6 +813,7 @@ __global__ void pack_qkv_kernel(int D, const float* __restrict__ wq, float* __re
 // the rest 0.0) and extracts the index.  Sets *bad otherwise.
 __global__ void one_hot_decode_kernel(int rows, int V, const float* __restrict__ oh, uint32_t* __restrict__ ids, int* bad)
 {
+    HX_PDL_PROLOGUE();
     const int lane = threadIdx.x & 31;
     const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (row >= rows) return;

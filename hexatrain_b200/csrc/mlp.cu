@@ -24,6 +24,7 @@ namespace hx {
 __global__ void mse_reduce_kernel(const float* __restrict__ e, size_t n, size_t chunk, double* __restrict__ part,
                                   unsigned int* __restrict__ done, float* __restrict__ loss)
 {
+    HX_PDL_PROLOGUE();
     __shared__ double wsum[32];
     __shared__ bool last;
     const int w = threadIdx.x / 32, l = threadIdx.x % 32, nw = blockDim.x / 32;
@@ -74,7 +75,7 @@ void launch_mse_reduce(hx_runtime* rt, const float* e, size_t n, double* part, u
     blocks = std::max<size_t>(1, std::min<size_t>(blocks, std::min<size_t>(kMseMaxBlocks, 2 * size_t(rt->sm_count))));
     const size_t chunk = (n + blocks - 1) / blocks;
     blocks = std::max<size_t>(1, (n + chunk - 1) / chunk);
-    mse_reduce_kernel<<<(unsigned)blocks, 1024, 0, rt->stream>>>(e, n, chunk, part, done, loss);
+    ::hx::pdl_launch(mse_reduce_kernel, (unsigned)blocks, 1024, 0, rt->stream, e, n, chunk, part, done, loss);
     HX_LAUNCHED(rt);
 }
 
@@ -131,9 +132,9 @@ void mlp_enqueue(hx_runtime* rt, const MlpPlan& pl, const MlpBinding& b)
         const MlpFusedArgs fa{b.x, b.y, b.w1, b.w2, b.loss, b.w1n, b.w2n, b.h, b.p, b.e, b.dp, b.dw2, b.dh, b.dz1,
                               b.dw1, b.mask, pl.arena.at<double>(pl.mse_part), b.lr, B, I, H, O};
         if (mlp_fused_cluster16(rt))
-            mlp_fused_step_kernel<16><<<16, kMlpFusedThreads, kMlpFusedSmemBytes, rt->stream>>>(fa);
+            ::hx::pdl_launch(mlp_fused_step_kernel<16>, 16, kMlpFusedThreads, kMlpFusedSmemBytes, rt->stream, fa);
         else
-            mlp_fused_step_kernel<8><<<8, kMlpFusedThreads, kMlpFusedSmemBytes, rt->stream>>>(fa);
+            ::hx::pdl_launch(mlp_fused_step_kernel<8>, 8, kMlpFusedThreads, kMlpFusedSmemBytes, rt->stream, fa);
         HX_LAUNCHED(rt);
         return;
     }

@@ -26,6 +26,8 @@
 // GEMM epilogues do (E = P - Y, dP = E * s, W - lr*dW with two roundings).
 #pragma once
 
+#include "pdl.cuh"
+
 #include "hx_internal.cuh"
 #include "tc_ptx.cuh"
 
@@ -64,6 +66,7 @@ template <int CL>
 __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(kMlpFusedThreads, 1)
 mlp_fused_step_kernel(MlpFusedArgs a)
 {
+    HX_PDL_PROLOGUE();
     extern __shared__ float4 smem4[];
     float* Xs = reinterpret_cast<float*>(smem4);
     float* As = Xs + kMlpFusedX;

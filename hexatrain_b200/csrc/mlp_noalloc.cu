@@ -143,8 +143,7 @@ void gemm_noalloc(hx_runtime* rt, int M, int N, int K, const float* A, long lda,
         using S = SimtShape<T::BM, T::BN, T::BK, T::TX, T::TY>;
         const int chunk = K > 0 ? ((K + T::BK - 1) / T::BK) * T::BK : T::BK;
         dim3 grid((N + T::BN - 1) / T::BN, (M + T::BM - 1) / T::BM, 1);
-        gemm_simt_kernel<S, T::BM, T::BN, T::BK, T::TX, T::TY, AT, BT, Epi>
-            <<<grid, S::kThreads, 0, rt->stream>>>(M, N, K, A, lda, B, ldb, chunk, epi, nullptr);
+        ::hx::pdl_launch(gemm_simt_kernel<S, T::BM, T::BN, T::BK, T::TX, T::TY, AT, BT, Epi>, grid, S::kThreads, 0, rt->stream, M, N, K, A, lda, B, ldb, chunk, epi, nullptr);
         HX_LAUNCHED(rt);
     };
     const long mn = (long)M * N;

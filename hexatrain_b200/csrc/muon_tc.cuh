@@ -21,6 +21,8 @@
 // kMuonTcErr in the runtime's error word, frees its TMEM and returns.
 #pragma once
 
+#include "pdl.cuh"
+
 #include <cuda_bf16.h>
 
 #include <cstddef>
@@ -98,6 +100,7 @@ __global__ void __launch_bounds__(kMuonTcThreads, 1)
 muon_tc_kernel(const MuonMatrix* __restrict__ mats, MuonScalars s, const float* __restrict__ lr_dev,
                int* __restrict__ err)
 {
+    HX_PDL_PROLOGUE();
     extern __shared__ uint8_t smem_raw[];
     MuonTcSmem& sm = *reinterpret_cast<MuonTcSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const int t = threadIdx.x, warp = t >> 5;

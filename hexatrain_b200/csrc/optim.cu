@@ -13,6 +13,7 @@ namespace hx {
 // first), A [R][R], Bm [R][R].  Limits: R <= 128, R*C <= 16384.
 __global__ void muon_kernel(const MuonMatrix* __restrict__ mats, MuonScalars s, const float* __restrict__ lr_dev)
 {
+    HX_PDL_PROLOGUE();
     if (lr_dev) s.lr = *lr_dev;
     extern __shared__ float sm[];
     const MuonMatrix mt = mats[blockIdx.x];
@@ -113,9 +114,9 @@ void launch_adam(hx_runtime* rt, bool graph_order, size_t n, const float* w, con
     const size_t work = graph_order ? n : (n + 3) / 4;
     const int blocks = (int)std::min<size_t>((work + threads - 1) / threads, size_t(rt->sm_count) * 16);
     if (graph_order)
-        adam_kernel<true><<<blocks, threads, 0, rt->stream>>>(n, w, g, m, v, wn, mn, vn, s, t, scale_dev, s_dev);
+        ::hx::pdl_launch(adam_kernel<true>, blocks, threads, 0, rt->stream, n, w, g, m, v, wn, mn, vn, s, t, scale_dev, s_dev);
     else
-        adam_kernel<false><<<blocks, threads, 0, rt->stream>>>(n, w, g, m, v, wn, mn, vn, s, t, scale_dev, s_dev);
+        ::hx::pdl_launch(adam_kernel<false>, blocks, threads, 0, rt->stream, n, w, g, m, v, wn, mn, vn, s, t, scale_dev, s_dev);
     HX_LAUNCHED(rt);
 }
 
@@ -123,6 +124,7 @@ __global__ void momentum_kernel(size_t n, const float* w, const float* __restric
                                 float* w_next, float* vel_next, float lr, float momentum,
                                 const float* __restrict__ lr_dev)
 {
+    HX_PDL_PROLOGUE();
     if (lr_dev) lr = *lr_dev;
     const size_t stride = (size_t)gridDim.x * blockDim.x;
     const size_t tid = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -165,7 +167,7 @@ void launch_momentum(hx_runtime* rt, size_t n, const float* w, const float* g, c
     ProfScope prof(rt, kTagOptimizer, 3.0 * n, 20.0 * n);
     const int threads = 256;
     const int blocks = (int)std::min<size_t>(((n + 3) / 4 + threads - 1) / threads, size_t(rt->sm_count) * 16);
-    momentum_kernel<<<blocks, threads, 0, rt->stream>>>(n, w, g, vel, wn, veln, lr, momentum, lr_dev);
+    ::hx::pdl_launch(momentum_kernel, blocks, threads, 0, rt->stream, n, w, g, vel, wn, veln, lr, momentum, lr_dev);
     HX_LAUNCHED(rt);
 }
 
@@ -175,6 +177,7 @@ __global__ void __launch_bounds__(kNormThreads) grad_sumsq_kernel(const float* _
                                                                   const GradTensor* __restrict__ tensors,
                                                                   double* __restrict__ sumsq)
 {
+    HX_PDL_PROLOGUE();
     const GradTensor t = tensors[blockIdx.x];
     const float* p = g + t.offset;
     double s = 0.0;
@@ -196,6 +199,7 @@ __global__ void __launch_bounds__(kNormThreads) grad_sumsq_kernel(const float* _
 __global__ void clip_scale_kernel(const double* __restrict__ sumsq, int tensors, float threshold,
                                   double* __restrict__ norm_out, float* __restrict__ scale_out)
 {
+    HX_PDL_PROLOGUE();
     if (threadIdx.x != 0 || blockIdx.x != 0) return;
     double sum = 0.0;
     for (int i = 0; i < tensors; ++i) {
@@ -213,9 +217,9 @@ void launch_clip_scale(hx_runtime* rt, const float* g, const GradTensor* tensors
                        float threshold, double* norm_out, float* scale_out)
 {
     ProfScope prof(rt, kTagReduce, 0.0, 0.0);
-    grad_sumsq_kernel<<<count, kNormThreads, 0, rt->stream>>>(g, tensors, sumsq);
+    ::hx::pdl_launch(grad_sumsq_kernel, count, kNormThreads, 0, rt->stream, g, tensors, sumsq);
     HX_LAUNCHED(rt);
-    clip_scale_kernel<<<1, 32, 0, rt->stream>>>(sumsq, count, threshold, norm_out, scale_out);
+    ::hx::pdl_launch(clip_scale_kernel, 1, 32, 0, rt->stream, sumsq, count, threshold, norm_out, scale_out);
     HX_LAUNCHED(rt);
 }
 
@@ -249,13 +253,13 @@ void launch_muon(hx_runtime* rt, const MuonMatrix* d_mats, int count, size_t sme
     if (s.bf16 && tc_shapes && rt->gemm_backend != HX_GEMM_CUDA_CORES) {
         HX_CUDA(cudaFuncSetAttribute(muon_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      (int)kMuonTcSmemBytes));
-        muon_tc_kernel<<<count, kMuonTcThreads, kMuonTcSmemBytes, rt->stream>>>(d_mats, s, lr_dev,
+        ::hx::pdl_launch(muon_tc_kernel, count, kMuonTcThreads, kMuonTcSmemBytes, rt->stream, d_mats, s, lr_dev,
                                                                                rt->device_error());
         HX_LAUNCHED(rt);
         return;
     }
     HX_CUDA(cudaFuncSetAttribute(muon_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    muon_kernel<<<count, 1024, smem, rt->stream>>>(d_mats, s, lr_dev);
+    ::hx::pdl_launch(muon_kernel, count, 1024, smem, rt->stream, d_mats, s, lr_dev);
     HX_LAUNCHED(rt);
 }
 

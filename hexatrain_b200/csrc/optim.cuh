@@ -2,6 +2,8 @@
 // accesses) and Muon's momentum + Newton-Schulz orthogonalisation.
 #pragma once
 
+#include "pdl.cuh"
+
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <cstdint>
@@ -58,6 +60,7 @@ __global__ void adam_kernel(size_t n, const float* w, const float* __restrict__ 
                             const float* v, float* w_next, float* m_next, float* v_next, AdamScalars s,
                             AdamTaps t, const float* __restrict__ scale_dev, const AdamScalars* __restrict__ s_dev)
 {
+    HX_PDL_PROLOGUE();
     // Scalars in device memory (a captured training step, whose learning
     // rate and bias corrections change every step) replace the by-value
     // ones; a gradient scale computed on the device (the global-norm clip)

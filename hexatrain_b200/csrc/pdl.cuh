@@ -1,0 +1,26 @@
+// pdl.cuh -- programmatic dependent launch between consecutive kernels.
+//
+// Every kernel of the library is launched with programmatic stream
+// serialisation allowed and starts with HX_PDL_PROLOGUE(), a
+// griddepcontrol.wait: it returns once every grid this one depends on has
+// completed and its writes are visible (a no-op without a dependency).
+// No kernel triggers its dependents early, so the next kernel of the stream
+// is launched as the CTAs of this one exit (the implicit trigger) instead of
+// after the whole grid has drained and its completion has reached the host
+// queue: its launch overlaps this kernel's tail and memory flush.
+//
+// Measured on B200 (one step of the tiny-Transformer LM, CUDA graph):
+//   no PDL                                     cfg4 763 us, cfg3 325 us, b64 3.678 ms
+//   wait + launch_dependents at kernel entry   cfg4 844 us, cfg3 324 us, b64 3.643 ms
+//   wait only (this prologue)                  cfg4 717-725 us, cfg3 312 us, b64 3.622 ms
+// An entry trigger lets the next kernel's CTAs sit resident, waiting, on the
+// SMs the side stream's weight-gradient GEMMs would use, which costs more than
+// the launch latency it hides.
+//
+// Because every kernel waits before its first instruction, completion is
+// transitive along the stream: kernel k+2 may read what kernel k wrote.
+// The wait comes before anything else, so no CTA holds tensor memory or
+// spins on a barrier while a grid it depends on is still running.
+#pragma once
+
+#define HX_PDL_PROLOGUE() asm volatile("griddepcontrol.wait;" ::: "memory")

@@ -29,6 +29,7 @@ namespace {
 // Nothing else is in flight in this block (no TMA copy, no MMA, no TMEM).
 __global__ void wait_timeout_probe_kernel(long long limit, int* err)
 {
+    HX_PDL_PROLOGUE();
     __shared__ __align__(8) uint64_t bar;
     if (threadIdx.x == 0) {
         hx::tc::mbar_init(&bar, 1);
@@ -166,7 +167,7 @@ int hx_runtime_check_wait_timeout(hx_runtime* rt, long long cycles) {
     return hx_guard(rt, [&] {
         hx::require(cycles > 0 && cycles <= 4000000000LL, HX_ERR_ARGUMENT,
                     "wait self-test: cycles must be in (0, 4e9]");
-        wait_timeout_probe_kernel<<<1, 32, 0, rt->stream>>>(cycles, rt->device_error());
+        ::hx::pdl_launch(wait_timeout_probe_kernel, 1, 32, 0, rt->stream, cycles, rt->device_error());
         HX_LAUNCHED(rt);
         rt->check_device_error();
     });
