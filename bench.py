@@ -91,14 +91,40 @@ def measured_peaks():
 
 
 class ClockSampler:
-    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+    """SM clocks and throttle reasons sampled during the timed region: NVML
+    read every 10 ms from a host thread (read-only queries), or nvidia-smi at
+    200 ms where NVML is unavailable."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = (("hw_slowdown", 0x8), ("hw_thermal_slowdown", 0x40), ("sw_thermal_slowdown", 0x20),
+               ("sw_power_cap", 0x4))
 
-    def __init__(self, gpu_index: int):
-        self.gpu = gpu_index
+    def __init__(self, gpu_index: int, period_s: float = 0.01):
+        import threading
+
+        self.gpu, self.p, self.thread = gpu_index, None, None
+        self.mhz, self.mx, self.reasons = [], [], set()
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self.nvml = pynvml
+            self.handle = pynvml.nvmlDeviceGetHandleByIndex(gpu_index)
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM))
+        except Exception:
+            self.nvml = None
+        if self.nvml is not None:
+            self.done = threading.Event()
+
+            def loop():
+                while not self.done.wait(period_s):
+                    self.sample()
+
+            self.thread = threading.Thread(target=loop, daemon=True)
+            self.thread.start()
+            return
         try:
             self.p = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
                                        "-i", str(gpu_index), "-lms", "200"], stdout=subprocess.PIPE,
@@ -106,7 +132,29 @@ class ClockSampler:
         except OSError:
             self.p = None
 
+    def sample(self):
+        try:
+            mhz = float(self.nvml.nvmlDeviceGetClockInfo(self.handle, self.nvml.NVML_CLOCK_SM))
+            mask = int(self.nvml.nvmlDeviceGetCurrentClocksEventReasons(self.handle))
+        except Exception:
+            return
+        self.mhz.append(mhz)
+        self.mx.append(self.max_mhz)
+        for n, bit in self.REASONS:
+            if mask & bit:
+                self.reasons.add(n)
+
     def stop(self):
+        if self.thread is not None:
+            self.done.set()
+            self.thread.join(timeout=5)
+            if not self.mhz:
+                self.sample()  # a region shorter than the period: one sample at its end
+            try:
+                self.nvml.nvmlShutdown()
+            except Exception:
+                pass
+            return self.summary("nvml, 10 ms")
         if self.p is None:
             return None
         self.p.terminate()
@@ -115,24 +163,26 @@ class ClockSampler:
         except subprocess.TimeoutExpired:
             self.p.kill()
             out = self.p.communicate()[0]
-        mhz, mx, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        names = [n for n, _ in self.REASONS]
         for line in out.strip().splitlines():
             parts = [x.strip() for x in line.split(",")]
             if len(parts) < 9:
                 continue
             try:
-                mhz.append(float(parts[1]))
-                mx.append(float(parts[2]))
+                self.mhz.append(float(parts[1]))
+                self.mx.append(float(parts[2]))
             except ValueError:
                 continue
             for n, v in zip(names, parts[5:9]):
                 if v.lower().startswith("active"):
-                    reasons.add(n)
-        if not mhz:
+                    self.reasons.add(n)
+        return self.summary("nvidia-smi, 200 ms")
+
+    def summary(self, source):
+        if not self.mhz:
             return None
-        return {"sm_mhz": statistics.median(mhz), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
-                "samples": len(mhz)}
+        return {"sm_mhz": statistics.median(self.mhz), "sm_max_mhz": max(self.mx), "reasons": sorted(self.reasons),
+                "samples": len(self.mhz), "source": source}
 
 
 def physical_gpu(local_rank: int) -> int:
