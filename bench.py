@@ -9,7 +9,7 @@ seeded Zipf(1.1) token ids split evenly over ranks; per-step gradient
 all-reduce (NCCL) for N > 1.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                  [--config lm-cfg5|lm-cfg3|lm-cfg4|mlp-cfg1|mlp-cfg2a|mlp-cfg2b]
+                  [--config lm-t256-d256-f1024-l4-h8|lm-t64-d64-f64-l2-h4|lm-t64-d48-f48-l4-h4-muon|mlp-8x128x128x64|mlp-32x256x256x128|mlp-4096x1024x1024x512]
 
 Prints one JSON line (rank 0).  `value` is device-timed whole-job tokens/s
 with the step's inputs already in HBM (steps replay captured CUDA graphs);
@@ -42,14 +42,14 @@ FP32_CUDA_CORE_PEAK_TFLOPS = 148 * 128 * 2 * 1.965e9 / 1e12  # nominal, at max S
 # The five configurations.  LM: (V, T, D, F, L, H), batch, optimizer.  MLP:
 # B/I/H/O, SGD learning rate, sample-set size (cyclic batches) and steps.
 CONFIGS = {
-    "lm-cfg5": dict(kind="lm", shape=(1024, 256, 256, 1024, 4, 8), batch=512, opt="adam"),
-    "lm-cfg3": dict(kind="lm", shape=(1024, 64, 64, 64, 2, 4), batch=16, opt="adam"),
-    "lm-cfg4": dict(kind="lm", shape=(1024, 64, 48, 48, 4, 4), batch=32, opt="muon"),
-    "mlp-cfg1": dict(kind="mlp", dims=(8, 128, 128, 64), lr=0.5, samples=512, steps=640),
-    "mlp-cfg2a": dict(kind="mlp", dims=(32, 256, 256, 128), lr=0.05, samples=4 * 32, steps=1000),
-    "mlp-cfg2b": dict(kind="mlp", dims=(4096, 1024, 1024, 512), lr=0.05, samples=4 * 4096, steps=1000),
+    "lm-t256-d256-f1024-l4-h8": dict(kind="lm", shape=(1024, 256, 256, 1024, 4, 8), batch=512, opt="adam"),
+    "lm-t64-d64-f64-l2-h4": dict(kind="lm", shape=(1024, 64, 64, 64, 2, 4), batch=16, opt="adam"),
+    "lm-t64-d48-f48-l4-h4-muon": dict(kind="lm", shape=(1024, 64, 48, 48, 4, 4), batch=32, opt="muon"),
+    "mlp-8x128x128x64": dict(kind="mlp", dims=(8, 128, 128, 64), lr=0.5, samples=512, steps=640),
+    "mlp-32x256x256x128": dict(kind="mlp", dims=(32, 256, 256, 128), lr=0.05, samples=4 * 32, steps=1000),
+    "mlp-4096x1024x1024x512": dict(kind="mlp", dims=(4096, 1024, 1024, 512), lr=0.05, samples=4 * 4096, steps=1000),
 }
-SMALL = ["mlp-cfg1", "mlp-cfg2a", "mlp-cfg2b", "lm-cfg3", "lm-cfg4"]
+SMALL = ["mlp-8x128x128x64", "mlp-32x256x256x128", "mlp-4096x1024x1024x512", "lm-t64-d64-f64-l2-h4", "lm-t64-d48-f48-l4-h4-muon"]
 
 
 def lm_workload(name):
@@ -73,7 +73,7 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=sorted(CONFIGS), default="lm-cfg5")
+    ap.add_argument("--config", choices=sorted(CONFIGS), default="lm-t256-d256-f1024-l4-h8")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-small-configs", action="store_true")
     ap.add_argument("--global-batch", type=int, default=None,
@@ -682,7 +682,7 @@ def run_ours(args):
                 B = c["dims"][0]
                 cb = cpu_mlp_sample(name, steps=3, warmup=1, rows=64 if B > 64 else None)
             line["cpu_baseline"] = cb
-        if world == 1 and name == "lm-cfg5" and not args.no_small_configs:
+        if world == 1 and name == "lm-t256-d256-f1024-l4-h8" and not args.no_small_configs:
             line["small_configs"] = {n: small_config_entry(n, cpu=not args.no_cpu_baseline) for n in SMALL}
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -9,10 +9,12 @@
 // after the whole grid has drained and its completion has reached the host
 // queue: its launch overlaps this kernel's tail and memory flush.
 //
-// Measured on B200 (one step of the tiny-Transformer LM, CUDA graph):
-//   no PDL                                     cfg4 763 us, cfg3 325 us, b64 3.678 ms
-//   wait + launch_dependents at kernel entry   cfg4 844 us, cfg3 324 us, b64 3.643 ms
-//   wait only (this prologue)                  cfg4 717-725 us, cfg3 312 us, b64 3.622 ms
+// Measured on B200 (one step of the tiny-Transformer LM, CUDA graph; A =
+// T64 D48 F48 L4 H4 with Muon, 32 sequences; B = T64 D64 F64 L2 H4 with Adam,
+// 16 sequences; C = T256 D256 F1024 L4 H8, 64 sequences):
+//   no PDL                                     A 763 us, B 325 us, C 3.678 ms
+//   wait + launch_dependents at kernel entry   A 844 us, B 324 us, C 3.643 ms
+//   wait only (this prologue)                  A 717-725 us, B 312 us, C 3.622 ms
 // An entry trigger lets the next kernel's CTAs sit resident, waiting, on the
 // SMs the side stream's weight-gradient GEMMs would use, which costs more than
 // the launch latency it hides.

@@ -12,7 +12,7 @@ docs/results/qnn-htp-full-training-step-2026-07/seeds.csv), which reports
 initial and final loss per seed and their spread.
 
   python -m torch.distributed.run --nproc-per-node 8 --master-addr 127.0.0.1 \\
-      -m hexatrain_b200.replicas --config lm-cfg5 --steps 50 --out sweep.json
+      -m hexatrain_b200.replicas --config lm-t256-d256-f1024-l4-h8 --steps 50 --out sweep.json
 
 The training function is injectable so that the host logic (seed
 assignment, gather, summary) is tested with CPU stand-ins.
@@ -31,9 +31,9 @@ FIRST_SEED = 20260710
 
 # (V, T, D, F, L, H), batch, optimizer: the LM configurations.
 LM_CONFIGS = {
-    "lm-cfg3": ((1024, 64, 64, 64, 2, 4), 16, "adam"),
-    "lm-cfg4": ((1024, 64, 48, 48, 4, 4), 32, "muon"),
-    "lm-cfg5": ((1024, 256, 256, 1024, 4, 8), 512, "adam"),
+    "lm-t64-d64-f64-l2-h4": ((1024, 64, 64, 64, 2, 4), 16, "adam"),
+    "lm-t64-d48-f48-l4-h4-muon": ((1024, 64, 48, 48, 4, 4), 32, "muon"),
+    "lm-t256-d256-f1024-l4-h8": ((1024, 256, 256, 1024, 4, 8), 512, "adam"),
 }
 
 
@@ -132,7 +132,7 @@ def run(config: str, steps: int, out: Optional[str], first_seed: int = FIRST_SEE
 
 def main() -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--config", choices=sorted(LM_CONFIGS), default="lm-cfg5")
+    ap.add_argument("--config", choices=sorted(LM_CONFIGS), default="lm-t256-d256-f1024-l4-h8")
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--first-seed", type=int, default=FIRST_SEED)
     ap.add_argument("--batch", type=int, default=None, help="sequences per replica step (default: the config's)")

@@ -67,7 +67,7 @@ def mlp_cases(ref: Reference):
 
 
 def mlp_trajectory(ref: Reference):
-    """cfg1-shaped trajectory: 64 samples, cyclic batches of 8, 16 steps."""
+    """Trajectory of the 8/128/128/64 MLP: 64 samples, cyclic batches of 8, 16 steps."""
     rng = np.random.default_rng(7)
     B, I, H, O, lr, samples, steps = 8, 128, 128, 64, 0.5, 64, 16
     X = rng.uniform(-1, 1, (samples, I)).astype(np.float32)
@@ -83,7 +83,7 @@ def mlp_trajectory(ref: Reference):
         w1, w2 = s.w1_next, s.w2_next
         c1.append(summary(w1)["checksum"])
         c2.append(summary(w2)["checksum"])
-    save("mlp_trajectory_cfg1.npz", X=X, Y=Y, w1_init=w1_0, w2_init=w2_0, lr=np.float32(lr),
+    save("mlp_trajectory_8x128x128x64.npz", X=X, Y=Y, w1_init=w1_0, w2_init=w2_0, lr=np.float32(lr),
          batch=np.int64(B), losses=np.array(losses, np.float32), w1_checksums=np.array(c1),
          w2_checksums=np.array(c2), w1_final=w1, w2_final=w2)
 
@@ -113,7 +113,7 @@ def lm_small(ref: Reference):
 
 
 def lm_large(ref: Reference):
-    """Baseline-shaped single sequences (cfg3 / cfg4 shapes), summarised."""
+    """Single sequences of the benchmarked LM shapes (T64 D64 F64 L2 H4 and T64 D48 F48 L4 H4), summarised."""
     rng = np.random.default_rng(1234)
     for (V, T, D, F, L, H) in [(1024, 64, 64, 64, 2, 4), (1024, 64, 48, 48, 4, 4)]:
         cfg = LmConfig.make(V, T, D, F, L, H)

@@ -9,7 +9,7 @@ import pytest
 from conftest import ROOT
 
 
-@pytest.mark.parametrize("config", ["mlp-cfg1", "lm-cfg3"])
+@pytest.mark.parametrize("config", ["mlp-8x128x128x64", "lm-t64-d64-f64-l2-h4"])
 def test_reference_arm_prints_one_contract_line(config):
     from oracle.oracle import reference_available
     if not reference_available():

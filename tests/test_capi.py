@@ -70,8 +70,8 @@ def test_parameter_count_matches_registry(cfg, oracle):
     assert last[1] + int(np.prod(last[2])) == c.parameter_count()
 
 
-def test_baseline_parameter_counts():
-    # SURVEY-computed per-sequence parameter counts of the three LM configurations
+def test_lm_parameter_counts():
+    # per-sequence parameter counts of the three LM configurations (V1024: T64 D64 F64 L2 H4, T64 D48 F48 L4 H4, T256 D256 F1024 L4 H8)
     assert hx.LmConfig(1024, 64, 64, 64, 2, 4).parameter_count() == 180736
     assert hx.LmConfig(1024, 64, 48, 48, 4, 4).parameter_count() == 154368
     assert hx.LmConfig(1024, 256, 256, 1024, 4, 8).parameter_count() == 3674112

@@ -16,7 +16,7 @@ reference's sources) or with the oracle pinned to it:
   O64 and 1000 ping-pong steps at B32 I256 H256 O128, gated like the
   reference driver (qnn/qnn_mlp_training.cpp:783-787).
 
-Tolerances (north_star): per-step loss and every gradient tensor within 1e-4
+Tolerances: per-step loss and every gradient tensor within 1e-4
 relative (max|got-want| / max|want|), weights within 1e-2 max-abs after the
 stated steps.  The tests also record tighter figures in their messages.
 """
@@ -69,7 +69,7 @@ def test_benchmark_shape_16_sequences_matches_reference(gpu_runtime, reference):
     worst = _grads_per_tensor(cfg, m, rm)
     assert np.max(np.abs(params - rp)) <= W_ABS
     assert rel_err(v, rv) <= 2 * TOL, rel_err(v, rv)
-    print(f"cfg5 B16: loss {loss} ref {rloss}; worst gradient tensor {worst:.2e}")
+    print(f"T256 D256 F1024 L4 H8, B16: loss {loss} ref {rloss}; worst gradient tensor {worst:.2e}")
 
 
 def test_benchmark_shape_learned_positions_matches_oracle(gpu_runtime, oracle):
@@ -119,8 +119,8 @@ def test_weight_gradient_split_k_131072_rows_against_fp64(gpu_runtime):
 ANCHORS = (2, 4, 8)
 
 
-def test_cfg3_reference_model_8_steps_matches_reference(gpu_runtime, reference):
-    """cfg3's shape and batch (V1024 T64 D64 F64 L2 H4, 16 sequences) on the
+def test_lm_t64_d64_reference_model_8_steps_matches_reference(gpu_runtime, reference):
+    """The T64 D64 L2 shape and batch (V1024 T64 D64 F64 L2 H4, 16 sequences) on the
     reference model, 8 Adam steps of hx_lm_train_step against the
     reference's own batched train step, loss every step, weights at the
     anchors."""
@@ -145,7 +145,7 @@ def test_cfg3_reference_model_8_steps_matches_reference(gpu_runtime, reference):
             assert np.max(np.abs(params - rp)) <= W_ABS, step
             if step == 2:
                 assert rel_err(m, rm) <= TOL, rel_err(m, rm)
-    print(f"cfg3 reference model: worst weight difference at anchors {worst_w:.2e}")
+    print(f"T64 D64 L2 reference model: worst weight difference at anchors {worst_w:.2e}")
 
 
 def _oracle_trajectory(oracle, oc, cfg, p0, B, T, V, seed, steps, muon):
@@ -176,11 +176,11 @@ def _oracle_trajectory(oracle, oc, cfg, p0, B, T, V, seed, steps, muon):
 
 
 @pytest.mark.parametrize("name,shape,B,muon", [
-    ("cfg3", (1024, 64, 64, 64, 2, 4), 16, False),
-    ("cfg4", (1024, 64, 48, 48, 4, 4), 32, True),
+    ("t64-d64-l2-adam", (1024, 64, 64, 64, 2, 4), 16, False),
+    ("t64-d48-l4-muon", (1024, 64, 48, 48, 4, 4), 32, True),
 ])
 def test_small_lm_configs_as_specified_8_steps_match_oracle(gpu_runtime, oracle, name, shape, B, muon):
-    """cfg3 (Adam) and cfg4 (Muon momentum 0.95 Nesterov, NS5 on bf16
+    """T64 D64 L2 H4 (Adam) and T64 D48 L4 H4 (Muon momentum 0.95 Nesterov, NS5 on bf16
     operands, Adam elsewhere) as specified: learned positions, N(0, 0.02),
     Zipf ids, their batch sizes, 8 steps; loss every step, weights at the
     anchors."""
@@ -222,8 +222,8 @@ def _mlp_gates(x, y, w1, w2, B, lr, steps, reference, step_fn):
     return cw1, cw2, worst_loss
 
 
-def test_mlp_cfg1_640_steps_matches_reference(gpu_runtime, reference):
-    """cfg1: B8 I128 H128 O64, lr 0.5, 512 samples, 10 epochs = 640 steps of
+def test_mlp_8x128x128x64_640_steps_matches_reference(gpu_runtime, reference):
+    """MLP B8 I128 H128 O64, lr 0.5, 512 samples, 10 epochs = 640 steps of
     the host-vector execute, ping-pong on the host."""
     B, I, H, O, S, lr = 8, 128, 128, 64, 512, 0.5
     x, y, w1, w2 = data.mlp_data(20260710, S, I, H, O)
@@ -240,11 +240,11 @@ def test_mlp_cfg1_640_steps_matches_reference(gpu_runtime, reference):
     rw1, rw2, wl = _mlp_gates(x, y, w1, w2, B, lr, 640, reference, step)
     d = max(float(np.max(np.abs(cur[0] - rw1.ravel()))), float(np.max(np.abs(cur[1] - rw2.ravel()))))
     assert d <= W_ABS, d
-    print(f"cfg1 640 steps: worst loss {wl:.2e} relative, final weights {d:.2e} max-abs")
+    print(f"MLP 8x128x128x64, 640 steps: worst loss {wl:.2e} relative, final weights {d:.2e} max-abs")
 
 
-def test_mlp_cfg2a_1000_ping_pong_steps_matches_reference(gpu_runtime, reference):
-    """cfg2a: B32 I256 H256 O128, lr 0.05, 1000 steps of the device step with
+def test_mlp_32x256x256x128_1000_ping_pong_steps_matches_reference(gpu_runtime, reference):
+    """MLP B32 I256 H256 O128, lr 0.05, 1000 steps of the device step with
     the two weight buffers swapped every step (no weight copies)."""
     import torch
     B, I, H, O, lr = 32, 256, 256, 128, 0.05
@@ -273,4 +273,4 @@ def test_mlp_cfg2a_1000_ping_pong_steps_matches_reference(gpu_runtime, reference
     d = max(float(np.max(np.abs(fin[0].cpu().numpy() - rw1.ravel()))),
             float(np.max(np.abs(fin[1].cpu().numpy() - rw2.ravel()))))
     assert d <= W_ABS, d
-    print(f"cfg2a 1000 steps: worst loss {wl:.2e} relative, final weights {d:.2e} max-abs")
+    print(f"MLP 32x256x256x128, 1000 steps: worst loss {wl:.2e} relative, final weights {d:.2e} max-abs")

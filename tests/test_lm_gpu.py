@@ -59,7 +59,7 @@ def test_lm_one_hot_execute_matches_golden(gpu_runtime, name):
 
 
 @pytest.mark.parametrize("name", ["lm_V1024_T64_D64_F64_L2_H4.npz", "lm_V1024_T64_D48_F48_L4_H4.npz"])
-def test_lm_baseline_shapes_match_golden(gpu_runtime, name):
+def test_lm_benchmark_shapes_match_golden(gpu_runtime, name):
     g = golden(name)
     V, T, D, F, L, H = (int(v) for v in g["cfg"])
     cfg = hx.LmConfig(V, T, D, F, L, H)
@@ -77,9 +77,9 @@ def test_lm_baseline_shapes_match_golden(gpu_runtime, name):
 
 
 @pytest.mark.parametrize("shape,B,learned,init", [
-    ((1024, 64, 64, 64, 2, 4), 4, False, "reference"),   # cfg3 shape
-    ((1024, 64, 48, 48, 4, 4), 4, False, "reference"),   # cfg4 shape
-    ((1024, 64, 64, 64, 2, 4), 3, True, "normal"),       # cfg3 as specified: learned positions, N(0, 0.02)
+    ((1024, 64, 64, 64, 2, 4), 4, False, "reference"),   # T64 D64 F64 L2 H4
+    ((1024, 64, 48, 48, 4, 4), 4, False, "reference"),   # T64 D48 F48 L4 H4
+    ((1024, 64, 64, 64, 2, 4), 3, True, "normal"),       # T64 D64 L2 as benchmarked: learned positions, N(0, 0.02)
     ((96, 20, 24, 40, 3, 2), 5, True, "normal"),
 ])
 def test_lm_batched_gradients_match_oracle(gpu_runtime, oracle, shape, B, learned, init):
@@ -162,7 +162,7 @@ def test_lm_data_parallel_split_equals_fused_step(gpu_runtime):
 
 
 def test_lm_muon_steps_match_oracle(gpu_runtime, oracle):
-    """cfg4 optimizer split on a small model: Muon (momentum 0.95, Nesterov,
+    """The Muon configuration's optimizer split on a small model: Muon (momentum 0.95, Nesterov,
     5 NS steps, bf16 operands) on wq,wk,wv,wo,ffn_w1,ffn_w2; Adam elsewhere."""
     V, T, D, F, L, H, B = 64, 16, 48, 48, 2, 4, 4
     cfg = hx.LmConfig(V, T, D, F, L, H, learned_position=True)

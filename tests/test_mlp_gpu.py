@@ -114,7 +114,7 @@ def test_mlp_largest_config_against_fp64(gpu_runtime):
 def test_mlp_trajectory_matches_golden(gpu_runtime):
     """16 cyclic-batch steps with ping-pong weights through the host API
     (trainFullStep, qnn/qnn_mlp_training.cpp:674-770)."""
-    g = golden("mlp_trajectory_cfg1.npz")
+    g = golden("mlp_trajectory_8x128x128x64.npz")
     X, Y, B = g["X"], g["Y"], int(g["batch"])
     I, H = g["w1_init"].shape
     O = g["w2_init"].shape[1]

@@ -67,7 +67,7 @@ def test_oracle_mlp_equals_golden(oracle, name):
 
 
 def test_oracle_mlp_trajectory_equals_golden(oracle):
-    g = golden("mlp_trajectory_cfg1.npz")
+    g = golden("mlp_trajectory_8x128x128x64.npz")
     X, Y, w1, w2, lr, B = g["X"], g["Y"], g["w1_init"], g["w2_init"], float(g["lr"]), int(g["batch"])
     for st, want in enumerate(g["losses"]):
         rows = (st * B + np.arange(B)) % X.shape[0]
@@ -89,7 +89,7 @@ def test_oracle_lm_equals_golden(oracle, name):
 
 
 @pytest.mark.parametrize("name", ["lm_V1024_T64_D64_F64_L2_H4.npz", "lm_V1024_T64_D48_F48_L4_H4.npz"])
-def test_oracle_lm_baseline_shapes_equal_golden(oracle, name):
+def test_oracle_lm_benchmark_shapes_equal_golden(oracle, name):
     import hexatrain_b200 as hx
     g = golden(name)
     V, T, D, F, L, H = (int(v) for v in g["cfg"])

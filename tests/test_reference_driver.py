@@ -32,7 +32,7 @@ def test_driver_fails_closed_without_a_device(driver):
 
 @pytest.mark.gpu
 def test_mlp_full_step_mode_32_passes_the_reference_gates(driver):
-    """cfg1 through the reference driver: 8/128/128/64, lr 0.5, 512 samples,
+    """The 8/128/128/64 MLP through the reference driver: 8/128/128/64, lr 0.5, 512 samples,
     10 epochs (640 steps) of executeMlpFullStep with all diagnostic outputs,
     each step compared with the driver's own pass()."""
     kv, text = driver.run_mode(32, 8, 128, 128, 64, epochs=10, sample_count=512, learning_rate=0.5)

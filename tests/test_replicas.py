@@ -34,7 +34,7 @@ def fake_train(config, seed, steps, device=0, batch=None):
 def _rank(rank, world, port, out):
     os.environ.update({"RANK": str(rank), "WORLD_SIZE": str(world), "LOCAL_RANK": str(rank),
                        "MASTER_ADDR": "127.0.0.1", "MASTER_PORT": str(port)})
-    replicas.run("lm-cfg3", 5, out if rank == 0 else None, train=fake_train)
+    replicas.run("lm-t64-d64-f64-l2-h4", 5, out if rank == 0 else None, train=fake_train)
 
 
 def test_two_gloo_ranks_train_their_own_seeds(tmp_path):
@@ -51,13 +51,13 @@ def test_two_gloo_ranks_train_their_own_seeds(tmp_path):
 def test_single_process_runs_the_first_seed(tmp_path, monkeypatch):
     for k in ("RANK", "WORLD_SIZE", "LOCAL_RANK"):
         monkeypatch.delenv(k, raising=False)
-    s = replicas.run("lm-cfg4", 3, None, first_seed=11, train=fake_train)
+    s = replicas.run("lm-t64-d48-f48-l4-h4-muon", 3, None, first_seed=11, train=fake_train)
     assert s["seeds"] == [11] and s["final_loss_stdev"] == 0.0
 
 
 @pytest.mark.gpu
 def test_two_seeds_on_one_gpu_match_the_oracle(oracle):
-    """Two replicas of cfg3's model (V1024 T64 D64 F64 L2 H4, learned
+    """Two replicas of the T64 D64 L2 model (V1024 T64 D64 F64 L2 H4, learned
     positions, N(0, 0.02), Adam) at 8 sequences, 4 steps each, each against
     the oracle's own trajectory for the same seed."""
     import hexatrain_b200 as hx
@@ -69,7 +69,7 @@ def test_two_seeds_on_one_gpu_match_the_oracle(oracle):
     oc = OC.make(V, T, D, F, L, H, learned_position=True)
     finals = []
     for seed in (20260710, 20260711):
-        rec = replicas.train_replica_gpu("lm-cfg3", seed, steps, batch=B)
+        rec = replicas.train_replica_gpu("lm-t64-d64-f64-l2-h4", seed, steps, batch=B)
         w = cfg.init_normal(seed, 0.02)
         m, v = np.zeros_like(w), np.zeros_like(w)
         for step in range(1, steps + 1):
