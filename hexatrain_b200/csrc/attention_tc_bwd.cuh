@@ -410,6 +410,9 @@ attention_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap map_qk, const __g
 // ---- dK / dV kernel ----------------------------------------------------------
 
 constexpr uint32_t kKvColS = 0, kKvColDp = 128, kKvColRing = 256, kKvColAcc = 384;
+// 16 softmax warps and two MMA-issuing warps (one per product chain)
+constexpr int kAtcKvIssuers = 2;
+constexpr int kAtcKvThreads = kAtcSoftThreads + 32 * kAtcKvIssuers;
 
 struct AtcKvSmem {
     float kh[kAtcTileFloats], kl[kAtcTileFloats];        // K of the key block, K-major
@@ -442,7 +445,7 @@ __device__ __forceinline__ int atc_kv_chunk_vis(int kb, int q, int qb, int c, bo
     return c == q ? 1 : 0;
 }
 
-__global__ void __launch_bounds__(kAtcThreads, 1)
+__global__ void __launch_bounds__(kAtcKvThreads, 1)
 attention_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid_constant__ CUtensorMap map_mn,
                              const __grid_constant__ CUtensorMap map_do, const __grid_constant__ CUtensorMap map_do_mn,
                              int T, int D, int H, float scale, const float* __restrict__ qkv,
@@ -464,14 +467,15 @@ attention_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap map_qk, const _
         tc::mbar_init(&sm.ld_q, 1);
         tc::mbar_init(&sm.conv_kv, kAtcSoftThreads);
         tc::mbar_init(&sm.conv_q, kAtcSoftThreads);
-        tc::mbar_init(&sm.sd_ready, 1);
-        tc::mbar_init(&sm.blk_done, 1);
+        // committed to by both issuers
+        tc::mbar_init(&sm.sd_ready, kAtcKvIssuers);
+        tc::mbar_init(&sm.blk_done, kAtcKvIssuers);
         tc::mbar_init(&sm.drained, kAtcSoftWarps);
-        tc::mbar_init(&sm.drain, 1);
+        tc::mbar_init(&sm.drain, kAtcKvIssuers);
         for (int i = 0; i < 2; ++i) {
             tc::mbar_init(&sm.ring_full[i], 4);
-            tc::mbar_init(&sm.ring_empty[i], 1);
-            tc::mbar_init(&sm.kv_chunk[i], 1);
+            tc::mbar_init(&sm.ring_empty[i], kAtcKvIssuers);
+            tc::mbar_init(&sm.kv_chunk[i], kAtcKvIssuers);
         }
         sm.abort = 0;
         tc::fence_mbar_init();
@@ -504,83 +508,85 @@ attention_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap map_qk, const _
             atc_prefetch_rows(dctx, D, nh * kAtcDH, r0, r1, threadIdx.x, kAtcSoftThreads);
         }
     }
-    if (warp == kAtcSoftWarps) {
+    if (warp >= kAtcSoftWarps) {
+        // Two issuers, one per product chain, on two warp schedulers:
+        // role 0 issues the TMA loads, S^T = K Q^T and dV_c = P^T_c dO_c;
+        // role 1 issues dP^T = V dO^T and dK_c = dS^T_c Q_c.  Each chain's
+        // MMAs keep the single-issuer term order, so the results are the
+        // same bit for bit; the barriers the chains share count both commits.
+        const int role = warp - kAtcSoftWarps;
         if (lane == 0) {
-            tc::prefetch_tensormap(&map_qk);
-            tc::prefetch_tensormap(&map_mn);
-            tc::prefetch_tensormap(&map_do);
-            tc::prefetch_tensormap(&map_do_mn);
             const int yk = y0 + kAtcTile * kb;
-            tc::mbar_arrive_expect_tx(&sm.ld_kv, 2 * kAtcTileFloats * 4);
-            tc::tma_load_2d(sm.kh, &map_qk, &sm.ld_kv, D + h * kAtcDH, yk);
-            tc::tma_load_2d(sm.vh, &map_qk, &sm.ld_kv, 2 * D + h * kAtcDH, yk);
-            const uint32_t kh = tc::smem_u32(sm.kh), kl = tc::smem_u32(sm.kl);
-            const uint32_t vh = tc::smem_u32(sm.vh), vl = tc::smem_u32(sm.vl);
-            const uint32_t qh = tc::smem_u32(sm.qh), ql = tc::smem_u32(sm.ql);
-            const uint32_t oh = tc::smem_u32(sm.oh), ol = tc::smem_u32(sm.ol);
-            const uint32_t qmh = tc::smem_u32(sm.qmh), qml = tc::smem_u32(sm.qml);
-            const uint32_t omh = tc::smem_u32(sm.omh), oml = tc::smem_u32(sm.oml);
+            if (role == 0) {
+                tc::prefetch_tensormap(&map_qk);
+                tc::prefetch_tensormap(&map_mn);
+                tc::prefetch_tensormap(&map_do);
+                tc::prefetch_tensormap(&map_do_mn);
+                tc::mbar_arrive_expect_tx(&sm.ld_kv, 2 * kAtcTileFloats * 4);
+                tc::tma_load_2d(sm.kh, &map_qk, &sm.ld_kv, D + h * kAtcDH, yk);
+                tc::tma_load_2d(sm.vh, &map_qk, &sm.ld_kv, 2 * D + h * kAtcDH, yk);
+            }
+            // this chain's A operand of the S^T / dP^T product (K or V) and
+            // B operand (Q or dO, K-major); its chunk products' B (dO or Q,
+            // MN-major)
+            const uint32_t ah = tc::smem_u32(role ? sm.vh : sm.kh), al = tc::smem_u32(role ? sm.vl : sm.kl);
+            const uint32_t bh = tc::smem_u32(role ? sm.oh : sm.qh), bl = tc::smem_u32(role ? sm.ol : sm.ql);
+            const uint32_t mh = tc::smem_u32(role ? sm.qmh : sm.omh), ml = tc::smem_u32(role ? sm.qml : sm.oml);
+            const uint32_t col_sd = role ? kKvColDp : kKvColS;
             constexpr uint32_t idesc_s = tc::idesc_tf32(kAtcTile, kAtcTile, false, false);
             uint32_t g = 0;  // chunks issued (ring and accumulator position)
             for (int i = 0; i < nqb; ++i) {
                 const int qb = kb + i;
                 // the previous block's MMAs are done before its tiles are overwritten
                 if (i > 0) atc_wait(sm.abort, err, kAtcErrMma, &sm.blk_done, (i - 1) & 1);
-                const int yq = y0 + kAtcTile * qb;
-                tc::mbar_arrive_expect_tx(&sm.ld_q, 4 * kAtcTileFloats * 4);
-                tc::tma_load_2d(sm.qh, &map_qk, &sm.ld_q, h * kAtcDH, yq);
-                tc::tma_load_2d(sm.qmh, &map_mn, &sm.ld_q, h * kAtcDH, yq);
-                tc::tma_load_2d(sm.oh, &map_do, &sm.ld_q, h * kAtcDH, yq);
-                tc::tma_load_2d(sm.omh, &map_do_mn, &sm.ld_q, h * kAtcDH, yq);
+                if (role == 0) {
+                    const int yq = y0 + kAtcTile * qb;
+                    tc::mbar_arrive_expect_tx(&sm.ld_q, 4 * kAtcTileFloats * 4);
+                    tc::tma_load_2d(sm.qh, &map_qk, &sm.ld_q, h * kAtcDH, yq);
+                    tc::tma_load_2d(sm.qmh, &map_mn, &sm.ld_q, h * kAtcDH, yq);
+                    tc::tma_load_2d(sm.oh, &map_do, &sm.ld_q, h * kAtcDH, yq);
+                    tc::tma_load_2d(sm.omh, &map_do_mn, &sm.ld_q, h * kAtcDH, yq);
+                }
                 if (i == 0) atc_wait(sm.abort, err, kAtcErrMma, &sm.conv_kv, 0);
                 atc_wait(sm.abort, err, kAtcErrMma, &sm.conv_q, i & 1);
                 // the previous block's accumulators, over S^T / dP^T, are read
                 if (i > 0) atc_wait(sm.abort, err, kAtcErrMma, &sm.drained, (i - 1) & 1);
                 tc::tc_fence_after();
-                // S^T = K Q^T, dP^T = V dO^T (A from shared memory, same term
-                // order), the two products' MMAs interleaved
-                // (descriptors built once, k-step k at + 2 k in the start
-                // address field)
-                const uint64_t dah[2] = {tc::smem_desc(kh, 16, 1024, tc::kLayoutSw128),
-                                         tc::smem_desc(vh, 16, 1024, tc::kLayoutSw128)};
-                const uint64_t dal[2] = {tc::smem_desc(kl, 16, 1024, tc::kLayoutSw128),
-                                         tc::smem_desc(vl, 16, 1024, tc::kLayoutSw128)};
-                const uint64_t dbh[2] = {tc::smem_desc(qh, 16, 1024, tc::kLayoutSw128),
-                                         tc::smem_desc(oh, 16, 1024, tc::kLayoutSw128)};
-                const uint64_t dbl[2] = {tc::smem_desc(ql, 16, 1024, tc::kLayoutSw128),
-                                         tc::smem_desc(ol, 16, 1024, tc::kLayoutSw128)};
+                // S^T = K Q^T or dP^T = V dO^T (A from shared memory; hi*lo
+                // and lo*hi per k-step, then hi*hi; descriptors built once,
+                // k-step k at + 2 k in the start address field)
+                {
+                    const uint64_t dah = tc::smem_desc(ah, 16, 1024, tc::kLayoutSw128);
+                    const uint64_t dal = tc::smem_desc(al, 16, 1024, tc::kLayoutSw128);
+                    const uint64_t dbh = tc::smem_desc(bh, 16, 1024, tc::kLayoutSw128);
+                    const uint64_t dbl = tc::smem_desc(bl, 16, 1024, tc::kLayoutSw128);
+                    const uint32_t d = tmem + col_sd;
 #pragma unroll
-                for (int k = 0; k < kAtcDH / 8; ++k)
-#pragma unroll
-                    for (int pass = 0; pass < 2; ++pass) {
-                        const uint32_t d = tmem + (pass ? kKvColDp : kKvColS);
-                        tc::mma_tf32(d, dal[pass] + 2 * k, dbh[pass] + 2 * k, idesc_s, k > 0 ? 1u : 0u);
-                        tc::mma_tf32(d, dah[pass] + 2 * k, dbl[pass] + 2 * k, idesc_s, 1u);
+                    for (int k = 0; k < kAtcDH / 8; ++k) {
+                        tc::mma_tf32(d, dal + 2 * k, dbh + 2 * k, idesc_s, k > 0 ? 1u : 0u);
+                        tc::mma_tf32(d, dah + 2 * k, dbl + 2 * k, idesc_s, 1u);
                     }
 #pragma unroll
-                for (int k = 0; k < kAtcDH / 8; ++k)
-#pragma unroll
-                    for (int pass = 0; pass < 2; ++pass)
-                        tc::mma_tf32(tmem + (pass ? kKvColDp : kKvColS), dah[pass] + 2 * k, dbh[pass] + 2 * k, idesc_s, 1u);
+                    for (int k = 0; k < kAtcDH / 8; ++k) tc::mma_tf32(d, dah + 2 * k, dbh + 2 * k, idesc_s, 1u);
+                }
                 tc::mma_commit(&sm.sd_ready);
-                // per 32-query chunk: dV_c = P^T_c dO_c, dK_c = dS^T_c Q_c
-                // per chunk, dV_c and dK_c with their MMAs interleaved;
-                // chunk c's slot in the 2-slot lo ring is g & 1
+                // per 32-query chunk: dV_c = P^T_c dO_c (role 0) or
+                // dK_c = dS^T_c Q_c (role 1); chunk c's slot in the 2-slot lo
+                // ring is g & 1
                 for (int c = 0; c < 4; ++c, ++g) {
                     const int slot = g & 1;
                     atc_wait(sm.abort, err, kAtcErrMma, &sm.ring_full[slot], (g >> 1) & 1);
-                    // chunk g - 2's MMAs have completed, so the S^T / dP^T
-                    // columns that chunk c - 2 read are free for chunk c's
-                    // results while chunk c - 1's MMAs still run
+                    // chunk g - 2's MMAs (both chains) have completed, so the
+                    // S^T / dP^T columns that chunk c - 2 read are free for
+                    // chunk c's results while chunk c - 1's MMAs still run
                     if (g >= 2) atc_wait(sm.abort, err, kAtcErrMma, &sm.kv_chunk[g & 1], ((g >> 1) & 1) ^ 1);
                     tc::tc_fence_after();
-                    const uint32_t ring = tmem + kKvColRing + 64 * slot;
                     const uint32_t row = uint32_t(32 * c) * 128;
-                    const uint32_t d[2] = {tmem + atc_kv_acc(c, false), tmem + atc_kv_acc(c, true)};
-                    const uint32_t ahi[2] = {tmem + kKvColS + 32 * c, tmem + kKvColDp + 32 * c};
-                    const uint32_t alo[2] = {ring, ring + 32};
-                    const uint32_t bhi[2] = {omh + row, qmh + row}, blo[2] = {oml + row, qml + row};
-                    atc_mma_chunks_mn<2>(d, ahi, alo, bhi, blo);
+                    const uint32_t d[1] = {tmem + atc_kv_acc(c, role == 1)};
+                    const uint32_t ahi[1] = {tmem + col_sd + 32 * c};
+                    const uint32_t alo[1] = {tmem + kKvColRing + 64 * slot + (role ? 32u : 0u)};
+                    const uint32_t bhi[1] = {mh + row}, blo[1] = {ml + row};
+                    atc_mma_chunks_mn<1>(d, ahi, alo, bhi, blo);
                     tc::mma_commit(&sm.ring_empty[slot]);
                     tc::mma_commit(&sm.kv_chunk[g & 1]);
                 }
@@ -588,8 +594,10 @@ attention_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap map_qk, const _
             }
             tc::mma_commit(&sm.drain);
             tc::mbar_wait(&sm.drain, 0);
-            tc::mbar_wait(&sm.ld_kv, 0);
-            if (nqb > 0) tc::mbar_wait(&sm.ld_q, (nqb - 1) & 1);
+            if (role == 0) {
+                tc::mbar_wait(&sm.ld_kv, 0);
+                if (nqb > 0) tc::mbar_wait(&sm.ld_q, (nqb - 1) & 1);
+            }
         }
     } else {
         const int st = threadIdx.x;

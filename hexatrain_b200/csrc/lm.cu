@@ -218,7 +218,7 @@ void attn_bwd_tc_launch(hx_runtime* rt, const LmPlan& p, const float* qkv, const
     HX_CUDA(cudaFuncSetAttribute(attention_bwd_dkdv_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)kAtcKvSmemBytes));
     const int ntile = p.T > uint32_t(kAtcTile) ? 2 : 1;
-    ::hx::pdl_launch(attention_bwd_dkdv_tc_kernel, dim3(p.H, p.B, ntile), kAtcThreads, kAtcKvSmemBytes, rt->stream, 
+    ::hx::pdl_launch(attention_bwd_dkdv_tc_kernel, dim3(p.H, p.B, ntile), kAtcKvThreads, kAtcKvSmemBytes, rt->stream, 
         mqk, mmn, mdo, mdo_mn, p.T, p.D, p.H, scale, qkv, dctx, rmax, bstat, dqkv, rt->device_error());
     HX_LAUNCHED(rt);
 }
