@@ -52,11 +52,14 @@ CONFIGS = {
 SMALL = ["mlp-8x128x128x64", "mlp-32x256x256x128", "mlp-4096x1024x1024x512", "lm-t64-d64-f64-l2-h4", "lm-t64-d48-f48-l4-h4-muon"]
 
 
-def lm_workload(name):
+def lm_workload(name, global_batch=None):
+    """Workload and metric names; the metric keeps the configuration's own
+    global batch, the workload names the batch actually run."""
     c = CONFIGS[name]
     V, T, D, F, L, H = c["shape"]
     opt = "Muon (hidden 2-D weights) + Adam" if c["opt"] == "muon" else "Adam"
-    return (f"tiny_lm_train_step V{V} T{T} D{D} F{F} L{L} H{H} {opt} learned-pos global_batch={c['batch']}",
+    gb = global_batch or c["batch"]
+    return (f"tiny_lm_train_step V{V} T{T} D{D} F{F} L{L} H{H} {opt} learned-pos global_batch={gb}",
             f"train-step tokens/s (LM V{V} T{T} D{D} F{F} L{L} H{H}, global batch {c['batch']})")
 
 
@@ -632,7 +635,7 @@ def run_ours(args):
     K, W = args.steps, max(3, args.warmup)
     if c["kind"] == "lm":
         r = run_lm(name, K, W, world, rank, local, args.global_batch, profile_steps=3, clocks=True, dist=dist)
-        workload, metric = lm_workload(name)
+        workload, metric = lm_workload(name, r["GB"])
         GB, T, B = r["GB"], r["T"], r["B"]
         tokens_per_step, unit = GB * T, "tokens/s"
         t_ms = r["t_ms"]
