@@ -60,6 +60,11 @@ constexpr int kAtcSoftThreads = 32 * kAtcSoftWarps;
 constexpr int kAtcThreads = kAtcSoftThreads + 32;
 constexpr int kAtcRing = 4;
 constexpr uint32_t kAtcCols = 512, kAtcColS = 0, kAtcColO = 256, kAtcColRing = 384;
+// The forward runs two MMA-issuing warps beside the softmax warps: one issues
+// the loads, the first S column half and the even chunks' E V products, the
+// other the second half and the odd chunks.
+constexpr int kAtcFwdIssuers = 2;
+constexpr int kAtcFwdThreads = kAtcSoftThreads + 32 * kAtcFwdIssuers;
 constexpr int kAtcTileFloats = kAtcTile * kAtcDH;  // 128 rows x 32 fp32 = 16 KB
 constexpr float kAtcLog2e = 1.4426950408889634f;
 
@@ -161,7 +166,7 @@ __device__ __forceinline__ void atc_split(float* hi, float* lo, int n4, int t, i
     }
 }
 
-__global__ void __launch_bounds__(kAtcThreads, 1)
+__global__ void __launch_bounds__(kAtcFwdThreads, 1)
 attention_fwd_tc_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid_constant__ CUtensorMap map_v, int T,
                         int D, int H, float scale, const float* __restrict__ qkv, float* __restrict__ ctx,
                         float* __restrict__ row_max, float* __restrict__ row_sum, int* __restrict__ err)
@@ -179,16 +184,16 @@ attention_fwd_tc_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid
         for (int i = 0; i < 2; ++i) {
             tc::mbar_init(&sm.ld[i], 1);
             tc::mbar_init(&sm.conv[i], kAtcSoftThreads);
-            tc::mbar_init(&sm.pv_done[i], 1);
+            tc::mbar_init(&sm.pv_done[i], kAtcFwdIssuers);  // both issuers commit
         }
-        tc::mbar_init(&sm.s_ready, 1);
+        tc::mbar_init(&sm.s_ready, kAtcFwdIssuers);
         for (int i = 0; i < 4; ++i) tc::mbar_init(&sm.pv_chunk[i], 1);
         for (int i = 0; i < kAtcRing; ++i) {
             tc::mbar_init(&sm.ring_full[i], 4);  // the four warps that own a chunk's 128 lanes
             tc::mbar_init(&sm.ring_empty[i], 1);
         }
         tc::mbar_init(&sm.drained, kAtcSoftWarps);
-        tc::mbar_init(&sm.drain, 1);
+        tc::mbar_init(&sm.drain, kAtcFwdIssuers);
         sm.abort = 0;
         tc::fence_mbar_init();
     }
@@ -210,17 +215,25 @@ attention_fwd_tc_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid
         }
     }
 
-    if (warp == kAtcSoftWarps) {
+    if (warp >= kAtcSoftWarps) {
+        // role 0: the loads, S column half 0 and the even chunks; role 1: S
+        // column half 1 and the odd chunks.  Chunk g's ring slot (g % 4) and
+        // accumulator barrier (g & 3) have g's parity, so each belongs to one
+        // issuer; s_ready, pv_done and drain count both issuers' commits.
+        // Every accumulator gets its MMAs in the single-issuer order.
+        const int role = warp - kAtcSoftWarps;
         if (lane == 0) {
-            // ---------------- loads ----------------
-            tc::prefetch_tensormap(&map_qk);
-            tc::prefetch_tensormap(&map_v);
-            for (int t = 0; t < ntile; ++t) {
-                tc::mbar_arrive_expect_tx(&sm.ld[t], 3 * kAtcTileFloats * 4);
-                const int y = y0 + kAtcTile * t;
-                tc::tma_load_2d(sm.qh + t * kAtcTileFloats, &map_qk, &sm.ld[t], h * kAtcDH, y);
-                tc::tma_load_2d(sm.kh + t * kAtcTileFloats, &map_qk, &sm.ld[t], D + h * kAtcDH, y);
-                tc::tma_load_2d(sm.vh + t * kAtcTileFloats, &map_v, &sm.ld[t], 2 * D + h * kAtcDH, y);
+            if (role == 0) {
+                // ---------------- loads ----------------
+                tc::prefetch_tensormap(&map_qk);
+                tc::prefetch_tensormap(&map_v);
+                for (int t = 0; t < ntile; ++t) {
+                    tc::mbar_arrive_expect_tx(&sm.ld[t], 3 * kAtcTileFloats * 4);
+                    const int y = y0 + kAtcTile * t;
+                    tc::tma_load_2d(sm.qh + t * kAtcTileFloats, &map_qk, &sm.ld[t], h * kAtcDH, y);
+                    tc::tma_load_2d(sm.kh + t * kAtcTileFloats, &map_qk, &sm.ld[t], D + h * kAtcDH, y);
+                    tc::tma_load_2d(sm.vh + t * kAtcTileFloats, &map_v, &sm.ld[t], 2 * D + h * kAtcDH, y);
+                }
             }
             // ---------------- MMA issuer ----------------
             const uint32_t qh = tc::smem_u32(sm.qh), ql = tc::smem_u32(sm.ql);
@@ -236,69 +249,57 @@ attention_fwd_tc_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid
                     atc_wait(sm.abort, err, kAtcErrMma, &sm.drained, 0);
                 }
                 tc::tc_fence_after();
-                // the key columns in two halves of nh keys each: independent
-                // accumulators whose MMAs interleave (B rows are 128 bytes)
+                // this role's half of the key columns (nh keys; B rows are
+                // 128 bytes); corrections (hi*lo, lo*hi) first, then hi*hi;
+                // descriptors built once, k-step k at + 32 k bytes (+ 2 k in
+                // the start address field)
                 const uint32_t nh = kAtcTile * (t + 1) / 2;
                 const uint32_t idesc_s = tc::idesc_tf32(kAtcTile, nh, false, false);
                 const uint32_t qo = uint32_t(t) * kAtcTileFloats * 4;
-                // corrections (hi*lo, lo*hi) first, then hi*hi
-                // descriptors built once, k-step k at + 32 k bytes (+ 2 k in
-                // the start address field)
-                const uint64_t ah = tc::smem_desc(qh + qo, 16, 1024, tc::kLayoutSw128);
-                const uint64_t al = tc::smem_desc(ql + qo, 16, 1024, tc::kLayoutSw128);
-                uint64_t bh[2], bl[2];
+                {
+                    const uint64_t ah = tc::smem_desc(qh + qo, 16, 1024, tc::kLayoutSw128);
+                    const uint64_t al = tc::smem_desc(ql + qo, 16, 1024, tc::kLayoutSw128);
+                    const uint64_t bh = tc::smem_desc(kh + uint32_t(role) * nh * 128, 16, 1024, tc::kLayoutSw128);
+                    const uint64_t bl = tc::smem_desc(kl + uint32_t(role) * nh * 128, 16, 1024, tc::kLayoutSw128);
+                    const uint32_t d = tmem + kAtcColS + uint32_t(role) * nh;
 #pragma unroll
-                for (uint32_t j = 0; j < 2; ++j) {
-                    bh[j] = tc::smem_desc(kh + j * nh * 128, 16, 1024, tc::kLayoutSw128);
-                    bl[j] = tc::smem_desc(kl + j * nh * 128, 16, 1024, tc::kLayoutSw128);
-                }
-#pragma unroll
-                for (int k = 0; k < kAtcDH / 8; ++k)
-#pragma unroll
-                    for (uint32_t j = 0; j < 2; ++j) {
-                        tc::mma_tf32(tmem + kAtcColS + j * nh, ah + 2 * k, bl[j] + 2 * k, idesc_s, k > 0 ? 1u : 0u);
-                        tc::mma_tf32(tmem + kAtcColS + j * nh, al + 2 * k, bh[j] + 2 * k, idesc_s, 1u);
+                    for (int k = 0; k < kAtcDH / 8; ++k) {
+                        tc::mma_tf32(d, ah + 2 * k, bl + 2 * k, idesc_s, k > 0 ? 1u : 0u);
+                        tc::mma_tf32(d, al + 2 * k, bh + 2 * k, idesc_s, 1u);
                     }
 #pragma unroll
-                for (int k = 0; k < kAtcDH / 8; ++k)
-#pragma unroll
-                    for (uint32_t j = 0; j < 2; ++j)
-                        tc::mma_tf32(tmem + kAtcColS + j * nh, ah + 2 * k, bh[j] + 2 * k, idesc_s, 1u);
+                    for (int k = 0; k < kAtcDH / 8; ++k) tc::mma_tf32(d, ah + 2 * k, bh + 2 * k, idesc_s, 1u);
+                }
                 tc::mma_commit(&sm.s_ready);
                 const int nch = 4 * (t + 1);
-                // chunks in pairs: the two accumulators' MMAs interleave
-                for (int c = 0; c < nch; c += 2, gch += 2) {
-                    uint32_t d[2], ahi[2], alo[2], bhi[2], blo[2];
-#pragma unroll
-                    for (int j = 0; j < 2; ++j) {
-                        const uint32_t g = gch + j;
-                        const uint32_t slot = g % kAtcRing;
-                        atc_wait(sm.abort, err, kAtcErrMma, &sm.ring_full[slot], (g / kAtcRing) & 1);
-                        // chunk g - 4's MMAs (two pairs back) have completed,
-                        // so the S columns that chunk c + j - 4 read are free
-                        // for this result while the previous pair still runs
-                        if (g >= 4) atc_wait(sm.abort, err, kAtcErrMma, &sm.pv_chunk[g & 3], ((g >> 2) & 1) ^ 1);
-                        d[j] = atc_fwd_acc(tmem, c + j);
-                        ahi[j] = tmem + kAtcColS + 32 * (c + j);
-                        alo[j] = tmem + kAtcColRing + 32 * slot;
-                        bhi[j] = vh + 32 * (c + j) * 128;  // V rows are 128-byte K-rows
-                        blo[j] = vl + 32 * (c + j) * 128;
-                    }
+                // this role's chunks c = role, role + 2, ...
+                for (int c = role; c < nch; c += 2) {
+                    const uint32_t g = gch + c;
+                    const uint32_t slot = g % kAtcRing;
+                    atc_wait(sm.abort, err, kAtcErrMma, &sm.ring_full[slot], (g / kAtcRing) & 1);
+                    // chunk g - 4's MMAs (this issuer's, two of its chunks
+                    // back) have completed, so the S columns that chunk c - 4
+                    // read are free for this result
+                    if (g >= 4) atc_wait(sm.abort, err, kAtcErrMma, &sm.pv_chunk[g & 3], ((g >> 2) & 1) ^ 1);
+                    const uint32_t d[1] = {atc_fwd_acc(tmem, c)};
+                    const uint32_t ahi[1] = {tmem + kAtcColS + 32 * c};
+                    const uint32_t alo[1] = {tmem + kAtcColRing + 32 * slot};
+                    const uint32_t bhi[1] = {vh + 32 * c * 128};  // V rows are 128-byte K-rows
+                    const uint32_t blo[1] = {vl + 32 * c * 128};
                     tc::tc_fence_after();
-                    atc_mma_chunks_mn<2>(d, ahi, alo, bhi, blo);
-#pragma unroll
-                    for (int j = 0; j < 2; ++j) {
-                        tc::mma_commit(&sm.ring_empty[(gch + j) % kAtcRing]);
-                        tc::mma_commit(&sm.pv_chunk[(gch + j) & 3]);
-                    }
+                    atc_mma_chunks_mn<1>(d, ahi, alo, bhi, blo);
+                    tc::mma_commit(&sm.ring_empty[slot]);
+                    tc::mma_commit(&sm.pv_chunk[g & 3]);
                 }
+                gch += nch;
                 tc::mma_commit(&sm.pv_done[t]);
             }
             // every MMA above has completed, and every load has landed,
             // before TMEM is freed and the CTA exits
             tc::mma_commit(&sm.drain);
             tc::mbar_wait(&sm.drain, 0);
-            for (int t = 0; t < ntile; ++t) tc::mbar_wait(&sm.ld[t], 0);
+            if (role == 0)
+                for (int t = 0; t < ntile; ++t) tc::mbar_wait(&sm.ld[t], 0);
         }
     } else {
         const int st = threadIdx.x;

@@ -169,7 +169,7 @@ void attn_fwd_tc_launch(hx_runtime* rt, const LmPlan& p, const float* qkv, float
     const CUtensorMap mv = make_map(qkv, w, rows, w, 32, kAtcTile, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
     HX_CUDA(cudaFuncSetAttribute(attention_fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)kAtcFwdSmemBytes));
-    ::hx::pdl_launch(attention_fwd_tc_kernel, dim3(p.H, p.B), kAtcThreads, kAtcFwdSmemBytes, rt->stream, 
+    ::hx::pdl_launch(attention_fwd_tc_kernel, dim3(p.H, p.B), kAtcFwdThreads, kAtcFwdSmemBytes, rt->stream, 
         mqk, mv, p.T, p.D, p.H, 1.0f / sqrtf((float)kAtcDH), qkv, ctx, rmax, rsum, rt->device_error());
     HX_LAUNCHED(rt);
 }
