@@ -60,10 +60,10 @@ constexpr int kAtcSoftThreads = 32 * kAtcSoftWarps;
 constexpr int kAtcThreads = kAtcSoftThreads + 32;
 constexpr int kAtcRing = 4;
 constexpr uint32_t kAtcCols = 512, kAtcColS = 0, kAtcColO = 256, kAtcColRing = 384;
-// The forward runs two MMA-issuing warps beside the softmax warps: one issues
-// the loads, the first S column half and the even chunks' E V products, the
-// other the second half and the odd chunks.
-constexpr int kAtcFwdIssuers = 2;
+// The forward runs four MMA-issuing warps beside the softmax warps, one per
+// warp scheduler: issuer r issues the E V products of the chunks c = r mod 4;
+// issuers 0 and 1 also issue the two S column halves, and issuer 0 the loads.
+constexpr int kAtcFwdIssuers = 4;
 constexpr int kAtcFwdThreads = kAtcSoftThreads + 32 * kAtcFwdIssuers;
 constexpr int kAtcTileFloats = kAtcTile * kAtcDH;  // 128 rows x 32 fp32 = 16 KB
 constexpr float kAtcLog2e = 1.4426950408889634f;
@@ -184,9 +184,9 @@ attention_fwd_tc_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid
         for (int i = 0; i < 2; ++i) {
             tc::mbar_init(&sm.ld[i], 1);
             tc::mbar_init(&sm.conv[i], kAtcSoftThreads);
-            tc::mbar_init(&sm.pv_done[i], kAtcFwdIssuers);  // both issuers commit
+            tc::mbar_init(&sm.pv_done[i], kAtcFwdIssuers);  // every issuer commits
         }
-        tc::mbar_init(&sm.s_ready, kAtcFwdIssuers);
+        tc::mbar_init(&sm.s_ready, 2);  // the two issuers of the S halves
         for (int i = 0; i < 4; ++i) tc::mbar_init(&sm.pv_chunk[i], 1);
         for (int i = 0; i < kAtcRing; ++i) {
             tc::mbar_init(&sm.ring_full[i], 4);  // the four warps that own a chunk's 128 lanes
@@ -216,11 +216,12 @@ attention_fwd_tc_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid
     }
 
     if (warp >= kAtcSoftWarps) {
-        // role 0: the loads, S column half 0 and the even chunks; role 1: S
-        // column half 1 and the odd chunks.  Chunk g's ring slot (g % 4) and
-        // accumulator barrier (g & 3) have g's parity, so each belongs to one
-        // issuer; s_ready, pv_done and drain count both issuers' commits.
-        // Every accumulator gets its MMAs in the single-issuer order.
+        // role r < 2: S column half r (role 0 also the loads); every role:
+        // the chunks c = r mod 4.  Chunk g's ring slot (g % 4) and
+        // accumulator barrier (g & 3) equal its role, so each belongs to one
+        // issuer; pv_done and drain count every issuer's commit, s_ready the
+        // two S issuers'.  Every accumulator gets its MMAs in the
+        // single-issuer order.
         const int role = warp - kAtcSoftWarps;
         if (lane == 0) {
             if (role == 0) {
@@ -256,7 +257,7 @@ attention_fwd_tc_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid
                 const uint32_t nh = kAtcTile * (t + 1) / 2;
                 const uint32_t idesc_s = tc::idesc_tf32(kAtcTile, nh, false, false);
                 const uint32_t qo = uint32_t(t) * kAtcTileFloats * 4;
-                {
+                if (role < 2) {
                     const uint64_t ah = tc::smem_desc(qh + qo, 16, 1024, tc::kLayoutSw128);
                     const uint64_t al = tc::smem_desc(ql + qo, 16, 1024, tc::kLayoutSw128);
                     const uint64_t bh = tc::smem_desc(kh + uint32_t(role) * nh * 128, 16, 1024, tc::kLayoutSw128);
@@ -270,16 +271,16 @@ attention_fwd_tc_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid
 #pragma unroll
                     for (int k = 0; k < kAtcDH / 8; ++k) tc::mma_tf32(d, ah + 2 * k, bh + 2 * k, idesc_s, 1u);
                 }
-                tc::mma_commit(&sm.s_ready);
+                if (role < 2) tc::mma_commit(&sm.s_ready);
                 const int nch = 4 * (t + 1);
-                // this role's chunks c = role, role + 2, ...
-                for (int c = role; c < nch; c += 2) {
+                // this role's chunks c = role, role + 4
+                for (int c = role; c < nch; c += kAtcFwdIssuers) {
                     const uint32_t g = gch + c;
                     const uint32_t slot = g % kAtcRing;
                     atc_wait(sm.abort, err, kAtcErrMma, &sm.ring_full[slot], (g / kAtcRing) & 1);
-                    // chunk g - 4's MMAs (this issuer's, two of its chunks
-                    // back) have completed, so the S columns that chunk c - 4
-                    // read are free for this result
+                    // chunk g - 4's MMAs (this issuer's previous chunk) have
+                    // completed, so the S columns that chunk c - 4 read are
+                    // free for this result
                     if (g >= 4) atc_wait(sm.abort, err, kAtcErrMma, &sm.pv_chunk[g & 3], ((g >> 2) & 1) ^ 1);
                     const uint32_t d[1] = {atc_fwd_acc(tmem, c)};
                     const uint32_t ahi[1] = {tmem + kAtcColS + 32 * c};
