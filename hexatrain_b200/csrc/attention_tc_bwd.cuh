@@ -410,8 +410,11 @@ attention_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap map_qk, const __g
 // ---- dK / dV kernel ----------------------------------------------------------
 
 constexpr uint32_t kKvColS = 0, kKvColDp = 128, kKvColRing = 256, kKvColAcc = 384;
-// 16 softmax warps and two MMA-issuing warps (one per product chain)
-constexpr int kAtcKvIssuers = 2;
+// 16 softmax warps and four MMA-issuing warps, one per warp scheduler: issuer
+// r takes product chain r & 1 (0: S^T and dV, 1: dP^T and dK) for the chunks
+// of parity r >> 1; issuers 0 and 1 also issue S^T and dP^T, issuer 0 the
+// loads.
+constexpr int kAtcKvIssuers = 4;
 constexpr int kAtcKvThreads = kAtcSoftThreads + 32 * kAtcKvIssuers;
 
 struct AtcKvSmem {
@@ -467,15 +470,14 @@ attention_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap map_qk, const _
         tc::mbar_init(&sm.ld_q, 1);
         tc::mbar_init(&sm.conv_kv, kAtcSoftThreads);
         tc::mbar_init(&sm.conv_q, kAtcSoftThreads);
-        // committed to by both issuers
-        tc::mbar_init(&sm.sd_ready, kAtcKvIssuers);
-        tc::mbar_init(&sm.blk_done, kAtcKvIssuers);
+        tc::mbar_init(&sm.sd_ready, 2);              // the S^T and dP^T issuers
+        tc::mbar_init(&sm.blk_done, kAtcKvIssuers);  // every issuer
         tc::mbar_init(&sm.drained, kAtcSoftWarps);
         tc::mbar_init(&sm.drain, kAtcKvIssuers);
         for (int i = 0; i < 2; ++i) {
             tc::mbar_init(&sm.ring_full[i], 4);
-            tc::mbar_init(&sm.ring_empty[i], kAtcKvIssuers);
-            tc::mbar_init(&sm.kv_chunk[i], kAtcKvIssuers);
+            tc::mbar_init(&sm.ring_empty[i], 2);  // the two chains' issuers of slot i's parity
+            tc::mbar_init(&sm.kv_chunk[i], 2);
         }
         sm.abort = 0;
         tc::fence_mbar_init();
@@ -509,12 +511,15 @@ attention_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap map_qk, const _
         }
     }
     if (warp >= kAtcSoftWarps) {
-        // Two issuers, one per product chain, on two warp schedulers:
-        // role 0 issues the TMA loads, S^T = K Q^T and dV_c = P^T_c dO_c;
-        // role 1 issues dP^T = V dO^T and dK_c = dS^T_c Q_c.  Each chain's
-        // MMAs keep the single-issuer term order, so the results are the
-        // same bit for bit; the barriers the chains share count both commits.
+        // Four issuers on the four warp schedulers.  Chain role & 1: 0 is
+        // S^T = K Q^T and dV_c = P^T_c dO_c, 1 is dP^T = V dO^T and
+        // dK_c = dS^T_c Q_c; issuers 0 and 1 issue S^T and dP^T (and 0 the
+        // TMA loads), issuer r the chunks c of parity r >> 1, so chunk g's
+        // ring slot and accumulator barrier (g & 1) belong to the two
+        // issuers of that parity.  Each accumulator's MMAs keep the
+        // single-issuer term order, so the results are the same bit for bit.
         const int role = warp - kAtcSoftWarps;
+        const int chain = role & 1, par = role >> 1;
         if (lane == 0) {
             const int yk = y0 + kAtcTile * kb;
             if (role == 0) {
@@ -529,12 +534,12 @@ attention_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap map_qk, const _
             // this chain's A operand of the S^T / dP^T product (K or V) and
             // B operand (Q or dO, K-major); its chunk products' B (dO or Q,
             // MN-major)
-            const uint32_t ah = tc::smem_u32(role ? sm.vh : sm.kh), al = tc::smem_u32(role ? sm.vl : sm.kl);
-            const uint32_t bh = tc::smem_u32(role ? sm.oh : sm.qh), bl = tc::smem_u32(role ? sm.ol : sm.ql);
-            const uint32_t mh = tc::smem_u32(role ? sm.qmh : sm.omh), ml = tc::smem_u32(role ? sm.qml : sm.oml);
-            const uint32_t col_sd = role ? kKvColDp : kKvColS;
+            const uint32_t ah = tc::smem_u32(chain ? sm.vh : sm.kh), al = tc::smem_u32(chain ? sm.vl : sm.kl);
+            const uint32_t bh = tc::smem_u32(chain ? sm.oh : sm.qh), bl = tc::smem_u32(chain ? sm.ol : sm.ql);
+            const uint32_t mh = tc::smem_u32(chain ? sm.qmh : sm.omh), ml = tc::smem_u32(chain ? sm.qml : sm.oml);
+            const uint32_t col_sd = chain ? kKvColDp : kKvColS;
             constexpr uint32_t idesc_s = tc::idesc_tf32(kAtcTile, kAtcTile, false, false);
-            uint32_t g = 0;  // chunks issued (ring and accumulator position)
+            uint32_t g0 = 0;  // chunks of earlier blocks (ring and accumulator position)
             for (int i = 0; i < nqb; ++i) {
                 const int qb = kb + i;
                 // the previous block's MMAs are done before its tiles are overwritten
@@ -555,7 +560,7 @@ attention_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap map_qk, const _
                 // S^T = K Q^T or dP^T = V dO^T (A from shared memory; hi*lo
                 // and lo*hi per k-step, then hi*hi; descriptors built once,
                 // k-step k at + 2 k in the start address field)
-                {
+                if (role < 2) {
                     const uint64_t dah = tc::smem_desc(ah, 16, 1024, tc::kLayoutSw128);
                     const uint64_t dal = tc::smem_desc(al, 16, 1024, tc::kLayoutSw128);
                     const uint64_t dbh = tc::smem_desc(bh, 16, 1024, tc::kLayoutSw128);
@@ -569,11 +574,12 @@ attention_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap map_qk, const _
 #pragma unroll
                     for (int k = 0; k < kAtcDH / 8; ++k) tc::mma_tf32(d, dah + 2 * k, dbh + 2 * k, idesc_s, 1u);
                 }
-                tc::mma_commit(&sm.sd_ready);
-                // per 32-query chunk: dV_c = P^T_c dO_c (role 0) or
-                // dK_c = dS^T_c Q_c (role 1); chunk c's slot in the 2-slot lo
-                // ring is g & 1
-                for (int c = 0; c < 4; ++c, ++g) {
+                if (role < 2) tc::mma_commit(&sm.sd_ready);
+                // per 32-query chunk of this issuer's parity: dV_c = P^T_c dO_c
+                // (chain 0) or dK_c = dS^T_c Q_c (chain 1); chunk c's slot in
+                // the 2-slot lo ring is g & 1
+                for (int c = par; c < 4; c += 2) {
+                    const uint32_t g = g0 + c;
                     const int slot = g & 1;
                     atc_wait(sm.abort, err, kAtcErrMma, &sm.ring_full[slot], (g >> 1) & 1);
                     // chunk g - 2's MMAs (both chains) have completed, so the
@@ -582,14 +588,15 @@ attention_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap map_qk, const _
                     if (g >= 2) atc_wait(sm.abort, err, kAtcErrMma, &sm.kv_chunk[g & 1], ((g >> 1) & 1) ^ 1);
                     tc::tc_fence_after();
                     const uint32_t row = uint32_t(32 * c) * 128;
-                    const uint32_t d[1] = {tmem + atc_kv_acc(c, role == 1)};
+                    const uint32_t d[1] = {tmem + atc_kv_acc(c, chain == 1)};
                     const uint32_t ahi[1] = {tmem + col_sd + 32 * c};
-                    const uint32_t alo[1] = {tmem + kKvColRing + 64 * slot + (role ? 32u : 0u)};
+                    const uint32_t alo[1] = {tmem + kKvColRing + 64 * slot + (chain ? 32u : 0u)};
                     const uint32_t bhi[1] = {mh + row}, blo[1] = {ml + row};
                     atc_mma_chunks_mn<1>(d, ahi, alo, bhi, blo);
                     tc::mma_commit(&sm.ring_empty[slot]);
                     tc::mma_commit(&sm.kv_chunk[g & 1]);
                 }
+                g0 += 4;
                 tc::mma_commit(&sm.blk_done);
             }
             tc::mma_commit(&sm.drain);
