@@ -48,6 +48,11 @@ namespace hx {
 // ---- dQ kernel ---------------------------------------------------------------
 
 constexpr uint32_t kDqColQ = 0, kDqColDo = 64, kDqColS = 128, kDqColDp = 256, kDqColAcc = 384;
+// 16 softmax warps and four MMA-issuing warps, one per warp scheduler:
+// issuer r issues the dQ products of chunk r; issuer 0 also the loads and S,
+// issuer 1 dP
+constexpr int kAtcDqIssuers = 4;
+constexpr int kAtcDqThreads = kAtcSoftThreads + 32 * kAtcDqIssuers;
 
 struct AtcDqSmem {
     float kh[2 * kAtcTileFloats], kl[2 * kAtcTileFloats];    // K, K-major
@@ -117,6 +122,21 @@ __device__ __forceinline__ void atc_mma_ts_kmajor2(const uint32_t (&d)[2], const
         for (int j = 0; j < 2; ++j) tc::mma_tf32_ts(d[j], a_col[j] + 8 * k, bh[j] + 2 * k, idesc, 1u);
 }
 
+// The same for one product D = A B^T over K = 32 (A hi/lo in TMEM at a_col,
+// B hi/lo K-major in shared memory), in the same term order.
+__device__ __forceinline__ void atc_mma_ts_kmajor1(uint32_t d, uint32_t a_col, uint32_t b_hi, uint32_t b_lo,
+                                                   uint32_t idesc) {
+    const uint64_t bh = tc::smem_desc(b_hi, 16, 1024, tc::kLayoutSw128);
+    const uint64_t bl = tc::smem_desc(b_lo, 16, 1024, tc::kLayoutSw128);
+#pragma unroll
+    for (int k = 0; k < kAtcDH / 8; ++k) {
+        tc::mma_tf32_ts(d, a_col + 8 * k, bl + 2 * k, idesc, k > 0 ? 1u : 0u);
+        tc::mma_tf32_ts(d, a_col + 32 + 8 * k, bh + 2 * k, idesc, 1u);
+    }
+#pragma unroll
+    for (int k = 0; k < kAtcDH / 8; ++k) tc::mma_tf32_ts(d, a_col + 8 * k, bh + 2 * k, idesc, 1u);
+}
+
 // Visibility of a 32-key chunk (keys 128 kb + 32 c ..) to the 32 query rows
 // 128 t + 32 q .. of a warp: 2 all visible, 1 diagonal, 0 none.
 __device__ __forceinline__ int atc_chunk_vis(int t, int q, int kb, int c, bool rows_valid) {
@@ -125,7 +145,7 @@ __device__ __forceinline__ int atc_chunk_vis(int t, int q, int kb, int c, bool r
     return c == q ? 1 : 0;
 }
 
-__global__ void __launch_bounds__(kAtcThreads, 1)
+__global__ void __launch_bounds__(kAtcDqThreads, 1)
 attention_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid_constant__ CUtensorMap map_mn, int T,
                            int D, int H, float scale, const float* __restrict__ qkv, const float* __restrict__ dctx,
                            const float* __restrict__ row_max, float* __restrict__ bstat, float* __restrict__ dqkv,
@@ -144,10 +164,11 @@ attention_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap map_qk, const __g
         tc::mbar_init(&sm.ld, 1);
         tc::mbar_init(&sm.conv, kAtcSoftThreads);
         tc::mbar_init(&sm.a_ready, kAtcSoftWarps);
-        tc::mbar_init(&sm.sd_ready, 1);
+        // S and dP by issuers 0 and 1; dq_done and drain by every issuer
+        tc::mbar_init(&sm.sd_ready, 2);
         tc::mbar_init(&sm.sd_free, kAtcSoftWarps);
-        tc::mbar_init(&sm.dq_done, 1);
-        tc::mbar_init(&sm.drain, 1);
+        tc::mbar_init(&sm.dq_done, kAtcDqIssuers);
+        tc::mbar_init(&sm.drain, kAtcDqIssuers);
         for (int i = 0; i < 4; ++i) {
             tc::mbar_init(&sm.ds_full[i], 4);
             tc::mbar_init(&sm.acc_full[i], 1);
@@ -177,22 +198,33 @@ attention_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap map_qk, const __g
                 atc_prefetch_rows(qkv, 3L * D, part * D + nh * kAtcDH, ny, ny + T, threadIdx.x, kAtcSoftThreads);
         }
     }
-    if (warp == kAtcSoftWarps) {
+    if (warp >= kAtcSoftWarps) {
+        // Four issuers on the four warp schedulers: issuer r issues the dQ
+        // products of chunk r, issuer 0 also the TMA loads and S, issuer 1
+        // dP.  Each accumulator gets its MMAs in the single-issuer order, so
+        // the results are the same bit for bit; sd_ready counts the S and dP
+        // issuers' commits, dq_done and drain every issuer's.
+        const int role = warp - kAtcSoftWarps;
         if (lane == 0) {
-            // ---------------- loads: K, V (K-major) and K (MN-major), all rows
-            tc::prefetch_tensormap(&map_qk);
-            tc::prefetch_tensormap(&map_mn);
-            tc::mbar_arrive_expect_tx(&sm.ld, 3 * ntile * kAtcTileFloats * 4);
-            for (int t = 0; t < ntile; ++t) {
-                const int y = y0 + kAtcTile * t;
-                tc::tma_load_2d(sm.kh + t * kAtcTileFloats, &map_qk, &sm.ld, D + h * kAtcDH, y);
-                tc::tma_load_2d(sm.vh + t * kAtcTileFloats, &map_qk, &sm.ld, 2 * D + h * kAtcDH, y);
-                tc::tma_load_2d(sm.kmh + t * kAtcTileFloats, &map_mn, &sm.ld, D + h * kAtcDH, y);
+            if (role == 0) {
+                // ---------------- loads: K, V (K-major) and K (MN-major), all rows
+                tc::prefetch_tensormap(&map_qk);
+                tc::prefetch_tensormap(&map_mn);
+                tc::mbar_arrive_expect_tx(&sm.ld, 3 * ntile * kAtcTileFloats * 4);
+                for (int t = 0; t < ntile; ++t) {
+                    const int y = y0 + kAtcTile * t;
+                    tc::tma_load_2d(sm.kh + t * kAtcTileFloats, &map_qk, &sm.ld, D + h * kAtcDH, y);
+                    tc::tma_load_2d(sm.vh + t * kAtcTileFloats, &map_qk, &sm.ld, 2 * D + h * kAtcDH, y);
+                    tc::tma_load_2d(sm.kmh + t * kAtcTileFloats, &map_mn, &sm.ld, D + h * kAtcDH, y);
+                }
             }
             // ---------------- MMA issuer ----------------
-            const uint32_t kh = tc::smem_u32(sm.kh), kl = tc::smem_u32(sm.kl);
-            const uint32_t vh = tc::smem_u32(sm.vh), vl = tc::smem_u32(sm.vl);
+            // this role's product: S = Q K^T (role 0) or dP = dO V^T (role 1)
+            const uint32_t bh0 = tc::smem_u32(role == 1 ? sm.vh : sm.kh), bl0 = tc::smem_u32(role == 1 ? sm.vl : sm.kl);
+            const uint32_t d_sd = tmem + (role == 1 ? kDqColDp : kDqColS);
+            const uint32_t a_sd = tmem + (role == 1 ? kDqColDo : kDqColQ);
             const uint32_t kmh = tc::smem_u32(sm.kmh), kml = tc::smem_u32(sm.kml);
+            const int c = role;  // this issuer's dQ chunk
             constexpr uint32_t idesc_s = tc::idesc_tf32(kAtcTile, kAtcTile, false, false);
             atc_wait(sm.abort, err, kAtcErrMma, &sm.conv, 0);
             uint32_t v = 0, u = 0;  // S/dP blocks issued, pass-B blocks issued
@@ -209,33 +241,26 @@ attention_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap map_qk, const __g
                         if (dq_pending) atc_wait(sm.abort, err, kAtcErrMma, &sm.dq_done, (u - 1) & 1);
                         dq_pending = false;
                         tc::tc_fence_after();
-                        if (pass == 0 || i > 0) {
+                        if (role < 2 && (pass == 0 || i > 0)) {
                             const uint32_t ko = uint32_t(kb) * kAtcTileFloats * 4;
-                            const uint32_t d[2] = {tmem + kDqColS, tmem + kDqColDp};
-                            const uint32_t a[2] = {tmem + kDqColQ, tmem + kDqColDo};
-                            const uint32_t bh[2] = {kh + ko, vh + ko}, bl[2] = {kl + ko, vl + ko};
-                            atc_mma_ts_kmajor2(d, a, bh, bl, idesc_s);
+                            atc_mma_ts_kmajor1(d_sd, a_sd, bh0 + ko, bl0 + ko, idesc_s);
                         }
-                        tc::mma_commit(&sm.sd_ready);
+                        if (role < 2) tc::mma_commit(&sm.sd_ready);
                         ++v;
                         if (pass == 0) continue;
-                        // the four chunks' dQ products, their MMAs interleaved
-                        uint32_t d[4], ahi[4], alo[4], bhi[4], blo[4];
-#pragma unroll
-                        for (int c = 0; c < 4; ++c) {
-                            atc_wait(sm.abort, err, kAtcErrMma, &sm.ds_full[c], u & 1);
-                            atc_wait(sm.abort, err, kAtcErrMma, &sm.acc_empty[c], (u & 1) ^ 1);
+                        // this issuer's chunk's dQ product
+                        atc_wait(sm.abort, err, kAtcErrMma, &sm.ds_full[c], u & 1);
+                        atc_wait(sm.abort, err, kAtcErrMma, &sm.acc_empty[c], (u & 1) ^ 1);
+                        {
                             const uint32_t row = uint32_t(kAtcTile * kb + 32 * c) * 128;
-                            d[c] = tmem + kDqColAcc + 32 * c;
-                            ahi[c] = tmem + kDqColS + 32 * c;
-                            alo[c] = tmem + kDqColDp + 32 * c;
-                            bhi[c] = kmh + row;
-                            blo[c] = kml + row;
+                            const uint32_t d[1] = {tmem + kDqColAcc + 32 * c};
+                            const uint32_t ahi[1] = {tmem + kDqColS + 32 * c};
+                            const uint32_t alo[1] = {tmem + kDqColDp + 32 * c};
+                            const uint32_t bhi[1] = {kmh + row}, blo[1] = {kml + row};
+                            tc::tc_fence_after();
+                            atc_mma_chunks_mn<1>(d, ahi, alo, bhi, blo);
                         }
-                        tc::tc_fence_after();
-                        atc_mma_chunks_mn<4>(d, ahi, alo, bhi, blo);
-#pragma unroll
-                        for (int c = 0; c < 4; ++c) tc::mma_commit(&sm.acc_full[c]);
+                        tc::mma_commit(&sm.acc_full[c]);
                         tc::mma_commit(&sm.dq_done);
                         ++u;
                         dq_pending = true;
@@ -244,7 +269,7 @@ attention_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap map_qk, const __g
             }
             tc::mma_commit(&sm.drain);
             tc::mbar_wait(&sm.drain, 0);
-            tc::mbar_wait(&sm.ld, 0);
+            if (role == 0) tc::mbar_wait(&sm.ld, 0);
         }
     } else {
         const int st = threadIdx.x;

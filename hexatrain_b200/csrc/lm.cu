@@ -212,7 +212,7 @@ void attn_bwd_tc_launch(hx_runtime* rt, const LmPlan& p, const float* qkv, const
     const float scale = 1.0f / sqrtf((float)kAtcDH);
     HX_CUDA(cudaFuncSetAttribute(attention_bwd_dq_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)kAtcDqSmemBytes));
-    ::hx::pdl_launch(attention_bwd_dq_tc_kernel, dim3(p.H, p.B), kAtcThreads, kAtcDqSmemBytes, rt->stream, 
+    ::hx::pdl_launch(attention_bwd_dq_tc_kernel, dim3(p.H, p.B), kAtcDqThreads, kAtcDqSmemBytes, rt->stream, 
         mqk, mmn, p.T, p.D, p.H, scale, qkv, dctx, rmax, bstat, dqkv, rt->device_error());
     HX_LAUNCHED(rt);
     HX_CUDA(cudaFuncSetAttribute(attention_bwd_dkdv_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
