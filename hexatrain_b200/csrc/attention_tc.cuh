@@ -7,10 +7,13 @@
 //
 // Forward (tiny_language_model_cpu.cpp:44-45: scores, causal softmax,
 // context), one CTA per (head, sequence), query rows in tiles of 128:
-//   warp 16 lane 0 TMA: Q, K, V rows [128t, 128t+128) of this head for each
-//                  tile t, Q/K in the 128-byte swizzle (K-major operands),
-//                  V in the 128-byte/32-byte-atom swizzle (MN-major B);
-//                  then the MMA issuer.
+//   warps 16-19    lane 0 of each issues MMAs, one issuing warp per warp
+//                  scheduler: warp 16 + r issues the E V products of the
+//                  chunks c = r mod 4, warps 16 and 17 the two S column
+//                  halves, and warp 16 first the TMA loads: Q, K, V rows
+//                  [128t, 128t+128) of this head for each tile t, Q/K in the
+//                  128-byte swizzle (K-major operands), V in the
+//                  128-byte/32-byte-atom swizzle (MN-major B).
 //   warps 0-15     split each landed tile into hi (in place) and lo (tile
 //                  1 after tile 0's pass 2); the softmax of tile t, one
 //                  TMEM lane (query row) per
@@ -306,7 +309,7 @@ attention_fwd_tc_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid
         const int st = threadIdx.x;
         const int q = warp & 3, grp = warp >> 2;
         // ---------------- hi/lo split of a landed tile ----------------
-        // tile 0 here; tile 1 after tile 0's pass 2, while the MMA issuer
+        // tile 0 here; tile 1 after tile 0's pass 2, while the MMA issuers
         // runs tile 0's E V, so that it does not compete with the S MMAs of
         // tile 0 for shared memory
         auto split_tile = [&](int t) {
@@ -358,7 +361,7 @@ attention_fwd_tc_kernel(const __grid_constant__ CUtensorMap map_qk, const __grid
             float oacc[8];
 #pragma unroll
             for (int i = 0; i < 8; ++i) oacc[i] = 0.f;
-            // pass 2: e, its hi/lo split, the hand-over to the MMA issuer
+            // pass 2: e, its hi/lo split, the hand-over to the MMA issuers
             for (int c = grp; c < nch; c += kAtcGroups) {
                 const uint32_t g = gch + c;
                 const int slot = g % kAtcRing;

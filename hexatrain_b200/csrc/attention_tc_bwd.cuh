@@ -35,8 +35,10 @@
 //   thread adds into FP32 registers once the block's MMAs have completed.
 // Thread layout in both: 16 warps of four groups (warp w: TMEM lane quadrant
 // w % 4, group w / 4 owns 32-column chunk w / 4 of each 128-column block;
-// each thread drains 8 of the 32 output columns) plus one warp whose lane 0
-// issues the TMA loads and the MMAs.  Waits are bounded as in the forward.
+// each thread drains 8 of the 32 output columns) plus four warps, one per
+// warp scheduler, whose lane 0 issues MMAs (the split is given at each
+// kernel); the first of them also issues the TMA loads.  Waits are bounded
+// as in the forward.
 #pragma once
 
 #include "pdl.cuh"
@@ -361,7 +363,7 @@ attention_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap map_qk, const __g
 #pragma unroll
             for (int i = 0; i < 8; ++i) dq[i] = 0.f;
             for (int i = 0; i <= t; ++i, ++v, ++u) {
-                const int kb = t - i;  // the MMA issuer's pass-B order
+                const int kb = t - i;  // the MMA issuers' pass-B order
                 atc_wait(sm.abort, err, kAtcErrSoftmax, &sm.sd_ready, v & 1);
                 tc::tc_fence_after();
                 const int vis = atc_chunk_vis(t, q, kb, grp, rows_valid);
